@@ -1,0 +1,377 @@
+#!/usr/bin/env python3
+"""Benchmark of the MiniMax-M2.7 MoE block (decode, T = 1 token) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--layers L]
+
+Workload: one MoE block per step for one token — router f32 [256, 3072],
+sigmoid + bias top-8, 8 experts with Q4_K gate/up [1536, 3072] and Q5_K down [3072, 1536],
+Q8_1 activations, + residual.  Each step uses the next of L synthetic layers (default 8 x 2.19 GB
+of expert weights, a 17.5 GB working set that defeats the 126 MB L2 between consecutive uses of
+a layer) and a fresh seeded token.  Steps are replayed from CUDA graphs of up to 64 launches.
+
+One JSON line is printed by rank 0.  `value` = MoE-block tokens/s (whole job), device-timed with
+CUDA events; `e2e` = the same through the public API with the token copied from pinned host
+memory and the output copied back inside every step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+E, H, I, TOPK = 256, 3072, 1536, 8
+Q4K, Q5K = 1, 4
+SEED = 1001  # config index 1 x 1000 + 1
+
+
+def algorithmic_bytes(E=E, H=H, I=I, residual=True) -> int:
+    """Bytes one decode MoE block must move: the router, 8 experts' Q4_K gate/up + Q5_K down,
+    the token, the residual and the output."""
+    router = E * H * 4
+    experts = TOPK * (2 * I * (H // 256) * 144 + H * (I // 256) * 176)
+    return router + experts + H * 4 * (3 if residual else 2)
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+        except Exception:
+            pass
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples over the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path or not os.path.exists(self.path):
+            return None
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[4:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [r[0] for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3][1:]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(r[1] for r in rows),
+                "power_w_max": max(r[2] for r in rows), "samples": len(rows), "reasons": reasons}
+
+
+def build_layers(pkg, synth, dev, n_layers: int, inter: int = I, experts: int = E):
+    import torch
+    layers = []
+    for l in range(n_layers):
+        st = synth.layer_streams(l)
+        router = torch.empty(experts, H, dtype=torch.float32, device=dev)
+        pkg.synth_normal(router, SEED, st["router"], 0.02)
+        bias = torch.empty(experts, dtype=torch.float32, device=dev)
+        pkg.synth_normal(bias, SEED, st["bias"], 0.01)
+        gate = torch.empty(experts * inter * pkg.row_bytes(Q4K, H), dtype=torch.uint8, device=dev)
+        up = torch.empty_like(gate)
+        down = torch.empty(experts * H * pkg.row_bytes(Q5K, inter), dtype=torch.uint8, device=dev)
+        pkg.synth_kquant(gate, Q4K, SEED, st["gate"], experts, inter, H)
+        pkg.synth_kquant(up, Q4K, SEED, st["up"], experts, inter, H)
+        pkg.synth_kquant(down, Q5K, SEED, st["down"], experts, H, inter)
+        layers.append(pkg.MoeLayer(router, bias, gate, up, down, Q4K, Q5K))
+    return layers
+
+
+def cpu_decode_sample(layer, xs_host, res_host, budget_s: float):
+    """The CPU oracle (OpenMP, all host threads) on a bounded sample of decode tokens."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as orc
+    router = layer.router.cpu().numpy()
+    bias = layer.bias.cpu().numpy()
+    gate, up, down = layer.gate.cpu().numpy(), layer.up.cpu().numpy(), layer.down.cpu().numpy()
+    orc.moe_block(router, bias, gate, up, down, Q4K, Q5K, xs_host[0:1], res_host[0:1])  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        i = n % len(xs_host)
+        orc.moe_block(router, bias, gate, up, down, Q4K, Q5K, xs_host[i:i + 1], res_host[i:i + 1])
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s and n >= 3:
+            break
+    return n / el, n, el, orc.num_threads()
+
+
+def run_reference(args):
+    """Reference arm: the CPU restatement of the reference's MoE decode block (the reference's
+    own CPU path, Candle's quantized matmul, cannot be built here: no Rust toolchain), on all
+    host threads, same metric and config, each step one token."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+    import __graft_entry__ as ge
+    pkg, synth = ge.load_package(), ge.load_synth()
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    layer = build_layers(pkg, synth, dev, 1)[0]
+    xs = torch.empty(16, H, dtype=torch.float32, device=dev)
+    pkg.synth_normal(xs, SEED, 100, 1.0, bf16=True)
+    res = torch.empty(16, H, dtype=torch.float32, device=dev)
+    pkg.synth_normal(res, SEED, 101, 1.0)
+    torch.cuda.synchronize()
+    xs_h, res_h = xs.cpu().numpy(), res.cpu().numpy()
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as orc
+    router, bias = layer.router.cpu().numpy(), layer.bias.cpu().numpy()
+    gate, up, down = layer.gate.cpu().numpy(), layer.up.cpu().numpy(), layer.down.cpu().numpy()
+    del layer
+    torch.cuda.empty_cache()
+    for i in range(min(args.warmup, 3)):
+        orc.moe_block(router, bias, gate, up, down, Q4K, Q5K, xs_h[i:i + 1], res_h[i:i + 1])
+    budget = 60.0
+    n, t0 = 0, time.perf_counter()
+    while n < args.steps:
+        i = n % len(xs_h)
+        orc.moe_block(router, bias, gate, up, down, Q4K, Q5K, xs_h[i:i + 1], res_h[i:i + 1])
+        n += 1
+        if time.perf_counter() - t0 > budget:
+            break
+    el = time.perf_counter() - t0
+    v = n / el
+    out = {"metric": "moe_block_decode_tokens_per_s", "value": v, "unit": "tokens/s", "impl": "reference",
+           "n_gpus": args.gpus, "steps": n, "warmup": min(args.warmup, 3), "ms_per_step": 1e3 * el / n,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xq4k/q5k->f32",
+           "data": "synthetic (seeded, device-generated, copied to host)",
+           "config": {"workload": "decode T=1 MoE block (BASELINE configs[1]), 1 layer, fresh token per step",
+                      "experts": E, "hidden": H, "inter": I, "topk": TOPK, "gate_up": "Q4_K", "down": "Q5_K"},
+           "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": orc.num_threads(), "kind": "port",
+                            "sample": f"{n} decode tokens (time-bounded at {budget:.0f} s of the requested "
+                                      f"{args.steps} steps)"},
+           "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+           "note": "CPU restatement (oracle/moe_oracle.c) of the reference's GGUF MoE arithmetic; the "
+                   "reference's Candle CPU path is unavailable (no Rust toolchain on this box)"}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--layers", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=2000)
+    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import __graft_entry__ as ge
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    pkg, synth = ge.load_package(), ge.load_synth()
+    layers = build_layers(pkg, synth, dev, args.layers)
+    n_tok = 512
+    xs = torch.empty(n_tok, H, dtype=torch.float32, device=dev)
+    pkg.synth_normal(xs, SEED + rank, 100, 1.0, bf16=True)
+    res = torch.empty(n_tok, H, dtype=torch.float32, device=dev)
+    pkg.synth_normal(res, SEED + rank, 101, 1.0)
+    ys = torch.empty(n_tok, H, dtype=torch.float32, device=dev)
+    for L in layers:
+        L.workspace(1)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()
+
+    def step(i, s):
+        L = layers[i % len(layers)]
+        t = i % n_tok
+        L.forward(xs[t:t + 1], residual=res[t:t + 1], y=ys[t:t + 1], stream=s)
+
+    # CUDA graph of G consecutive steps (G multiple of the layer count)
+    G = max(len(layers), 64 // len(layers) * len(layers))
+    graphs = []
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i, stream)
+        stream.synchronize()
+        try:
+            for gi in range(n_tok // G if n_tok % G == 0 else 1):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    for j in range(G):
+                        step(gi * G + j, stream)
+                graphs.append(g)
+        except Exception as e:  # capture unsupported: fall back to direct launches
+            print(f"[bench] graph capture failed ({e}); timing direct launches", file=sys.stderr)
+            graphs = []
+    torch.cuda.synchronize()
+    for L in layers:
+        assert L.status() == 0, "device-side timeout during warm-up"
+
+    n_graph_reps = (args.steps + G - 1) // G if graphs else 0
+    steps = n_graph_reps * G if graphs else args.steps
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            if graphs:
+                for r in range(n_graph_reps):
+                    graphs[r % len(graphs)].replay()
+            else:
+                for i in range(steps):
+                    step(i, stream)
+            end.record(stream)
+        end.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    for L in layers:
+        assert L.status() == 0, "device-side timeout in the timed region"
+    ms_t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    clocks = clk.summary()
+
+    # e2e: public API, host buffers, copies inside every step
+    x_host = torch.empty(n_tok, H, dtype=torch.float32, pin_memory=True)
+    x_host.copy_(xs.cpu())
+    y_host = torch.empty(n_tok, H, dtype=torch.float32, pin_memory=True)
+    x_dev = torch.empty(1, H, dtype=torch.float32, device=dev)
+    y_dev = torch.empty(1, H, dtype=torch.float32, device=dev)
+    e2e_steps = min(args.e2e_steps, steps)
+    with torch.cuda.stream(stream):
+        for i in range(8):
+            t = i % n_tok
+            x_dev.copy_(x_host[t:t + 1], non_blocking=True)
+            layers[i % len(layers)].forward(x_dev, residual=res[t:t + 1], y=y_dev, stream=stream)
+            y_host[t:t + 1].copy_(y_dev, non_blocking=True)
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(e2e_steps):
+            t = i % n_tok
+            x_dev.copy_(x_host[t:t + 1], non_blocking=True)
+            layers[i % len(layers)].forward(x_dev, residual=res[t:t + 1], y=y_dev, stream=stream)
+            y_host[t:t + 1].copy_(y_dev, non_blocking=True)
+        e1.record(stream)
+        e1.synchronize()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms.item())
+
+    value = world * steps / (ms_max / 1e3)
+    e2e_value = world * e2e_steps / (e2e_ms / 1e3)
+    per_launch_s = (ms / 1e3) / steps
+    alg = algorithmic_bytes()
+    peaks = measured_peaks()
+    achieved = alg / per_launch_s / 1e9
+    traffic = None
+    tp = ROOT / "profiles" / "decode_traffic.json"
+    if tp.exists():
+        try:
+            traffic = json.loads(tp.read_text()).get("dram_bytes_per_launch")
+        except Exception:
+            traffic = None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, n, el, cores = cpu_decode_sample(layers[0], xs[:16].cpu().numpy(), res[:16].cpu().numpy(),
+                                            args.cpu_budget)
+        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"{n} decode tokens of layer 0 in {el:.1f} s (oracle/moe_oracle.c, OpenMP)"}
+
+    if rank == 0:
+        out = {
+            "metric": "moe_block_decode_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": ms_max / steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8xq4k/q5k->f32", "data": "synthetic",
+            "config": {"workload": "decode T=1 MoE block (BASELINE configs[1])", "experts": E, "hidden": H,
+                       "inter": I, "topk": TOPK, "gate_up": "Q4_K", "down": "Q5_K", "activations": "Q8_1",
+                       "residual": True, "layers_rotated": len(layers),
+                       "l2": f"inputs larger than L2: {len(layers)} layers x "
+                             f"{layers[0].gate.numel() * 2 + layers[0].down.numel() + E * H * 4:.3e} B rotated",
+                       "parallelism": "replicas" if world > 1 else "single GPU",
+                       "graph_steps": G if graphs else 0},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
+                         "peak_source": peaks["source"], "algorithmic_bytes_per_launch": alg,
+                         "kernel": "moe_decode_fused_kernel"},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": H * 4,
+                    "d2h_bytes_per_step": H * 4},
+            "gpu_launches": steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        graphs.clear()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,133 @@
+/*
+ * minimax_moe.h — C ABI of the B200-native MiniMax-M2.7 sparse-MoE hot path.
+ *
+ * Two groups of entry points:
+ *
+ *  1. Drop-in replacements for the reference's launchers.  Names, argument order and meaning
+ *     follow the reference's Rust FFI declarations (vendor/candle-kernels/src/ffi.rs) so that the
+ *     reference's `extern "C"` block links against this library unchanged.  Like the reference
+ *     they return void; host-side validation failures and launch errors are recorded in a
+ *     thread-local status readable with mmrs_last_error().  Device pointers and a CUDA stream
+ *     (passed as a handle, `i64` / `*mut c_void` on the Rust side) are the only arguments.
+ *
+ *  2. New fused entry points (prefix mmrs_) that return an int status (MMRS_OK == 0).
+ *
+ * All buffers are device memory owned by the caller unless stated otherwise.  Expert weights
+ * are raw GGUF block bytes laid out [experts][rows][k/256 blocks], rows contiguous (the layout
+ * of the reference's QTensor storage), 16-byte aligned.
+ */
+#ifndef MINIMAX_MOE_H
+#define MINIMAX_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *mmrs_stream_t; /* == cudaStream_t */
+
+#if defined(__GNUC__)
+#define MMRS_API __attribute__((visibility("default")))
+#else
+#define MMRS_API
+#endif
+
+/* ---- status codes ------------------------------------------------------------------- */
+#define MMRS_OK 0
+#define MMRS_ERR_ARG 1         /* invalid shape, pointer, alignment or enum                  */
+#define MMRS_ERR_UNSUPPORTED 2 /* GGUF type or shape this build does not implement          */
+#define MMRS_ERR_LAUNCH 3      /* CUDA launch / runtime error                                 */
+#define MMRS_ERR_TIMEOUT 4     /* a bounded device-side wait (grid barrier, peer flag) expired */
+#define MMRS_ERR_ALLOC 5       /* device allocation failed                                    */
+
+/* ---- GGUF type codes (candle-nn/src/moe.rs:293-306) ---------------------------------- */
+#define MMRS_Q8_0 0
+#define MMRS_Q4K 1
+#define MMRS_Q2K 2
+#define MMRS_Q3K 3
+#define MMRS_Q5K 4
+#define MMRS_Q6K 5
+
+/* ===================================================================================== */
+/* 1. Reference launchers (vendor/candle-kernels/src/ffi.rs)                              */
+/* ===================================================================================== */
+
+/* ffi.rs:41-49 — replaces moe_gguf.cu:94-100 (minimax_moe_decode_topk_kernel).
+ * logits[256], bias[256] f32 -> sigmoid, top-8 of sigmoid+bias, renormalised weights, plus the
+ * expert-id-sorted (expert_ids, route_ids) pair consumed by the decode MoE kernels. */
+MMRS_API void minimax_moe_decode_topk(const float *logits, const float *bias, uint32_t *topk_ids,
+                             float *topk_weights, uint32_t *expert_ids, uint32_t *route_ids,
+                             mmrs_stream_t stream);
+
+/* ffi.rs:51-67 — replaces moe_gguf.cu:426-567 (moe_gemm_gguf_decode_silu).
+ * One token, topk == 8: y[hidden] = sum_k w_k * down_k(silu(gate_k x) * up_k x).
+ * sorted_token_ids / expert_ids are the (route, expert) pairs in expert order; topk_weights is
+ * indexed by route.  Types: gate/up Q4_K or Q5_K, down Q4_K or Q5_K. */
+MMRS_API void moe_gemm_gguf_decode_silu(const float *input, const void *gate_weights,
+                               const void *up_weights, const void *down_weights,
+                               const int32_t *sorted_token_ids, const int32_t *expert_ids,
+                               const float *topk_weights, float *output, int num_experts,
+                               int topk, int hidden_size, int intermediate_size,
+                               int gate_up_gguf_dtype, int down_gguf_dtype, mmrs_stream_t stream);
+
+/* Status of the last reference-ABI call made by this host thread (MMRS_OK when it launched). */
+MMRS_API int mmrs_last_error(void);
+
+/* ===================================================================================== */
+/* 2. Fused MoE block                                                                     */
+/* ===================================================================================== */
+
+/* Weights of one MoE layer (one rank's shard under tensor parallelism).  Mirrors the fields of
+ * FusedMoeGGUF (vendor/candle-transformers/src/fused_moe.rs:162-175). */
+typedef struct {
+    const float *router; /* [num_experts][hidden] f32 (ffn_gate_inp, dequantised)        */
+    const float *bias;   /* [num_experts] f32 (exp_probs_b, e_score_correction_bias)     */
+    const void *gate;    /* [num_experts][inter][hidden] GGUF blocks                     */
+    const void *up;      /* [num_experts][inter][hidden]                                 */
+    const void *down;    /* [num_experts][hidden][inter]                                 */
+    int gate_up_type;    /* MMRS_Q4K or MMRS_Q5K                                          */
+    int down_type;       /* MMRS_Q4K or MMRS_Q5K                                          */
+    int num_experts;     /* 256 for MiniMax-M2.7                                          */
+    int topk;            /* 8                                                             */
+    int hidden;          /* 3072 (multiple of 256)                                        */
+    int inter;           /* 1536, or 768 per rank at TP=2 (multiple of 256)               */
+} MmrsMoeWeights;
+
+/* Device workspace the block needs for up to max_tokens tokens.  The workspace must be zeroed
+ * once before first use (it holds the grid-barrier state) and again after any call that
+ * returned MMRS_ERR_TIMEOUT. */
+MMRS_API size_t mmrs_moe_workspace_bytes(const MmrsMoeWeights *w, int max_tokens);
+
+/* y[T][hidden] = MoE(x[T][hidden]) (+ residual[T][hidden] when non-null), f32.
+ * Replaces FusedMoeGGUF::forward (fused_moe.rs:251-334) + the residual add of
+ * Layer::forward (src/model.rs:213-218).  topk_ids [T][topk] / topk_weights [T][topk]
+ * (nullable) receive the routing.  T == 1 runs the fused decode kernel. */
+MMRS_API int mmrs_moe_block_forward(const MmrsMoeWeights *w, const float *x, const float *residual,
+                           float *y, int num_tokens, uint32_t *topk_ids, float *topk_weights,
+                           void *workspace, size_t workspace_bytes, mmrs_stream_t stream);
+
+/* Reads back (synchronising `stream`) and clears the device-side status word of a workspace. */
+MMRS_API int mmrs_moe_workspace_status(void *workspace, mmrs_stream_t stream);
+
+/* ===================================================================================== */
+/* 3. Seeded synthetic data (bench / test inputs; same generator as the numpy mirror)     */
+/* ===================================================================================== */
+
+/* dst[i] = scale * N(0,1)_i (Irwin-Hall(8) of 16-bit uniforms from a counter-based SplitMix64
+ * stream), optionally rounded to bf16 (stored as f32). */
+MMRS_API int mmrs_synth_normal_f32(float *dst, int64_t n, uint64_t seed, uint32_t stream_id, float scale,
+                          int round_bf16, mmrs_stream_t stream);
+
+/* Writes the [row0, row0+nrows) x [kblk0, kblk0+nkblk) window of a synthetic k-quant tensor of
+ * shape [experts][rows][k/256 blocks] into dst (laid out [experts][nrows][nkblk]).  Every byte is
+ * uniform except each block's half2 (d, dmin) = fp16(|N(0,1)| * 0.01). */
+MMRS_API int mmrs_synth_kquant(void *dst, int gguf_type, uint64_t seed, uint32_t stream_id, int experts,
+                      int rows, int k, int row0, int nrows, int kblk0, int nkblk,
+                      mmrs_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MINIMAX_MOE_H */

@@ -1,0 +1,149 @@
+"""Python binding of the B200-native MiniMax-M2.7 MoE hot path (ctypes over the C ABI).
+
+The compute lives in lib/libminimax_moe.so (hand-written sm_100a CUDA, see csrc/).  This module
+only declares the C prototypes of include/minimax_moe.h and offers thin helpers that take torch
+CUDA tensors.  There is no CPU fallback: every entry point raises when the library is missing.
+
+The directory name contains a dash, so import it by path:
+
+    import importlib.util, sys
+    spec = importlib.util.spec_from_file_location("minimax_rs_b200", "<repo>/minimax-rs_b200/__init__.py",
+                                                  submodule_search_locations=["<repo>/minimax-rs_b200"])
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+PKG_DIR = Path(__file__).resolve().parent
+LIB_PATH = PKG_DIR / "lib" / "libminimax_moe.so"
+HEADER = PKG_DIR.parent / "include" / "minimax_moe.h"
+
+MMRS_OK, MMRS_ERR_ARG, MMRS_ERR_UNSUPPORTED, MMRS_ERR_LAUNCH, MMRS_ERR_TIMEOUT, MMRS_ERR_ALLOC = range(6)
+Q8_0, Q4K, Q2K, Q3K, Q5K, Q6K = 0, 1, 2, 3, 4, 5
+ERROR_NAMES = {0: "ok", 1: "invalid argument", 2: "unsupported", 3: "launch failure", 4: "device wait timed out",
+               5: "allocation failure"}
+
+
+class MoeError(RuntimeError):
+    def __init__(self, code: int, what: str):
+        super().__init__(f"{what}: {ERROR_NAMES.get(code, code)} ({code})")
+        self.code = code
+
+
+class MmrsMoeWeights(C.Structure):
+    _fields_ = [("router", C.c_void_p), ("bias", C.c_void_p), ("gate", C.c_void_p), ("up", C.c_void_p),
+                ("down", C.c_void_p), ("gate_up_type", C.c_int), ("down_type", C.c_int),
+                ("num_experts", C.c_int), ("topk", C.c_int), ("hidden", C.c_int), ("inter", C.c_int)]
+
+
+_VP, _I, _U32, _U64, _I64, _F = C.c_void_p, C.c_int, C.c_uint32, C.c_uint64, C.c_int64, C.c_float
+_SZ = C.c_size_t
+
+# name -> (restype, argtypes)
+PROTOTYPES = {
+    "minimax_moe_decode_topk": (None, [_VP] * 7),
+    "moe_gemm_gguf_decode_silu": (None, [_VP] * 8 + [_I] * 6 + [_VP]),
+    "mmrs_last_error": (_I, []),
+    "mmrs_moe_workspace_bytes": (_SZ, [C.POINTER(MmrsMoeWeights), _I]),
+    "mmrs_moe_block_forward": (_I, [C.POINTER(MmrsMoeWeights), _VP, _VP, _VP, _I, _VP, _VP, _VP, _SZ, _VP]),
+    "mmrs_moe_workspace_status": (_I, [_VP, _VP]),
+    "mmrs_synth_normal_f32": (_I, [_VP, _I64, _U64, _U32, _F, _I, _VP]),
+    "mmrs_synth_kquant": (_I, [_VP, _I, _U64, _U32] + [_I] * 7 + [_VP]),
+}
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Loads the CUDA library (raises if it has not been built: there is no fallback)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing: run `python minimax-rs_b200/build.py` "
+                               "(the MoE path has no CPU fallback)")
+        l = C.CDLL(str(LIB_PATH), mode=C.RTLD_GLOBAL)
+        for name, (res, args) in PROTOTYPES.items():
+            f = getattr(l, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = l
+    return _lib
+
+
+def check(code: int, what: str) -> None:
+    if code != MMRS_OK:
+        raise MoeError(code, what)
+
+
+def last_error() -> int:
+    return lib().mmrs_last_error()
+
+
+# ---------------------------------------------------------------------------------------------
+# torch helpers
+# ---------------------------------------------------------------------------------------------
+def _ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream=None) -> int:
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def row_bytes(gguf_type: int, k: int) -> int:
+    return (k // 256) * (176 if gguf_type == Q5K else 144)
+
+
+class MoeLayer:
+    """Device-resident weights of one MoE layer + the C struct that points at them."""
+
+    def __init__(self, router, bias, gate, up, down, gate_up_type: int, down_type: int, topk: int = 8):
+        self.router, self.bias, self.gate, self.up, self.down = router, bias, gate, up, down
+        self.num_experts, self.hidden = router.shape
+        self.inter = gate.numel() // (self.num_experts * row_bytes(gate_up_type, self.hidden))
+        self.c = MmrsMoeWeights(router.data_ptr(), bias.data_ptr(), gate.data_ptr(), up.data_ptr(),
+                                down.data_ptr(), gate_up_type, down_type, self.num_experts, topk,
+                                self.hidden, self.inter)
+        self.topk = topk
+        self._ws = None
+
+    def workspace(self, max_tokens: int):
+        import torch
+        nbytes = lib().mmrs_moe_workspace_bytes(C.byref(self.c), max_tokens)
+        if self._ws is None or self._ws.numel() < nbytes:
+            self._ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.router.device)
+        return self._ws
+
+    def forward(self, x, residual=None, y=None, topk_ids=None, topk_w=None, stream=None):
+        """y = MoE(x) (+ residual); x [T, hidden] f32 CUDA tensor."""
+        import torch
+        T = x.shape[0]
+        if y is None:
+            y = torch.empty_like(x)
+        ws = self.workspace(T)
+        rc = lib().mmrs_moe_block_forward(C.byref(self.c), x.data_ptr(), _ptr(residual), y.data_ptr(), T,
+                                          _ptr(topk_ids), _ptr(topk_w), ws.data_ptr(), ws.numel(), _stream(stream))
+        check(rc, "mmrs_moe_block_forward")
+        return y
+
+    def status(self, stream=None) -> int:
+        return lib().mmrs_moe_workspace_status(self._ws.data_ptr(), _stream(stream)) if self._ws is not None else 0
+
+
+def synth_normal(t, seed: int, stream_id: int, scale: float = 1.0, bf16: bool = False, stream=None):
+    check(lib().mmrs_synth_normal_f32(t.data_ptr(), t.numel(), seed, stream_id, scale, int(bf16), _stream(stream)),
+          "mmrs_synth_normal_f32")
+    return t
+
+
+def synth_kquant(t, gguf_type: int, seed: int, stream_id: int, experts: int, rows: int, k: int,
+                 row0: int = 0, nrows: int | None = None, kblk0: int = 0, nkblk: int | None = None, stream=None):
+    nrows = rows - row0 if nrows is None else nrows
+    nkblk = k // 256 - kblk0 if nkblk is None else nkblk
+    check(lib().mmrs_synth_kquant(t.data_ptr(), gguf_type, seed, stream_id, experts, rows, k, row0, nrows, kblk0,
+                                  nkblk, _stream(stream)), "mmrs_synth_kquant")
+    return t

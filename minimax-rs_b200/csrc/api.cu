@@ -1,0 +1,248 @@
+// C ABI entry points: host-side validation, workspace layout and dispatch.
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+#include "decode.cuh"
+
+namespace mmrs {
+
+static thread_local int g_last_error = MMRS_OK;
+static int set_err(int e) {
+    g_last_error = e;
+    return e;
+}
+
+static int device_sms() {
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+static int device_max_smem() {
+    int dev = 0, v = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    return v;
+}
+
+static bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
+// Default bound on any device-side wait: 2 s.
+constexpr uint64_t kTimeoutNs = 2000000000ull;
+
+// ------------------------------------------------------------------------------------------
+// minimax_moe_decode_topk: one CTA of 256 threads, thread e owns expert e.
+// Same arithmetic as minimax_moe_decode_topk_kernel (moe_gguf.cu:34-100): s = 1/(1+expf(-l)),
+// stable descending order of s+bias (lower id first on ties, as the stable radix sort),
+// weights s/((s0+s4)+(s2+s6))+((s1+s5)+(s3+s7)), then (expert, route) sorted by expert id.
+// ------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) decode_topk_kernel(const float *__restrict__ logits,
+                                                          const float *__restrict__ bias, uint32_t *topk_ids,
+                                                          float *topk_weights, uint32_t *expert_ids,
+                                                          uint32_t *route_ids) {
+    __shared__ float sel[256];
+    __shared__ float sig[256];
+    __shared__ int ids[8];
+    const int e = threadIdx.x;
+    const float sg = __fdiv_rn(1.0f, 1.0f + expf(-logits[e]));
+    sig[e] = sg;
+    sel[e] = sg + bias[e];
+    __syncthreads();
+    const float me = sel[e];
+    int rank = 0;
+#pragma unroll 8
+    for (int j = 0; j < 256; ++j) {
+        const float o = sel[j];
+        rank += (o > me) || (o == me && j < e);
+    }
+    if (rank < 8) ids[rank] = e;
+    __syncthreads();
+    if (e == 0) {
+        float v[8];
+        for (int k = 0; k < 8; ++k) v[k] = sig[ids[k]];
+        const float denom = ((v[0] + v[4]) + (v[2] + v[6])) + ((v[1] + v[5]) + (v[3] + v[7]));
+        int se[8], sr[8];
+        for (int k = 0; k < 8; ++k) {
+            topk_ids[k] = (uint32_t)ids[k];
+            topk_weights[k] = __fdiv_rn(v[k], denom);
+            se[k] = ids[k];
+            sr[k] = k;
+        }
+        for (int i = 1; i < 8; ++i) {
+            const int key = se[i], rt = sr[i];
+            int j = i - 1;
+            while (j >= 0 && se[j] > key) {
+                se[j + 1] = se[j];
+                sr[j + 1] = sr[j];
+                --j;
+            }
+            se[j + 1] = key;
+            sr[j + 1] = rt;
+        }
+        for (int k = 0; k < 8; ++k) {
+            expert_ids[k] = (uint32_t)se[k];
+            route_ids[k] = (uint32_t)sr[k];
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Workspace layout of the fused block: [GridBarrier 256 B][logits E f32][act 8*I f32]
+// ------------------------------------------------------------------------------------------
+struct WsLayout {
+    size_t bar, logits, act, total;
+};
+static WsLayout ws_layout(int E, int I, int max_tokens) {
+    (void)max_tokens;
+    WsLayout l;
+    l.bar = 0;
+    l.logits = 256;
+    l.act = l.logits + ((size_t)E * 4 + 255) / 256 * 256;
+    l.total = l.act + ((size_t)8 * I * 4 + 255) / 256 * 256;
+    return l;
+}
+
+static int validate_weights(const MmrsMoeWeights *w) {
+    if (!w || !w->router || !w->bias || !w->gate || !w->up || !w->down) return MMRS_ERR_ARG;
+    if (w->hidden <= 0 || w->inter <= 0 || w->hidden % QK_K || w->inter % QK_K) return MMRS_ERR_ARG;
+    if ((w->gate_up_type != MMRS_Q4K && w->gate_up_type != MMRS_Q5K) ||
+        (w->down_type != MMRS_Q4K && w->down_type != MMRS_Q5K))
+        return MMRS_ERR_UNSUPPORTED;
+    if (w->topk != 8 || w->num_experts < 8 || w->num_experts > 1024) return MMRS_ERR_UNSUPPORTED;
+    if (!aligned16(w->gate) || !aligned16(w->up) || !aligned16(w->down) || !aligned16(w->router))
+        return MMRS_ERR_ARG;
+    return MMRS_OK;
+}
+
+}  // namespace mmrs
+
+using namespace mmrs;
+
+extern "C" int mmrs_last_error(void) { return g_last_error; }
+
+extern "C" void minimax_moe_decode_topk(const float *logits, const float *bias, uint32_t *topk_ids,
+                                        float *topk_weights, uint32_t *expert_ids, uint32_t *route_ids,
+                                        mmrs_stream_t stream) {
+    if (!logits || !bias || !topk_ids || !topk_weights || !expert_ids || !route_ids) {
+        set_err(MMRS_ERR_ARG);
+        return;
+    }
+    decode_topk_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(logits, bias, topk_ids, topk_weights, expert_ids,
+                                                            route_ids);
+    set_err(cudaGetLastError() == cudaSuccess ? MMRS_OK : MMRS_ERR_LAUNCH);
+}
+
+extern "C" void moe_gemm_gguf_decode_silu(const float *input, const void *gate_weights, const void *up_weights,
+                                          const void *down_weights, const int32_t *sorted_token_ids,
+                                          const int32_t *expert_ids, const float *topk_weights, float *output,
+                                          int num_experts, int topk, int hidden_size, int intermediate_size,
+                                          int gate_up_gguf_dtype, int down_gguf_dtype, mmrs_stream_t stream) {
+    // The reference returns without work for topk != 8 (moe_gguf.cu:457-459); so does this path,
+    // but it records the condition.
+    if (topk != 8) {
+        set_err(MMRS_ERR_UNSUPPORTED);
+        return;
+    }
+    if (!input || !gate_weights || !up_weights || !down_weights || !sorted_token_ids || !expert_ids ||
+        !topk_weights || !output || hidden_size <= 0 || intermediate_size <= 0) {
+        set_err(MMRS_ERR_ARG);
+        return;
+    }
+    if (!aligned16(gate_weights) || !aligned16(up_weights) || !aligned16(down_weights) || !aligned16(input)) {
+        set_err(MMRS_ERR_ARG);
+        return;
+    }
+    DecodeParams p = {};
+    p.x = input;
+    p.gate = (const uint8_t *)gate_weights;
+    p.up = (const uint8_t *)up_weights;
+    p.down = (const uint8_t *)down_weights;
+    p.y = output;
+    p.ext_route = sorted_token_ids;
+    p.ext_expert = expert_ids;
+    p.ext_w = topk_weights;
+    p.internal_routing = 0;
+    p.E = num_experts;
+    p.H = hidden_size;
+    p.I = intermediate_size;
+    p.gu_type = gate_up_gguf_dtype;
+    p.dn_type = down_gguf_dtype;
+    p.timeout_ns = kTimeoutNs;
+    int rc = decode_configure(p, device_sms(), device_max_smem());
+    if (rc != MMRS_OK) {
+        set_err(rc);
+        return;
+    }
+    // Scratch on the stream's pool, like the reference (moe_gguf.cu:468-472).
+    const WsLayout l = ws_layout(num_experts, intermediate_size, 1);
+    cudaStream_t s = (cudaStream_t)stream;
+    uint8_t *ws = nullptr;
+    if (cudaMallocAsync((void **)&ws, l.total, s) != cudaSuccess) {
+        set_err(MMRS_ERR_ALLOC);
+        return;
+    }
+    cudaMemsetAsync(ws, 0, 256, s);
+    p.bar = reinterpret_cast<GridBarrier *>(ws + l.bar);
+    p.logits = reinterpret_cast<float *>(ws + l.logits);
+    p.act = reinterpret_cast<float *>(ws + l.act);
+    rc = decode_launch(p, s);
+    cudaFreeAsync(ws, s);
+    set_err(rc);
+}
+
+extern "C" size_t mmrs_moe_workspace_bytes(const MmrsMoeWeights *w, int max_tokens) {
+    if (!w) return 0;
+    return ws_layout(w->num_experts, w->inter, max_tokens).total;
+}
+
+extern "C" int mmrs_moe_block_forward(const MmrsMoeWeights *w, const float *x, const float *residual, float *y,
+                                      int num_tokens, uint32_t *topk_ids, float *topk_weights, void *workspace,
+                                      size_t workspace_bytes, mmrs_stream_t stream) {
+    int rc = validate_weights(w);
+    if (rc != MMRS_OK) return rc;
+    if (!x || !y || num_tokens < 0 || !workspace) return MMRS_ERR_ARG;
+    if (num_tokens == 0) return MMRS_OK;
+    const WsLayout l = ws_layout(w->num_experts, w->inter, num_tokens);
+    if (workspace_bytes < l.total || !aligned16(workspace) || !aligned16(x)) return MMRS_ERR_ARG;
+    if (num_tokens != 1) return MMRS_ERR_UNSUPPORTED;
+    uint8_t *ws = (uint8_t *)workspace;
+    DecodeParams p = {};
+    p.x = x;
+    p.router = w->router;
+    p.bias = w->bias;
+    p.gate = (const uint8_t *)w->gate;
+    p.up = (const uint8_t *)w->up;
+    p.down = (const uint8_t *)w->down;
+    p.residual = residual;
+    p.y = y;
+    p.topk_ids_out = topk_ids;
+    p.topk_w_out = topk_weights;
+    p.internal_routing = 1;
+    p.logits = reinterpret_cast<float *>(ws + l.logits);
+    p.act = reinterpret_cast<float *>(ws + l.act);
+    p.bar = reinterpret_cast<GridBarrier *>(ws + l.bar);
+    p.E = w->num_experts;
+    p.H = w->hidden;
+    p.I = w->inter;
+    p.gu_type = w->gate_up_type;
+    p.dn_type = w->down_type;
+    p.timeout_ns = kTimeoutNs;
+    rc = decode_configure(p, device_sms(), device_max_smem());
+    if (rc != MMRS_OK) return rc;
+    return decode_launch(p, (cudaStream_t)stream);
+}
+
+extern "C" int mmrs_moe_workspace_status(void *workspace, mmrs_stream_t stream) {
+    if (!workspace) return MMRS_ERR_ARG;
+    GridBarrier gb;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (cudaMemcpyAsync(&gb, workspace, sizeof(gb), cudaMemcpyDeviceToHost, s) != cudaSuccess) return MMRS_ERR_LAUNCH;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return MMRS_ERR_LAUNCH;
+    if (gb.status != 0) {
+        // reset the barrier state so the workspace is usable again
+        cudaMemsetAsync(workspace, 0, sizeof(GridBarrier), s);
+        cudaStreamSynchronize(s);
+    }
+    return (int)gb.status;
+}

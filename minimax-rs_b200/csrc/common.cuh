@@ -1,0 +1,202 @@
+// Shared device helpers for the MiniMax MoE hot path on B200 (sm_100a).
+//
+// GGUF k-quant block layouts (byte-compatible with the reference's vendored Candle kernels,
+// candle-kernels/src/moe/gguf.cuh:341-406):
+//   Q4_K  144 B per 256 weights: half2 dm | 12 B packed 6-bit scales+mins | 128 B nibbles
+//   Q5_K  176 B per 256 weights: half2 dm | 12 B scales+mins | 32 B high bits | 128 B nibbles
+//   Q8_1   36 B per  32 values : half2 (d, sum) | 32 x int8
+// Element order inside a super-block (quantized.cu:943-1004): element 64j+l is the low nibble of
+// qs[32j+l] (sub-block 2j), element 64j+32+l the high nibble (sub-block 2j+1); Q5_K adds 16 when
+// bit 2j (resp. 2j+1) of qh[l] is set.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/minimax_moe.h"
+
+namespace mmrs {
+
+constexpr int QK_K = 256;
+constexpr int Q4K_BYTES = 144;
+constexpr int Q5K_BYTES = 176;
+constexpr int Q81_BYTES = 36;
+
+__host__ __device__ inline int kq_block_bytes(int t) { return t == MMRS_Q5K ? Q5K_BYTES : Q4K_BYTES; }
+__host__ __device__ inline size_t kq_row_bytes(int t, int k) { return (size_t)(k / QK_K) * kq_block_bytes(t); }
+__host__ __device__ inline int pad_to(int v, int p) { return (v + p - 1) / p * p; }
+
+// ------------------------------------------------------------------------------------------
+// Scale / min unpacking: get_scale_min_k4 (quantized.cu:926-933) for sub-blocks 2j and 2j+1
+// from the 12 packed bytes, read as three little-endian 32-bit words w0,w1,w2.
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ void kq_scale_min_pair(uint32_t w0, uint32_t w1, uint32_t w2, int j,
+                                                  int &sc0, int &m0, int &sc1, int &m1) {
+    // byte(q, i): byte i of the 12-byte array
+    auto byte_of = [&](int i) -> uint32_t {
+        const uint32_t w = i < 4 ? w0 : (i < 8 ? w1 : w2);
+        return (w >> (8 * (i & 3))) & 0xffu;
+    };
+    const int a = 2 * j, b = 2 * j + 1;
+    if (a < 4) {
+        sc0 = byte_of(a) & 63;
+        m0 = byte_of(a + 4) & 63;
+        sc1 = byte_of(b) & 63;
+        m1 = byte_of(b + 4) & 63;
+    } else {
+        sc0 = (byte_of(a + 4) & 0xF) | ((byte_of(a - 4) >> 6) << 4);
+        m0 = (byte_of(a + 4) >> 4) | ((byte_of(a) >> 6) << 4);
+        sc1 = (byte_of(b + 4) & 0xF) | ((byte_of(b - 4) >> 6) << 4);
+        m1 = (byte_of(b + 4) >> 4) | ((byte_of(b) >> 6) << 4);
+    }
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
+    return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xffffu)));
+}
+
+// ------------------------------------------------------------------------------------------
+// Warp helpers
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum_butterfly(float v) {
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+    return v;
+}
+__device__ __forceinline__ float warp_max_butterfly(float v) {
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
+    return v;
+}
+
+// ------------------------------------------------------------------------------------------
+// Time (ns) for bounded waits
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ------------------------------------------------------------------------------------------
+// mbarrier + bulk async copy (TMA, non-tensor) wrappers
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile(
+        "{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+            smem_u32(bar)),
+        "r"(bytes)
+        : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: returns false when the deadline (globaltimer ns) passes.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint64_t deadline) {
+    uint32_t spins = 0;
+    while (!mbar_try_wait(bar, parity)) {
+        if ((++spins & 1023u) == 0 && globaltimer_ns() > deadline) return false;
+    }
+    return true;
+}
+// 1-D bulk copy global -> shared, completion counted on an mbarrier (bytes % 16 == 0,
+// both addresses 16-byte aligned).
+__device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, uint32_t bytes,
+                                         uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void prefetch_l2_bulk(const void *gmem_src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gmem_src), "r"(bytes) : "memory");
+}
+
+// ------------------------------------------------------------------------------------------
+// Global acquire / release helpers for the software grid barrier and peer flags.
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Self-resetting generation barrier over all CTAs of one grid: {count, gen, status}.
+// Every CTA must call it the same number of times.  Returns false (and records
+// MMRS_ERR_TIMEOUT in status) when the deadline passes; the caller must then stop.
+struct GridBarrier {
+    uint32_t count;
+    uint32_t gen;
+    uint32_t status;
+    uint32_t pad;
+};
+
+// Call with all participating threads of the CTA; `nthreads` of them hit named barrier `id`.
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ inline bool grid_barrier(GridBarrier *gb, uint32_t nblocks, uint64_t deadline,
+                                    volatile int *s_flag, int bar_id, int nthreads) {
+    named_sync(bar_id, nthreads);
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        const uint32_t g = ld_acquire_gpu(&gb->gen);
+        __threadfence();
+        const uint32_t arrived = atomicAdd(&gb->count, 1u);
+        if (arrived == nblocks - 1) {
+            atomicExch(&gb->count, 0u);
+            __threadfence();
+            st_release_gpu(&gb->gen, g + 1);
+        } else {
+            uint32_t spins = 0;
+            while (ld_acquire_gpu(&gb->gen) == g) {
+                if ((++spins & 255u) == 0 && globaltimer_ns() > deadline) {
+                    atomicExch(&gb->status, (uint32_t)MMRS_ERR_TIMEOUT);
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        *s_flag = ok;
+    }
+    named_sync(bar_id, nthreads);
+    return *s_flag != 0;
+}
+
+}  // namespace mmrs

@@ -1,0 +1,42 @@
+// Parameters of the fused single-token MoE kernel (decode.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mmrs {
+
+struct GridBarrier;
+
+struct DecodeParams {
+    const float *x;       // [H] f32
+    const float *router;  // [E][H] f32 (internal routing only)
+    const float *bias;    // [E] f32 (internal routing only)
+    const uint8_t *gate;  // [E][I][H] GGUF
+    const uint8_t *up;    // [E][I][H]
+    const uint8_t *down;  // [E][H][I]
+    const float *residual;  // [H] or null
+    float *y;               // [H]
+    uint32_t *topk_ids_out;  // [8] or null
+    float *topk_w_out;       // [8] or null
+    // external routing (moe_gemm_gguf_decode_silu): pairs in expert order, weights by route
+    const int32_t *ext_route;
+    const int32_t *ext_expert;
+    const float *ext_w;
+    int internal_routing;
+    // workspace
+    float *logits;  // [E]
+    float *act;     // [8][I]
+    GridBarrier *bar;
+    // shape
+    int E, H, I;
+    int gu_type, dn_type;
+    // launch configuration (decode_configure)
+    int gu_rows, dn_rows, n_gu_units, n_dn_units, stages, stage_bytes, grid;
+    uint64_t timeout_ns;
+};
+
+size_t decode_smem_bytes(const DecodeParams &p);
+int decode_configure(DecodeParams &p, int num_sms, int max_smem);
+int decode_launch(const DecodeParams &p, cudaStream_t stream);
+
+}  // namespace mmrs
