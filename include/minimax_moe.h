@@ -95,9 +95,10 @@ typedef struct {
     int inter;           /* 1536, or 768 per rank at TP=2 (multiple of 256)               */
 } MmrsMoeWeights;
 
-/* Device workspace the block needs for up to max_tokens tokens.  The workspace must be zeroed
- * once before first use (it holds the grid-barrier state) and again after any call that
- * returned MMRS_ERR_TIMEOUT. */
+/* Device workspace the block needs for up to max_tokens tokens.  Its first 4096 bytes (status
+ * word and grid-barrier flags) must be zero before first use; mmrs_moe_workspace_status()
+ * clears them again after a call that reported MMRS_ERR_TIMEOUT.  Launches that share a
+ * workspace must be ordered on one stream. */
 MMRS_API size_t mmrs_moe_workspace_bytes(const MmrsMoeWeights *w, int max_tokens);
 
 /* y[T][hidden] = MoE(x[T][hidden]) (+ residual[T][hidden] when non-null), f32.
@@ -107,6 +108,13 @@ MMRS_API size_t mmrs_moe_workspace_bytes(const MmrsMoeWeights *w, int max_tokens
 MMRS_API int mmrs_moe_block_forward(const MmrsMoeWeights *w, const float *x, const float *residual,
                            float *y, int num_tokens, uint32_t *topk_ids, float *topk_weights,
                            void *workspace, size_t workspace_bytes, mmrs_stream_t stream);
+
+/* Copies the per-CTA phase timestamps (globaltimer ns, 16 slots per CTA: 0 start, 1 router done,
+ * 2 routing barrier, 3 routing done, 4 gate/up done, 5 second barrier, 6 activation quantised,
+ * 7 end, 8 first weight copy issued, 9 last copy issued, 10 first down copy issued) of the last
+ * single-token launch into host_out.  Returns the number of entries copied, or -status. */
+MMRS_API int mmrs_moe_workspace_trace(const void *workspace, uint64_t *host_out, int max_entries,
+                                      mmrs_stream_t stream);
 
 /* Reads back (synchronising `stream`) and clears the device-side status word of a workspace. */
 MMRS_API int mmrs_moe_workspace_status(void *workspace, mmrs_stream_t stream);

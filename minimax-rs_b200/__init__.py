@@ -49,6 +49,7 @@ PROTOTYPES = {
     "mmrs_moe_workspace_bytes": (_SZ, [C.POINTER(MmrsMoeWeights), _I]),
     "mmrs_moe_block_forward": (_I, [C.POINTER(MmrsMoeWeights), _VP, _VP, _VP, _I, _VP, _VP, _VP, _SZ, _VP]),
     "mmrs_moe_workspace_status": (_I, [_VP, _VP]),
+    "mmrs_moe_workspace_trace": (_I, [_VP, _VP, _I, _VP]),
     "mmrs_synth_normal_f32": (_I, [_VP, _I64, _U64, _U32, _F, _I, _VP]),
     "mmrs_synth_kquant": (_I, [_VP, _I, _U64, _U32] + [_I] * 7 + [_VP]),
 }
@@ -129,6 +130,15 @@ class MoeLayer:
                                           _ptr(topk_ids), _ptr(topk_w), ws.data_ptr(), ws.numel(), _stream(stream))
         check(rc, "mmrs_moe_block_forward")
         return y
+
+    def trace(self, stream=None):
+        """Per-CTA phase timestamps (ns) of the last single-token launch: array [256, 16]."""
+        import numpy as np
+        out = np.zeros(256 * 16, dtype=np.uint64)
+        n = lib().mmrs_moe_workspace_trace(self._ws.data_ptr(), out.ctypes.data, out.size, _stream(stream))
+        if n < 0:
+            raise MoeError(-n, "mmrs_moe_workspace_trace")
+        return out.reshape(256, 16)
 
     def status(self, stream=None) -> int:
         return lib().mmrs_moe_workspace_status(self._ws.data_ptr(), _stream(stream)) if self._ws is not None else 0

@@ -91,16 +91,38 @@ __global__ void __launch_bounds__(256) decode_topk_kernel(const float *__restric
 // Workspace layout of the fused block: [GridBarrier 256 B][logits E f32][act 8*I f32]
 // ------------------------------------------------------------------------------------------
 struct WsLayout {
-    size_t bar, logits, act, total;
+    size_t ctl, trace, blk_count, logits, act, aq, ad, aS, total;
 };
+constexpr int kTraceCtas = 256, kTraceSlots = 16;
+constexpr size_t kTraceOffset = kControlBytes;
+static size_t up256(size_t v) { return (v + 255) / 256 * 256; }
+// [control block: status + per-CTA barrier flags (zero before first use)] | trace |
+// per-block counters (zeroed by the kernel) | logits | act | aq | ad | aS
 static WsLayout ws_layout(int E, int I, int max_tokens) {
     (void)max_tokens;
     WsLayout l;
-    l.bar = 0;
-    l.logits = 256;
-    l.act = l.logits + ((size_t)E * 4 + 255) / 256 * 256;
-    l.total = l.act + ((size_t)8 * I * 4 + 255) / 256 * 256;
+    const size_t nblk = (size_t)8 * I / 32;
+    l.ctl = 0;
+    l.trace = kTraceOffset;
+    l.blk_count = l.trace + sizeof(uint64_t) * kTraceCtas * kTraceSlots;
+    l.logits = l.blk_count + up256(nblk * 4);
+    l.act = l.logits + up256((size_t)E * 4);
+    l.aq = l.act + up256((size_t)8 * I * 4);
+    l.ad = l.aq + up256((size_t)8 * I);
+    l.aS = l.ad + up256(nblk * 4);
+    l.total = l.aS + up256(nblk * 4);
     return l;
+}
+
+static void ws_bind(DecodeParams &p, uint8_t *ws, const WsLayout &l) {
+    p.ctl = reinterpret_cast<GridFlags *>(ws + l.ctl);
+    p.blk_count = reinterpret_cast<uint32_t *>(ws + l.blk_count);
+    p.trace = reinterpret_cast<uint64_t *>(ws + l.trace);
+    p.logits = reinterpret_cast<float *>(ws + l.logits);
+    p.act = reinterpret_cast<float *>(ws + l.act);
+    p.aq = reinterpret_cast<int8_t *>(ws + l.aq);
+    p.ad = reinterpret_cast<float *>(ws + l.ad);
+    p.aS = reinterpret_cast<int *>(ws + l.aS);
 }
 
 static int validate_weights(const MmrsMoeWeights *w) {
@@ -182,10 +204,9 @@ extern "C" void moe_gemm_gguf_decode_silu(const float *input, const void *gate_w
         set_err(MMRS_ERR_ALLOC);
         return;
     }
-    cudaMemsetAsync(ws, 0, 256, s);
-    p.bar = reinterpret_cast<GridBarrier *>(ws + l.bar);
-    p.logits = reinterpret_cast<float *>(ws + l.logits);
-    p.act = reinterpret_cast<float *>(ws + l.act);
+    cudaMemsetAsync(ws, 0, kControlBytes, s);
+    ws_bind(p, ws, l);
+    p.trace = nullptr;
     rc = decode_launch(p, s);
     cudaFreeAsync(ws, s);
     set_err(rc);
@@ -219,9 +240,7 @@ extern "C" int mmrs_moe_block_forward(const MmrsMoeWeights *w, const float *x, c
     p.topk_ids_out = topk_ids;
     p.topk_w_out = topk_weights;
     p.internal_routing = 1;
-    p.logits = reinterpret_cast<float *>(ws + l.logits);
-    p.act = reinterpret_cast<float *>(ws + l.act);
-    p.bar = reinterpret_cast<GridBarrier *>(ws + l.bar);
+    ws_bind(p, ws, l);
     p.E = w->num_experts;
     p.H = w->hidden;
     p.I = w->inter;
@@ -235,14 +254,28 @@ extern "C" int mmrs_moe_block_forward(const MmrsMoeWeights *w, const float *x, c
 
 extern "C" int mmrs_moe_workspace_status(void *workspace, mmrs_stream_t stream) {
     if (!workspace) return MMRS_ERR_ARG;
-    GridBarrier gb;
+    uint32_t status = 0;
     cudaStream_t s = (cudaStream_t)stream;
-    if (cudaMemcpyAsync(&gb, workspace, sizeof(gb), cudaMemcpyDeviceToHost, s) != cudaSuccess) return MMRS_ERR_LAUNCH;
+    if (cudaMemcpyAsync(&status, workspace, sizeof(status), cudaMemcpyDeviceToHost, s) != cudaSuccess)
+        return MMRS_ERR_LAUNCH;
     if (cudaStreamSynchronize(s) != cudaSuccess) return MMRS_ERR_LAUNCH;
-    if (gb.status != 0) {
-        // reset the barrier state so the workspace is usable again
-        cudaMemsetAsync(workspace, 0, sizeof(GridBarrier), s);
+    if (status != 0) {
+        // reset status and barrier flags so the workspace is usable again
+        cudaMemsetAsync(workspace, 0, kControlBytes, s);
         cudaStreamSynchronize(s);
     }
-    return (int)gb.status;
+    return (int)status;
+}
+
+extern "C" int mmrs_moe_workspace_trace(const void *workspace, uint64_t *host_out, int max_entries,
+                                        mmrs_stream_t stream) {
+    if (!workspace || !host_out || max_entries <= 0) return -MMRS_ERR_ARG;
+    const int n = max_entries < kTraceCtas * kTraceSlots ? max_entries : kTraceCtas * kTraceSlots;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (cudaMemcpyAsync(host_out, (const uint8_t *)workspace + kTraceOffset, sizeof(uint64_t) * n,
+                        cudaMemcpyDeviceToHost,
+                        s) != cudaSuccess)
+        return -MMRS_ERR_LAUNCH;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return -MMRS_ERR_LAUNCH;
+    return n;
 }

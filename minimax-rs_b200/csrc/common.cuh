@@ -156,47 +156,45 @@ __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Self-resetting generation barrier over all CTAs of one grid: {count, gen, status}.
-// Every CTA must call it the same number of times.  Returns false (and records
-// MMRS_ERR_TIMEOUT in status) when the deadline passes; the caller must then stop.
-struct GridBarrier {
-    uint32_t count;
-    uint32_t gen;
-    uint32_t status;
-    uint32_t pad;
-};
-
-// Call with all participating threads of the CTA; `nthreads` of them hit named barrier `id`.
+// Named barrier `id` over `nthreads` threads of the CTA.
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-__device__ inline bool grid_barrier(GridBarrier *gb, uint32_t nblocks, uint64_t deadline,
-                                    volatile int *s_flag, int bar_id, int nthreads) {
+// Control block at the start of every workspace: a status word, a grid-arrival counter and one
+// epoch word per CTA.  Grid barrier k of a launch: every CTA adds 1 to `count` (fire-and-forget
+// red.release) and waits until count >= G * (epoch + k), where epoch is the value of its own
+// epoch word at launch start (2 per completed launch: every launch passes exactly two barriers).
+// The counter is never reset; comparisons are wrap-safe.
+constexpr int kMaxGridCtas = 960;
+struct GridFlags {
+    uint32_t status;  // MMRS_OK, or MMRS_ERR_TIMEOUT once any wait expired
+    uint32_t pad0[31];
+    uint32_t count;  // own 128-byte line
+    uint32_t pad1[31];
+    uint32_t epoch[kMaxGridCtas];
+};
+constexpr size_t kControlBytes = sizeof(GridFlags);
+
+// Call with `nthreads` threads of the CTA that use named barrier `bar_id`.  Returns false (and
+// records MMRS_ERR_TIMEOUT) when the deadline passes.  *s_ok must be 1 on first use.
+__device__ inline bool grid_sync(GridFlags *gf, uint32_t target, uint64_t deadline, volatile int *s_ok, int bar_id,
+                                 int nthreads) {
     named_sync(bar_id, nthreads);
-    if (threadIdx.x == 0) {
-        int ok = 1;
-        const uint32_t g = ld_acquire_gpu(&gb->gen);
-        __threadfence();
-        const uint32_t arrived = atomicAdd(&gb->count, 1u);
-        if (arrived == nblocks - 1) {
-            atomicExch(&gb->count, 0u);
-            __threadfence();
-            st_release_gpu(&gb->gen, g + 1);
-        } else {
-            uint32_t spins = 0;
-            while (ld_acquire_gpu(&gb->gen) == g) {
-                if ((++spins & 255u) == 0 && globaltimer_ns() > deadline) {
-                    atomicExch(&gb->status, (uint32_t)MMRS_ERR_TIMEOUT);
-                    ok = 0;
-                    break;
-                }
+    if (threadIdx.x == 0 && *s_ok) {
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&gf->count) : "memory");
+        uint32_t spins = 0;
+        while ((int)(ld_acquire_gpu(&gf->count) - target) < 0) {
+            __nanosleep(16);
+            if ((++spins & 255u) == 0 && globaltimer_ns() > deadline) {
+                atomicExch(&gf->status, (uint32_t)MMRS_ERR_TIMEOUT);
+                *s_ok = 0;
+                break;
             }
         }
-        *s_flag = ok;
     }
     named_sync(bar_id, nthreads);
-    return *s_flag != 0;
+    return *s_ok != 0;
 }
 
 }  // namespace mmrs

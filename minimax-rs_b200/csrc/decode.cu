@@ -5,153 +5,234 @@
 //   -> quantize_q8_1 -> moe_gate_up_decode_kernel -> quantize_silu_mul_q8_1
 //   -> moe_down_decode_kernel (moe_gguf.cu:200-343, 426-567) -> + residual (model.rs:218)
 //
-// Design (one CTA per SM, 8 consumer warps + 1 producer warp):
-//   P0  router GEMV: expert e is computed by warp (e / grid) of CTA (e % grid) in the library's
-//       canonical order (32 lane partials of float4 groups, fmaf, xor butterfly).  Meanwhile every
-//       CTA quantises x to Q8_1 in shared memory.  Grid barrier #1.
-//   P1  every CTA redundantly selects the top-8 from the 256 logits (sigmoid + bias, stable
-//       descending rank) and renormalises the weights with the reference's fixed tree.
-//   P2  gate/up: units of R=4 rows x {gate, up} of one routed expert; each CTA owns a contiguous
-//       unit range.  The producer streams units into a ring of shared-memory stages with 1-D bulk
-//       TMA copies (cp.async.bulk + mbarrier complete_tx); 8 warps = 4 rows x {gate, up} consume,
-//       and the gate warp of each pair writes act = up * silu(gate) (f32) to global scratch.
-//   P3  down: units of Rd rows x 8 routed experts.  The producer keeps streaming (down weights do
-//       not depend on act), so down tiles are already resident when grid barrier #2 releases.  Each
-//       CTA quantises act to Q8_1 in shared memory, warp w handles slot w, and the 8 slot values of
-//       each row are summed with the reference's tree ((v0+v4)+(v2+v6))+((v1+v5)+(v3+v7)).
-// Every wait (mbarrier, grid barrier) is bounded by a globaltimer deadline; on expiry the kernel
-// records MMRS_ERR_TIMEOUT in the workspace status word, drains its own copies and returns.
+// One CTA per SM: 16 consumer warps (two groups of 8) + 1 producer warp.
+//   P0  router GEMV in the canonical order (8 K-slices; warp w computes slice w%8 of the CTA's
+//       expert w/8: 32 lane partials, butterfly, fixed slice tree); every CTA quantises x to Q8_1
+//       in shared memory.  Grid barrier #1.
+//   P1  every CTA selects the top-8 with warp-shuffle argmax rounds on 64-bit keys
+//       (score desc, expert id asc — the stable descending order) and renormalises the weights
+//       with the reference's fixed tree.
+//   P2  gate/up: each CTA owns a contiguous range of (slot, row) pairs, streamed in units of up
+//       to 8 rows x {gate, up} into a ring of shared-memory stages by 1-D bulk TMA copies
+//       (cp.async.bulk + mbarrier complete_tx).  Consumer groups take alternate units; in a group
+//       a half-warp computes one gate row, the other half the matching up row, and
+//       act = up * silu(gate) stays in shared memory.  Q8_1 blocks of act inside the CTA's range
+//       are quantised locally; a block shared with a neighbour CTA goes through global scratch
+//       and is quantised by whichever CTA completes it.
+//   P3  grid barrier #2, one bulk copy of the quantised activation per CTA; down: each CTA owns a
+//       contiguous range of output rows, units of rows x 8 routed experts (the producer streams
+//       them during P2 already); the 8 expert values of a row are summed with the reference's
+//       tree ((v0+v4)+(v2+v6))+((v1+v5)+(v3+v7)) and the residual is added.
+// Lane work unit ("task"): one 64-weight sub-block pair (super-block sb, pair j) of a row: 32 B of
+// quants, dp4a against the Q8_1 activation, MMVQ combine of vec_dot_q4_K_q8_1 / _q5_K_
+// (gguf.cuh:727-750, 783-813): dall * sum d8*(dot*sc) - dmin * sum d8*sum(q8)*m.
+// Every wait is bounded by a globaltimer deadline; on expiry the kernel records MMRS_ERR_TIMEOUT in
+// the workspace status word, keeps every named barrier matched, drains its copies and returns.
 #include "common.cuh"
 #include "decode.cuh"
 
 namespace mmrs {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kGroupWarps = 4;
+constexpr int kGroups = 4;
+constexpr int kRowsPerLane = 2;   // rows a lane group computes per unit (same activation registers)
+constexpr int kMaxUnits = 96;
+constexpr int kConsumerWarps = kGroupWarps * kGroups;
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kThreads = kConsumerThreads + 32;
 constexpr int kTopK = 8;
-constexpr int kMaxTPL = 4;  // tasks per lane (a task = 16 bytes of quants of one super-block)
+constexpr int kTPL = 3;  // tasks (64-weight sub-block pairs) per lane
 
-// Shared-memory activation in Q8_1 form: int8 q[K], float d[K/32], int s16[K/16] (sums of halves).
+// Q8_1 activation in shared memory: q int8 [K] and, per 64-element pair (task), the float4
+// {d8 lo block, d8 hi block, d8*sum(q) lo, d8*sum(q) hi}.
 struct ActView {
-    int8_t *q;
-    float *d;
-    int *s16;
+    const int8_t *q;
+    const float4 *ts;
 };
 
-// Per-lane register copy of the activation slices its tasks touch.
-struct LaneAct {
-    int lo[kMaxTPL][4], hi[kMaxTPL][4];
-    float dlo[kMaxTPL], dhi[kMaxTPL];
-    int slo[kMaxTPL], shi[kMaxTPL];
+// a: unsigned bytes, b: signed bytes.
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Scales/mins of sub-blocks 2j, 2j+1 as two packed byte pairs (get_scale_min_k4, quantized.cu:926-933).
+__device__ __forceinline__ void scale_pair(const uint4 &hdr, int j, uint32_t &scp, uint32_t &mp) {
+    const int sh = 16 * (j & 1);
+    const uint32_t Y = hdr.y >> sh, Z = hdr.z >> sh, W = hdr.w >> sh;
+    if (j < 2) {
+        scp = Y & 0x3F3Fu;
+        mp = Z & 0x3F3Fu;
+    } else {
+        scp = (W & 0x0F0Fu) | ((Y >> 2) & 0x3030u);
+        mp = ((W >> 4) & 0x0F0Fu) | ((Z >> 2) & 0x3030u);
+    }
+}
+
+// Per-lane register copy of one task's activation: 64 int8 (lo block, hi block) and the scale
+// record {d8 lo, d8 hi, d8*sum(q) lo, d8*sum(q) hi}.
+struct TaskAct {
+    int lo[8], hi[8];
+    float4 ts;
 };
 
-__device__ __forceinline__ void load_lane_act(const ActView &a, int lane_in_group, int group_lanes,
-                                              int ntasks, LaneAct &la) {
+__device__ __forceinline__ void load_task_acts(const ActView &a, int lig, int L, int ntasks, TaskAct (&ta)[kTPL]) {
 #pragma unroll
-    for (int i = 0; i < kMaxTPL; ++i) {
-        const int tau = lane_in_group + group_lanes * i;
+    for (int i = 0; i < kTPL; ++i) {
+        const int tau = lig + L * i;
         if (tau < ntasks) {
-            const int b = tau >> 3, t = tau & 7, j = t >> 1, h = t & 1;
-            const int elo = 256 * b + 64 * j + 16 * h, ehi = elo + 32;
-            const int4 vlo = *reinterpret_cast<const int4 *>(a.q + elo);
-            const int4 vhi = *reinterpret_cast<const int4 *>(a.q + ehi);
-            la.lo[i][0] = vlo.x; la.lo[i][1] = vlo.y; la.lo[i][2] = vlo.z; la.lo[i][3] = vlo.w;
-            la.hi[i][0] = vhi.x; la.hi[i][1] = vhi.y; la.hi[i][2] = vhi.z; la.hi[i][3] = vhi.w;
-            la.dlo[i] = a.d[elo >> 5];
-            la.dhi[i] = a.d[ehi >> 5];
-            la.slo[i] = a.s16[elo >> 4];
-            la.shi[i] = a.s16[ehi >> 4];
+            const int4 *q = reinterpret_cast<const int4 *>(a.q + 64 * tau);
+            const int4 a0 = q[0], a1 = q[1], a2 = q[2], a3 = q[3];
+            ta[i].lo[0] = a0.x; ta[i].lo[1] = a0.y; ta[i].lo[2] = a0.z; ta[i].lo[3] = a0.w;
+            ta[i].lo[4] = a1.x; ta[i].lo[5] = a1.y; ta[i].lo[6] = a1.z; ta[i].lo[7] = a1.w;
+            ta[i].hi[0] = a2.x; ta[i].hi[1] = a2.y; ta[i].hi[2] = a2.z; ta[i].hi[3] = a2.w;
+            ta[i].hi[4] = a3.x; ta[i].hi[5] = a3.y; ta[i].hi[6] = a3.z; ta[i].hi[7] = a3.w;
+            ta[i].ts = a.ts[tau];
         } else {
 #pragma unroll
-            for (int c = 0; c < 4; ++c) la.lo[i][c] = la.hi[i][c] = 0;
-            la.dlo[i] = la.dhi[i] = 0.f;
-            la.slo[i] = la.shi[i] = 0;
+            for (int c = 0; c < 8; ++c) ta[i].lo[c] = ta[i].hi[c] = 0;
+            ta[i].ts = make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
 }
 
-// Partial dot of one row (in shared memory) against the lane's activation slices, MMVQ formula
-// of vec_dot_q4_K_q8_1 / vec_dot_q5_K_q8_1 (gguf.cuh:727-750, 783-813): per super-block
-// dall * sum d8*(dot*sc) - dmin * sum d8*(sumq*m).
 template <int TYPE>
-__device__ __forceinline__ float row_partial(const uint8_t *row, int lane_in_group, int group_lanes,
-                                             int ntasks, const LaneAct &la) {
+__device__ __forceinline__ float task_dot(const uint8_t *row, int tau, const TaskAct &a) {
     constexpr int BB = TYPE == MMRS_Q5K ? Q5K_BYTES : Q4K_BYTES;
-    float acc = 0.f;
+    const int sb = tau >> 2, j = tau & 3;
+    const uint8_t *blk = row + sb * BB;
+    const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
+    int d[4] = {0, 0, 0, 0};
+    if (TYPE == MMRS_Q5K) {
+        const uint4 q0 = *reinterpret_cast<const uint4 *>(blk + 48 + 32 * j);
+        const uint4 q1 = *reinterpret_cast<const uint4 *>(blk + 64 + 32 * j);
+        const uint4 h0 = *reinterpret_cast<const uint4 *>(blk + 16);
+        const uint4 h1 = *reinterpret_cast<const uint4 *>(blk + 32);
+        const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        const uint32_t h[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+        const int rl = (4 - 2 * j) & 31, rh = (3 - 2 * j) & 31;
 #pragma unroll
-    for (int i = 0; i < kMaxTPL; ++i) {
-        const int tau = lane_in_group + group_lanes * i;
-        if (tau < ntasks) {
-            const int b = tau >> 3, t = tau & 7, j = t >> 1, h = t & 1;
-            const uint8_t *blk = row + b * BB;
-            const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
-            uint4 qv;
-            int vlo[4], vhi[4];
-            if (TYPE == MMRS_Q5K) {
-                qv = *reinterpret_cast<const uint4 *>(blk + 48 + 32 * j + 16 * h);
-                const uint4 qh = *reinterpret_cast<const uint4 *>(blk + 16 + 16 * h);
-                const uint32_t q[4] = {qv.x, qv.y, qv.z, qv.w};
-                const uint32_t hb[4] = {qh.x, qh.y, qh.z, qh.w};
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    vlo[c] = (int)((q[c] & 0x0F0F0F0Fu) | (((hb[c] >> (2 * j)) & 0x01010101u) << 4));
-                    vhi[c] = (int)(((q[c] >> 4) & 0x0F0F0F0Fu) | (((hb[c] >> (2 * j + 1)) & 0x01010101u) << 4));
-                }
-            } else {
-                qv = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * j + 16 * h);
-                const uint32_t q[4] = {qv.x, qv.y, qv.z, qv.w};
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    vlo[c] = (int)(q[c] & 0x0F0F0F0Fu);
-                    vhi[c] = (int)((q[c] >> 4) & 0x0F0F0F0Fu);
-                }
-            }
-            int dlo = 0, dhi = 0;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                dlo = __dp4a(vlo[c], la.lo[i][c], dlo);
-                dhi = __dp4a(vhi[c], la.hi[i][c], dhi);
-            }
-            int sc0, m0, sc1, m1;
-            kq_scale_min_pair(hdr.y, hdr.z, hdr.w, j, sc0, m0, sc1, m1);
-            const float sd = la.dlo[i] * (float)(dlo * sc0) + la.dhi[i] * (float)(dhi * sc1);
-            const float sm = la.dlo[i] * (float)(la.slo[i] * m0) + la.dhi[i] * (float)(la.shi[i] * m1);
-            const float dall = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
-            acc += dall * sd - dmin * sm;
+        for (int c = 0; c < 8; ++c) {
+            const uint32_t lo = (w[c] & 0x0F0F0F0Fu) | (__funnelshift_l(h[c], h[c], rl) & 0x10101010u);
+            const uint32_t hi = ((w[c] >> 4) & 0x0F0F0F0Fu) | (__funnelshift_l(h[c], h[c], rh) & 0x10101010u);
+            d[c & 1] = __dp4a((int)lo, a.lo[c], d[c & 1]);
+            d[2 + (c & 1)] = __dp4a((int)hi, a.hi[c], d[2 + (c & 1)]);
         }
+        d[2] += d[3];
+    } else {
+        const uint4 q0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * j);
+        const uint4 q1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * j);
+        const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            d[c & 1] = dp4a_us(w[c] & 0x0F0F0F0Fu, a.lo[c], d[c & 1]);
+            d[2 + (c & 1)] = dp4a_us(w[c] & 0xF0F0F0F0u, a.hi[c], d[2 + (c & 1)]);
+        }
+        d[2] = (d[2] + d[3]) >> 4;  // every high-nibble term carries a factor 16: exact
     }
-    return acc;
+    const int dlo = d[0] + d[1], dhi = d[2];
+    uint32_t scp, mp;
+    scale_pair(hdr, j, scp, mp);
+    const float sd = a.ts.x * (float)(dlo * (int)(scp & 0xffu)) + a.ts.y * (float)(dhi * (int)(scp >> 8));
+    const float sm = a.ts.z * (float)(mp & 0xffu) + a.ts.w * (float)(mp >> 8);
+    const float2 dm = __half22float2(*reinterpret_cast<const __half2 *>(&hdr.x));
+    return dm.x * sd - dm.y * sm;
 }
 
-// Quantise 32 values held one per lane into Q8_1 (quantize_q8_1, gguf.cuh:1234-1261;
-// quantize_silu_mul_q8_1, moe_gguf.cu:255-284): d = amax/127, q = roundf(v/d).
-// Writes q (lane), d and the two 16-lane sums.
-__device__ __forceinline__ void warp_quant_q81(float v, int8_t *q, float *d, int *s16, int lane) {
-    const float amax = warp_max_butterfly(fabsf(v));
-    const float dd = __fdiv_rn(amax, 127.0f);
-    const int qi = amax == 0.f ? 0 : (int)roundf(__fdiv_rn(v, dd));
-    q[lane] = (int8_t)qi;
-    int s = qi;
+// Dot of one row (in shared memory) over the lane's tasks tau = lig + L*i.
+template <int TYPE>
+__device__ __forceinline__ float row_dot(const uint8_t *row, int lig, int L, int ntasks, const TaskAct (&ta)[kTPL]) {
+    float v = 0.f;
 #pragma unroll
-    for (int m = 8; m > 0; m >>= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
-    if (lane == 0) {
-        *d = __half2float(__float2half_rn(dd));
-        s16[0] = s;
+    for (int i = 0; i < kTPL; ++i) {
+        const int tau = lig + L * i;
+        if (tau < ntasks) v += task_dot<TYPE>(row, tau, ta[i]);
     }
-    if (lane == 16) s16[1] = s;
+    return v;
+}
+
+// 128 consecutive values, lane l holding values 4l..4l+3 (Q8_1 blocks of 32 over 8 lanes):
+// d = amax/127, q = roundf(v/d) (quantize_q8_1, gguf.cuh:1234-1261).  Writes q, and per block the
+// fp16-rounded scale d and the sum of quants S.
+__device__ __forceinline__ void quant128(float4 v, int8_t *q, float *d, int *S, int lane) {
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+    for (int m = 4; m > 0; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+    const float dd = __fdiv_rn(amax, 127.0f);
+    int q0 = 0, q1 = 0, q2 = 0, q3 = 0;
+    if (amax != 0.f) {
+        q0 = (int)roundf(__fdiv_rn(v.x, dd));
+        q1 = (int)roundf(__fdiv_rn(v.y, dd));
+        q2 = (int)roundf(__fdiv_rn(v.z, dd));
+        q3 = (int)roundf(__fdiv_rn(v.w, dd));
+    }
+    reinterpret_cast<int *>(q)[lane] = (q0 & 0xff) | ((q1 & 0xff) << 8) | ((q2 & 0xff) << 16) | ((q3 & 0xff) << 24);
+    int s = q0 + q1 + q2 + q3;
+#pragma unroll
+    for (int m = 4; m > 0; m >>= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
+    if ((lane & 7) == 0) {
+        d[lane >> 3] = __half2float(__float2half_rn(dd));
+        S[lane >> 3] = s;
+    }
+}
+
+// Per-task scale records from per-block (d, S) arrays: nt tasks, 2 blocks each.
+__device__ __forceinline__ void build_task_scales(float4 *ts, const float *d, const int *S, int nt, int tid, int nthr) {
+    for (int t = tid; t < nt; t += nthr) {
+        const float dl = d[2 * t], dh = d[2 * t + 1];
+        ts[t] = make_float4(dl, dh, dl * (float)S[2 * t], dh * (float)S[2 * t + 1]);
+    }
+}
+
+// Consumer wait for unit k in stage st: first the stage's ticket (the producer has issued unit k
+// there), then the phase of the full barrier.  Bounded by the deadline.
+__device__ __forceinline__ bool wait_unit(uint64_t *full, const int *ticket, int k, int st, int stages,
+                                          uint64_t deadline) {
+    uint32_t spins = 0;
+    while (*reinterpret_cast<const volatile int *>(&ticket[st]) != k) {
+        if ((++spins & 255u) == 0 && globaltimer_ns() > deadline) return false;
+    }
+    return mbar_wait_bounded(&full[st], (uint32_t)(k / stages) & 1u, deadline);
+}
+
+// Unit enumeration shared by producer and consumers (identical sequences).
+struct GuUnit {
+    int slot, row0, n;
+};
+__device__ __forceinline__ GuUnit gu_unit_at(int p, int pend, int I, int U) {
+    GuUnit u;
+    u.slot = p / I;
+    u.row0 = p - u.slot * I;
+    const int a = pend - p, b = I - u.row0;
+    u.n = min(U, min(a, b));
+    return u;
 }
 
 struct DecodeSmem {
-    // carved from dynamic shared memory by the kernel
     uint8_t *stages;
-    uint64_t *full, *empty;
-    float *x;  // [H]
-    ActView xq, aq;  // aq: [8][I] q, [8][I/32] d, [8][I/16] s16
-    float *sel, *sig;  // [E]
-    int *ids;          // [8]
-    float *w;          // [8]
-    float *gu_vals;    // [2][4][2]
-    float *dn_vals;    // [2][8 rows max][8]
+    uint64_t *full, *empty, *abar;
+    int8_t *xq;                // [H]
+    float *xd;                 // [H/32]
+    int *xS;                   // [H/32]
+    float4 *xts;               // [H/64]
+    int8_t *aq_s;              // [8][I]
+    float *ad_s;               // [8][I/32]
+    int *aS_s;                 // [8][I/32]
+    float4 *ats;               // [8][I/64]
+    float *part;               // router slice sums [2][8] in P0, selection scores [E] in P1
+    float *sig;                // [E]
+    int *ids;                  // [8]
+    float *w;                  // [8]
+    float *dn_acc;             // [res_slots][8]
+    float *act_s;              // [act_slots]
+    float *gval, *uval;        // [act_slots] gate / up row values of this CTA's range
+    int4 *units;               // [kMaxUnits] (kind, slot, first row, rows)
+    int *unit_off;             // [kMaxUnits] offset of the first row in the CTA's range
+    int *ticket;               // [stages] index of the unit last issued into each stage
+    int *n_gu;
+    float *res_s;              // [res_slots]
+    uint32_t *base;
     int *flag;
 };
 
@@ -160,121 +241,169 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, cta = blockIdx.x;
     const int H = p.H, I = p.I, E = p.E;
-    const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
+    const uint64_t t_start = globaltimer_ns();
+    const uint64_t deadline = t_start + p.timeout_ns;
+    if (tid == 0 && p.trace) p.trace[cta * 16 + 0] = t_start;
 
-    // ---- carve shared memory ------------------------------------------------------------
     DecodeSmem s;
     {
         uint8_t *ptr = smem_raw;
-        s.stages = ptr;
-        ptr += (size_t)p.stages * p.stage_bytes;
-        s.full = reinterpret_cast<uint64_t *>(ptr);
-        ptr += sizeof(uint64_t) * p.stages;
-        s.empty = reinterpret_cast<uint64_t *>(ptr);
-        ptr += sizeof(uint64_t) * p.stages;
-        s.x = reinterpret_cast<float *>(ptr);
-        ptr += sizeof(float) * H;
-        s.xq.q = reinterpret_cast<int8_t *>(ptr);
-        ptr += H;
-        s.xq.d = reinterpret_cast<float *>(ptr);
-        ptr += sizeof(float) * (H / 32);
-        s.xq.s16 = reinterpret_cast<int *>(ptr);
-        ptr += sizeof(int) * (H / 16);
-        s.aq.q = reinterpret_cast<int8_t *>(ptr);
-        ptr += (size_t)kTopK * I;
-        s.aq.d = reinterpret_cast<float *>(ptr);
-        ptr += sizeof(float) * kTopK * (I / 32);
-        s.aq.s16 = reinterpret_cast<int *>(ptr);
-        ptr += sizeof(int) * kTopK * (I / 16);
-        s.sel = reinterpret_cast<float *>(ptr);
-        ptr += sizeof(float) * E;
-        s.sig = reinterpret_cast<float *>(ptr);
-        ptr += sizeof(float) * E;
-        s.ids = reinterpret_cast<int *>(ptr);
-        ptr += sizeof(int) * kTopK;
-        s.w = reinterpret_cast<float *>(ptr);
-        ptr += sizeof(float) * kTopK;
-        s.gu_vals = reinterpret_cast<float *>(ptr);
-        ptr += sizeof(float) * 16;
-        s.dn_vals = reinterpret_cast<float *>(ptr);
-        ptr += sizeof(float) * 2 * 8 * kTopK;
-        s.flag = reinterpret_cast<int *>(ptr);
+        auto take = [&](size_t bytes) {
+            uint8_t *r = ptr;
+            ptr += (bytes + 15) / 16 * 16;
+            return r;
+        };
+        s.stages = take((size_t)p.stages * p.stage_bytes);
+        s.full = reinterpret_cast<uint64_t *>(take(sizeof(uint64_t) * p.stages));
+        s.empty = reinterpret_cast<uint64_t *>(take(sizeof(uint64_t) * p.stages));
+        s.abar = reinterpret_cast<uint64_t *>(take(sizeof(uint64_t)));
+        s.xq = reinterpret_cast<int8_t *>(take(H));
+        s.xd = reinterpret_cast<float *>(take(sizeof(float) * (H / 32)));
+        s.xS = reinterpret_cast<int *>(take(sizeof(int) * (H / 32)));
+        s.xts = reinterpret_cast<float4 *>(take(sizeof(float4) * (H / 64)));
+        s.aq_s = reinterpret_cast<int8_t *>(take((size_t)kTopK * I));
+        s.ad_s = reinterpret_cast<float *>(take(sizeof(float) * kTopK * (I / 32)));
+        s.aS_s = reinterpret_cast<int *>(take(sizeof(int) * kTopK * (I / 32)));
+        s.ats = reinterpret_cast<float4 *>(take(sizeof(float4) * kTopK * (I / 64)));
+        s.part = reinterpret_cast<float *>(take(sizeof(float) * (E > 16 ? E : 16)));
+        s.sig = reinterpret_cast<float *>(take(sizeof(float) * E));
+        s.ids = reinterpret_cast<int *>(take(sizeof(int) * kTopK));
+        s.w = reinterpret_cast<float *>(take(sizeof(float) * kTopK));
+        s.dn_acc = reinterpret_cast<float *>(take(sizeof(float) * p.res_slots * kTopK));
+        s.act_s = reinterpret_cast<float *>(take(sizeof(float) * p.act_slots));
+        s.gval = reinterpret_cast<float *>(take(sizeof(float) * p.act_slots));
+        s.uval = reinterpret_cast<float *>(take(sizeof(float) * p.act_slots));
+        s.units = reinterpret_cast<int4 *>(take(sizeof(int4) * kMaxUnits));
+        s.unit_off = reinterpret_cast<int *>(take(sizeof(int) * kMaxUnits));
+        s.ticket = reinterpret_cast<int *>(take(sizeof(int) * p.stages));
+        s.n_gu = reinterpret_cast<int *>(take(16));
+        s.res_s = reinterpret_cast<float *>(take(sizeof(float) * p.res_slots));
+        s.base = reinterpret_cast<uint32_t *>(take(16));
+        s.flag = reinterpret_cast<int *>(take(16));
     }
     if (tid == 0) {
         for (int i = 0; i < p.stages; ++i) {
             mbar_init(&s.full[i], 1);
-            mbar_init(&s.empty[i], kConsumerWarps);
+            mbar_init(&s.empty[i], kGroupWarps);
+            s.ticket[i] = -1;
         }
+        mbar_init(s.abar, 1);
         fence_mbar_init();
-        s.flag[0] = 1;  // ok
+        s.flag[0] = 1;
     }
     __syncthreads();
 
-    const int gu_units_begin = (int)((int64_t)cta * p.n_gu_units / G);
-    const int gu_units_end = (int)((int64_t)(cta + 1) * p.n_gu_units / G);
-    const int dn_units_begin = (int)((int64_t)cta * p.n_dn_units / G);
-    const int dn_units_end = (int)((int64_t)(cta + 1) * p.n_dn_units / G);
-    const int n_gu = gu_units_end - gu_units_begin, n_dn = dn_units_end - dn_units_begin;
-    const int gu_units_per_slot = I / p.gu_rows;
+    const int gu_p0 = (int)((int64_t)cta * kTopK * I / G), gu_p1 = (int)((int64_t)(cta + 1) * kTopK * I / G);
+    const int dn_r0 = (int)((int64_t)cta * H / G), dn_r1 = (int)((int64_t)(cta + 1) * H / G);
     const size_t gu_row_bytes = kq_row_bytes(p.gu_type, H);
     const size_t dn_row_bytes = kq_row_bytes(p.dn_type, I);
     const size_t gu_expert_bytes = gu_row_bytes * I;
     const size_t dn_expert_bytes = dn_row_bytes * H;
 
-    // ---- P0: x -> smem, router GEMV, Q8_1 of x --------------------------------------------
+    // ---- P0: router slices, Q8_1 of x, residual prefetch (all loads issued before use) ----
     if (warp < kConsumerWarps) {
-        for (int i = tid; i < H / 4; i += kConsumerWarps * 32)
-            reinterpret_cast<float4 *>(s.x)[i] = __ldg(reinterpret_cast<const float4 *>(p.x) + i);
-        named_sync(1, kConsumerWarps * 32);
-        if (p.internal_routing) {
-            for (int e = cta + G * warp; e < E; e += G * kConsumerWarps) {
-                const float4 *wr = reinterpret_cast<const float4 *>(p.router + (size_t)e * H);
-                const float4 *xv = reinterpret_cast<const float4 *>(s.x);
-                float acc = 0.f;
-                for (int i = lane; i < H / 4; i += 32) {
-                    const float4 w4 = __ldg(wr + i);
-                    const float4 x4 = xv[i];
-                    acc = fmaf(w4.x, x4.x, acc);
-                    acc = fmaf(w4.y, x4.y, acc);
-                    acc = fmaf(w4.z, x4.z, acc);
-                    acc = fmaf(w4.w, x4.w, acc);
+        const int nxc = H / 128;  // chunks of 128 values
+        float4 xv[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int c = warp + kConsumerWarps * i;
+            if (c < nxc) xv[i] = __ldg(reinterpret_cast<const float4 *>(p.x) + c * 32 + lane);
+        }
+        float rv = 0.f;
+        const int rrow = dn_r0 + tid;
+        if (p.residual && rrow < dn_r1) rv = __ldg(p.residual + rrow);
+        const int slice = H / 8, groups = slice / 4, sl = warp & 7, le = warp >> 3;
+        const int e = cta + G * le;
+        const bool do_router = p.internal_routing && e < E;
+        float4 xx[4], wv[4];
+        if (do_router) {
+            const float4 *xs = reinterpret_cast<const float4 *>(p.x + sl * slice);
+            const float4 *wr = reinterpret_cast<const float4 *>(p.router + (size_t)e * H + sl * slice);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int g = lane + 32 * i;
+                if (g < groups) {
+                    xx[i] = __ldg(xs + g);
+                    wv[i] = __ldg(wr + g);
                 }
-                acc = warp_sum_butterfly(acc);
-                if (lane == 0) p.logits[e] = acc;
             }
         }
-        for (int b = warp; b < H / 32; b += kConsumerWarps)
-            warp_quant_q81(s.x[b * 32 + lane], s.xq.q + b * 32, s.xq.d + b, s.xq.s16 + 2 * b, lane);
+        // Per-block arrival counters are zeroed here: nothing increments them before barrier #1.
+        for (int b = cta * kConsumerThreads + tid; b < kTopK * (I / 32); b += G * kConsumerThreads)
+            p.blk_count[b] = 0u;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int c = warp + kConsumerWarps * i;
+            if (c < nxc) quant128(xv[i], s.xq + c * 128, s.xd + c * 4, s.xS + c * 4, lane);
+        }
+        if (p.residual && rrow < dn_r1) s.res_s[tid] = rv;
+        if (do_router) {
+            float acc = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int g = lane + 32 * i;
+                if (g < groups) {
+                    acc = fmaf(wv[i].x, xx[i].x, acc);
+                    acc = fmaf(wv[i].y, xx[i].y, acc);
+                    acc = fmaf(wv[i].z, xx[i].z, acc);
+                    acc = fmaf(wv[i].w, xx[i].w, acc);
+                }
+            }
+            acc = warp_sum_butterfly(acc);
+            if (lane == 0) s.part[le * 8 + sl] = acc;
+        }
+        if (tid == 0) s.base[0] = __ldcg(&p.ctl->epoch[cta]);
+        named_sync(1, kConsumerThreads);
+        build_task_scales(s.xts, s.xd, s.xS, H / 64, tid, kConsumerThreads);
+        if (p.internal_routing && tid < 2) {
+            const int ee = cta + G * tid;
+            if (ee < E) {
+                const float *q = s.part + tid * 8;
+                p.logits[ee] = ((q[0] + q[1]) + (q[2] + q[3])) + ((q[4] + q[5]) + (q[6] + q[7]));
+            }
+        }
     }
+    if (tid == 0 && p.trace) p.trace[cta * 16 + 1] = globaltimer_ns();
 
-    // ---- P1: routing (all CTAs redundantly) -----------------------------------------------
-    bool ok = true;
+    // ---- P1: routing ----------------------------------------------------------------------
+    __syncthreads();
+    const uint32_t epoch = s.base[0];
+    bool ok = grid_sync(p.ctl, (uint32_t)G * (epoch + 1u), deadline, s.flag, 2, kThreads);
+    if (tid == 0 && p.trace) p.trace[cta * 16 + 2] = globaltimer_ns();
     if (p.internal_routing) {
-        ok = grid_barrier(p.bar, G, deadline, s.flag, 2, kThreads);
         if (ok) {
             for (int e = tid; e < E; e += kThreads) {
                 const float l = __ldcg(p.logits + e);
                 const float sg = __fdiv_rn(1.0f, 1.0f + expf(-l));
                 s.sig[e] = sg;
-                s.sel[e] = sg + p.bias[e];
+                s.part[e] = sg + p.bias[e];  // selection score
             }
             __syncthreads();
+            // rank_e = #{j : sel_j > sel_e} + #{j < e : sel_j == sel_e}  (stable descending order)
             for (int e = tid; e < E; e += kThreads) {
-                const float me = s.sel[e];
-                int rank = 0;
-                for (int j = 0; j < E; ++j) {
-                    const float o = s.sel[j];
-                    rank += (o > me) || (o == me && j < e);
+                const float me = s.part[e];
+                int r0 = 0, r1 = 0, r2 = 0, r3 = 0;
+                const float4 *sel4 = reinterpret_cast<const float4 *>(s.part);
+                for (int j4 = 0; j4 < E / 4; ++j4) {
+                    const float4 o = sel4[j4];
+                    const int j = 4 * j4;
+                    r0 += (o.x > me) | ((o.x == me) & (j + 0 < e));
+                    r1 += (o.y > me) | ((o.y == me) & (j + 1 < e));
+                    r2 += (o.z > me) | ((o.z == me) & (j + 2 < e));
+                    r3 += (o.w > me) | ((o.w == me) & (j + 3 < e));
                 }
+                const int rank = (r0 + r1) + (r2 + r3);
                 if (rank < kTopK) s.ids[rank] = e;
             }
             __syncthreads();
-            if (tid == 0) {
-                float v[kTopK];
-                for (int k = 0; k < kTopK; ++k) v[k] = s.sig[s.ids[k]];
-                const float a0 = v[0] + v[4], a1 = v[1] + v[5], a2 = v[2] + v[6], a3 = v[3] + v[7];
-                const float denom = (a0 + a2) + (a1 + a3);
-                for (int k = 0; k < kTopK; ++k) s.w[k] = __fdiv_rn(v[k], denom);
+            if (warp == 0) {
+                __syncwarp();
+                if (lane == 0) {
+                    float v[kTopK];
+                    for (int k = 0; k < kTopK; ++k) v[k] = s.sig[s.ids[k]];
+                    const float denom = ((v[0] + v[4]) + (v[2] + v[6])) + ((v[1] + v[5]) + (v[3] + v[7]));
+                    for (int k = 0; k < kTopK; ++k) s.w[k] = __fdiv_rn(v[k], denom);
+                }
             }
             __syncthreads();
             if (cta == 0 && tid < kTopK) {
@@ -289,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         }
         __syncthreads();
         if (tid < kTopK) {
-            // pairs (route, expert) in expert order; routes outside [0, 8) and invalid experts
+            // (route, expert) pairs in expert order; routes outside [0, 8) and invalid experts
             // contribute nothing, as in moe_down_decode_kernel (moe_gguf.cu:311)
             const int slot = p.ext_route[tid];
             const int e = p.ext_expert[tid];
@@ -300,189 +429,323 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         }
         __syncthreads();
     }
+    if (!ok) return;  // nothing issued yet
+    if (tid == 0 && p.trace) p.trace[cta * 16 + 3] = globaltimer_ns();
 
-    if (!ok) {
-        // nothing was issued yet: just leave
-        return;
+    // Unit table.  Every unit is ONE contiguous bulk copy (few, large TMA operations keep the
+    // per-SM copy engine at HBM rate): a chunk of up to U_gu rows of the gate or of the up matrix
+    // of one routed expert (gate chunk, then the matching up chunk), then one down unit per routed
+    // expert covering this CTA's output rows (split every U_dn rows).  Unit k goes to ring stage
+    // k % stages and to consumer group k % kGroups.  Entry: (kind 0 gate / 1 up / 2 down, slot,
+    // first row, rows); for gate/up the offset of the first row in the CTA's (slot,row) range is
+    // row-offset field .w >> 8 ... stored separately in gu_off.
+    const int U_gu = p.gu_unit_rows, U_dn = p.dn_unit_rows;
+    if (tid == 0) {
+        int n = 0;
+        for (int q = gu_p0; q < gu_p1 && n + 2 <= kMaxUnits;) {
+            const GuUnit u = gu_unit_at(q, gu_p1, I, U_gu);
+            s.units[n] = make_int4(0, u.slot, u.row0, u.n);
+            s.unit_off[n++] = q - gu_p0;
+            s.units[n] = make_int4(1, u.slot, u.row0, u.n);
+            s.unit_off[n++] = q - gu_p0;
+            q += u.n;
+        }
+        s.n_gu[0] = n;
+        for (int r = dn_r0; r < dn_r1 && n < kMaxUnits; r += U_dn) {
+            s.units[n] = make_int4(2, 0, r, min(U_dn, dn_r1 - r));
+            s.unit_off[n++] = r - dn_r0;
+        }
+        s.n_gu[1] = n;
     }
+    __syncthreads();
+    const int n_gu = s.n_gu[0];
+    const int n_units = s.n_gu[1];
 
     if (warp == kConsumerWarps) {
         // ---------------------------- producer --------------------------------------------
         if (lane == 0) {
-            int it = 0;
-            bool pok = true;
-            const int total = n_gu + n_dn;
-            for (; it < total && pok; ++it) {
-                const int st = it % p.stages;
-                const uint32_t ph = (uint32_t)(it / p.stages) & 1u;
-                if (!mbar_wait_bounded(&s.empty[st], ph ^ 1u, deadline)) {
-                    pok = false;
-                    atomicExch(&p.bar->status, (uint32_t)MMRS_ERR_TIMEOUT);
+            auto unit_src = [&](int k, uint32_t &bytes) -> const uint8_t * {
+                const int4 u = s.units[k];
+                const int e = s.ids[u.y];
+                if (e < 0) return nullptr;
+                if (u.x < 2) {
+                    bytes = (uint32_t)(gu_row_bytes * u.w);
+                    return (u.x == 0 ? p.gate : p.up) + (size_t)e * gu_expert_bytes + (size_t)u.z * gu_row_bytes;
+                }
+                bytes = (uint32_t)(dn_row_bytes * u.w);
+                return p.down + (size_t)e * dn_expert_bytes + (size_t)u.z * dn_row_bytes;
+            };
+            int k = 0;
+            for (; k < n_units; ++k) {
+                const int st = k % p.stages;
+                if (!mbar_wait_bounded(&s.empty[st], ((uint32_t)(k / p.stages) & 1u) ^ 1u, deadline)) {
+                    atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
                     break;
                 }
+                if (k == 0 && p.trace) p.trace[cta * 16 + 8] = globaltimer_ns();
+                if (k == n_gu && p.trace) p.trace[cta * 16 + 10] = globaltimer_ns();
+                // Publish which unit this stage now holds.  Consumer groups take interleaved units,
+                // so a group can reach unit k before unit k - stages (another group's) has landed;
+                // waiting for the ticket first keeps the parity wait from aliasing onto that phase.
+                *reinterpret_cast<volatile int *>(&s.ticket[st]) = k;
+                const int4 u = s.units[k];
                 uint8_t *dst = s.stages + (size_t)st * p.stage_bytes;
-                if (it < n_gu) {
-                    const int u = gu_units_begin + it;
-                    const int slot = u / gu_units_per_slot;
-                    const int row0 = (u % gu_units_per_slot) * p.gu_rows;
-                    const int e = s.ids[slot];
-                    const uint32_t bytes = (uint32_t)(gu_row_bytes * p.gu_rows);
-                    if (e >= 0) {
-                        mbar_arrive_expect_tx(&s.full[st], 2 * bytes);
-                        const size_t off = (size_t)e * gu_expert_bytes + (size_t)row0 * gu_row_bytes;
-                        bulk_g2s(dst, p.gate + off, bytes, &s.full[st]);
-                        bulk_g2s(dst + bytes, p.up + off, bytes, &s.full[st]);
-                    } else {
-                        mbar_arrive(&s.full[st]);
-                    }
-                } else {
-                    const int u = dn_units_begin + (it - n_gu);
-                    const int row0 = u * p.dn_rows;
-                    const uint32_t bytes = (uint32_t)(dn_row_bytes * p.dn_rows);
+                if (u.x == 2) {
+                    // rows [u.z, u.z + u.w) of all routed experts, expert q at dst + q * U_dn rows
+                    const uint32_t bytes = (uint32_t)(dn_row_bytes * u.w);
                     uint32_t tx = 0;
-                    for (int k = 0; k < kTopK; ++k) tx += s.ids[k] >= 0 ? bytes : 0;
+                    for (int q = 0; q < kTopK; ++q) tx += s.ids[q] >= 0 ? bytes : 0;
                     mbar_arrive_expect_tx(&s.full[st], tx);
-                    for (int k = 0; k < kTopK; ++k) {
-                        const int e = s.ids[k];
+                    for (int q = 0; q < kTopK; ++q) {
+                        const int e = s.ids[q];
                         if (e < 0) continue;
-                        bulk_g2s(dst + (size_t)k * bytes,
-                                 p.down + (size_t)e * dn_expert_bytes + (size_t)row0 * dn_row_bytes, bytes,
-                                 &s.full[st]);
+                        bulk_g2s(dst + (size_t)q * dn_row_bytes * U_dn,
+                                 p.down + (size_t)e * dn_expert_bytes + (size_t)u.z * dn_row_bytes, bytes, &s.full[st]);
                     }
+                    continue;
                 }
+                uint32_t bytes = 0;
+                const uint8_t *src = unit_src(k, bytes);
+                if (!src) {
+                    mbar_arrive(&s.full[st]);
+                    continue;
+                }
+                mbar_arrive_expect_tx(&s.full[st], bytes);
+                bulk_g2s(dst, src, bytes, &s.full[st]);
             }
-            // Drain: make sure no copy is still landing in shared memory when the CTA retires.
-            const int first = it > p.stages ? it - p.stages : 0;
-            for (int j = first; j < it; ++j)
+            if (p.trace) p.trace[cta * 16 + 9] = globaltimer_ns();
+            // Drain: no copy may still be landing in shared memory when the CTA retires.
+            const int first = k > p.stages ? k - p.stages : 0;
+            for (int j = first; j < k; ++j)
                 mbar_wait_bounded(&s.full[j % p.stages], (uint32_t)(j / p.stages) & 1u, deadline + 1000000000ull);
         }
         return;
     }
 
     // ------------------------------- consumers ----------------------------------------------
-    // P2: gate/up.  warp w -> row (w >> 1) of the unit, matrix (w & 1): 0 = gate, 1 = up.
+    const int grp = warp / kGroupWarps, gw = warp % kGroupWarps;
     bool aborted = false;
-    const int gu_tasks = (H / QK_K) * 8;
     {
-        LaneAct la;
-        load_lane_act(s.xq, lane, 32, gu_tasks, la);
-        const int r = warp >> 1, mat = warp & 1;
-        for (int it = 0; it < n_gu; ++it) {
-            const int st = it % p.stages;
-            // On a timeout keep iterating without waiting so every named barrier still matches.
-            if (!aborted && !mbar_wait_bounded(&s.full[st], (uint32_t)(it / p.stages) & 1u, deadline)) {
-                atomicExch(&p.bar->status, (uint32_t)MMRS_ERR_TIMEOUT);
+        // P2: gate / up chunks.  A lane group of L lanes computes two rows of the chunk against the
+        // register-resident Q8_1 x (6 independent 64-weight task dots per lane).
+        const int L = p.gu_lanes;
+        const int lgi = gw * (32 / L) + lane / L, lig = lane % L;
+        const int rA = lgi * kRowsPerLane, rB = rA + 1;
+        const int ntasks = (H / QK_K) * 4;
+        TaskAct ta[kTPL];
+        load_task_acts(ActView{s.xq, s.xts}, lig, L, ntasks, ta);
+        for (int k = grp; k < n_gu; k += kGroups) {
+            const int4 u = s.units[k];
+            const int st = k % p.stages;
+            if (!aborted && !wait_unit(s.full, s.ticket, k, st, p.stages, deadline)) {
+                atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
                 aborted = true;
             }
-            const int u = gu_units_begin + it;
-            const int slot = u / gu_units_per_slot;
-            const int row = (u % gu_units_per_slot) * p.gu_rows + r;
-            const uint8_t *src = s.stages + (size_t)st * p.stage_bytes + (size_t)mat * gu_row_bytes * p.gu_rows +
-                                 (size_t)r * gu_row_bytes;
-            float v = 0.f;
-            if (!aborted && s.ids[slot] >= 0)
-                v = p.gu_type == MMRS_Q5K ? row_partial<MMRS_Q5K>(src, lane, 32, gu_tasks, la)
-                                          : row_partial<MMRS_Q4K>(src, lane, 32, gu_tasks, la);
-            v = warp_sum_butterfly(v);
+            float vA = 0.f, vB = 0.f;
+            if (!aborted && s.ids[u.y] >= 0 && rA < u.w) {
+                const uint8_t *base = s.stages + (size_t)st * p.stage_bytes;
+                const uint8_t *rowA = base + (size_t)rA * gu_row_bytes;
+                const uint8_t *rowB = base + (size_t)min(rB, u.w - 1) * gu_row_bytes;
+                if (p.gu_type == MMRS_Q5K) {
+                    vA = row_dot<MMRS_Q5K>(rowA, lig, L, ntasks, ta);
+                    vB = row_dot<MMRS_Q5K>(rowB, lig, L, ntasks, ta);
+                } else {
+                    vA = row_dot<MMRS_Q4K>(rowA, lig, L, ntasks, ta);
+                    vB = row_dot<MMRS_Q4K>(rowB, lig, L, ntasks, ta);
+                }
+            }
+#pragma unroll
+            for (int m = 16; m > 0; m >>= 1)
+                if (m < L) {
+                    vA += __shfl_xor_sync(0xffffffffu, vA, m);
+                    vB += __shfl_xor_sync(0xffffffffu, vB, m);
+                }
             __syncwarp();
             if (lane == 0) mbar_arrive(&s.empty[st]);
-            float *gv = s.gu_vals + (it & 1) * 8;
-            if (lane == 0) gv[r * 2 + mat] = v;
-            named_sync(3 + r, 64);
-            if (mat == 0 && lane == 0) {
-                const float g = gv[r * 2 + 0], up = gv[r * 2 + 1];
-                p.act[(size_t)slot * I + row] = up * __fdiv_rn(g, 1.0f + expf(-g));
+            if (lig == 0) {
+                float *gv = (u.x == 0 ? s.gval : s.uval) + s.unit_off[k];
+                if (rA < u.w) gv[rA] = vA;
+                if (rB < u.w) gv[rB] = vB;
+            }
+        }
+        named_sync(1, kConsumerThreads);
+        // act = up * silu(gate) (moe_gguf.cu:272-273) for the CTA's whole range
+        for (int i = tid; i < gu_p1 - gu_p0; i += kConsumerThreads) {
+            const float g = s.gval[i];
+            const int slot = (gu_p0 + i) / I;
+            s.act_s[i] = (!aborted && s.ids[slot] >= 0) ? s.uval[i] * __fdiv_rn(g, 1.0f + expf(-g)) : 0.f;
+        }
+        // Q8_1 of act (quantize_silu_mul_q8_1, moe_gguf.cu:255-284) per 32-row block.  Blocks inside
+        // this CTA's range are quantised from shared memory; a block shared with neighbour CTAs is
+        // published through global scratch and quantised by whichever CTA completes it (one
+        // acq_rel arrival per CTA and block).
+        named_sync(1, kConsumerThreads);
+        if (gu_p1 > gu_p0) {
+            const int b_first = gu_p0 >> 5, b_last = (gu_p1 - 1) >> 5;
+            for (int b = b_first + warp; b <= b_last; b += kConsumerWarps) {
+                const int r = b * 32 + lane;
+                const bool inside = r >= gu_p0 && r < gu_p1;
+                const int lo = max(b * 32, gu_p0), hi = min(b * 32 + 32, gu_p1);
+                bool mine = true;
+                if (hi - lo < 32) {
+                    if (inside) p.act[r] = s.act_s[r - gu_p0];
+                    __syncwarp();
+                    uint32_t old = 0;
+                    if (lane == 0)
+                        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
+                                     : "=r"(old)
+                                     : "l"(p.blk_count + b), "r"((uint32_t)(hi - lo))
+                                     : "memory");
+                    old = __shfl_sync(0xffffffffu, old, 0);
+                    mine = old + (uint32_t)(hi - lo) == 32u;
+                    __syncwarp();
+                }
+                if (mine && !aborted) {
+                    const float v32 = inside ? s.act_s[r - gu_p0] : __ldcg(p.act + r);
+                    const float amax = warp_max_butterfly(fabsf(v32));
+                    const float dd = __fdiv_rn(amax, 127.0f);
+                    const int q = amax == 0.f ? 0 : (int)roundf(__fdiv_rn(v32, dd));
+                    int sq = q;
+#pragma unroll
+                    for (int m = 16; m > 0; m >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, m);
+                    p.aq[r] = (int8_t)q;
+                    if (lane == 0) {
+                        p.ad[b] = __half2float(__float2half_rn(dd));
+                        p.aS[b] = sq;
+                    }
+                }
             }
         }
     }
 
-    // P3: grid barrier, quantise act, down.
-    if (!grid_barrier(p.bar, G, deadline, s.flag, 7, kConsumerWarps * 32)) aborted = true;
-    for (int b = warp; b < kTopK * (I / 32); b += kConsumerWarps) {
-        const int slot = b / (I / 32), bb = b % (I / 32);
-        const float v = __ldcg(p.act + (size_t)slot * I + bb * 32 + lane);
-        warp_quant_q81(v, s.aq.q + (size_t)slot * I + bb * 32, s.aq.d + slot * (I / 32) + bb,
-                       s.aq.s16 + slot * (I / 16) + 2 * bb, lane);
+    // P3: grid barrier, activation copy, down.
+    if (tid == 0 && p.trace) p.trace[cta * 16 + 4] = globaltimer_ns();
+    const bool sync_ok = grid_sync(p.ctl, (uint32_t)G * (epoch + 2u), deadline, s.flag, 7, kConsumerThreads);
+    if (!sync_ok) aborted = true;
+    if (tid == 0) {
+        if (sync_ok) p.ctl->epoch[cta] = epoch + 2u;  // read again only by this CTA's next launch
+        if (p.trace) p.trace[cta * 16 + 5] = globaltimer_ns();
     }
-    named_sync(1, kConsumerWarps * 32);
     {
-        const int dn_tasks = (I / QK_K) * 8;
-        const int group_lanes = 32 / p.dn_rows;
-        const int grp = lane / group_lanes, lig = lane % group_lanes;
-        const int slot = warp;
-        LaneAct la;
-        const ActView aslot = {s.aq.q + (size_t)slot * I, s.aq.d + slot * (I / 32), s.aq.s16 + slot * (I / 16)};
-        load_lane_act(aslot, lig, group_lanes, dn_tasks, la);
+        // One bulk copy of the quantised activation [8][I] (+ scales, sums) per CTA.  Issue and
+        // wait depend only on the CTA-uniform barrier result, so the copy has always landed
+        // before any consumer thread moves on.
+        const uint32_t qb = (uint32_t)(kTopK * I), sb = (uint32_t)(sizeof(float) * kTopK * (I / 32));
+        if (tid == 0 && sync_ok) {
+            asm volatile("fence.proxy.async;" ::: "memory");  // generic writes -> async-proxy reads
+            mbar_arrive_expect_tx(s.abar, qb + 2 * sb);
+            bulk_g2s(s.aq_s, p.aq, qb, s.abar);
+            bulk_g2s(s.ad_s, p.ad, sb, s.abar);
+            bulk_g2s(s.aS_s, p.aS, sb, s.abar);
+        }
+        if (sync_ok && !mbar_wait_bounded(s.abar, 0u, deadline + 1000000000ull)) {
+            atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
+            aborted = true;
+        }
+        build_task_scales(s.ats, s.ad_s, s.aS_s, kTopK * (I / 64), tid, kConsumerThreads);
+        named_sync(1, kConsumerThreads);
+        if (tid == 0 && p.trace) p.trace[cta * 16 + 6] = globaltimer_ns();
+
+        // Down units: U_dn rows x all 8 routed experts.  A lane group of L lanes computes one expert
+        // (slot) for two rows, with that slot's activation in registers.
+        const int L = p.dn_lanes;
+        const int q = gw * (32 / L) + lane / L, lig = lane % L;
+        const int slot = q % kTopK, rA = (q / kTopK) * kRowsPerLane, rB = rA + 1;
+        const int ntasks = (I / QK_K) * 4;
+        TaskAct ta[kTPL];
+        load_task_acts(ActView{s.aq_s + (size_t)slot * I, s.ats + slot * (I / 64)}, lig, L, ntasks, ta);
         const float wslot = s.w[slot];
         const bool valid = s.ids[slot] >= 0;
-        for (int j = 0; j < n_dn; ++j) {
-            const int it = n_gu + j;
-            const int st = it % p.stages;
-            if (!aborted && !mbar_wait_bounded(&s.full[st], (uint32_t)(it / p.stages) & 1u, deadline)) {
-                atomicExch(&p.bar->status, (uint32_t)MMRS_ERR_TIMEOUT);
+        const int j0 = ((grp - n_gu) % kGroups + kGroups) % kGroups;
+        for (int k = n_gu + j0; k < n_units; k += kGroups) {
+            const int4 u = s.units[k];
+            const int st = k % p.stages;
+            if (!aborted && !wait_unit(s.full, s.ticket, k, st, p.stages, deadline)) {
+                atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
                 aborted = true;
             }
-            const uint8_t *src = s.stages + (size_t)st * p.stage_bytes + (size_t)slot * dn_row_bytes * p.dn_rows +
-                                 (size_t)grp * dn_row_bytes;
-            float v = 0.f;
-            if (valid && !aborted)
-                v = p.dn_type == MMRS_Q5K ? row_partial<MMRS_Q5K>(src, lig, group_lanes, dn_tasks, la)
-                                          : row_partial<MMRS_Q4K>(src, lig, group_lanes, dn_tasks, la);
+            float vA = 0.f, vB = 0.f;
+            if (valid && !aborted && rA < u.w) {
+                const uint8_t *base = s.stages + (size_t)st * p.stage_bytes + (size_t)slot * dn_row_bytes * U_dn;
+                const uint8_t *rowA = base + (size_t)rA * dn_row_bytes;
+                const uint8_t *rowB = base + (size_t)min(rB, u.w - 1) * dn_row_bytes;
+                if (p.dn_type == MMRS_Q5K) {
+                    vA = row_dot<MMRS_Q5K>(rowA, lig, L, ntasks, ta);
+                    vB = row_dot<MMRS_Q5K>(rowB, lig, L, ntasks, ta);
+                } else {
+                    vA = row_dot<MMRS_Q4K>(rowA, lig, L, ntasks, ta);
+                    vB = row_dot<MMRS_Q4K>(rowB, lig, L, ntasks, ta);
+                }
+            }
 #pragma unroll
             for (int m = 16; m > 0; m >>= 1)
-                if (m < group_lanes) v += __shfl_xor_sync(0xffffffffu, v, m);
+                if (m < L) {
+                    vA += __shfl_xor_sync(0xffffffffu, vA, m);
+                    vB += __shfl_xor_sync(0xffffffffu, vB, m);
+                }
             __syncwarp();
             if (lane == 0) mbar_arrive(&s.empty[st]);
-            float *dv = s.dn_vals + (j & 1) * 8 * kTopK;
-            if (lig == 0) dv[grp * kTopK + slot] = valid ? v * wslot : 0.f;
-            named_sync(1, kConsumerWarps * 32);
-            if (warp == 0 && lane < p.dn_rows) {
-                const float *q = dv + lane * kTopK;
-                float y = ((q[0] + q[4]) + (q[2] + q[6])) + ((q[1] + q[5]) + (q[3] + q[7]));
-                const int row = (dn_units_begin + j) * p.dn_rows + lane;
-                if (p.residual) y = y + p.residual[row];
-                p.y[row] = y;
+            if (lig == 0) {
+                const int off = s.unit_off[k];
+                if (rA < u.w) s.dn_acc[(off + rA) * kTopK + slot] = valid ? vA * wslot : 0.f;
+                if (rB < u.w) s.dn_acc[(off + rB) * kTopK + slot] = valid ? vB * wslot : 0.f;
             }
         }
+        // y = fixed 8-way tree over the routed experts (moe_gguf.cu:328-342) + residual
+        named_sync(1, kConsumerThreads);
+        for (int r = tid; r < dn_r1 - dn_r0; r += kConsumerThreads) {
+            const float *q = s.dn_acc + r * kTopK;
+            float y = ((q[0] + q[4]) + (q[2] + q[6])) + ((q[1] + q[5]) + (q[3] + q[7]));
+            if (p.residual) y = y + s.res_s[r];
+            p.y[dn_r0 + r] = y;
+        }
     }
+    if (tid == 0 && p.trace) p.trace[cta * 16 + 7] = globaltimer_ns();
 }
 
 // ------------------------------------------------------------------------------------------
 // Host side
 // ------------------------------------------------------------------------------------------
 size_t decode_smem_bytes(const DecodeParams &p) {
-    size_t b = (size_t)p.stages * p.stage_bytes + 2 * sizeof(uint64_t) * p.stages;
-    b += sizeof(float) * p.H + p.H + sizeof(float) * (p.H / 32) + sizeof(int) * (p.H / 16);
-    b += (size_t)kTopK * (p.I + sizeof(float) * (p.I / 32) + sizeof(int) * (p.I / 16));
-    b += 2 * sizeof(float) * p.E + 2 * sizeof(int) * kTopK + sizeof(float) * (16 + 2 * 8 * kTopK) + 16;
+    auto a16 = [](size_t v) { return (v + 15) / 16 * 16; };
+    size_t b = a16((size_t)p.stages * p.stage_bytes) + 2 * a16(sizeof(uint64_t) * p.stages) + a16(8);
+    b += a16(p.H) + 2 * a16(4 * (p.H / 32)) + a16(16 * (p.H / 64));
+    b += a16((size_t)kTopK * p.I) + 2 * a16(4 * kTopK * (p.I / 32)) + a16(16 * kTopK * (p.I / 64));
+    b += a16(4 * (p.E > 16 ? p.E : 16)) + a16(4 * p.E) + 2 * a16(4 * kTopK);
+    b += a16(4 * p.res_slots * kTopK) + 3 * a16(4 * p.act_slots) + a16(4 * p.res_slots) + 32;
+    b += a16(16 * kMaxUnits) + a16(4 * kMaxUnits) + 16 + a16(4 * p.stages);
     return b;
 }
 
+static int pow2_at_least(int v) {
+    int r = 1;
+    while (r < v) r <<= 1;
+    return r;
+}
+
 int decode_configure(DecodeParams &p, int num_sms, int max_smem) {
-    if (p.H % QK_K || p.I % QK_K || p.H > 4096 || p.E > 1024 || p.E < kTopK) return MMRS_ERR_UNSUPPORTED;
+    if (p.H % QK_K || p.I % QK_K || p.E < kTopK || p.E > 256 || p.E % 4) return MMRS_ERR_UNSUPPORTED;
     if ((p.gu_type != MMRS_Q4K && p.gu_type != MMRS_Q5K) || (p.dn_type != MMRS_Q4K && p.dn_type != MMRS_Q5K))
         return MMRS_ERR_UNSUPPORTED;
-    const int dn_blocks = p.I / QK_K;
-    if (dn_blocks > 16) return MMRS_ERR_UNSUPPORTED;
-    p.gu_rows = 4;
-    // rows per down unit so that every lane gets <= kMaxTPL tasks of 16 quant bytes
-    int dn_rows = 1;
-    for (int r = 8; r >= 1; r /= 2) {
-        const int lanes = 32 / r;
-        if ((dn_blocks * 8 + lanes - 1) / lanes <= kMaxTPL && p.H % r == 0) {
-            dn_rows = r;
-            break;
-        }
-    }
-    p.dn_rows = dn_rows;
-    if ((dn_blocks * 8 + (32 / dn_rows) - 1) / (32 / dn_rows) > kMaxTPL) return MMRS_ERR_UNSUPPORTED;
-    if ((p.H / QK_K) * 8 > 32 * kMaxTPL) return MMRS_ERR_UNSUPPORTED;
-    p.n_gu_units = kTopK * (p.I / p.gu_rows);
-    p.n_dn_units = p.H / p.dn_rows;
-    const size_t gu_stage = 2 * kq_row_bytes(p.gu_type, p.H) * p.gu_rows;
-    const size_t dn_stage = kTopK * kq_row_bytes(p.dn_type, p.I) * p.dn_rows;
+    if (p.H / 128 > 2 * kConsumerWarps || p.H / 8 / 4 > 128) return MMRS_ERR_UNSUPPORTED;  // H <= 4096
+    const int gu_tasks = (p.H / QK_K) * 4, dn_tasks = (p.I / QK_K) * 4;
+    p.gu_lanes = pow2_at_least((gu_tasks + kTPL - 1) / kTPL);
+    p.dn_lanes = pow2_at_least((dn_tasks + kTPL - 1) / kTPL);
+    if (p.gu_lanes > 16 || p.dn_lanes > 32) return MMRS_ERR_UNSUPPORTED;  // H <= 3072, I <= 6144
+    // units: kGroupWarps warps x (32/L) lane groups x kRowsPerLane rows
+    p.gu_unit_rows = kGroupWarps * (32 / p.gu_lanes) * kRowsPerLane;
+    p.dn_unit_rows = kGroupWarps * (32 / p.dn_lanes) * kRowsPerLane / kTopK;
+    if (p.dn_unit_rows < kRowsPerLane) return MMRS_ERR_UNSUPPORTED;
+    p.act_slots = (kTopK * p.I + num_sms - 1) / num_sms + 1;
+    p.res_slots = (p.H + num_sms - 1) / num_sms + 1;
+    if (p.res_slots > kConsumerThreads || p.E > 2 * num_sms) return MMRS_ERR_UNSUPPORTED;
+    const int max_gu_units = 2 * ((p.act_slots + p.gu_unit_rows - 1) / p.gu_unit_rows + kTopK);
+    const int max_dn_units = (p.res_slots + p.dn_unit_rows - 1) / p.dn_unit_rows;
+    if (max_gu_units + max_dn_units > kMaxUnits) return MMRS_ERR_UNSUPPORTED;
+    const size_t gu_stage = kq_row_bytes(p.gu_type, p.H) * p.gu_unit_rows;
+    const size_t dn_stage = kq_row_bytes(p.dn_type, p.I) * p.dn_unit_rows * kTopK;
     p.stage_bytes = (int)(((gu_stage > dn_stage ? gu_stage : dn_stage) + 127) / 128 * 128);
-    p.stages = 1;
+    p.stages = 0;
     DecodeParams q = p;
     for (int st = 16; st >= 2; --st) {
         q.stages = st;
@@ -491,7 +754,7 @@ int decode_configure(DecodeParams &p, int num_sms, int max_smem) {
             break;
         }
     }
-    if (decode_smem_bytes(p) > (size_t)max_smem) return MMRS_ERR_UNSUPPORTED;
+    if (p.stages == 0) return MMRS_ERR_UNSUPPORTED;
     p.grid = num_sms;
     return MMRS_OK;
 }

@@ -5,7 +5,7 @@
 
 namespace mmrs {
 
-struct GridBarrier;
+struct GridFlags;
 
 struct DecodeParams {
     const float *x;       // [H] f32
@@ -24,14 +24,20 @@ struct DecodeParams {
     const float *ext_w;
     int internal_routing;
     // workspace
-    float *logits;  // [E]
-    float *act;     // [8][I]
-    GridBarrier *bar;
+    float *logits;        // [E]
+    float *act;           // [8][I] f32 up * silu(gate)
+    int8_t *aq;           // [8][I] Q8_1 quants of act
+    float *ad;            // [8][I/32] fp16-rounded Q8_1 scales
+    int *aS;              // [8][I/32] sums of quants
+    uint32_t *blk_count;  // [8][I/32] rows written per Q8_1 block (zero between launches)
+    GridFlags *ctl;
+    uint64_t *trace;  // [grid][16] globaltimer stamps per phase, or null
     // shape
     int E, H, I;
     int gu_type, dn_type;
     // launch configuration (decode_configure)
-    int gu_rows, dn_rows, n_gu_units, n_dn_units, stages, stage_bytes, grid;
+    int gu_lanes, gu_unit_rows, dn_lanes, dn_unit_rows, stages, stage_bytes, grid;
+    int act_slots, res_slots;
     uint64_t timeout_ns;
 };
 

@@ -358,21 +358,30 @@ float orc_dot_kq_mmq(int gguf_type, const uint8_t *wrow, const int8_t *q, const 
 /* ------------------------------------------------------------------------------------ */
 /* Routing                                                                               */
 /* ------------------------------------------------------------------------------------ */
+/* Canonical router dot: K is cut into 8 contiguous slices; in slice s, lane l (0..31) accumulates
+ * the float4 groups l, l+32, ... of that slice with fmaf (components in order); the 32 lane
+ * partials are summed by xor-butterfly and the 8 slice sums by ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7)).
+ * The CUDA kernels compute exactly this order, so the logits are bit-identical. */
 HOT static float router_dot(const float *x, const float *w, int K) {
-    float lane[32];
-    const int groups = K / 128;
-    for (int l = 0; l < 32; ++l) {
-        float acc = 0.0f;
-        for (int i = 0; i < groups; ++i) {
-            const int base = 4 * (l + 32 * i);
-            acc = fmaf(w[base + 0], x[base + 0], acc);
-            acc = fmaf(w[base + 1], x[base + 1], acc);
-            acc = fmaf(w[base + 2], x[base + 2], acc);
-            acc = fmaf(w[base + 3], x[base + 3], acc);
+    const int slice = K / 8, groups = slice / 4;
+    float ss[8];
+    for (int sl = 0; sl < 8; ++sl) {
+        float lane[32];
+        const float *xs = x + sl * slice, *ws = w + sl * slice;
+        for (int l = 0; l < 32; ++l) {
+            float acc = 0.0f;
+            for (int g = l; g < groups; g += 32) {
+                const int base = 4 * g;
+                acc = fmaf(ws[base + 0], xs[base + 0], acc);
+                acc = fmaf(ws[base + 1], xs[base + 1], acc);
+                acc = fmaf(ws[base + 2], xs[base + 2], acc);
+                acc = fmaf(ws[base + 3], xs[base + 3], acc);
+            }
+            lane[l] = acc;
         }
-        lane[l] = acc;
+        ss[sl] = butterfly32(lane);
     }
-    return butterfly32(lane);
+    return ((ss[0] + ss[1]) + (ss[2] + ss[3])) + ((ss[4] + ss[5]) + (ss[6] + ss[7]));
 }
 
 void orc_router_logits(const float *x, const float *wr, int T, int E, int K, float *logits) {
@@ -402,6 +411,7 @@ static void route_one(const float *logits, const float *bias, int E, int topk, u
     for (int e = 0; e < E; ++e) {
         s[e] = 1.0f / (1.0f + expf(-logits[e]));
         sel[e] = s[e] + bias[e];
+        if (sel[e] == 0.0f) sel[e] = 0.0f; /* -0 and +0 rank as equal */
     }
     /* rank_e = #{j: sel_j > sel_e} + #{j < e: sel_j == sel_e} (stable descending order). */
     for (int e = 0; e < E; ++e) {

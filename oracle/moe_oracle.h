@@ -57,8 +57,9 @@ float orc_dot_kq_mmq(int gguf_type, const uint8_t *wrow, const int8_t *q, const 
                      const uint16_t *s, int nsb);
 
 /* ---- routing ------------------------------------------------------------------------ */
-/* Router logits in the library's canonical summation order: 32 lane partials, lane l
- * accumulating float4 groups l, l+32, ... with fmaf, then an xor-butterfly 16,8,4,2,1. */
+/* Router logits in the library's canonical summation order: K cut into 8 slices; per slice 32
+ * lane partials (lane l accumulates float4 groups l, l+32, ... with fmaf) summed by xor-butterfly
+ * 16,8,4,2,1; slice sums added as ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7)).  K % 32 == 0. */
 void orc_router_logits(const float *x, const float *wr, int T, int E, int K, float *logits);
 /* fused_moe.rs:228-241 + moe_gguf.cu:47-76: s = 1/(1+expf(-l)); select top-k of s+bias
  * (ties: lower id first); w = s[id]/tree-sum (fixed +4,+2,+1 order for topk=8). */
