@@ -41,6 +41,8 @@ typedef struct CUstream_st *mmrs_stream_t; /* == cudaStream_t */
 #define MMRS_ERR_LAUNCH 3      /* CUDA launch / runtime error                                 */
 #define MMRS_ERR_TIMEOUT 4     /* a bounded device-side wait (grid barrier, peer flag) expired */
 #define MMRS_ERR_ALLOC 5       /* device allocation failed                                    */
+#define MMRS_ERR_SCRATCH_LIMIT 6 /* problem larger than the fixed scratch of                  */
+                                 /* mmrs_moe_block_decode_static                              */
 
 /* ---- GGUF type codes (candle-nn/src/moe.rs:293-306) ---------------------------------- */
 #define MMRS_Q8_0 0
@@ -115,6 +117,21 @@ MMRS_API int mmrs_moe_block_forward(const MmrsMoeWeights *w, const float *x, con
  * single-token launch into host_out.  Returns the number of entries copied, or -status. */
 MMRS_API int mmrs_moe_workspace_trace(const void *workspace, uint64_t *host_out, int max_entries,
                                       mmrs_stream_t stream);
+
+/* No counterpart in the reference.  Same single-token block as mmrs_moe_block_forward with
+ * num_tokens == 1, for callers that cannot allocate device memory when they call it: an engine
+ * whose device memory is fully pre-reserved by its own allocator, or a call site that, like the
+ * reference's FFI, passes only tensor pointers and has no workspace to hand over.  It allocates
+ * nothing: its scratch is a fixed 128 KiB device array inside this library, held by every GPU
+ * that loads the library until the process exits.
+ * Limits: num_experts <= 256, inter <= 1536, hidden <= 3072; larger problems return
+ * MMRS_ERR_SCRATCH_LIMIT without launching.  The first call on a device resolves the array's
+ * device address and caches it, so make that first call before any stream capture.  All calls
+ * on a device share the array; each clears the part that must start at zero on `stream`, so
+ * calls that overlap on the GPU (unordered streams or host threads) race. */
+MMRS_API int mmrs_moe_block_decode_static(const MmrsMoeWeights *w, const float *x,
+                                          const float *residual, float *y, uint32_t *topk_ids,
+                                          float *topk_weights, mmrs_stream_t stream);
 
 /* Reads back (synchronising `stream`) and clears the device-side status word of a workspace. */
 MMRS_API int mmrs_moe_workspace_status(void *workspace, mmrs_stream_t stream);

@@ -21,9 +21,10 @@ LIB_PATH = PKG_DIR / "lib" / "libminimax_moe.so"
 HEADER = PKG_DIR.parent / "include" / "minimax_moe.h"
 
 MMRS_OK, MMRS_ERR_ARG, MMRS_ERR_UNSUPPORTED, MMRS_ERR_LAUNCH, MMRS_ERR_TIMEOUT, MMRS_ERR_ALLOC = range(6)
+MMRS_ERR_SCRATCH_LIMIT = 6
 Q8_0, Q4K, Q2K, Q3K, Q5K, Q6K = 0, 1, 2, 3, 4, 5
 ERROR_NAMES = {0: "ok", 1: "invalid argument", 2: "unsupported", 3: "launch failure", 4: "device wait timed out",
-               5: "allocation failure"}
+               5: "allocation failure", 6: "problem exceeds the fixed scratch"}
 
 
 class MoeError(RuntimeError):
@@ -49,6 +50,7 @@ PROTOTYPES = {
     "mmrs_moe_workspace_bytes": (_SZ, [C.POINTER(MmrsMoeWeights), _I]),
     "mmrs_moe_block_forward": (_I, [C.POINTER(MmrsMoeWeights), _VP, _VP, _VP, _I, _VP, _VP, _VP, _SZ, _VP]),
     "mmrs_moe_workspace_status": (_I, [_VP, _VP]),
+    "mmrs_moe_block_decode_static": (_I, [C.POINTER(MmrsMoeWeights), _VP, _VP, _VP, _VP, _VP, _VP]),
     "mmrs_moe_workspace_trace": (_I, [_VP, _VP, _I, _VP]),
     "mmrs_synth_normal_f32": (_I, [_VP, _I64, _U64, _U32, _F, _I, _VP]),
     "mmrs_synth_kquant": (_I, [_VP, _I, _U64, _U32] + [_I] * 7 + [_VP]),

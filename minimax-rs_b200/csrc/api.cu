@@ -4,6 +4,7 @@
 
 #include "common.cuh"
 #include "decode.cuh"
+#include "workspace.cuh"
 
 namespace mmrs {
 
@@ -90,15 +91,12 @@ __global__ void __launch_bounds__(256) decode_topk_kernel(const float *__restric
 // ------------------------------------------------------------------------------------------
 // Workspace layout of the fused block: [GridBarrier 256 B][logits E f32][act 8*I f32]
 // ------------------------------------------------------------------------------------------
-struct WsLayout {
-    size_t ctl, trace, blk_count, logits, act, aq, ad, aS, total;
-};
 constexpr int kTraceCtas = 256, kTraceSlots = 16;
 constexpr size_t kTraceOffset = kControlBytes;
 static size_t up256(size_t v) { return (v + 255) / 256 * 256; }
 // [control block: status + per-CTA barrier flags (zero before first use)] | trace |
 // per-block counters (zeroed by the kernel) | logits | act | aq | ad | aS
-static WsLayout ws_layout(int E, int I, int max_tokens) {
+WsLayout ws_layout(int E, int I, int max_tokens) {
     (void)max_tokens;
     WsLayout l;
     const size_t nblk = (size_t)8 * I / 32;
@@ -114,7 +112,7 @@ static WsLayout ws_layout(int E, int I, int max_tokens) {
     return l;
 }
 
-static void ws_bind(DecodeParams &p, uint8_t *ws, const WsLayout &l) {
+void ws_bind(DecodeParams &p, uint8_t *ws, const WsLayout &l) {
     p.ctl = reinterpret_cast<GridFlags *>(ws + l.ctl);
     p.blk_count = reinterpret_cast<uint32_t *>(ws + l.blk_count);
     p.trace = reinterpret_cast<uint64_t *>(ws + l.trace);
@@ -125,7 +123,7 @@ static void ws_bind(DecodeParams &p, uint8_t *ws, const WsLayout &l) {
     p.aS = reinterpret_cast<int *>(ws + l.aS);
 }
 
-static int validate_weights(const MmrsMoeWeights *w) {
+int validate_weights(const MmrsMoeWeights *w) {
     if (!w || !w->router || !w->bias || !w->gate || !w->up || !w->down) return MMRS_ERR_ARG;
     if (w->hidden <= 0 || w->inter <= 0 || w->hidden % QK_K || w->inter % QK_K) return MMRS_ERR_ARG;
     if ((w->gate_up_type != MMRS_Q4K && w->gate_up_type != MMRS_Q5K) ||

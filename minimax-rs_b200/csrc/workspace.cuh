@@ -1,0 +1,21 @@
+// Workspace layout of the fused MoE block (shared by the entry points in api.cu and noalloc.cu).
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+
+#include "decode.cuh"
+#include "../../include/minimax_moe.h"
+
+namespace mmrs {
+
+struct WsLayout {
+    size_t ctl, trace, blk_count, logits, act, aq, ad, aS, total;
+};
+
+// [control block: status + barrier counter + per-CTA epochs (zero before first use)] | trace |
+// per-block counters (zeroed by the kernel) | logits | act | aq | ad | aS
+WsLayout ws_layout(int E, int I, int max_tokens);
+void ws_bind(DecodeParams &p, uint8_t *ws, const WsLayout &l);
+int validate_weights(const MmrsMoeWeights *w);
+
+}  // namespace mmrs
