@@ -66,7 +66,7 @@ def lib() -> C.CDLL:
         if not LIB_PATH.exists():
             raise RuntimeError(f"{LIB_PATH} is missing: run `python minimax-rs_b200/build.py` "
                                "(the MoE path has no CPU fallback)")
-        l = C.CDLL(str(LIB_PATH), mode=C.RTLD_GLOBAL)
+        l = C.CDLL(str(LIB_PATH))
         for name, (res, args) in PROTOTYPES.items():
             f = getattr(l, name)
             f.restype = res
