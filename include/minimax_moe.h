@@ -74,6 +74,34 @@ MMRS_API void moe_gemm_gguf_decode_silu(const float *input, const void *gate_wei
                                int topk, int hidden_size, int intermediate_size,
                                int gate_up_gguf_dtype, int down_gguf_dtype, mmrs_stream_t stream);
 
+/* ffi.rs:25-39 — replaces moe_gguf.cu:357-424 (moe_gemm_gguf, the generic path for T < 32).
+ * output[route][size_n] = W[expert] . q8_1(input[row]) for every (route, expert) pair of the
+ * expert-sorted lists sorted_token_ids / expert_ids (size_m entries).  Input row = route / topk
+ * when topk_weights is NULL (gate / up), else route, and the row is scaled by
+ * topk_weights[route] (down).  Q8_1 as quantize_q8_1 (d = amax/127, q = round(x/d)).
+ * Types: Q4_K, Q5_K (others: MMRS_ERR_UNSUPPORTED, nothing launched). */
+MMRS_API void moe_gemm_gguf(const float *input, const void *weights, const int32_t *sorted_token_ids,
+                            const int32_t *expert_ids, const float *topk_weights, float *output,
+                            int num_experts, int topk, int size_m, int size_n, int size_k,
+                            int gguf_dtype, mmrs_stream_t stream);
+
+/* ffi.rs:86-100 — replaces mmq_gguf/mmq_moe.cu:69-165 (moe_gemm_mmq_gguf, T >= 32).
+ * Same contract as moe_gemm_gguf with the MMQ numerics: quantize_mmq_q8_1<DS4>
+ * (d_inv = 127/amax, q = round(x*d_inv)) and the per-32-block combine dmA.x*d8*C + dmA.y*s8.
+ * Types other than Q4_K / Q5_K do nothing (as the reference) and record MMRS_ERR_UNSUPPORTED. */
+MMRS_API void moe_gemm_mmq_gguf(const float *input, const void *weights,
+                                const int32_t *sorted_token_ids, const int32_t *expert_ids,
+                                const float *topk_weights, float *output, int num_experts, int topk,
+                                int size_m, int size_n, int size_k, int gguf_dtype,
+                                mmrs_stream_t stream);
+
+/* ffi.rs:102-109 — replaces moe/moe_sort.cu:21-51 (CUB radix sort of (key, route) pairs).
+ * Stable sort of size keys on bits [0, end_bit): expert_ids_sorted receives the keys,
+ * route_ids_sorted the original positions.  end_bit <= 10 (MMRS_ERR_UNSUPPORTED beyond). */
+MMRS_API void moe_sort_routes(const uint32_t *expert_ids_unsorted, uint32_t *expert_ids_sorted,
+                              uint32_t *route_ids_sorted, int size, int end_bit,
+                              mmrs_stream_t stream);
+
 /* Status of the last reference-ABI call made by this host thread (MMRS_OK when it launched). */
 MMRS_API int mmrs_last_error(void);
 
@@ -106,7 +134,9 @@ MMRS_API size_t mmrs_moe_workspace_bytes(const MmrsMoeWeights *w, int max_tokens
 /* y[T][hidden] = MoE(x[T][hidden]) (+ residual[T][hidden] when non-null), f32.
  * Replaces FusedMoeGGUF::forward (fused_moe.rs:251-334) + the residual add of
  * Layer::forward (src/model.rs:213-218).  topk_ids [T][topk] / topk_weights [T][topk]
- * (nullable) receive the routing.  T == 1 runs the fused decode kernel. */
+ * (nullable) receive the routing.  T == 1 runs the fused decode kernel; T > 1 runs routing,
+ * stable bucketing, gathered Q8_1 and the grouped tensor-core expert GEMMs (MMQ numerics for
+ * T >= 32, the generic ones below, as fused_moe.rs:296-316).  x, y, residual 16-byte aligned. */
 MMRS_API int mmrs_moe_block_forward(const MmrsMoeWeights *w, const float *x, const float *residual,
                            float *y, int num_tokens, uint32_t *topk_ids, float *topk_weights,
                            void *workspace, size_t workspace_bytes, mmrs_stream_t stream);

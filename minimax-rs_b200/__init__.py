@@ -46,6 +46,9 @@ _SZ = C.c_size_t
 PROTOTYPES = {
     "minimax_moe_decode_topk": (None, [_VP] * 7),
     "moe_gemm_gguf_decode_silu": (None, [_VP] * 8 + [_I] * 6 + [_VP]),
+    "moe_gemm_gguf": (None, [_VP] * 6 + [_I] * 6 + [_VP]),
+    "moe_gemm_mmq_gguf": (None, [_VP] * 6 + [_I] * 6 + [_VP]),
+    "moe_sort_routes": (None, [_VP] * 3 + [_I] * 2 + [_VP]),
     "mmrs_last_error": (_I, []),
     "mmrs_moe_workspace_bytes": (_SZ, [C.POINTER(MmrsMoeWeights), _I]),
     "mmrs_moe_block_forward": (_I, [C.POINTER(MmrsMoeWeights), _VP, _VP, _VP, _I, _VP, _VP, _VP, _SZ, _VP]),
@@ -144,6 +147,27 @@ class MoeLayer:
 
     def status(self, stream=None) -> int:
         return lib().mmrs_moe_workspace_status(self._ws.data_ptr(), _stream(stream)) if self._ws is not None else 0
+
+
+def moe_gemm(inp, weights, sorted_token_ids, expert_ids, topk_weights, out, num_experts: int, topk: int,
+             size_n: int, size_k: int, gguf_type: int, mmq: bool = False, stream=None):
+    """moe_gemm_gguf / moe_gemm_mmq_gguf through the reference ABI; raises on a recorded error."""
+    fn = lib().moe_gemm_mmq_gguf if mmq else lib().moe_gemm_gguf
+    fn(inp.data_ptr(), weights.data_ptr(), sorted_token_ids.data_ptr(), expert_ids.data_ptr(), _ptr(topk_weights),
+       out.data_ptr(), num_experts, topk, sorted_token_ids.numel(), size_n, size_k, gguf_type, _stream(stream))
+    check(last_error(), "moe_gemm_mmq_gguf" if mmq else "moe_gemm_gguf")
+    return out
+
+
+def sort_routes(expert_ids, end_bit: int, stream=None):
+    """moe_sort_routes: stable sort of u32 keys on bits [0, end_bit) -> (sorted keys, positions)."""
+    import torch
+    n = expert_ids.numel()
+    keys = torch.empty(n, dtype=torch.int32, device=expert_ids.device)
+    routes = torch.empty(n, dtype=torch.int32, device=expert_ids.device)
+    lib().moe_sort_routes(expert_ids.data_ptr(), keys.data_ptr(), routes.data_ptr(), n, end_bit, _stream(stream))
+    check(last_error(), "moe_sort_routes")
+    return keys, routes
 
 
 def synth_normal(t, seed: int, stream_id: int, scale: float = 1.0, bf16: bool = False, stream=None):

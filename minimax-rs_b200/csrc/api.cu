@@ -4,6 +4,7 @@
 
 #include "common.cuh"
 #include "decode.cuh"
+#include "prefill.cuh"
 #include "workspace.cuh"
 
 namespace mmrs {
@@ -123,6 +124,117 @@ void ws_bind(DecodeParams &p, uint8_t *ws, const WsLayout &l) {
     p.aS = reinterpret_cast<int *>(ws + l.aS);
 }
 
+// ------------------------------------------------------------------------------------------
+// Multi-token scratch, placed after the single-token layout in the same workspace.
+// ------------------------------------------------------------------------------------------
+struct PfLayout {
+    size_t logits, ids, wts, skeys, sroutes, count, first, seg, tiles, row_route, aq_h, ads_h, gate, up, aq_i,
+        ads_i, dn, total;
+    int ppad;
+};
+static PfLayout pf_layout(size_t base, int E, int H, int I, int T) {
+    PfLayout l;
+    const size_t M = (size_t)T * 8;
+    l.ppad = pf_ppad((int)M, E);
+    size_t o = up256(base);
+    auto take = [&](size_t bytes) {
+        const size_t at = o;
+        o = up256(o + bytes);
+        return at;
+    };
+    l.logits = take((size_t)T * E * 4);
+    l.ids = take(M * 4);
+    l.wts = take(M * 4);
+    l.skeys = take(M * 4);
+    l.sroutes = take(M * 4);
+    l.count = take((size_t)E * 4);
+    l.first = take((size_t)E * 4);
+    l.seg = take((size_t)E * 4);
+    l.tiles = take((size_t)(E + 1) * 4);
+    l.row_route = take((size_t)l.ppad * 4);
+    l.aq_h = take((size_t)H * l.ppad);
+    l.ads_h = take((size_t)(H / 32) * l.ppad * 8);
+    l.gate = take(M * I * 4);
+    l.up = take(M * I * 4);
+    l.aq_i = take((size_t)I * l.ppad);
+    l.ads_i = take((size_t)(I / 32) * l.ppad * 8);
+    l.dn = take(M * H * 4);
+    l.total = o;
+    return l;
+}
+static PfPlan pf_bind_plan(uint8_t *ws, const PfLayout &l) {
+    PfPlan p;
+    p.count = reinterpret_cast<int *>(ws + l.count);
+    p.first = reinterpret_cast<int *>(ws + l.first);
+    p.seg = reinterpret_cast<int *>(ws + l.seg);
+    p.tiles = reinterpret_cast<int *>(ws + l.tiles);
+    p.row_route = reinterpret_cast<int *>(ws + l.row_route);
+    p.ppad = l.ppad;
+    return p;
+}
+static int bits_for(int n) {  // smallest b with (n - 1) < 2^b
+    int b = 0;
+    while ((1 << b) < n) ++b;
+    return b;
+}
+
+// One routed expert GEMM over scratch it allocates on the stream (the reference's launchers
+// also allocate their scratch per call, moe_gguf.cu:381, mmq_moe.cu:105-135).
+static int routed_gemm(const float *input, const void *weights, const int32_t *sorted_token_ids,
+                       const int32_t *expert_ids, const float *topk_weights, float *output, int num_experts,
+                       int topk, int size_m, int size_n, int size_k, int gtype, int mode, cudaStream_t s) {
+    if (size_m <= 0) return MMRS_OK;
+    if (!input || !weights || !sorted_token_ids || !expert_ids || !output || topk <= 0 || size_n <= 0 ||
+        size_k <= 0 || size_k % QK_K || num_experts <= 0)
+        return MMRS_ERR_ARG;
+    if (gtype != MMRS_Q4K && gtype != MMRS_Q5K) return MMRS_ERR_UNSUPPORTED;
+    if (num_experts > kPfMaxExperts) return MMRS_ERR_UNSUPPORTED;
+    if (!aligned16(input) || !aligned16(weights)) return MMRS_ERR_ARG;
+    const int ppad = pf_ppad(size_m, num_experts);
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = o;
+        o = up256(o + bytes);
+        return at;
+    };
+    const size_t o_cnt = take((size_t)num_experts * 4), o_first = take((size_t)num_experts * 4),
+                 o_seg = take((size_t)num_experts * 4), o_tiles = take((size_t)(num_experts + 1) * 4),
+                 o_rr = take((size_t)ppad * 4), o_q = take((size_t)size_k * ppad),
+                 o_ds = take((size_t)(size_k / 32) * ppad * 8), o_st = take(256);
+    uint8_t *ws = nullptr;
+    if (cudaMallocAsync((void **)&ws, o, s) != cudaSuccess) return MMRS_ERR_ALLOC;
+    cudaMemsetAsync(ws + o_st, 0, 4, s);
+    PfPlan plan;
+    plan.count = reinterpret_cast<int *>(ws + o_cnt);
+    plan.first = reinterpret_cast<int *>(ws + o_first);
+    plan.seg = reinterpret_cast<int *>(ws + o_seg);
+    plan.tiles = reinterpret_cast<int *>(ws + o_tiles);
+    plan.row_route = reinterpret_cast<int *>(ws + o_rr);
+    plan.ppad = ppad;
+    PfActs acts{reinterpret_cast<int8_t *>(ws + o_q), reinterpret_cast<float2 *>(ws + o_ds)};
+    int rc = pf_build_plan(expert_ids, sorted_token_ids, size_m, num_experts, plan, s);
+    if (rc == MMRS_OK)
+        rc = pf_quantize(input, nullptr, topk_weights ? 1 : topk, size_k, mode, plan, acts, ppad, s);
+    if (rc == MMRS_OK) {
+        PfGemmParams g = {};
+        g.aq = acts.q;
+        g.ads = acts.ds;
+        g.plan = plan;
+        g.route_scale = topk_weights;
+        g.out = output;
+        g.E = num_experts;
+        g.N = size_n;
+        g.K = size_k;
+        g.gtype = gtype;
+        g.mode = mode;
+        g.status = reinterpret_cast<uint32_t *>(ws + o_st);
+        g.timeout_ns = kTimeoutNs;
+        rc = pf_gemm(weights, g, ppad, s);
+    }
+    cudaFreeAsync(ws, s);
+    return rc;
+}
+
 int validate_weights(const MmrsMoeWeights *w) {
     if (!w || !w->router || !w->bias || !w->gate || !w->up || !w->down) return MMRS_ERR_ARG;
     if (w->hidden <= 0 || w->inter <= 0 || w->hidden % QK_K || w->inter % QK_K) return MMRS_ERR_ARG;
@@ -210,9 +322,100 @@ extern "C" void moe_gemm_gguf_decode_silu(const float *input, const void *gate_w
     set_err(rc);
 }
 
+extern "C" void moe_gemm_gguf(const float *input, const void *weights, const int32_t *sorted_token_ids,
+                              const int32_t *expert_ids, const float *topk_weights, float *output, int num_experts,
+                              int topk, int size_m, int size_n, int size_k, int gguf_dtype, mmrs_stream_t stream) {
+    set_err(routed_gemm(input, weights, sorted_token_ids, expert_ids, topk_weights, output, num_experts, topk,
+                        size_m, size_n, size_k, gguf_dtype, kPfModeGeneric, (cudaStream_t)stream));
+}
+
+extern "C" void moe_gemm_mmq_gguf(const float *input, const void *weights, const int32_t *sorted_token_ids,
+                                  const int32_t *expert_ids, const float *topk_weights, float *output,
+                                  int num_experts, int topk, int size_m, int size_n, int size_k, int gguf_dtype,
+                                  mmrs_stream_t stream) {
+    // Like the reference (mmq_moe.cu:84-86) types other than Q4_K / Q5_K do nothing; the
+    // condition is recorded for mmrs_last_error().
+    set_err(routed_gemm(input, weights, sorted_token_ids, expert_ids, topk_weights, output, num_experts, topk,
+                        size_m, size_n, size_k, gguf_dtype, kPfModeMmq, (cudaStream_t)stream));
+}
+
+extern "C" void moe_sort_routes(const uint32_t *expert_ids_unsorted, uint32_t *expert_ids_sorted,
+                                uint32_t *route_ids_sorted, int size, int end_bit, mmrs_stream_t stream) {
+    if (size > 0 && (!expert_ids_unsorted || !expert_ids_sorted || !route_ids_sorted)) {
+        set_err(MMRS_ERR_ARG);
+        return;
+    }
+    set_err(pf_sort_routes(expert_ids_unsorted, size, end_bit, expert_ids_sorted, route_ids_sorted,
+                           (cudaStream_t)stream));
+}
+
 extern "C" size_t mmrs_moe_workspace_bytes(const MmrsMoeWeights *w, int max_tokens) {
     if (!w) return 0;
-    return ws_layout(w->num_experts, w->inter, max_tokens).total;
+    const size_t single = ws_layout(w->num_experts, w->inter, 1).total;
+    if (max_tokens <= 1) return single;
+    return pf_layout(single, w->num_experts, w->hidden, w->inter, max_tokens).total;
+}
+
+// T > 1: router GEMM, top-8, stable bucketing, gathered Q8_1 (MMQ numerics for T >= 32, the
+// generic ones below, as fused_moe.rs:296-316 selects), gate / up GEMMs, SiLU * up fused into
+// the down operand's quantisation, down GEMM scaled by the route weight, top-8 sum + residual.
+static int block_forward_multi(const MmrsMoeWeights *w, const float *x, const float *residual, float *y, int T,
+                               uint32_t *topk_ids, float *topk_weights, uint8_t *ws, cudaStream_t s) {
+    const int E = w->num_experts, H = w->hidden, I = w->inter, M = T * 8;
+    const PfLayout l = pf_layout(ws_layout(E, I, 1).total, E, H, I, T);
+    float *logits = reinterpret_cast<float *>(ws + l.logits);
+    uint32_t *ids = topk_ids ? topk_ids : reinterpret_cast<uint32_t *>(ws + l.ids);
+    float *wts = topk_weights ? topk_weights : reinterpret_cast<float *>(ws + l.wts);
+    uint32_t *skeys = reinterpret_cast<uint32_t *>(ws + l.skeys), *sroutes = reinterpret_cast<uint32_t *>(ws + l.sroutes);
+    const PfPlan plan = pf_bind_plan(ws, l);
+    const PfActs xh{reinterpret_cast<int8_t *>(ws + l.aq_h), reinterpret_cast<float2 *>(ws + l.ads_h)};
+    const PfActs xi{reinterpret_cast<int8_t *>(ws + l.aq_i), reinterpret_cast<float2 *>(ws + l.ads_i)};
+    float *g = reinterpret_cast<float *>(ws + l.gate), *u = reinterpret_cast<float *>(ws + l.up);
+    float *dn = reinterpret_cast<float *>(ws + l.dn);
+    const int mode_gu = T >= 32 ? kPfModeMmq : kPfModeGeneric;
+    const int mode_dn = T >= 32 ? kPfModeMmq : kPfModeGeneric;
+    uint32_t *status = reinterpret_cast<uint32_t *>(ws);  // workspace status word
+
+    int rc = pf_router_logits(x, w->router, T, E, H, logits, s);
+    if (rc == MMRS_OK) rc = pf_route_topk(logits, w->bias, T, E, ids, wts, s);
+    if (rc == MMRS_OK) rc = pf_sort_routes(ids, M, bits_for(E), skeys, sroutes, s);
+    if (rc == MMRS_OK)
+        rc = pf_build_plan(reinterpret_cast<const int32_t *>(skeys), reinterpret_cast<const int32_t *>(sroutes), M, E,
+                           plan, s);
+    if (rc == MMRS_OK) rc = pf_quantize(x, nullptr, 8, H, mode_gu, plan, xh, l.ppad, s);
+    PfGemmParams gp = {};
+    gp.plan = plan;
+    gp.E = E;
+    gp.status = status;
+    gp.timeout_ns = kTimeoutNs;
+    if (rc == MMRS_OK) {
+        gp.aq = xh.q;
+        gp.ads = xh.ds;
+        gp.N = I;
+        gp.K = H;
+        gp.gtype = w->gate_up_type;
+        gp.mode = mode_gu;
+        gp.out = g;
+        rc = pf_gemm(w->gate, gp, l.ppad, s);
+        if (rc == MMRS_OK) {
+            gp.out = u;
+            rc = pf_gemm(w->up, gp, l.ppad, s);
+        }
+    }
+    if (rc == MMRS_OK) rc = pf_quantize(g, u, 1, I, mode_dn, plan, xi, l.ppad, s);
+    if (rc == MMRS_OK) {
+        gp.aq = xi.q;
+        gp.ads = xi.ds;
+        gp.N = H;
+        gp.K = I;
+        gp.gtype = w->down_type;
+        gp.mode = mode_dn;
+        gp.route_scale = wts;
+        gp.out = dn;
+        rc = pf_gemm(w->down, gp, l.ppad, s);
+    }
+    if (rc == MMRS_OK) rc = pf_reduce_topk(dn, residual, T, H, y, s);
+    return rc;
 }
 
 extern "C" int mmrs_moe_block_forward(const MmrsMoeWeights *w, const float *x, const float *residual, float *y,
@@ -222,10 +425,13 @@ extern "C" int mmrs_moe_block_forward(const MmrsMoeWeights *w, const float *x, c
     if (rc != MMRS_OK) return rc;
     if (!x || !y || num_tokens < 0 || !workspace) return MMRS_ERR_ARG;
     if (num_tokens == 0) return MMRS_OK;
-    const WsLayout l = ws_layout(w->num_experts, w->inter, num_tokens);
-    if (workspace_bytes < l.total || !aligned16(workspace) || !aligned16(x)) return MMRS_ERR_ARG;
-    if (num_tokens != 1) return MMRS_ERR_UNSUPPORTED;
+    const WsLayout l = ws_layout(w->num_experts, w->inter, 1);
+    if (workspace_bytes < mmrs_moe_workspace_bytes(w, num_tokens) || !aligned16(workspace) || !aligned16(x) ||
+        !aligned16(y) || (residual && !aligned16(residual)))
+        return MMRS_ERR_ARG;
     uint8_t *ws = (uint8_t *)workspace;
+    if (num_tokens > 1) return block_forward_multi(w, x, residual, y, num_tokens, topk_ids, topk_weights, ws,
+                                                   (cudaStream_t)stream);
     DecodeParams p = {};
     p.x = x;
     p.router = w->router;

@@ -5,11 +5,12 @@ from __future__ import annotations
 import numpy as np
 
 
-def make_layer(pkg, synth, dev, E, H, I, gu_type, dn_type, seed, layer=0, T=1, x_bf16=True, zipf=False):
+def make_layer(pkg, synth, dev, E, H, I, gu_type, dn_type, seed, layer=0, T=1, x_bf16=True, zipf=False,
+               x_scale=1.0):
     import torch
     st = synth.layer_streams(layer)
     x = torch.empty(T * H, dtype=torch.float32, device=dev)
-    pkg.synth_normal(x, seed, st["x"], 1.0, bf16=x_bf16)
+    pkg.synth_normal(x, seed, st["x"], x_scale, bf16=x_bf16)
     router = torch.empty(E * H, dtype=torch.float32, device=dev)
     pkg.synth_normal(router, seed, st["router"], 0.02)
     if zipf:
