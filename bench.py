@@ -11,7 +11,9 @@ a layer) and a fresh seeded token.  Steps are replayed from CUDA graphs of up to
 
 One JSON line is printed by rank 0.  `value` = MoE-block tokens/s (whole job), device-timed with
 CUDA events; `e2e` = the same through the public API with the token copied from pinned host
-memory and the output copied back inside every step.
+memory and the output copied back inside every step.  The line also carries `prefill`: the
+same measurements for BASELINE configs[2] (T = 512 tokens per step, Zipf-skewed experts, two
+alternating layers), skipped with --no-prefill.
 """
 from __future__ import annotations
 
@@ -145,6 +147,150 @@ def cpu_decode_sample(layer, xs_host, res_host, budget_s: float):
     return n / el, n, el, orc.num_threads()
 
 
+PF_T = 512
+PF_SEED = 2001  # config index 2 x 1000 + 1
+
+
+def expert_bytes(I=I, H=H) -> int:
+    return 2 * I * (H // 256) * 144 + H * (I // 256) * 176
+
+
+def build_prefill_layers(pkg, synth, dev, n_layers: int):
+    """Config 2 layers: as config 1 but the correction bias is drawn so that top-8 hits follow a
+    Zipf(1.1) popularity over the 256 experts."""
+    import torch
+    layers = []
+    for l in range(n_layers):
+        st = synth.layer_streams(l)
+        router = torch.empty(E, H, dtype=torch.float32, device=dev)
+        pkg.synth_normal(router, PF_SEED, st["router"], 0.02)
+        bias = torch.from_numpy(synth.zipf_bias(E, PF_SEED + l)).to(dev)
+        gate = torch.empty(E * I * pkg.row_bytes(Q4K, H), dtype=torch.uint8, device=dev)
+        up = torch.empty_like(gate)
+        down = torch.empty(E * H * pkg.row_bytes(Q5K, I), dtype=torch.uint8, device=dev)
+        pkg.synth_kquant(gate, Q4K, PF_SEED, st["gate"], E, I, H)
+        pkg.synth_kquant(up, Q4K, PF_SEED, st["up"], E, I, H)
+        pkg.synth_kquant(down, Q5K, PF_SEED, st["down"], E, H, I)
+        layers.append(pkg.MoeLayer(router, bias, gate, up, down, Q4K, Q5K))
+    return layers
+
+
+def run_prefill(pkg, synth, dev, args, rank: int, world: int):
+    """Config 2: one T = 512 MoE block per step (Zipf-skewed routing), alternating between two
+    layers (2 x 2.19 GB of expert weights, larger than L2)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    layers = build_prefill_layers(pkg, synth, dev, 2)
+    xs = torch.empty(2, PF_T, H, dtype=torch.float32, device=dev)
+    pkg.synth_normal(xs, PF_SEED + rank, 200, 1.0)
+    ys = torch.empty(PF_T, H, dtype=torch.float32, device=dev)
+    ids = torch.empty(2, PF_T, TOPK, dtype=torch.int32, device=dev)
+    wts = torch.empty(2, PF_T, TOPK, dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    for L in layers:
+        L.workspace(PF_T)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(max(3, args.warmup if args.warmup < 10 else 3)):
+            L = i % 2
+            layers[L].forward(xs[L], y=ys, topk_ids=ids[L], topk_w=wts[L], stream=stream)
+        stream.synchronize()
+    for L in layers:
+        assert L.status() == 0, "device-side timeout in prefill warm-up"
+    steps = args.prefill_steps
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for i in range(steps):
+                L = i % 2
+                layers[L].forward(xs[L], y=ys, topk_ids=ids[L], topk_w=wts[L], stream=stream)
+            e1.record(stream)
+        e1.synchronize()
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    for L in layers:
+        assert L.status() == 0, "device-side timeout in prefill"
+    # e2e through the public API: x from pinned host memory, y back to pinned host memory
+    x_host = torch.empty(PF_T, H, dtype=torch.float32, pin_memory=True)
+    x_host.copy_(xs[0].cpu())
+    y_host = torch.empty(PF_T, H, dtype=torch.float32, pin_memory=True)
+    x_dev = torch.empty(PF_T, H, dtype=torch.float32, device=dev)
+    e2e_steps = max(4, min(steps, 20))
+    with torch.cuda.stream(stream):
+        for i in range(2):
+            x_dev.copy_(x_host, non_blocking=True)
+            layers[i % 2].forward(x_dev, y=ys, stream=stream)
+            y_host.copy_(ys, non_blocking=True)
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for i in range(e2e_steps):
+            x_dev.copy_(x_host, non_blocking=True)
+            layers[i % 2].forward(x_dev, y=ys, stream=stream)
+            y_host.copy_(ys, non_blocking=True)
+        f1.record(stream)
+        f1.synchronize()
+    e2e_ms = torch.tensor([f0.elapsed_time(f1)], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms.item())
+
+    ids_np = ids.cpu().numpy()
+    distinct = [len(np.unique(ids_np[l])) for l in range(2)]
+    counts = np.bincount(ids_np[0].reshape(-1), minlength=E)
+    alg_bytes = statistics.mean(distinct) * expert_bytes() + E * H * 4 + 2 * PF_T * H * 4
+    ops = 2 * PF_T * TOPK * (2 * I * H + H * I)
+    per_step_s = ms / 1e3 / steps
+    peaks = measured_peaks()
+    achieved = alg_bytes / per_step_s / 1e9
+    out = {"metric": "moe_block_prefill_tokens_per_s", "value": world * PF_T * steps / (ms / 1e3),
+           "unit": "tokens/s", "steps": steps, "ms_per_step": ms / steps,
+           "config": {"workload": "prefill T=512 MoE block (BASELINE configs[2]), Zipf(1.1) expert popularity",
+                      "tokens_per_step": PF_T, "layers_rotated": 2, "distinct_experts": distinct,
+                      "max_routes_per_expert": int(counts.max()), "mode": "MMQ numerics (T >= 32)",
+                      "x": "N(0,1) f32 (MMQ half block sums of the down input overflow with these synthetic "
+                           "weights, as in the reference's numerics; timing is unaffected)",
+                      "l2": "2 layers x 2.19e9 B rotated (> L2)"},
+           "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                        "frac": achieved / peaks["hbm_gbs"], "traffic": None, "peak_source": peaks["source"],
+                        "algorithmic_bytes_per_step": alg_bytes,
+                        "scope": "whole block step (10 launches; the expert GEMMs dominate, see profiles/)",
+                        "int8_tops": ops / per_step_s / 1e12, "int8_frac_of_nominal_4500": ops / per_step_s / 4.5e15},
+           "e2e": {"value": world * PF_T * e2e_steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                   "h2d_bytes_per_step": PF_T * H * 4, "d2h_bytes_per_step": PF_T * H * 4},
+           "gpu_launches": 10 * steps, "clocks": clk.summary()}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import oracle as orc
+        L = layers[0]
+        router, bias = L.router.cpu().numpy(), L.bias.cpu().numpy()
+        gate, up, down = L.gate.cpu().numpy(), L.up.cpu().numpy(), L.down.cpu().numpy()
+        xh = xs[0].cpu().numpy()
+        n_tok, t0 = 0, time.perf_counter()
+        while True:
+            orc.moe_block(router, bias, gate, up, down, Q4K, Q5K, xh[n_tok % PF_T:n_tok % PF_T + 32])
+            n_tok += 32
+            el = time.perf_counter() - t0
+            if el >= args.cpu_budget:
+                break
+        out["cpu_baseline"] = {"value": n_tok / el, "unit": "tokens/s", "cores": orc.num_threads(), "kind": "port",
+                               "sample": f"{n_tok} prefill tokens in chunks of 32 (MMQ numerics) of layer 0 in "
+                                         f"{el:.1f} s (oracle/moe_oracle.c, OpenMP)"}
+    del layers
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_reference(args):
     """Reference arm: the CPU restatement of the reference's MoE decode block (the reference's
     own CPU path, Candle's quantized matmul, cannot be built here: no Rust toolchain), on all
@@ -206,6 +352,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=2000)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill-steps", type=int, default=40)
+    ap.add_argument("--no-prefill", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -345,6 +493,13 @@ def main():
         cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": f"{n} decode tokens of layer 0 in {el:.1f} s (oracle/moe_oracle.c, OpenMP)"}
 
+    n_layers = len(layers)
+    graph_steps = G if graphs else 0
+    layer_bytes = layers[0].gate.numel() * 2 + layers[0].down.numel() + E * H * 4
+    del layers, graphs
+    torch.cuda.empty_cache()
+    prefill = None if args.no_prefill else run_prefill(pkg, synth, dev, args, rank, world)
+
     if rank == 0:
         out = {
             "metric": "moe_block_decode_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
@@ -352,11 +507,10 @@ def main():
             "scaling": "weak", "vs_baseline": None, "dtype": "int8xq4k/q5k->f32", "data": "synthetic",
             "config": {"workload": "decode T=1 MoE block (BASELINE configs[1])", "experts": E, "hidden": H,
                        "inter": I, "topk": TOPK, "gate_up": "Q4_K", "down": "Q5_K", "activations": "Q8_1",
-                       "residual": True, "layers_rotated": len(layers),
-                       "l2": f"inputs larger than L2: {len(layers)} layers x "
-                             f"{layers[0].gate.numel() * 2 + layers[0].down.numel() + E * H * 4:.3e} B rotated",
+                       "residual": True, "layers_rotated": n_layers,
+                       "l2": f"inputs larger than L2: {n_layers} layers x {layer_bytes:.3e} B rotated",
                        "parallelism": "replicas" if world > 1 else "single GPU",
-                       "graph_steps": G if graphs else 0},
+                       "graph_steps": graph_steps},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
                          "peak_source": peaks["source"], "algorithmic_bytes_per_launch": alg,
@@ -366,10 +520,10 @@ def main():
             "gpu_launches": steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
+            "prefill": prefill,
         }
         print(json.dumps(out), flush=True)
     if world > 1:
-        graphs.clear()
         dist.destroy_process_group()
 
 

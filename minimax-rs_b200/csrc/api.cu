@@ -211,7 +211,7 @@ static int routed_gemm(const float *input, const void *weights, const int32_t *s
     plan.tiles = reinterpret_cast<int *>(ws + o_tiles);
     plan.row_route = reinterpret_cast<int *>(ws + o_rr);
     plan.ppad = ppad;
-    PfActs acts{reinterpret_cast<int8_t *>(ws + o_q), reinterpret_cast<float2 *>(ws + o_ds)};
+    PfActs acts{reinterpret_cast<int8_t *>(ws + o_q), reinterpret_cast<float *>(ws + o_ds)};
     int rc = pf_build_plan(expert_ids, sorted_token_ids, size_m, num_experts, plan, s);
     if (rc == MMRS_OK)
         rc = pf_quantize(input, nullptr, topk_weights ? 1 : topk, size_k, mode, plan, acts, ppad, s);
@@ -368,8 +368,8 @@ static int block_forward_multi(const MmrsMoeWeights *w, const float *x, const fl
     float *wts = topk_weights ? topk_weights : reinterpret_cast<float *>(ws + l.wts);
     uint32_t *skeys = reinterpret_cast<uint32_t *>(ws + l.skeys), *sroutes = reinterpret_cast<uint32_t *>(ws + l.sroutes);
     const PfPlan plan = pf_bind_plan(ws, l);
-    const PfActs xh{reinterpret_cast<int8_t *>(ws + l.aq_h), reinterpret_cast<float2 *>(ws + l.ads_h)};
-    const PfActs xi{reinterpret_cast<int8_t *>(ws + l.aq_i), reinterpret_cast<float2 *>(ws + l.ads_i)};
+    const PfActs xh{reinterpret_cast<int8_t *>(ws + l.aq_h), reinterpret_cast<float *>(ws + l.ads_h)};
+    const PfActs xi{reinterpret_cast<int8_t *>(ws + l.aq_i), reinterpret_cast<float *>(ws + l.ads_i)};
     float *g = reinterpret_cast<float *>(ws + l.gate), *u = reinterpret_cast<float *>(ws + l.up);
     float *dn = reinterpret_cast<float *>(ws + l.dn);
     const int mode_gu = T >= 32 ? kPfModeMmq : kPfModeGeneric;

@@ -8,13 +8,14 @@
 
 namespace mmrs {
 
-constexpr int kPfNT = 64;           // routes per GEMM tile (MMA N)
+constexpr int kPfNT = 32;           // routes per GEMM tile (MMA N <= 32)
 constexpr int kPfMT = 128;          // weight rows per GEMM tile (MMA M)
 constexpr int kPfSegAlign = 16;     // each expert's route segment is padded to this many rows
 constexpr int kPfRawStages = 4;     // raw GGUF weight tiles in flight (TMA)
 constexpr int kPfOpStages = 2;      // unpacked operand stages (A int8, B int8, scales)
-constexpr int kPfSlots = 8;         // TMEM accumulator slots of kPfNT columns (8 x 64 = 512)
-constexpr int kPfThreads = 448;     // 14 warps: TMA, MMA, 4 unpack, 8 epilogue
+constexpr int kPfGroups = 3;        // TMEM group slots of 128 columns (sub-block accumulators)
+constexpr int kPfEpiWarps = 8;      // epilogue warps: 4 TMEM lane quarters x 2 sub-block phases
+constexpr int kPfThreads = 32 * (6 + kPfEpiWarps);  // TMA, MMA, 4 unpack, 8 epilogue
 constexpr int kPfMaxExperts = 1024;
 
 // Activation quantisation numerics.
@@ -42,16 +43,17 @@ __host__ __device__ inline int pf_ppad(int routes, int E) {
 // column k (k < K, K a multiple of 256), the int8 lives at
 //   (k / 256) * ppad * 256 + (p / 8) * 2048 + ((k % 256) / 16) * 128 + (p % 8) * 16 + k % 16
 // i.e. per 256-column chunk, 8-row groups of sixteen 8x16-byte core matrices (the canonical
-// no-swizzle K-major layout of a UMMA operand), and ds[(k / 256) * ppad * 8 + p * 8 + (k % 256) / 32]
-// holds (d8, s8) of the 32-block as float2.
+// no-swizzle K-major layout of a UMMA operand).  The block scales of 16 consecutive rows form one
+// 1 KiB record per chunk, d8 plane then s8 plane:
+//   ds[((k / 256) * (ppad / 16) + p / 16) * 256 + plane * 128 + ((k % 256) / 32) * 16 + p % 16]
 struct PfActs {
     int8_t *q;
-    float2 *ds;
+    float *ds;
 };
 
 struct PfGemmParams {
     const int8_t *aq;
-    const float2 *ads;
+    const float *ads;
     PfPlan plan;
     const float *route_scale;  // nullable: output row of route r is multiplied by route_scale[r]
     float *out;                // [routes][N], row = route id

@@ -60,11 +60,8 @@ def test_expert_gemm_vs_reference_and_oracle(pkg, dev, orc, c):
     assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 1e-5
     orc_out = orc.moe_gemm_gguf(inp, w, sorted_ids, experts, tw, c["E"], 8, c["M"], c["N"], c["K"], c["type"],
                                 mmq=c["mmq"])
-    if c["mmq"]:
-        # same per-32-block fma order as the oracle's MMQ combine: bit-exact
-        assert np.array_equal(got.view(np.uint32), orc_out.view(np.uint32))
-    else:
-        assert np.linalg.norm(got - orc_out) / np.linalg.norm(orc_out) < 1e-6
+    # integer block dots are exact; only the f32 summation order differs from the oracle
+    assert np.linalg.norm(got - orc_out) / np.linalg.norm(orc_out) < 1e-6
 
 
 @pytest.mark.parametrize("mmq", [True, False])
@@ -94,10 +91,7 @@ def test_expert_gemm_shapes(pkg, synth, dev, orc, mmq, E, N, K, T, gt, down):
                  mmq=mmq)
     got = out.cpu().numpy()
     ref = orc.moe_gemm_gguf(inp, w, order, experts, tw, E, 8, M, N, K, gt, mmq=mmq)
-    if mmq:
-        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
-    else:
-        assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 1e-6
+    assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 1e-6
 
 
 def test_mmq_gemm_other_type_does_nothing(pkg, dev):
