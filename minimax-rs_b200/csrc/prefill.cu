@@ -488,51 +488,46 @@ int pf_reduce_topk(const float *dn, const float *residual, int T, int H, float *
 // ==========================================================================================
 // 7. Grouped expert GEMM on tcgen05 (kind::i8, accumulators in TMEM).
 //
-//    Work item = (expert e, route tile of <= 64 routes, 128 weight rows).  Per 256-column chunk:
-//      warp 0      TMA (tensor map) of the raw GGUF tile: 128 rows x one super-block
-//      warps 2-5   unpack: nibbles (+ high bits) -> int8 A operand in the canonical K-major
-//                  layout, per row and 32-block the scale dmx (and dmy), bulk copy of the route
-//                  tile's int8 activations (B operand) and (d8, s8) pairs
-//      warp 1      one thread issues 8 MMAs (M=128, N=routes rounded to 16, K=32), one per
-//                  32-block, each into its own TMEM slot and committed to that slot's mbarrier.
-//                  MMQ numerics: the min term sum_j dmy_j * s8_j (both half values, exact
-//                  products) is one more MMA (kind::f16, K = 8 blocks + 8 zeros) accumulated
-//                  over the whole K range in its own TMEM region
-//      warps 6-21  epilogue: 4 TMEM lane quarters x 4 column groups of 8-route units; per slot
-//                  sum = fma(dmx * d8, C, sum) (generic numerics: + fma(dmy, s8, sum)), then the
-//                  min accumulator is added and the route rows are written (times the route
+//    Work item = (expert e, route tile of <= 32 routes, 128 weight rows).  Per 256-column chunk
+//    (one GGUF super-block of every row):
+//      warp 0      TMA: the raw weight tile (tensor map, 128 rows x one super-block), the route
+//                  tile's int8 activations (B operand) and their block scales, into a 4-deep ring
+//      warps 2-5   unpack (one thread per row): nibbles (+ high bits) -> int8 A operand in the
+//                  canonical no-swizzle K-major shared-memory layout; per 32-block and row the
+//                  scales (dmx, dmy); the route tile's (d8, s8) planes for the epilogue
+//      warp 1      one thread issues the chunk's 8 MMAs (M=128, N=routes rounded to 16, K=32),
+//                  one per 32-block, each into its own accumulator of the chunk's TMEM group
+//                  (8 x N columns), then one commit for the group
+//      warps 6-13  epilogue: 4 TMEM lane quarters x 2 halves of the route columns; per 32-block
+//                  sum = fma(dmx * d8, C, sum); sum = fma(dmy, s8, sum) in K order (the MMQ combine
+//                  of mmq_gguf.cuh vec_dot_q8_1_q8_1_mma, or with the generic numerics' scales the
+//                  vec_dot_q*_K_q8_1 combine), then the route rows are written (times the route
 //                  weight when given).
 //    Every wait is bounded by a %globaltimer deadline; on expiry the CTA records
 //    MMRS_ERR_TIMEOUT, stops, waits (bounded) for its own copies and MMAs and frees its TMEM.
 // ==========================================================================================
 constexpr int kPfRawW = kPfMT * Q5K_BYTES;      // 22528: raw weight tile
-constexpr int kPfRawQ = kPfNT * QK_K;           // 16384: int8 activations of the route tile (B operand)
+constexpr int kPfRawQ = kPfNT * QK_K;           // 8192: int8 activations of the route tile (B operand)
 constexpr int kPfRawD = kPfNT * 8 * 8;          // 2048: d8 and s8 planes of the route tile
 constexpr int kPfRawBytes = kPfRawW + kPfRawQ + kPfRawD;
 constexpr int kPfABytes = kPfMT * QK_K;         // 32768
-constexpr int kPfEpiWarp0 = 6;
-constexpr int kPfGroupCols = 128;                    // one group slot: G sub-blocks x n16 routes
-constexpr int kPfMinCol = kPfGroups * kPfGroupCols;  // 384: min-term accumulator (n16 columns)
-constexpr int kPfRedCol = kPfMinCol + kPfNT;         // 416: partial sums handed between epilogue phases
-constexpr int kPfTmemCols = 512;
+constexpr int kPfEpiWarp0 = 2 + kPfUnpackWarps;
+constexpr int kPfGroupCols = 8 * kPfNT;         // 256: the 8 block accumulators of one chunk
+constexpr int kPfTmemCols = kPfGroups * kPfGroupCols;
+static_assert(kPfTmemCols == 512, "two chunk groups fill the tensor memory");
+static_assert(kPfNT == 32 && kPfEpiWarps == 8, "epilogue geometry: 4 lane quarters x 2 x 16 route columns");
 
-// Sub-blocks per TMEM group for a route tile of n16 columns (a group fills <= 128 columns).
-__host__ __device__ constexpr int pf_group_size(int n16) { return n16 <= 16 ? 8 : 4; }
-static_assert(kPfNT == 32, "group geometry assumes route tiles of at most 32 columns");
-
-// Raw stage (TMA / bulk copies, 3 deep): weights, activations and their scales of one chunk.
-// Operand stage (2 deep): what the unpack warps derive from a raw stage for the MMAs and epilogue.
+// Raw stage (TMA / bulk copies): weights, activations and their scales of one chunk.
+// Operand stage: what the unpack warps derive from a raw stage for the MMAs and the epilogue.
 struct PfSmem {
     uint8_t raw[kPfRawStages][kPfRawBytes];
     uint8_t a[kPfOpStages][kPfABytes];
-    uint8_t amin[kPfOpStages][kPfMT * 32];   // dmy halves, K-major f16 operand (8 + 8 zero)
-    uint8_t bmin[kPfOpStages][kPfNT * 32];   // s8 halves
     float2 sc[kPfOpStages][8 * kPfMT];       // (dmx, dmy) per 32-block and row
     float dst[kPfOpStages][2][8][kPfNT];     // [d8 | s8][32-block][route]
     uint64_t rfull[kPfRawStages], rempty[kPfRawStages];
     uint64_t oempty[kPfOpStages], aready[kPfOpStages];
     uint64_t gfull[kPfGroups], gfree[kPfGroups];
-    uint64_t minfull, minfree, redready, redfree, mdone;
+    uint64_t mdone;
     int tiles[kPfMaxExperts + 1];            // route-tile prefix of the plan (item decoding)
     uint32_t tmem_base;
     int abort;
@@ -551,10 +546,6 @@ __host__ __device__ constexpr uint32_t umma_idesc_i8(int m, int n) {
     // N >> 3 at bit 17, M >> 4 at bit 24.
     return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
-__host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n) {
-    // kind::f16 instruction descriptor: D f32 (1 << 4), A f16 (0), B f16 (0), both K-major.
-    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
-}
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -565,17 +556,16 @@ __device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint6
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                           uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
 __device__ __forceinline__ void tc_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
+}
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
 }
 __device__ __forceinline__ void tc_ld8(uint32_t taddr, uint32_t (&v)[8]) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
@@ -611,17 +601,17 @@ __device__ __forceinline__ PfItem pf_item(const PfGemmParams &p, const int *tile
     return it;
 }
 
-// Unpack one raw GGUF super-block row into the int8 A tile (canonical layout), its 8 scale pairs
-// and (MMQ) the row of the f16 min-term operand.
+// Unpack half hh (sub-block pairs 2hh, 2hh+1) of one raw GGUF super-block row into the int8 A tile
+// (canonical no-swizzle K-major layout: 8-row groups 2048 B apart, 16-byte K slices 128 B apart,
+// rows 16 B apart) and its 4 scale pairs.
 template <int GT, int MODE>
-__device__ __forceinline__ void pf_unpack_row(const uint8_t *blk, uint8_t *a_tile, float2 *sc_col, uint8_t *amin,
-                                              int r) {
+__device__ __forceinline__ void pf_unpack_row(const uint8_t *blk, uint8_t *a_tile, float2 *sc_col, int r, int hh) {
     const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
     const float dall = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
     const uint32_t w0 = hdr.y, w1 = hdr.z, w2 = hdr.w;  // the 12 packed scale bytes
-    uint32_t hpack[4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int jj = 0; jj < 4; ++jj) {
+        const int j = 4 * hh + jj;
         // get_scale_min_k4 (quantized.cu:926-933) on bytes of w0..w2
         const auto byte = [&](int i) -> uint32_t {
             const uint32_t w = i < 4 ? w0 : (i < 8 ? w1 : w2);
@@ -636,19 +626,12 @@ __device__ __forceinline__ void pf_unpack_row(const uint8_t *blk, uint8_t *a_til
             mn = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
         }
         float dmx = __fmul_rn(dall, (float)sc), dmy = __fmul_rn(-dmin, (float)mn);
-        if (MODE == kPfModeMmq) {
-            const __half hx = __float2half_rn(dmx), hy = __float2half_rn(dmy);
-            dmx = __half2float(hx);
-            dmy = __half2float(hy);
-            const uint32_t hb = (uint32_t)__half_as_ushort(hy);
-            if (j & 1) hpack[j >> 1] |= hb << 16;
-            else hpack[j >> 1] = hb;
+        if (MODE == kPfModeMmq) {  // the MMQ tile loader rounds both products to half
+            dmx = __half2float(__float2half_rn(dmx));
+            dmy = __half2float(__float2half_rn(dmy));
         }
         sc_col[j * kPfMT] = make_float2(dmx, dmy);
     }
-    if (MODE == kPfModeMmq)
-        *reinterpret_cast<uint4 *>(amin + (r >> 3) * 256 + (r & 7) * 16) =
-            make_uint4(hpack[0], hpack[1], hpack[2], hpack[3]);
     const uint8_t *qs = blk + (GT == MMRS_Q5K ? 48 : 16);
     uint4 qh0 = make_uint4(0, 0, 0, 0), qh1 = make_uint4(0, 0, 0, 0);
     if (GT == MMRS_Q5K) {
@@ -657,8 +640,8 @@ __device__ __forceinline__ void pf_unpack_row(const uint8_t *blk, uint8_t *a_til
     }
     uint8_t *arow = a_tile + (r >> 3) * 2048 + (r & 7) * 16;
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-        const int jp = q >> 1, hf = q & 1;
+    for (int qq = 0; qq < 4; ++qq) {
+        const int q = 4 * hh + qq, jp = q >> 1, hf = q & 1;
         const uint4 v = *reinterpret_cast<const uint4 *>(qs + 16 * q);
         uint4 lo, hi;
         lo.x = v.x & 0x0F0F0F0Fu;
@@ -712,138 +695,39 @@ __device__ __forceinline__ bool pf_wait(uint64_t *bar, uint32_t parity, uint64_t
     return false;
 }
 
-__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-        : "r"(taddr));
+// Packed fp32 pairs (two IEEE operations per instruction, the same results as the scalar forms).
+__device__ __forceinline__ unsigned long long f2_bits(float2 v) { return *reinterpret_cast<unsigned long long *>(&v); }
+__device__ __forceinline__ float2 bits_f2(unsigned long long v) { return *reinterpret_cast<float2 *>(&v); }
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    unsigned long long r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+    return bits_f2(r);
 }
-__device__ __forceinline__ void tc_st16(uint32_t taddr, const float *a) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-            taddr),
-        "f"(a[0]), "f"(a[1]), "f"(a[2]), "f"(a[3]), "f"(a[4]), "f"(a[5]), "f"(a[6]), "f"(a[7]), "f"(a[8]), "f"(a[9]),
-        "f"(a[10]), "f"(a[11]), "f"(a[12]), "f"(a[13]), "f"(a[14]), "f"(a[15])
-        : "memory");
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+    unsigned long long r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return bits_f2(r);
 }
-__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// One work item of an epilogue warp for a route tile of 16 * NQ columns.  Groups hold
-// G = pf_group_size(16 NQ) sub-blocks; the warp reads its G / 2 of them in passes of two 16-column
-// loads (<= 32 values in flight), releases the group after the last load and accumulates
-// sum = fma(dmx * d8, C, sum) (generic numerics: + fma(dmy, s8, sum)).
-template <int NQ, int MODE>
-__device__ __forceinline__ bool pf_epi_item(PfSmem &sm, const PfGemmParams &p, const PfItem &it, uint32_t tq, int r,
-                                            int ph, int lane, int nkc, uint32_t nitem, uint32_t &c, uint32_t &q,
-                                            uint64_t deadline) {
-    constexpr int N = 16 * NQ;
-    constexpr int G = pf_group_size(N);
-    constexpr int LOADS = (G / 2) * NQ;  // 16-column loads per group and warp: 4
-    constexpr int PL = 2;                // loads per pass
-    constexpr int PASSES = (LOADS + PL - 1) / PL;
-    float acc[N];
+// Scale-and-accumulate 8 route columns of one 32-block: per column
+// sum = fma(dmx * d8, C, sum); sum = fma(dmy, s8, sum).
+__device__ __forceinline__ void pf_accumulate8(float2 (&acc)[4], const uint32_t (&v)[8], float2 scr, const float *dcol,
+                                               const float *scol) {
+    const float2 dmx = make_float2(scr.x, scr.x), dmy = make_float2(scr.y, scr.y);
 #pragma unroll
-    for (int i = 0; i < N; ++i) acc[i] = 0.0f;
-    for (int kc = 0; kc < nkc; ++kc, ++c) {
-        const int o = c % kPfOpStages;
-        if (!pf_wait(&sm.aready[o], (c / kPfOpStages) & 1, deadline, sm, p.status)) return false;
-        for (int j0 = 0; j0 < 8; j0 += G, ++q) {
-            const int gs = q % kPfGroups;
-            if (!pf_wait(&sm.gfull[gs], (q / kPfGroups) & 1, deadline, sm, p.status)) return false;
-            tc_fence_after();
-            const uint32_t gbase = tq + gs * kPfGroupCols;
+    for (int h4 = 0; h4 < 2; ++h4) {
+        const float4 d4 = *reinterpret_cast<const float4 *>(dcol + 4 * h4);
+        const float4 s4 = *reinterpret_cast<const float4 *>(scol + 4 * h4);
+        const float2 dp[2] = {make_float2(d4.x, d4.y), make_float2(d4.z, d4.w)};
+        const float2 sp[2] = {make_float2(s4.x, s4.y), make_float2(s4.z, s4.w)};
 #pragma unroll
-            for (int pass = 0; pass < PASSES; ++pass) {
-                uint32_t v[PL][16];
-#pragma unroll
-                for (int l = 0; l < PL; ++l) {
-                    const int t = pass * PL + l;
-                    if (t < LOADS) tc_ld16(gbase + (ph + 2 * (t / NQ)) * N + (t % NQ) * 16, v[l]);
-                }
-                tc_wait_ld();
-                if (pass == PASSES - 1) {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&sm.gfree[gs]);  // the group's values are in registers
-                }
-#pragma unroll
-                for (int l = 0; l < PL; ++l) {
-                    const int t = pass * PL + l;
-                    if (t >= LOADS) continue;
-                    const int cq = t % NQ;
-                    const int j = j0 + ph + 2 * (t / NQ);
-                    const float2 scr = sm.sc[o][j * kPfMT + r];
-#pragma unroll
-                    for (int i4 = 0; i4 < 4; ++i4) {
-                        const float4 d4 = *reinterpret_cast<const float4 *>(&sm.dst[o][0][j][cq * 16 + i4 * 4]);
-                        const float dd[4] = {d4.x, d4.y, d4.z, d4.w};
-                        float ss[4] = {0.f, 0.f, 0.f, 0.f};
-                        if (MODE == kPfModeGeneric) {
-                            const float4 s4 = *reinterpret_cast<const float4 *>(&sm.dst[o][1][j][cq * 16 + i4 * 4]);
-                            ss[0] = s4.x;
-                            ss[1] = s4.y;
-                            ss[2] = s4.z;
-                            ss[3] = s4.w;
-                        }
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            float &a = acc[cq * 16 + i4 * 4 + u];
-                            a = fmaf(__fmul_rn(scr.x, dd[u]), __int2float_rn((int)v[l][i4 * 4 + u]), a);
-                            if (MODE == kPfModeGeneric) a = fmaf(scr.y, ss[u], a);
-                        }
-                    }
-                }
-            }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.oempty[o]);
-    }
-    if (ph == 1) {
-        // hand the odd sub-blocks' partial sums to phase 0 through TMEM
-        if (!pf_wait(&sm.redfree, (nitem & 1) ^ 1, deadline, sm, p.status)) return false;
-        tc_fence_after();
-#pragma unroll
-        for (int cq = 0; cq < NQ; ++cq) tc_st16(tq + kPfRedCol + cq * 16, &acc[cq * 16]);
-        tc_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.redready);
-        return true;
-    }
-    if (!pf_wait(&sm.redready, nitem & 1, deadline, sm, p.status)) return false;
-    if (MODE == kPfModeMmq && !pf_wait(&sm.minfull, nitem & 1, deadline, sm, p.status)) return false;
-    tc_fence_after();
-#pragma unroll
-    for (int cq = 0; cq < NQ; ++cq) {
-        uint32_t a[16], m[16];
-        tc_ld16(tq + kPfRedCol + cq * 16, a);
-        if (MODE == kPfModeMmq) tc_ld16(tq + kPfMinCol + cq * 16, m);
-        tc_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            acc[cq * 16 + i] += __uint_as_float(a[i]);
-            if (MODE == kPfModeMmq) acc[cq * 16 + i] += __uint_as_float(m[i]);
+        for (int u = 0; u < 2; ++u) {
+            const int i = 2 * h4 + u;
+            const float2 cf = make_float2(__int2float_rn((int)v[2 * i]), __int2float_rn((int)v[2 * i + 1]));
+            acc[i] = ffma2(fmul2(dmx, dp[u]), cf, acc[i]);
+            acc[i] = ffma2(dmy, sp[u], acc[i]);
         }
     }
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) {
-        mbar_arrive(&sm.redfree);
-        if (MODE == kPfModeMmq) mbar_arrive(&sm.minfree);
-    }
-    const int row = it.m0 + r;
-    if (row < p.N) {
-#pragma unroll
-        for (int col = 0; col < N; ++col) {
-            if (col < it.nvalid) {
-                const int route = p.plan.row_route[it.p0 + col];
-                const float v = acc[col];
-                p.out[(size_t)route * p.N + row] = p.route_scale ? __fmul_rn(v, p.route_scale[route]) : v;
-            }
-        }
-    }
-    return true;
 }
 
 template <int GT, int MODE>
@@ -860,47 +744,33 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
     if (tid == 0) {
         for (int i = 0; i < kPfRawStages; ++i) {
             mbar_init(&sm.rfull[i], 1);
-            mbar_init(&sm.rempty[i], 4 + 1);  // unpack warps + MMA commit
+            mbar_init(&sm.rempty[i], kPfUnpackWarps + 1);  // unpack warps + MMA commit
         }
         for (int i = 0; i < kPfOpStages; ++i) {
             mbar_init(&sm.oempty[i], 1 + kPfEpiWarps);
-            mbar_init(&sm.aready[i], 4);
+            mbar_init(&sm.aready[i], kPfUnpackWarps);
         }
         for (int i = 0; i < kPfGroups; ++i) {
             mbar_init(&sm.gfull[i], 1);
             mbar_init(&sm.gfree[i], kPfEpiWarps);
         }
-        mbar_init(&sm.minfull, 1);
-        mbar_init(&sm.minfree, 4);
-        mbar_init(&sm.redready, 4);
-        mbar_init(&sm.redfree, 4);
         mbar_init(&sm.mdone, 1);
         sm.abort = 0;
         fence_mbar_init();
     }
-    // the zero halves (K 8..15) of the f16 min-term operands are written once
-    for (int i = tid; i < kPfOpStages * kPfMT; i += blockDim.x) {
-        const int o = i / kPfMT, rr = i % kPfMT;
-        *reinterpret_cast<uint4 *>(&sm.amin[o][(rr >> 3) * 256 + 128 + (rr & 7) * 16]) = make_uint4(0, 0, 0, 0);
-    }
     for (int i = tid; i <= p.E; i += blockDim.x) sm.tiles[i] = p.plan.tiles[i];
-    for (int i = tid; i < kPfOpStages * kPfNT; i += blockDim.x) {
-        const int o = i / kPfNT, c = i % kPfNT;
-        *reinterpret_cast<uint4 *>(&sm.bmin[o][(c >> 3) * 256 + 128 + (c & 7) * 16]) = make_uint4(0, 0, 0, 0);
-    }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm.tmem_base)),
                      "r"(kPfTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
 
     if (warp == 0) {
-        // ---------------- TMA producer: raw weight tiles ----------------
+        // ---------------- TMA producer ----------------
         if (lane == 0) {
             uint32_t c = 0;
             for (int item = blockIdx.x; item < total && !pf_aborted(sm); item += gridDim.x) {
@@ -915,8 +785,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                     tma_load_2d(sm.raw[s], &wmap, kc * (bb / 4), row0, &sm.rfull[s]);
                     bulk_g2s(sm.raw[s] + kPfRawW, p.aq + (size_t)kc * p.plan.ppad * QK_K + (size_t)it.p0 * QK_K, qb,
                              &sm.rfull[s]);
-                    bulk_g2s(sm.raw[s] + kPfRawW + kPfRawQ, p.ads + ((size_t)kc * (p.plan.ppad / 16) + it.p0 / 16) * 256,
-                             db, &sm.rfull[s]);
+                    bulk_g2s(sm.raw[s] + kPfRawW + kPfRawQ,
+                             p.ads + ((size_t)kc * (p.plan.ppad / 16) + it.p0 / 16) * 256, db, &sm.rfull[s]);
                 }
             }
             // drain: every issued copy lands before the CTA can exit
@@ -927,61 +797,41 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            uint32_t c = 0, q = 0, nitem = 0;  // q: group counter
+            uint32_t c = 0;
             bool ok = true;
-            for (int item = blockIdx.x; item < total && ok && !pf_aborted(sm); item += gridDim.x, ++nitem) {
+            for (int item = blockIdx.x; item < total && ok && !pf_aborted(sm); item += gridDim.x) {
                 const PfItem it = pf_item(p, sm.tiles, item);
                 const int n16 = pad_to(it.nvalid, 16);
-                const int G = pf_group_size(n16);
                 const uint32_t idesc = umma_idesc_i8(kPfMT, n16);
-                for (int kc = 0; kc < nkc && ok; ++kc, ++c) {
-                    const int o = c % kPfOpStages, s = c % kPfRawStages;
+                for (int kc = 0; kc < nkc; ++kc, ++c) {
+                    const int o = c % kPfOpStages, s = c % kPfRawStages, g = c % kPfGroups;
                     if (!pf_wait(&sm.aready[o], (c / kPfOpStages) & 1, deadline, sm, p.status) ||
-                        !pf_wait(&sm.rfull[s], (c / kPfRawStages) & 1, deadline, sm, p.status)) {
+                        !pf_wait(&sm.rfull[s], (c / kPfRawStages) & 1, deadline, sm, p.status) ||
+                        !pf_wait(&sm.gfree[g], ((c / kPfGroups) & 1) ^ 1, deadline, sm, p.status)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint32_t abase = smem_u32(sm.a[o]), bbase = smem_u32(sm.raw[s] + kPfRawW);
-                    for (int j0 = 0; j0 < 8; j0 += G, ++q) {
-                        const int gs = q % kPfGroups;
-                        if (!pf_wait(&sm.gfree[gs], ((q / kPfGroups) & 1) ^ 1, deadline, sm, p.status)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                        for (int i = 0; i < G; ++i)
-                            tc_mma_i8(tmem + gs * kPfGroupCols + i * n16, umma_smem_desc(abase + (j0 + i) * 256, 128, 2048),
-                                      umma_smem_desc(bbase + (j0 + i) * 256, 128, 2048), idesc, 0);
-                        tc_commit(&sm.gfull[gs]);
-                    }
-                    if (!ok) break;
-                    if (MODE == kPfModeMmq) {
-                        if (kc == 0) {
-                            if (!pf_wait(&sm.minfree, (nitem & 1) ^ 1, deadline, sm, p.status)) {
-                                ok = false;
-                                break;
-                            }
-                            tc_fence_after();
-                        }
-                        tc_mma_f16(tmem + kPfMinCol, umma_smem_desc(smem_u32(sm.amin[o]), 128, 256),
-                                   umma_smem_desc(smem_u32(sm.bmin[o]), 128, 256), umma_idesc_f16(kPfMT, n16),
-                                   kc > 0 ? 1u : 0u);
-                    }
+                    const uint32_t dbase = tmem + g * kPfGroupCols;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        tc_mma_i8(dbase + j * n16, umma_smem_desc(abase + j * 256, 128, 2048),
+                                  umma_smem_desc(bbase + j * 256, 128, 2048), idesc, 0);
+                    tc_commit(&sm.gfull[g]);
                     tc_commit(&sm.rempty[s]);
                     tc_commit(&sm.oempty[o]);
                 }
-                if (ok && MODE == kPfModeMmq) tc_commit(&sm.minfull);
             }
             // all MMAs issued by this thread complete before TMEM is released
-            if (q > 0) {
+            if (c > 0) {
                 tc_commit(&sm.mdone);
                 mbar_wait_bounded(&sm.mdone, 0, deadline + p.timeout_ns);
             }
         }
     } else if (warp < kPfEpiWarp0) {
         // ---------------- unpack (128 threads, one weight row each) ----------------
-        const int r = tid - 64;
+        const int t = tid - 64, r = t;
         uint32_t c = 0;
         for (int item = blockIdx.x; item < total && !pf_aborted(sm); item += gridDim.x) {
             const PfItem it = pf_item(p, sm.tiles, item);
@@ -989,32 +839,19 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
             bool ok = true;
             for (int kc = 0; kc < nkc; ++kc, ++c) {
                 const int s = c % kPfRawStages, o = c % kPfOpStages;
-                const uint32_t opar = (c / kPfOpStages) & 1;
-                if (!pf_wait(&sm.oempty[o], opar ^ 1, deadline, sm, p.status) ||
+                if (!pf_wait(&sm.oempty[o], ((c / kPfOpStages) & 1) ^ 1, deadline, sm, p.status) ||
                     !pf_wait(&sm.rfull[s], (c / kPfRawStages) & 1, deadline, sm, p.status)) {
                     ok = false;
                     break;
                 }
-                pf_unpack_row<GT, MODE>(sm.raw[s] + r * bb, sm.a[o], &sm.sc[o][r], sm.amin[o], r);
+                pf_unpack_row<GT, MODE>(sm.raw[s] + r * bb, sm.a[o], &sm.sc[o][r], r, 0);
+                pf_unpack_row<GT, MODE>(sm.raw[s] + r * bb, sm.a[o], &sm.sc[o][r], r, 1);
                 // block scales of the route tile: 16-route records [d8 plane | s8 plane][32-block][16]
                 const float *dsraw = reinterpret_cast<const float *>(sm.raw[s] + kPfRawW + kPfRawQ);
-                if (r < n16 * 4) {  // float4 r of the records -> dst[plane][j][route]
-                    const int b = r >> 6, plane = (r >> 5) & 1, j = (r >> 2) & 7, c4 = r & 3;
+                if (t < n16 * 4) {  // float4 t of the records -> dst[plane][j][route]
+                    const int b = t >> 6, plane = (t >> 5) & 1, j = (t >> 2) & 7, c4 = t & 3;
                     *reinterpret_cast<float4 *>(&sm.dst[o][plane][j][b * 16 + c4 * 4]) =
-                        *reinterpret_cast<const float4 *>(dsraw + r * 4);
-                }
-                if (MODE == kPfModeMmq && r < n16) {
-                    // route r: s8 halves of its 8 blocks for the min-term MMA
-                    uint32_t hs[4];
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const float v = dsraw[(r >> 4) * 256 + 128 + j * 16 + (r & 15)];
-                        const uint32_t hb = (uint32_t)__half_as_ushort(__float2half_rn(v));
-                        if (j & 1) hs[j >> 1] |= hb << 16;
-                        else hs[j >> 1] = hb;
-                    }
-                    *reinterpret_cast<uint4 *>(&sm.bmin[o][(r >> 3) * 256 + (r & 7) * 16]) =
-                        make_uint4(hs[0], hs[1], hs[2], hs[3]);
+                        *reinterpret_cast<const float4 *>(dsraw + t * 4);
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -1027,20 +864,73 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
         }
     } else {
         // ---------------- epilogue (8 warps) ----------------
-        // warp = (TMEM lane quarter qd, phase ph): phase ph takes the sub-blocks ph, ph + 2, ... of
-        // every TMEM group for all route columns; phase 1 hands its partial sums to phase 0
-        // through TMEM at the end of the item, phase 0 adds them (and the min term) and writes.
-        const int qd = warp & 3, ph = (warp - kPfEpiWarp0) >> 2;
+        // warp = (TMEM lane quarter qd, route half h): route columns [16 h, 16 h + 16) of the rows
+        // 32 qd .. 32 qd + 31, read in units of 8 columns (only units holding a route); per chunk
+        // one group wait, then four passes of two 32-blocks.
+        const int qd = warp & 3, h = (warp - kPfEpiWarp0) >> 2;
         const int r = qd * 32 + lane;
         const uint32_t tq = tmem + ((uint32_t)(qd * 32) << 16);
-        uint32_t c = 0, q = 0, nitem = 0;
-        for (int item = blockIdx.x; item < total && !pf_aborted(sm); item += gridDim.x, ++nitem) {
+        uint32_t c = 0;
+        for (int item = blockIdx.x; item < total && !pf_aborted(sm); item += gridDim.x) {
             const PfItem it = pf_item(p, sm.tiles, item);
-            const int nq = pad_to(it.nvalid, 16) / 16;
-            bool ok;
-            if (nq == 1) ok = pf_epi_item<1, MODE>(sm, p, it, tq, r, ph, lane, nkc, nitem, c, q, deadline);
-            else ok = pf_epi_item<2, MODE>(sm, p, it, tq, r, ph, lane, nkc, nitem, c, q, deadline);
+            const int n16 = pad_to(it.nvalid, 16);
+            const bool has0 = 16 * h < it.nvalid, has1 = 16 * h + 8 < it.nvalid;
+            float2 acc[2][4];
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[u][i] = make_float2(0.0f, 0.0f);
+            bool ok = true;
+            for (int kc = 0; kc < nkc; ++kc, ++c) {
+                const int o = c % kPfOpStages, g = c % kPfGroups;
+                if (!pf_wait(&sm.aready[o], (c / kPfOpStages) & 1, deadline, sm, p.status) ||
+                    !pf_wait(&sm.gfull[g], (c / kPfGroups) & 1, deadline, sm, p.status)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t gbase = tq + g * kPfGroupCols + 16 * h;
+#pragma unroll
+                for (int pass = 0; pass < 4; ++pass) {
+                    uint32_t v[2][2][8];  // [32-block][unit][column]
+#pragma unroll
+                    for (int b = 0; b < 2; ++b) {
+                        if (has0) tc_ld8(gbase + (2 * pass + b) * n16, v[b][0]);
+                        if (has1) tc_ld8(gbase + (2 * pass + b) * n16 + 8, v[b][1]);
+                    }
+                    if (has0) tc_wait_ld();
+                    if (pass == 3) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&sm.gfree[g]);  // the group's values are in registers
+                    }
+#pragma unroll
+                    for (int b = 0; b < 2; ++b) {
+                        const int j = 2 * pass + b;
+                        const float2 scr = sm.sc[o][j * kPfMT + r];
+                        if (has0) pf_accumulate8(acc[0], v[b][0], scr, &sm.dst[o][0][j][16 * h], &sm.dst[o][1][j][16 * h]);
+                        if (has1)
+                            pf_accumulate8(acc[1], v[b][1], scr, &sm.dst[o][0][j][16 * h + 8],
+                                           &sm.dst[o][1][j][16 * h + 8]);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.oempty[o]);
+            }
             if (!ok) break;
+            const int row = it.m0 + r;
+            if (has0 && row < p.N) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int col = 16 * h + i;
+                    if (col < it.nvalid) {
+                        const int route = p.plan.row_route[it.p0 + col];
+                        const float2 a2 = acc[i >> 3][(i & 7) >> 1];
+                        const float v = (i & 1) ? a2.y : a2.x;
+                        p.out[(size_t)route * p.N + row] = p.route_scale ? __fmul_rn(v, p.route_scale[route]) : v;
+                    }
+                }
+            }
         }
     }
 

@@ -11,11 +11,12 @@ namespace mmrs {
 constexpr int kPfNT = 32;           // routes per GEMM tile (MMA N <= 32)
 constexpr int kPfMT = 128;          // weight rows per GEMM tile (MMA M)
 constexpr int kPfSegAlign = 16;     // each expert's route segment is padded to this many rows
-constexpr int kPfRawStages = 4;     // raw GGUF weight tiles in flight (TMA)
-constexpr int kPfOpStages = 2;      // unpacked operand stages (A int8, B int8, scales)
-constexpr int kPfGroups = 3;        // TMEM group slots of 128 columns (sub-block accumulators)
-constexpr int kPfEpiWarps = 8;      // epilogue warps: 4 TMEM lane quarters x 2 sub-block phases
-constexpr int kPfThreads = 32 * (6 + kPfEpiWarps);  // TMA, MMA, 4 unpack, 8 epilogue
+constexpr int kPfRawStages = 3;     // raw GGUF weight tiles in flight (TMA)
+constexpr int kPfOpStages = 3;      // unpacked operand stages (A int8, scales)
+constexpr int kPfGroups = 2;        // TMEM groups: the 8 block accumulators of one chunk each
+constexpr int kPfEpiWarps = 8;      // epilogue warps: 4 TMEM lane quarters x 2 halves of the routes
+constexpr int kPfUnpackWarps = 4;   // one thread per weight row
+constexpr int kPfThreads = 32 * (2 + kPfUnpackWarps + kPfEpiWarps);  // TMA, MMA, unpack, epilogue
 constexpr int kPfMaxExperts = 1024;
 
 // Activation quantisation numerics.
