@@ -167,6 +167,72 @@ MMRS_API int mmrs_moe_block_decode_static(const MmrsMoeWeights *w, const float *
 MMRS_API int mmrs_moe_workspace_status(void *workspace, mmrs_stream_t stream);
 
 /* ===================================================================================== */
+/* 2b. Multi-GPU: tensor parallel (TP=2, the reference layout) and expert parallel (W=4/8)  */
+/* ===================================================================================== */
+
+/* Reference two-rank peer collectives (ffi.rs:505-528; mmvq_gguf.cu:888-966).
+ * launch_tp2_peer_all_reduce_f32: output = local + peer (+ residual); with normalized_output,
+ * normalized_output = output * rsqrt(mean(output^2) + eps) * norm_weight.  Both ranks launch with
+ * the same epoch (0: self counter in self_signal[2]).  Signal buffers are 128-byte peer-visible
+ * words, zero before first use; waits are bounded (2 s) and an expiry sets self_signal[3] to
+ * MMRS_ERR_TIMEOUT.  Launch status: mmrs_last_error(). */
+MMRS_API void launch_tp2_peer_all_reduce_f32(const void *local, const void *peer, const void *residual,
+                                             const void *norm_weight, void *output,
+                                             void *normalized_output, void *self_signal,
+                                             void *peer_signal, unsigned int epoch, int count,
+                                             float norm_eps, void *stream);
+MMRS_API void launch_tp2_peer_broadcast_f32(const void *source, void *output, void *self_signal,
+                                            void *peer_signal, unsigned int epoch, int rank,
+                                            int count, void *stream);
+
+/* No counterpart struct in the reference (it passes peer pointers per call).  One rank's view of
+ * a group of `world` GPUs.  `mine` is this rank's exchange region (mmrs_peer_alloc of
+ * mmrs_xch_bytes(ar_capacity) bytes, zeroed); peers[r] is rank r's region as mapped in this
+ * process (CUDA IPC between processes, or plain device pointers with peer access inside one
+ * process); peers[rank] == mine.  expert_parallel = 0: tensor parallel, every rank holds
+ * gate/up rows [rank * inter, (rank + 1) * inter) and the matching down K range of every expert
+ * (MmrsMoeWeights.inter is the per-rank inter); 1: expert parallel, rank r holds the full
+ * experts e with e % world == r (MmrsMoeWeights still points at [num_experts] tensors; the
+ * non-owned experts' bytes are never read). */
+typedef struct {
+    int world;
+    int rank;
+    void *mine;
+    const void *peers[8];
+    size_t ar_capacity; /* floats per all-reduce buffer: >= T * hidden of the largest T > 1 call */
+    int expert_parallel;
+} MmrsPeerGroup;
+
+MMRS_API size_t mmrs_xch_bytes(size_t ar_capacity);
+MMRS_API int mmrs_peer_alloc(size_t bytes, void **ptr);       /* cudaMalloc + zero */
+MMRS_API int mmrs_peer_free(void *ptr);
+MMRS_API int mmrs_ipc_handle(void *ptr, uint8_t *handle64);    /* 64-byte CUDA IPC handle */
+MMRS_API int mmrs_ipc_open(const uint8_t *handle64, void **ptr);
+MMRS_API int mmrs_ipc_close(void *ptr);
+MMRS_API int mmrs_peer_enable(int peer_device);                /* one process, several GPUs */
+
+/* Multi-rank all-reduce of partial vectors: every rank writes its partial [count] f32 into
+ * mmrs_xch_ar_buffer(g, token) (earlier on `stream`), then all ranks call mmrs_peer_all_reduce
+ * with the same token (monotonic, starting at 1): y = sum over ranks in rank order (+ residual),
+ * bit-identical on all ranks.  count <= ar_capacity. */
+MMRS_API float *mmrs_xch_ar_buffer(const MmrsPeerGroup *g, uint32_t token);
+MMRS_API int mmrs_peer_all_reduce(const MmrsPeerGroup *g, const float *residual, float *y,
+                                  size_t count, uint32_t token, mmrs_stream_t stream);
+/* Reads back (synchronising `stream`) and clears the group's device status word. */
+MMRS_API int mmrs_peer_status(const MmrsPeerGroup *g, mmrs_stream_t stream);
+
+/* The MoE block on one rank of a group (replaces the TP rank worker's MoE call plus
+ * TensorParallelRankGroup::all_reduce_sum_with_residual, tensor_parallel.rs:786-812): y is the
+ * full block output (+ residual) on every rank.  T == 1: the fused decode kernel exchanges the
+ * ranks' partial rows over NVLink inside the same launch.  T > 1: the multi-token path on the
+ * rank's shard, then mmrs_peer_all_reduce with `token` (same on all ranks, monotonic). */
+MMRS_API int mmrs_moe_block_forward_group(const MmrsMoeWeights *w, const MmrsPeerGroup *g,
+                                          const float *x, const float *residual, float *y,
+                                          int num_tokens, uint32_t *topk_ids, float *topk_weights,
+                                          void *workspace, size_t workspace_bytes, uint32_t token,
+                                          mmrs_stream_t stream);
+
+/* ===================================================================================== */
 /* 3. Seeded synthetic data (bench / test inputs; same generator as the numpy mirror)     */
 /* ===================================================================================== */
 

@@ -39,6 +39,11 @@ class MmrsMoeWeights(C.Structure):
                 ("num_experts", C.c_int), ("topk", C.c_int), ("hidden", C.c_int), ("inter", C.c_int)]
 
 
+class MmrsPeerGroup(C.Structure):
+    _fields_ = [("world", C.c_int), ("rank", C.c_int), ("mine", C.c_void_p), ("peers", C.c_void_p * 8),
+                ("ar_capacity", C.c_size_t), ("expert_parallel", C.c_int)]
+
+
 _VP, _I, _U32, _U64, _I64, _F = C.c_void_p, C.c_int, C.c_uint32, C.c_uint64, C.c_int64, C.c_float
 _SZ = C.c_size_t
 
@@ -50,6 +55,20 @@ PROTOTYPES = {
     "moe_gemm_mmq_gguf": (None, [_VP] * 6 + [_I] * 6 + [_VP]),
     "moe_sort_routes": (None, [_VP] * 3 + [_I] * 2 + [_VP]),
     "mmrs_last_error": (_I, []),
+    "launch_tp2_peer_all_reduce_f32": (None, [_VP] * 8 + [C.c_uint, _I, _F, _VP]),
+    "launch_tp2_peer_broadcast_f32": (None, [_VP] * 4 + [C.c_uint, _I, _I, _VP]),
+    "mmrs_xch_bytes": (_SZ, [_SZ]),
+    "mmrs_peer_alloc": (_I, [_SZ, C.POINTER(C.c_void_p)]),
+    "mmrs_peer_free": (_I, [_VP]),
+    "mmrs_ipc_handle": (_I, [_VP, C.POINTER(C.c_uint8)]),
+    "mmrs_ipc_open": (_I, [C.POINTER(C.c_uint8), C.POINTER(C.c_void_p)]),
+    "mmrs_ipc_close": (_I, [_VP]),
+    "mmrs_peer_enable": (_I, [_I]),
+    "mmrs_xch_ar_buffer": (_VP, [C.POINTER(MmrsPeerGroup), _U32]),
+    "mmrs_peer_all_reduce": (_I, [C.POINTER(MmrsPeerGroup), _VP, _VP, _SZ, _U32, _VP]),
+    "mmrs_peer_status": (_I, [C.POINTER(MmrsPeerGroup), _VP]),
+    "mmrs_moe_block_forward_group": (_I, [C.POINTER(MmrsMoeWeights), C.POINTER(MmrsPeerGroup), _VP, _VP, _VP, _I,
+                                          _VP, _VP, _VP, _SZ, _U32, _VP]),
     "mmrs_moe_workspace_bytes": (_SZ, [C.POINTER(MmrsMoeWeights), _I]),
     "mmrs_moe_block_forward": (_I, [C.POINTER(MmrsMoeWeights), _VP, _VP, _VP, _I, _VP, _VP, _VP, _SZ, _VP]),
     "mmrs_moe_workspace_status": (_I, [_VP, _VP]),

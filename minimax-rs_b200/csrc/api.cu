@@ -4,6 +4,7 @@
 
 #include "common.cuh"
 #include "decode.cuh"
+#include "peer.cuh"
 #include "prefill.cuh"
 #include "workspace.cuh"
 
@@ -14,6 +15,7 @@ static int set_err(int e) {
     g_last_error = e;
     return e;
 }
+void record_error(int status) { g_last_error = status; }
 
 static int device_sms() {
     int dev = 0, sms = 0;
@@ -360,7 +362,8 @@ extern "C" size_t mmrs_moe_workspace_bytes(const MmrsMoeWeights *w, int max_toke
 // generic ones below, as fused_moe.rs:296-316 selects), gate / up GEMMs, SiLU * up fused into
 // the down operand's quantisation, down GEMM scaled by the route weight, top-8 sum + residual.
 static int block_forward_multi(const MmrsMoeWeights *w, const float *x, const float *residual, float *y, int T,
-                               uint32_t *topk_ids, float *topk_weights, uint8_t *ws, cudaStream_t s) {
+                               uint32_t *topk_ids, float *topk_weights, uint8_t *ws, cudaStream_t s,
+                               int own_world = 1, int own_rank = 0) {
     const int E = w->num_experts, H = w->hidden, I = w->inter, M = T * 8;
     const PfLayout l = pf_layout(ws_layout(E, I, 1).total, E, H, I, T);
     float *logits = reinterpret_cast<float *>(ws + l.logits);
@@ -381,7 +384,7 @@ static int block_forward_multi(const MmrsMoeWeights *w, const float *x, const fl
     if (rc == MMRS_OK) rc = pf_sort_routes(ids, M, bits_for(E), skeys, sroutes, s);
     if (rc == MMRS_OK)
         rc = pf_build_plan(reinterpret_cast<const int32_t *>(skeys), reinterpret_cast<const int32_t *>(sroutes), M, E,
-                           plan, s);
+                           plan, s, own_world, own_rank);
     if (rc == MMRS_OK) rc = pf_quantize(x, nullptr, 8, H, mode_gu, plan, xh, l.ppad, s);
     PfGemmParams gp = {};
     gp.plan = plan;
@@ -414,7 +417,7 @@ static int block_forward_multi(const MmrsMoeWeights *w, const float *x, const fl
         gp.out = dn;
         rc = pf_gemm(w->down, gp, l.ppad, s);
     }
-    if (rc == MMRS_OK) rc = pf_reduce_topk(dn, residual, T, H, y, s);
+    if (rc == MMRS_OK) rc = pf_reduce_topk(dn, residual, T, H, y, s, ids, own_world, own_rank);
     return rc;
 }
 
@@ -482,4 +485,65 @@ extern "C" int mmrs_moe_workspace_trace(const void *workspace, uint64_t *host_ou
         return -MMRS_ERR_LAUNCH;
     if (cudaStreamSynchronize(s) != cudaSuccess) return -MMRS_ERR_LAUNCH;
     return n;
+}
+
+extern "C" int mmrs_moe_block_forward_group(const MmrsMoeWeights *w, const MmrsPeerGroup *g, const float *x,
+                                            const float *residual, float *y, int num_tokens, uint32_t *topk_ids,
+                                            float *topk_weights, void *workspace, size_t workspace_bytes,
+                                            uint32_t token, mmrs_stream_t stream) {
+    if (!g || g->world < 1 || g->world > kMaxRanks || g->rank < 0 || g->rank >= g->world) return MMRS_ERR_ARG;
+    if (g->world == 1)
+        return mmrs_moe_block_forward(w, x, residual, y, num_tokens, topk_ids, topk_weights, workspace,
+                                      workspace_bytes, stream);
+    int rc = validate_weights(w);
+    if (rc != MMRS_OK) return rc;
+    if (!x || !y || num_tokens < 0 || !workspace || !g->mine) return MMRS_ERR_ARG;
+    for (int r = 0; r < g->world; ++r)
+        if (!g->peers[r]) return MMRS_ERR_ARG;
+    if (num_tokens == 0) return MMRS_OK;
+    if (workspace_bytes < mmrs_moe_workspace_bytes(w, num_tokens) || !aligned16(workspace) || !aligned16(x) ||
+        !aligned16(y) || (residual && !aligned16(residual)))
+        return MMRS_ERR_ARG;
+    if (w->hidden > kXchMaxHidden) return MMRS_ERR_UNSUPPORTED;
+    uint8_t *ws = (uint8_t *)workspace;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int ep = g->expert_parallel ? 1 : 0;
+    if (num_tokens > 1) {
+        // rank-local block into this rank's all-reduce buffer, then the peer all-reduce (+ residual)
+        const size_t count = (size_t)num_tokens * w->hidden;
+        if (count > g->ar_capacity || token == 0) return MMRS_ERR_ARG;
+        float *partial = mmrs_xch_ar_buffer(g, token);
+        rc = block_forward_multi(w, x, nullptr, partial, num_tokens, topk_ids, topk_weights, ws, s,
+                                 ep ? g->world : 1, ep ? g->rank : 0);
+        if (rc != MMRS_OK) return rc;
+        return mmrs_peer_all_reduce(g, residual, y, count, token, stream);
+    }
+    const WsLayout l = ws_layout(w->num_experts, w->inter, 1);
+    DecodeParams p = {};
+    p.x = x;
+    p.router = w->router;
+    p.bias = w->bias;
+    p.gate = (const uint8_t *)w->gate;
+    p.up = (const uint8_t *)w->up;
+    p.down = (const uint8_t *)w->down;
+    p.residual = residual;
+    p.y = y;
+    p.topk_ids_out = topk_ids;
+    p.topk_w_out = topk_weights;
+    p.internal_routing = 1;
+    ws_bind(p, ws, l);
+    p.E = w->num_experts;
+    p.H = w->hidden;
+    p.I = w->inter;
+    p.gu_type = w->gate_up_type;
+    p.dn_type = w->down_type;
+    p.timeout_ns = kTimeoutNs;
+    p.xch = static_cast<uint8_t *>(g->mine);
+    for (int r = 0; r < g->world; ++r) p.xpeer[r] = static_cast<const uint8_t *>(g->peers[r]);
+    p.world = g->world;
+    p.rank = g->rank;
+    p.ep = ep;
+    rc = decode_configure(p, device_sms(), device_max_smem());
+    if (rc != MMRS_OK) return rc;
+    return decode_launch(p, s);
 }

@@ -30,6 +30,7 @@
 // the workspace status word, keeps every named barrier matched, drains its copies and returns.
 #include "common.cuh"
 #include "decode.cuh"
+#include "peer.cuh"
 
 namespace mmrs {
 
@@ -290,6 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         mbar_init(s.abar, 1);
         fence_mbar_init();
         s.flag[0] = 1;
+        s.flag[1] = 0;
     }
     __syncthreads();
 
@@ -427,6 +429,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
                 s.w[slot] = p.ext_w[slot];
             }
         }
+        __syncthreads();
+    }
+    if (p.world > 1 && p.ep) {
+        // expert parallel: experts owned by other ranks contribute nothing here
+        __syncthreads();
+        if (tid < kTopK && s.ids[tid] >= 0 && s.ids[tid] % p.world != p.rank) s.ids[tid] = -1;
         __syncthreads();
     }
     if (!ok) return;  // nothing issued yet
@@ -693,11 +701,53 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         }
         // y = fixed 8-way tree over the routed experts (moe_gguf.cu:328-342) + residual
         named_sync(1, kConsumerThreads);
-        for (int r = tid; r < dn_r1 - dn_r0; r += kConsumerThreads) {
-            const float *q = s.dn_acc + r * kTopK;
-            float y = ((q[0] + q[4]) + (q[2] + q[6])) + ((q[1] + q[5]) + (q[3] + q[7]));
-            if (p.residual) y = y + s.res_s[r];
-            p.y[dn_r0 + r] = y;
+        if (p.world <= 1) {
+            for (int r = tid; r < dn_r1 - dn_r0; r += kConsumerThreads) {
+                const float *q = s.dn_acc + r * kTopK;
+                float y = ((q[0] + q[4]) + (q[2] + q[6])) + ((q[1] + q[5]) + (q[3] + q[7]));
+                if (p.residual) y = y + s.res_s[r];
+                p.y[dn_r0 + r] = y;
+            }
+        } else {
+            // Fused exchange of the partial rows with the other ranks over NVLink: publish this
+            // CTA's rows in the exchange region (buffer token & 1), release a per-CTA flag, wait
+            // (bounded) for the same CTA's flag on every peer, then sum the ranks' rows in rank
+            // order (bit-identical on all ranks) and add the residual
+            // (TensorParallelRankGroup::all_reduce_sum_with_residual, tensor_parallel.rs:786-812).
+            const uint32_t token = epoch / 2u + 1u;
+            const size_t part_off = kXchDPart + sizeof(float) * (size_t)(token & 1u) * kXchMaxHidden;
+            float *mine = reinterpret_cast<float *>(p.xch + part_off);
+            for (int r = tid; r < dn_r1 - dn_r0; r += kConsumerThreads) {
+                const float *q = s.dn_acc + r * kTopK;
+                mine[dn_r0 + r] = ((q[0] + q[4]) + (q[2] + q[6])) + ((q[1] + q[5]) + (q[3] + q[7]));
+            }
+            named_sync(1, kConsumerThreads);
+            if (tid == 0) {
+                st_release_sys(reinterpret_cast<uint32_t *>(p.xch + kXchDFlags) + cta, token);
+                const uint64_t xdl = globaltimer_ns() + p.timeout_ns;
+                for (int rk = 0; rk < p.world; ++rk) {
+                    if (rk == p.rank) continue;
+                    if (!wait_flag_sys(reinterpret_cast<const uint32_t *>(p.xpeer[rk] + kXchDFlags) + cta, token, xdl)) {
+                        atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
+                        atomicExch(reinterpret_cast<uint32_t *>(p.xch + kXchStatus), (uint32_t)MMRS_ERR_TIMEOUT);
+                        s.flag[1] = 1;
+                        break;
+                    }
+                }
+            }
+            named_sync(1, kConsumerThreads);
+            const bool xfail = *reinterpret_cast<volatile int *>(&s.flag[1]) != 0;
+            for (int r = tid; r < dn_r1 - dn_r0 && !xfail; r += kConsumerThreads) {
+                const int row = dn_r0 + r;
+                float y = 0.f;
+                for (int rk = 0; rk < p.world; ++rk) {
+                    const float v = rk == p.rank ? mine[row]
+                                                 : ld_volatile_f32(reinterpret_cast<const float *>(p.xpeer[rk] + part_off) + row);
+                    y = rk == 0 ? v : y + v;
+                }
+                if (p.residual) y = y + s.res_s[r];
+                p.y[row] = y;
+            }
         }
     }
     if (tid == 0 && p.trace) p.trace[cta * 16 + 7] = globaltimer_ns();

@@ -39,6 +39,11 @@ struct DecodeParams {
     int gu_lanes, gu_unit_rows, dn_lanes, dn_unit_rows, stages, stage_bytes, grid;
     int act_slots, res_slots;
     uint64_t timeout_ns;
+    // multi-GPU group (world > 1): this rank's exchange region and every rank's as mapped here;
+    // ep = 1: only experts e with e % world == rank are computed on this rank
+    uint8_t *xch;
+    const uint8_t *xpeer[8];
+    int world, rank, ep;
 };
 
 size_t decode_smem_bytes(const DecodeParams &p);

@@ -1,0 +1,59 @@
+// Peer-visible exchange memory for the multi-GPU MoE block (tensor parallel TP=2 and expert
+// parallel W=4/8): one region per rank, mapped into the other ranks' address spaces (CUDA IPC
+// between processes, or direct peer pointers inside one process).  The ranks' partial hidden
+// states are summed over NVLink with peer loads; every wait on a peer flag is bounded.
+#pragma once
+
+#include "common.cuh"
+
+namespace mmrs {
+
+constexpr int kMaxRanks = 8;
+constexpr int kXchMaxHidden = 8192;   // decode partial rows per buffer
+constexpr int kXchMaxCtas = 1024;
+
+// Layout of one rank's exchange region (bytes).  Flags hold the token of the last operation that
+// published data (monotonic; readers wait until flag >= token).  Partials are double buffered by
+// token parity: a rank writes buffer (token & 1) only after every peer has published a later
+// token than the last reader of that buffer.
+constexpr size_t kXchStatus = 0;       // u32: MMRS_ERR_TIMEOUT after an expired wait
+constexpr size_t kXchDFlags = 4096;    // u32[kXchMaxCtas]: fused decode kernel, one per CTA
+constexpr size_t kXchAFlags = 8192;    // u32[kXchMaxCtas]: all-reduce kernel, one per CTA
+constexpr size_t kXchDPart = 12288;    // f32[2][kXchMaxHidden]: decode partial y
+constexpr size_t kXchAPart = kXchDPart + 2 * sizeof(float) * kXchMaxHidden;  // f32[2][cap]
+
+__host__ __device__ inline size_t xch_bytes(size_t ar_capacity) {
+    return kXchAPart + 2 * sizeof(float) * ar_capacity;
+}
+
+struct PeerView {
+    int world, rank;
+    uint8_t *mine;
+    const uint8_t *peers[kMaxRanks];  // peers[rank] == mine
+    size_t ar_capacity;               // floats per all-reduce buffer
+};
+
+// Wrap-safe "a >= b" for monotonic tokens.
+__device__ __forceinline__ bool token_reached(uint32_t a, uint32_t b) { return (int)(a - b) >= 0; }
+
+// Bounded wait until *flag >= token (system-scope acquire).  false on timeout.
+__device__ __forceinline__ bool wait_flag_sys(const uint32_t *flag, uint32_t token, uint64_t deadline) {
+    uint32_t spins = 0;
+    while (!token_reached(ld_acquire_sys(flag), token)) {
+        __nanosleep(32);
+        if ((++spins & 63u) == 0 && globaltimer_ns() > deadline) return false;
+    }
+    return true;
+}
+
+// Load that bypasses the L1 (peer partials are rewritten between operations).
+__device__ __forceinline__ float ld_volatile_f32(const float *p) {
+    float v;
+    asm volatile("ld.volatile.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    return v;
+}
+
+int peer_all_reduce(const PeerView &g, const float *residual, float *y, size_t count, uint32_t token,
+                    uint64_t timeout_ns, cudaStream_t stream);
+
+}  // namespace mmrs

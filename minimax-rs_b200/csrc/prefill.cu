@@ -320,14 +320,14 @@ __device__ __forceinline__ int block_excl_scan_1024(int v, int *tmp /* >= 32 int
 
 __global__ void __launch_bounds__(1024) build_plan_kernel(const int32_t *__restrict__ se,
                                                           const int32_t *__restrict__ sr, int M, int E,
-                                                          PfPlan plan) {
+                                                          PfPlan plan, int own_world, int own_rank) {
     __shared__ int tmp[33];
     __shared__ int s_first[kPfMaxExperts], s_seg[kPfMaxExperts];
     const int e = threadIdx.x;
     int first = 0, cnt = 0;
     if (e < E) {
         first = lower_bound_i32(se, M, e);
-        cnt = lower_bound_i32(se, M, e + 1) - first;
+        cnt = e % own_world == own_rank ? lower_bound_i32(se, M, e + 1) - first : 0;
     }
     int total;
     const int seg = block_excl_scan_1024(e < E ? pad_to(cnt, kPfSegAlign) : 0, tmp, total);
@@ -345,15 +345,16 @@ __global__ void __launch_bounds__(1024) build_plan_kernel(const int32_t *__restr
     __syncthreads();
     for (int i = threadIdx.x; i < M; i += blockDim.x) {
         const int ex = se[i];
-        if (ex < 0 || ex >= E) continue;
+        if (ex < 0 || ex >= E || ex % own_world != own_rank) continue;
         plan.row_route[s_seg[ex] + i - s_first[ex]] = sr[i];
     }
 }
 
 int pf_build_plan(const int32_t *sorted_experts, const int32_t *sorted_routes, int M, int E, PfPlan plan,
-                  cudaStream_t s) {
+                  cudaStream_t s, int own_world, int own_rank) {
     if (E < 1 || E > kPfMaxExperts) return MMRS_ERR_UNSUPPORTED;
-    build_plan_kernel<<<1, 1024, 0, s>>>(sorted_experts, sorted_routes, M, E, plan);
+    if (own_world < 1 || own_rank < 0 || own_rank >= own_world) return MMRS_ERR_ARG;
+    build_plan_kernel<<<1, 1024, 0, s>>>(sorted_experts, sorted_routes, M, E, plan, own_world, own_rank);
     return cudaGetLastError() == cudaSuccess ? MMRS_OK : MMRS_ERR_LAUNCH;
 }
 
@@ -454,7 +455,8 @@ int pf_quantize(const float *x, const float *x2, int div, int K, int mode, PfPla
 // ==========================================================================================
 __global__ void __launch_bounds__(256) reduce_topk_kernel(const float *__restrict__ dn,
                                                           const float *__restrict__ residual, int T, int H,
-                                                          float *__restrict__ y) {
+                                                          float *__restrict__ y, const uint32_t *__restrict__ ids,
+                                                          int own_world, int own_rank) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;  // float4 index
     const size_t n4 = (size_t)T * H / 4;
     if (i >= n4) return;
@@ -462,6 +464,7 @@ __global__ void __launch_bounds__(256) reduce_topk_kernel(const float *__restric
     float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
+        if (own_world > 1 && ids[t * 8 + k] % (uint32_t)own_world != (uint32_t)own_rank) continue;
         const float4 v = *reinterpret_cast<const float4 *>(dn + ((t * 8 + k) * H + h));
         s.x = s.x + v.x;
         s.y = s.y + v.y;
@@ -478,10 +481,12 @@ __global__ void __launch_bounds__(256) reduce_topk_kernel(const float *__restric
     *reinterpret_cast<float4 *>(y + t * H + h) = s;
 }
 
-int pf_reduce_topk(const float *dn, const float *residual, int T, int H, float *y, cudaStream_t s) {
+int pf_reduce_topk(const float *dn, const float *residual, int T, int H, float *y, cudaStream_t s,
+                   const uint32_t *ids, int own_world, int own_rank) {
     if (T <= 0) return MMRS_OK;
+    if (own_world > 1 && !ids) return MMRS_ERR_ARG;
     const size_t n4 = (size_t)T * H / 4;
-    reduce_topk_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, s>>>(dn, residual, T, H, y);
+    reduce_topk_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, s>>>(dn, residual, T, H, y, ids, own_world, own_rank);
     return cudaGetLastError() == cudaSuccess ? MMRS_OK : MMRS_ERR_LAUNCH;
 }
 

@@ -69,14 +69,19 @@ int pf_route_topk(const float *logits, const float *bias, int T, int E, uint32_t
                   cudaStream_t s);
 int pf_sort_routes(const uint32_t *keys, int n, int end_bit, uint32_t *sorted_keys, uint32_t *sorted_routes,
                    cudaStream_t s);
+// Experts with e % own_world != own_rank are left out of the plan (expert parallel); own_world = 1
+// keeps every expert.
 int pf_build_plan(const int32_t *sorted_experts, const int32_t *sorted_routes, int M, int E, PfPlan plan,
-                  cudaStream_t s);
+                  cudaStream_t s, int own_world = 1, int own_rank = 0);
 // Quantise the gathered input rows: padded row p takes input row route / div (x) or, with x2,
 // the product x2 * silu(x) of route rows (silu = x / (1 + exp(-x))).
 int pf_quantize(const float *x, const float *x2, int div, int K, int mode, PfPlan plan, PfActs acts, int rows_max,
                 cudaStream_t s);
 int pf_gemm(const void *weights, PfGemmParams p, int rows_max, cudaStream_t s);
-int pf_reduce_topk(const float *dn, const float *residual, int T, int H, float *y, cudaStream_t s);
+// y[t] = sum over the token's 8 routes (ascending) of dn[route] (+ residual); with own_world > 1 only
+// the routes whose expert (ids) satisfies e % own_world == own_rank are summed.
+int pf_reduce_topk(const float *dn, const float *residual, int T, int H, float *y, cudaStream_t s,
+                   const uint32_t *ids = nullptr, int own_world = 1, int own_rank = 0);
 size_t pf_gemm_smem_bytes();
 
 }  // namespace mmrs

@@ -17,5 +17,7 @@ struct WsLayout {
 WsLayout ws_layout(int E, int I, int max_tokens);
 void ws_bind(DecodeParams &p, uint8_t *ws, const WsLayout &l);
 int validate_weights(const MmrsMoeWeights *w);
+// Status of the last reference-ABI launcher on this host thread (read by mmrs_last_error()).
+void record_error(int status);
 
 }  // namespace mmrs
