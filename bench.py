@@ -109,21 +109,30 @@ class ClockSampler:
                 "power_w_max": max(r[2] for r in rows), "samples": len(rows), "reasons": reasons}
 
 
-def build_layers(pkg, synth, dev, n_layers: int, inter: int = I, experts: int = E):
+def build_layers(pkg, synth, dev, n_layers: int, inter: int = I, experts: int = E, tp_world: int = 1,
+                 tp_rank: int = 0, seed: int = SEED, zipf: bool = False):
+    """Synthetic layers; with tp_world > 1 only this rank's TP shard is generated (gate/up rows
+    [r * I / w, (r + 1) * I / w), the matching down K blocks), bit-identical to slicing the full
+    tensors."""
     import torch
     layers = []
+    per = inter // tp_world
+    r0 = tp_rank * per
     for l in range(n_layers):
         st = synth.layer_streams(l)
         router = torch.empty(experts, H, dtype=torch.float32, device=dev)
-        pkg.synth_normal(router, SEED, st["router"], 0.02)
-        bias = torch.empty(experts, dtype=torch.float32, device=dev)
-        pkg.synth_normal(bias, SEED, st["bias"], 0.01)
-        gate = torch.empty(experts * inter * pkg.row_bytes(Q4K, H), dtype=torch.uint8, device=dev)
+        pkg.synth_normal(router, seed, st["router"], 0.02)
+        if zipf:
+            bias = torch.from_numpy(synth.zipf_bias(experts, seed + l)).to(dev)
+        else:
+            bias = torch.empty(experts, dtype=torch.float32, device=dev)
+            pkg.synth_normal(bias, seed, st["bias"], 0.01)
+        gate = torch.empty(experts * per * pkg.row_bytes(Q4K, H), dtype=torch.uint8, device=dev)
         up = torch.empty_like(gate)
-        down = torch.empty(experts * H * pkg.row_bytes(Q5K, inter), dtype=torch.uint8, device=dev)
-        pkg.synth_kquant(gate, Q4K, SEED, st["gate"], experts, inter, H)
-        pkg.synth_kquant(up, Q4K, SEED, st["up"], experts, inter, H)
-        pkg.synth_kquant(down, Q5K, SEED, st["down"], experts, H, inter)
+        down = torch.empty(experts * H * pkg.row_bytes(Q5K, per), dtype=torch.uint8, device=dev)
+        pkg.synth_kquant(gate, Q4K, seed, st["gate"], experts, inter, H, row0=r0, nrows=per)
+        pkg.synth_kquant(up, Q4K, seed, st["up"], experts, inter, H, row0=r0, nrows=per)
+        pkg.synth_kquant(down, Q5K, seed, st["down"], experts, H, inter, kblk0=r0 // 256, nkblk=per // 256)
         layers.append(pkg.MoeLayer(router, bias, gate, up, down, Q4K, Q5K))
     return layers
 
@@ -155,35 +164,27 @@ def expert_bytes(I=I, H=H) -> int:
     return 2 * I * (H // 256) * 144 + H * (I // 256) * 176
 
 
-def build_prefill_layers(pkg, synth, dev, n_layers: int):
+def build_prefill_layers(pkg, synth, dev, n_layers: int, tp_world: int = 1, tp_rank: int = 0):
     """Config 2 layers: as config 1 but the correction bias is drawn so that top-8 hits follow a
     Zipf(1.1) popularity over the 256 experts."""
-    import torch
-    layers = []
-    for l in range(n_layers):
-        st = synth.layer_streams(l)
-        router = torch.empty(E, H, dtype=torch.float32, device=dev)
-        pkg.synth_normal(router, PF_SEED, st["router"], 0.02)
-        bias = torch.from_numpy(synth.zipf_bias(E, PF_SEED + l)).to(dev)
-        gate = torch.empty(E * I * pkg.row_bytes(Q4K, H), dtype=torch.uint8, device=dev)
-        up = torch.empty_like(gate)
-        down = torch.empty(E * H * pkg.row_bytes(Q5K, I), dtype=torch.uint8, device=dev)
-        pkg.synth_kquant(gate, Q4K, PF_SEED, st["gate"], E, I, H)
-        pkg.synth_kquant(up, Q4K, PF_SEED, st["up"], E, I, H)
-        pkg.synth_kquant(down, Q5K, PF_SEED, st["down"], E, H, I)
-        layers.append(pkg.MoeLayer(router, bias, gate, up, down, Q4K, Q5K))
-    return layers
+    return build_layers(pkg, synth, dev, n_layers, tp_world=tp_world, tp_rank=tp_rank, seed=PF_SEED, zipf=True)
 
 
-def run_prefill(pkg, synth, dev, args, rank: int, world: int):
+def run_prefill(pkg, synth, dev, args, rank: int, world: int, group=None):
     """Config 2: one T = 512 MoE block per step (Zipf-skewed routing), alternating between two
-    layers (2 x 2.19 GB of expert weights, larger than L2)."""
+    layers (2 x 2.19 GB of expert weights, larger than L2).  With a group: TP = 2 shards or
+    expert parallel, and the hidden all-reduce [512, 3072] over the peer exchange."""
     import numpy as np
     import torch
     import torch.distributed as dist
-    layers = build_prefill_layers(pkg, synth, dev, 2)
+    tp = group is not None and not group.expert_parallel
+    layers = build_prefill_layers(pkg, synth, dev, 2, tp_world=world if tp else 1, tp_rank=rank if tp else 0)
+
+    def fwd(L, x, **kw):
+        return L.forward(x, **kw) if group is None else group.forward(L, x, **kw)
+
     xs = torch.empty(2, PF_T, H, dtype=torch.float32, device=dev)
-    pkg.synth_normal(xs, PF_SEED + rank, 200, 1.0)
+    pkg.synth_normal(xs, PF_SEED, 200, 1.0)
     ys = torch.empty(PF_T, H, dtype=torch.float32, device=dev)
     ids = torch.empty(2, PF_T, TOPK, dtype=torch.int32, device=dev)
     wts = torch.empty(2, PF_T, TOPK, dtype=torch.float32, device=dev)
@@ -194,7 +195,7 @@ def run_prefill(pkg, synth, dev, args, rank: int, world: int):
     with torch.cuda.stream(stream):
         for i in range(max(3, args.warmup if args.warmup < 10 else 3)):
             L = i % 2
-            layers[L].forward(xs[L], y=ys, topk_ids=ids[L], topk_w=wts[L], stream=stream)
+            fwd(layers[L], xs[L], y=ys, topk_ids=ids[L], topk_w=wts[L], stream=stream)
         stream.synchronize()
     for L in layers:
         assert L.status() == 0, "device-side timeout in prefill warm-up"
@@ -208,7 +209,7 @@ def run_prefill(pkg, synth, dev, args, rank: int, world: int):
             e0.record(stream)
             for i in range(steps):
                 L = i % 2
-                layers[L].forward(xs[L], y=ys, topk_ids=ids[L], topk_w=wts[L], stream=stream)
+                fwd(layers[L], xs[L], y=ys, topk_ids=ids[L], topk_w=wts[L], stream=stream)
             e1.record(stream)
         e1.synchronize()
     torch.cuda.synchronize()
@@ -227,7 +228,7 @@ def run_prefill(pkg, synth, dev, args, rank: int, world: int):
     with torch.cuda.stream(stream):
         for i in range(2):
             x_dev.copy_(x_host, non_blocking=True)
-            layers[i % 2].forward(x_dev, y=ys, stream=stream)
+            fwd(layers[i % 2], x_dev, y=ys, stream=stream)
             y_host.copy_(ys, non_blocking=True)
         stream.synchronize()
         if world > 1:
@@ -236,7 +237,7 @@ def run_prefill(pkg, synth, dev, args, rank: int, world: int):
         f0.record(stream)
         for i in range(e2e_steps):
             x_dev.copy_(x_host, non_blocking=True)
-            layers[i % 2].forward(x_dev, y=ys, stream=stream)
+            fwd(layers[i % 2], x_dev, y=ys, stream=stream)
             y_host.copy_(ys, non_blocking=True)
         f1.record(stream)
         f1.synchronize()
@@ -253,7 +254,7 @@ def run_prefill(pkg, synth, dev, args, rank: int, world: int):
     per_step_s = ms / 1e3 / steps
     peaks = measured_peaks()
     achieved = alg_bytes / per_step_s / 1e9
-    out = {"metric": "moe_block_prefill_tokens_per_s", "value": world * PF_T * steps / (ms / 1e3),
+    out = {"metric": "moe_block_prefill_tokens_per_s", "value": PF_T * steps / (ms / 1e3),
            "unit": "tokens/s", "steps": steps, "ms_per_step": ms / steps,
            "config": {"workload": "prefill T=512 MoE block (BASELINE configs[2]), Zipf(1.1) expert popularity",
                       "tokens_per_step": PF_T, "layers_rotated": 2, "distinct_experts": distinct,
@@ -266,7 +267,7 @@ def run_prefill(pkg, synth, dev, args, rank: int, world: int):
                         "algorithmic_bytes_per_step": alg_bytes,
                         "scope": "whole block step (10 launches; the expert GEMMs dominate, see profiles/)",
                         "int8_tops": ops / per_step_s / 1e12, "int8_frac_of_nominal_4500": ops / per_step_s / 4.5e15},
-           "e2e": {"value": world * PF_T * e2e_steps / (e2e_ms / 1e3), "unit": "tokens/s",
+           "e2e": {"value": PF_T * e2e_steps / (e2e_ms / 1e3), "unit": "tokens/s",
                    "h2d_bytes_per_step": PF_T * H * 4, "d2h_bytes_per_step": PF_T * H * 4},
            "gpu_launches": 10 * steps, "clocks": clk.summary()}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -375,12 +376,25 @@ def main():
         dist.init_process_group("nccl", device_id=dev)
 
     pkg, synth = ge.load_package(), ge.load_synth()
-    layers = build_layers(pkg, synth, dev, args.layers)
+    group = None
+    if world > 1:
+        # TP = 2 (the reference layout) at two GPUs, expert parallel (e % W) at four and eight
+        import importlib
+        gm = importlib.import_module("minimax_rs_b200.group")
+
+        def allgather(obj):
+            out = [None] * world
+            dist.all_gather_object(out, obj)
+            return out
+
+        group = gm.PeerGroup(world, rank, ar_capacity=PF_T * H, expert_parallel=world > 2, allgather=allgather)
+    tp = world == 2
+    layers = build_layers(pkg, synth, dev, args.layers, tp_world=2 if tp else 1, tp_rank=rank if tp else 0)
     n_tok = 512
     xs = torch.empty(n_tok, H, dtype=torch.float32, device=dev)
-    pkg.synth_normal(xs, SEED + rank, 100, 1.0, bf16=True)
+    pkg.synth_normal(xs, SEED, 100, 1.0, bf16=True)  # the same tokens on every rank (TP / EP)
     res = torch.empty(n_tok, H, dtype=torch.float32, device=dev)
-    pkg.synth_normal(res, SEED + rank, 101, 1.0)
+    pkg.synth_normal(res, SEED, 101, 1.0)
     ys = torch.empty(n_tok, H, dtype=torch.float32, device=dev)
     for L in layers:
         L.workspace(1)
@@ -390,7 +404,10 @@ def main():
     def step(i, s):
         L = layers[i % len(layers)]
         t = i % n_tok
-        L.forward(xs[t:t + 1], residual=res[t:t + 1], y=ys[t:t + 1], stream=s)
+        if group is None:
+            L.forward(xs[t:t + 1], residual=res[t:t + 1], y=ys[t:t + 1], stream=s)
+        else:
+            group.forward(L, xs[t:t + 1], residual=res[t:t + 1], y=ys[t:t + 1], stream=s)
 
     # CUDA graph of G consecutive steps (G multiple of the layer count)
     G = max(len(layers), 64 // len(layers) * len(layers))
@@ -443,6 +460,12 @@ def main():
     clocks = clk.summary()
 
     # e2e: public API, host buffers, copies inside every step
+    def fwd(L, xd, rd, yd):
+        if group is None:
+            L.forward(xd, residual=rd, y=yd, stream=stream)
+        else:
+            group.forward(L, xd, residual=rd, y=yd, stream=stream)
+
     x_host = torch.empty(n_tok, H, dtype=torch.float32, pin_memory=True)
     x_host.copy_(xs.cpu())
     y_host = torch.empty(n_tok, H, dtype=torch.float32, pin_memory=True)
@@ -453,7 +476,7 @@ def main():
         for i in range(8):
             t = i % n_tok
             x_dev.copy_(x_host[t:t + 1], non_blocking=True)
-            layers[i % len(layers)].forward(x_dev, residual=res[t:t + 1], y=y_dev, stream=stream)
+            fwd(layers[i % len(layers)], x_dev, res[t:t + 1], y_dev)
             y_host[t:t + 1].copy_(y_dev, non_blocking=True)
         stream.synchronize()
         if world > 1:
@@ -463,7 +486,7 @@ def main():
         for i in range(e2e_steps):
             t = i % n_tok
             x_dev.copy_(x_host[t:t + 1], non_blocking=True)
-            layers[i % len(layers)].forward(x_dev, residual=res[t:t + 1], y=y_dev, stream=stream)
+            fwd(layers[i % len(layers)], x_dev, res[t:t + 1], y_dev)
             y_host[t:t + 1].copy_(y_dev, non_blocking=True)
         e1.record(stream)
         e1.synchronize()
@@ -472,10 +495,14 @@ def main():
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_ms = float(e2e_ms.item())
 
-    value = world * steps / (ms_max / 1e3)
-    e2e_value = world * e2e_steps / (e2e_ms / 1e3)
+    # one token per step for the whole group (TP / EP split each token over the GPUs)
+    value = steps / (ms_max / 1e3)
+    e2e_value = e2e_steps / (e2e_ms / 1e3)
     per_launch_s = (ms / 1e3) / steps
     alg = algorithmic_bytes()
+    if world > 1:  # bytes one rank moves: the replicated router and io, 1/W of the experts' bytes
+        io, router = H * 4 * 3, E * H * 4
+        alg = router + io + (alg - router - io) // world
     peaks = measured_peaks()
     achieved = alg / per_launch_s / 1e9
     traffic = None
@@ -498,18 +525,21 @@ def main():
     layer_bytes = layers[0].gate.numel() * 2 + layers[0].down.numel() + E * H * 4
     del layers, graphs
     torch.cuda.empty_cache()
-    prefill = None if args.no_prefill else run_prefill(pkg, synth, dev, args, rank, world)
+    prefill = None if args.no_prefill else run_prefill(pkg, synth, dev, args, rank, world, group)
 
     if rank == 0:
         out = {
             "metric": "moe_block_decode_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": steps, "warmup": args.warmup, "ms_per_step": ms_max / steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8xq4k/q5k->f32", "data": "synthetic",
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "int8xq4k/q5k->f32",
+            "data": "synthetic",
             "config": {"workload": "decode T=1 MoE block (BASELINE configs[1])", "experts": E, "hidden": H,
                        "inter": I, "topk": TOPK, "gate_up": "Q4_K", "down": "Q5_K", "activations": "Q8_1",
                        "residual": True, "layers_rotated": n_layers,
                        "l2": f"inputs larger than L2: {n_layers} layers x {layer_bytes:.3e} B rotated",
-                       "parallelism": "replicas" if world > 1 else "single GPU",
+                       "parallelism": (f"tp{world} (gate/up rows, down K split; fused NVLink exchange)" if world == 2
+                                       else f"ep{world} (experts e % {world}; fused NVLink exchange)" if world > 2
+                                       else "single GPU"),
                        "graph_steps": graph_steps},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
@@ -524,6 +554,9 @@ def main():
         }
         print(json.dumps(out), flush=True)
     if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()  # no peer still reads this rank's exchange region
+        group.close()
         dist.destroy_process_group()
 
 
