@@ -224,6 +224,8 @@ struct DecodeSmem {
     float *part;               // router slice sums [2][8] in P0, selection scores [E] in P1
     float *sig;                // [E]
     int *ids;                  // [8]
+    int *vslot;                // [8] slots in gate/up position order (valid first under EP)
+    int *vpos;                 // [8] position block of each slot in act / aq
     float *w;                  // [8]
     float *dn_acc;             // [res_slots][8]
     float *act_s;              // [act_slots]
@@ -269,6 +271,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         s.part = reinterpret_cast<float *>(take(sizeof(float) * (E > 16 ? E : 16)));
         s.sig = reinterpret_cast<float *>(take(sizeof(float) * E));
         s.ids = reinterpret_cast<int *>(take(sizeof(int) * kTopK));
+        s.vslot = reinterpret_cast<int *>(take(sizeof(int) * kTopK));
+        s.vpos = reinterpret_cast<int *>(take(sizeof(int) * kTopK));
         s.w = reinterpret_cast<float *>(take(sizeof(float) * kTopK));
         s.dn_acc = reinterpret_cast<float *>(take(sizeof(float) * p.res_slots * kTopK));
         s.act_s = reinterpret_cast<float *>(take(sizeof(float) * p.act_slots));
@@ -281,6 +285,13 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         s.res_s = reinterpret_cast<float *>(take(sizeof(float) * p.res_slots));
         s.base = reinterpret_cast<uint32_t *>(take(16));
         s.flag = reinterpret_cast<int *>(take(16));
+        // the carve-up must fit the dynamic allocation computed by decode_smem_bytes()
+        uint32_t dyn = 0;
+        asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
+        if ((size_t)(ptr - smem_raw) > dyn) {
+            if (tid == 0) atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_LAUNCH);
+            return;
+        }
     }
     if (tid == 0) {
         for (int i = 0; i < p.stages; ++i) {
@@ -295,7 +306,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     }
     __syncthreads();
 
-    const int gu_p0 = (int)((int64_t)cta * kTopK * I / G), gu_p1 = (int)((int64_t)(cta + 1) * kTopK * I / G);
     const int dn_r0 = (int)((int64_t)cta * H / G), dn_r1 = (int)((int64_t)(cta + 1) * H / G);
     const size_t gu_row_bytes = kq_row_bytes(p.gu_type, H);
     const size_t dn_row_bytes = kq_row_bytes(p.dn_type, I);
@@ -431,12 +441,26 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         }
         __syncthreads();
     }
-    if (p.world > 1 && p.ep) {
-        // expert parallel: experts owned by other ranks contribute nothing here
-        __syncthreads();
-        if (tid < kTopK && s.ids[tid] >= 0 && s.ids[tid] % p.world != p.rank) s.ids[tid] = -1;
-        __syncthreads();
+    // Gate/up position space: the (slot, row) pairs of the computed experts, partitioned evenly
+    // over the CTAs.  Single GPU and TP: all 8 slots in order.  Expert parallel: experts owned by
+    // other ranks contribute nothing here and their slots are left out, so this rank's CTAs share
+    // only its own experts' rows.
+    const bool compact = p.world > 1 && p.ep;
+    __syncthreads();
+    if (compact && tid < kTopK && s.ids[tid] >= 0 && s.ids[tid] % p.world != p.rank) s.ids[tid] = -1;
+    __syncthreads();
+    if (tid == 0) {
+        int nv = 0;
+        for (int k = 0; k < kTopK; ++k)
+            if (!compact || s.ids[k] >= 0) s.vslot[nv++] = k;
+        s.n_gu[2] = nv;
+        for (int k = 0, m = nv; k < kTopK; ++k)
+            if (compact && s.ids[k] < 0) s.vslot[m++] = k;
+        for (int k = 0; k < kTopK; ++k) s.vpos[s.vslot[k]] = k;
     }
+    __syncthreads();
+    const int nvs = s.n_gu[2];
+    const int gu_p0 = (int)((int64_t)cta * nvs * I / G), gu_p1 = (int)((int64_t)(cta + 1) * nvs * I / G);
     if (!ok) return;  // nothing issued yet
     if (tid == 0 && p.trace) p.trace[cta * 16 + 3] = globaltimer_ns();
 
@@ -452,9 +476,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         int n = 0;
         for (int q = gu_p0; q < gu_p1 && n + 2 <= kMaxUnits;) {
             const GuUnit u = gu_unit_at(q, gu_p1, I, U_gu);
-            s.units[n] = make_int4(0, u.slot, u.row0, u.n);
+            const int slot = s.vslot[u.slot];
+            s.units[n] = make_int4(0, slot, u.row0, u.n);
             s.unit_off[n++] = q - gu_p0;
-            s.units[n] = make_int4(1, u.slot, u.row0, u.n);
+            s.units[n] = make_int4(1, slot, u.row0, u.n);
             s.unit_off[n++] = q - gu_p0;
             q += u.n;
         }
@@ -580,7 +605,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         // act = up * silu(gate) (moe_gguf.cu:272-273) for the CTA's whole range
         for (int i = tid; i < gu_p1 - gu_p0; i += kConsumerThreads) {
             const float g = s.gval[i];
-            const int slot = (gu_p0 + i) / I;
+            const int slot = s.vslot[(gu_p0 + i) / I];
             s.act_s[i] = (!aborted && s.ids[slot] >= 0) ? s.uval[i] * __fdiv_rn(g, 1.0f + expf(-g)) : 0.f;
         }
         // Q8_1 of act (quantize_silu_mul_q8_1, moe_gguf.cu:255-284) per 32-row block.  Blocks inside
@@ -661,7 +686,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         const int slot = q % kTopK, rA = (q / kTopK) * kRowsPerLane, rB = rA + 1;
         const int ntasks = (I / QK_K) * 4;
         TaskAct ta[kTPL];
-        load_task_acts(ActView{s.aq_s + (size_t)slot * I, s.ats + slot * (I / 64)}, lig, L, ntasks, ta);
+        const int vp = s.vpos[slot];  // position block of this slot's activation
+        load_task_acts(ActView{s.aq_s + (size_t)vp * I, s.ats + vp * (I / 64)}, lig, L, ntasks, ta);
         const float wslot = s.w[slot];
         const bool valid = s.ids[slot] >= 0;
         const int j0 = ((grp - n_gu) % kGroups + kGroups) % kGroups;
@@ -761,7 +787,7 @@ size_t decode_smem_bytes(const DecodeParams &p) {
     size_t b = a16((size_t)p.stages * p.stage_bytes) + 2 * a16(sizeof(uint64_t) * p.stages) + a16(8);
     b += a16(p.H) + 2 * a16(4 * (p.H / 32)) + a16(16 * (p.H / 64));
     b += a16((size_t)kTopK * p.I) + 2 * a16(4 * kTopK * (p.I / 32)) + a16(16 * kTopK * (p.I / 64));
-    b += a16(4 * (p.E > 16 ? p.E : 16)) + a16(4 * p.E) + 2 * a16(4 * kTopK);
+    b += a16(4 * (p.E > 16 ? p.E : 16)) + a16(4 * p.E) + 4 * a16(4 * kTopK);  // part, sig, ids, vslot, vpos, w
     b += a16(4 * p.res_slots * kTopK) + 3 * a16(4 * p.act_slots) + a16(4 * p.res_slots) + 32;
     b += a16(16 * kMaxUnits) + a16(4 * kMaxUnits) + 16 + a16(4 * p.stages);
     return b;
