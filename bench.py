@@ -292,6 +292,45 @@ def run_prefill(pkg, synth, dev, args, rank: int, world: int, group=None):
     return out
 
 
+def ar_sweep(group, world: int, dev, iters: int = 50) -> dict:
+    """Hidden-state all-reduce over T x 3072 f32 (T = 1, 8, 64, 512, 2048): the peer exchange of
+    this library (rank-ordered sum, residual fused) and NCCL's all_reduce for comparison.
+    busBW = algBW * 2 (W - 1) / W (NCCL convention); device time, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    out = {"unit": "GB/s (bus)", "ranks": world, "points": []}
+    for T in (1, 8, 64, 512, 2048):
+        count = T * H
+        y = torch.empty(count, dtype=torch.float32, device=dev)
+        res = torch.zeros(count, dtype=torch.float32, device=dev)
+        nccl_buf = torch.ones(count, dtype=torch.float32, device=dev)
+        row = {"T": T, "bytes": count * 4}
+        for name in ("peer", "nccl"):
+            for i in range(5):  # warm-up
+                if name == "peer":
+                    group.all_reduce(lambda ptr: None, count, residual=res, y=y)
+                else:
+                    dist.all_reduce(nccl_buf)
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(iters):
+                if name == "peer":
+                    group.all_reduce(lambda ptr: None, count, residual=res, y=y)
+                else:
+                    dist.all_reduce(nccl_buf)
+            e1.record()
+            e1.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) / iters], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            us = float(t.item()) * 1e3
+            alg = count * 4 / (us * 1e-6) / 1e9
+            row[name] = {"us": us, "bus_gbs": alg * 2 * (world - 1) / world}
+        out["points"].append(row)
+    return out
+
+
 def run_reference(args):
     """Reference arm: the CPU restatement of the reference's MoE decode block (the reference's
     own CPU path, Candle's quantized matmul, cannot be built here: no Rust toolchain), on all
@@ -355,6 +394,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill-steps", type=int, default=40)
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-ar-sweep", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -387,7 +427,7 @@ def main():
             dist.all_gather_object(out, obj)
             return out
 
-        group = gm.PeerGroup(world, rank, ar_capacity=PF_T * H, expert_parallel=world > 2, allgather=allgather)
+        group = gm.PeerGroup(world, rank, ar_capacity=2048 * H, expert_parallel=world > 2, allgather=allgather)
     tp = world == 2
     layers = build_layers(pkg, synth, dev, args.layers, tp_world=2 if tp else 1, tp_rank=rank if tp else 0)
     n_tok = 512
@@ -526,6 +566,7 @@ def main():
     del layers, graphs
     torch.cuda.empty_cache()
     prefill = None if args.no_prefill else run_prefill(pkg, synth, dev, args, rank, world, group)
+    allreduce = ar_sweep(group, world, dev) if world > 1 and not args.no_ar_sweep else None
 
     if rank == 0:
         out = {
@@ -551,6 +592,7 @@ def main():
             "clocks": clocks,
             "cpu_baseline": cpu,
             "prefill": prefill,
+            "allreduce_sweep": allreduce,
         }
         print(json.dumps(out), flush=True)
     if world > 1:

@@ -765,12 +765,16 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             const bool xfail = *reinterpret_cast<volatile int *>(&s.flag[1]) != 0;
             for (int r = tid; r < dn_r1 - dn_r0 && !xfail; r += kConsumerThreads) {
                 const int row = dn_r0 + r;
-                float y = 0.f;
-                for (int rk = 0; rk < p.world; ++rk) {
-                    const float v = rk == p.rank ? mine[row]
-                                                 : ld_volatile_f32(reinterpret_cast<const float *>(p.xpeer[rk] + part_off) + row);
-                    y = rk == 0 ? v : y + v;
-                }
+                float v[kMaxRanks];
+#pragma unroll
+                for (int rk = 0; rk < kMaxRanks; ++rk)  // all loads in flight before the sum
+                    if (rk < p.world)
+                        v[rk] = rk == p.rank ? mine[row]
+                                             : ld_relaxed_sys_f32(reinterpret_cast<const float *>(p.xpeer[rk] + part_off) + row);
+                float y = v[0];
+#pragma unroll
+                for (int rk = 1; rk < kMaxRanks; ++rk)
+                    if (rk < p.world) y = y + v[rk];
                 if (p.residual) y = y + s.res_s[r];
                 p.y[row] = y;
             }

@@ -32,8 +32,9 @@ struct PeerArParams {
 __global__ void __launch_bounds__(256) peer_allreduce_kernel(const PeerArParams p) {
     __shared__ int ok;
     const int b = blockIdx.x;
-    const size_t per = (p.count + gridDim.x - 1) / gridDim.x;
-    const size_t lo = (size_t)b * per, hi = lo + per < p.count ? lo + per : p.count;
+    const size_t per = ((p.count + gridDim.x - 1) / gridDim.x + 3) / 4 * 4;
+    const size_t lo = (size_t)b * per < p.count ? (size_t)b * per : p.count;
+    const size_t hi = lo + per < p.count ? lo + per : p.count;
     __syncthreads();
     if (threadIdx.x == 0) {
         const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
@@ -50,9 +51,36 @@ __global__ void __launch_bounds__(256) peer_allreduce_kernel(const PeerArParams 
     }
     __syncthreads();
     if (!ok) return;
-    for (size_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
-        float v = p.rank == 0 ? p.part[0][i] : ld_volatile_f32(p.part[0] + i);
-        for (int r = 1; r < p.world; ++r) v = v + (r == p.rank ? p.part[r][i] : ld_volatile_f32(p.part[r] + i));
+    // float4 body (chunk bounds are multiples of 4), every rank's vector loaded before the sum
+    for (size_t i = lo + 4 * threadIdx.x; i + 4 <= hi; i += 4 * blockDim.x) {
+        float4 v[kMaxRanks];
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r)
+            if (r < p.world)
+                v[r] = r == p.rank ? *reinterpret_cast<const float4 *>(p.part[r] + i)
+                                   : ld_relaxed_sys_f4(reinterpret_cast<const float4 *>(p.part[r] + i));
+        float4 a = v[0];
+#pragma unroll
+        for (int r = 1; r < kMaxRanks; ++r)
+            if (r < p.world) {
+                a.x = a.x + v[r].x;
+                a.y = a.y + v[r].y;
+                a.z = a.z + v[r].z;
+                a.w = a.w + v[r].w;
+            }
+        if (p.residual) {
+            const float4 rr = *reinterpret_cast<const float4 *>(p.residual + i);
+            a.x = a.x + rr.x;
+            a.y = a.y + rr.y;
+            a.z = a.z + rr.z;
+            a.w = a.w + rr.w;
+        }
+        *reinterpret_cast<float4 *>(p.y + i) = a;
+    }
+    // scalar tail of the last chunk
+    for (size_t i = hi - (hi - lo) % 4 + threadIdx.x; i < hi; i += blockDim.x) {
+        float v = p.rank == 0 ? p.part[0][i] : ld_relaxed_sys_f32(p.part[0] + i);
+        for (int r = 1; r < p.world; ++r) v = v + (r == p.rank ? p.part[r][i] : ld_relaxed_sys_f32(p.part[r] + i));
         if (p.residual) v = v + p.residual[i];
         p.y[i] = v;
     }
@@ -63,6 +91,8 @@ int peer_all_reduce(const PeerView &g, const float *residual, float *y, size_t c
     if (count == 0) return MMRS_OK;
     if (g.world < 1 || g.world > kMaxRanks || g.rank < 0 || g.rank >= g.world || !g.mine || count > g.ar_capacity)
         return MMRS_ERR_ARG;
+    // float4 access: 16-byte aligned buffers and an even split of the capacity
+    if ((g.ar_capacity & 3u) || ((uintptr_t)y & 15u) || (residual && ((uintptr_t)residual & 15u))) return MMRS_ERR_ARG;
     PeerArParams p = {};
     for (int r = 0; r < g.world; ++r) {
         if (!g.peers[r]) return MMRS_ERR_ARG;
@@ -120,7 +150,7 @@ __global__ void __launch_bounds__(256) tp2_peer_all_reduce_kernel(const float *l
     if (ok) {
         float sq = 0.0f;
         for (int i = tid; i < count; i += blockDim.x) {
-            const float reduced = local[i] + ld_volatile_f32(peer + i);
+            const float reduced = local[i] + ld_relaxed_sys_f32(peer + i);
             const float v = residual ? reduced + residual[i] : reduced;
             output[i] = v;
             sq = fmaf(v, v, sq);

@@ -46,10 +46,17 @@ __device__ __forceinline__ bool wait_flag_sys(const uint32_t *flag, uint32_t tok
     return true;
 }
 
-// Load that bypasses the L1 (peer partials are rewritten between operations).
-__device__ __forceinline__ float ld_volatile_f32(const float *p) {
+// System-scope relaxed loads of peer data (coherent, so never a stale L1 line; unlike volatile
+// loads, independent ones stay in flight together).  Issue them after the acquire of the flag
+// that published the data and a CTA barrier.
+__device__ __forceinline__ float ld_relaxed_sys_f32(const float *p) {
     float v;
-    asm volatile("ld.volatile.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.sys.global.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ float4 ld_relaxed_sys_f4(const float4 *p) {
+    float4 v;
+    asm volatile("ld.relaxed.sys.global.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
     return v;
 }
 

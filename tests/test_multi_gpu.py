@@ -122,7 +122,7 @@ def test_peer_all_reduce(pkg, synth):
     gm = _group_mod(pkg)
     world = min(_ngpu(), 4)
     count = 3 * 4096 + 17
-    groups = gm.PeerGroup.local(list(range(world)), ar_capacity=count, expert_parallel=False)
+    groups = gm.PeerGroup.local(list(range(world)), ar_capacity=(count + 3) // 4 * 4, expert_parallel=False)
     res = synth.normal_f32(count, 77, 9, 1.0)
     parts = [synth.normal_f32(count, 77, 10 + r, 1.0) for r in range(world)]
     expect = parts[0].copy()
