@@ -292,6 +292,81 @@ def run_prefill(pkg, synth, dev, args, rank: int, world: int, group=None):
     return out
 
 
+C0_T, C0_SEED = 32, 1  # configs[0]: T = 32, every expert Q4_K (seed = config 0 x 1000 + 1)
+
+
+def run_config0(pkg, synth, dev, args) -> dict:
+    """configs[0]: one T = 32 MoE block per step with all-Q4_K experts (gate/up/down), MMQ numerics;
+    two alternating layers (2 x 2.45 GB, larger than L2).  The CPU oracle runs the same blocks."""
+    import numpy as np
+    import torch
+    layers = []
+    for l in range(2):
+        st = synth.layer_streams(l)
+        router = torch.empty(E, H, dtype=torch.float32, device=dev)
+        pkg.synth_normal(router, C0_SEED, st["router"], 0.02)
+        bias = torch.empty(E, dtype=torch.float32, device=dev)
+        pkg.synth_normal(bias, C0_SEED, st["bias"], 0.01)
+        gate = torch.empty(E * I * pkg.row_bytes(Q4K, H), dtype=torch.uint8, device=dev)
+        up = torch.empty_like(gate)
+        down = torch.empty(E * H * pkg.row_bytes(Q4K, I), dtype=torch.uint8, device=dev)
+        pkg.synth_kquant(gate, Q4K, C0_SEED, st["gate"], E, I, H)
+        pkg.synth_kquant(up, Q4K, C0_SEED, st["up"], E, I, H)
+        pkg.synth_kquant(down, Q4K, C0_SEED, st["down"], E, H, I)
+        layers.append(pkg.MoeLayer(router, bias, gate, up, down, Q4K, Q4K))
+    xs = torch.empty(2, C0_T, H, dtype=torch.float32, device=dev)
+    pkg.synth_normal(xs, C0_SEED, 300, 1.0)
+    ys = torch.empty(C0_T, H, dtype=torch.float32, device=dev)
+    ids = torch.empty(2, C0_T, TOPK, dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    for L in layers:
+        L.workspace(C0_T)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(4):
+            layers[i % 2].forward(xs[i % 2], y=ys, topk_ids=ids[i % 2], stream=stream)
+        stream.synchronize()
+        steps = 40
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            layers[i % 2].forward(xs[i % 2], y=ys, stream=stream)
+        e1.record(stream)
+        e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    for L in layers:
+        assert L.status() == 0, "device-side timeout in configs[0]"
+    distinct = len(np.unique(ids[0].cpu().numpy()))
+    eb = 3 * I * (H // 256) * 144  # all-Q4_K expert
+    alg = distinct * eb + E * H * 4 + 2 * C0_T * H * 4
+    peaks = measured_peaks()
+    out = {"metric": "moe_block_tokens_per_s", "value": C0_T / (ms / 1e3), "unit": "tokens/s",
+           "ms_per_step": ms, "steps": steps,
+           "config": {"workload": "T=32 MoE block, all experts Q4_K (BASELINE configs[0]), MMQ numerics",
+                      "distinct_experts": distinct, "layers_rotated": 2},
+           "roofline": {"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                        "frac": alg / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], "algorithmic_bytes_per_step": alg}}
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import oracle as orc
+        L = layers[0]
+        args_np = (L.router.cpu().numpy(), L.bias.cpu().numpy(), L.gate.cpu().numpy(), L.up.cpu().numpy(),
+                   L.down.cpu().numpy(), Q4K, Q4K)
+        xh = xs[0].cpu().numpy()
+        n, t0 = 0, time.perf_counter()
+        while True:
+            orc.moe_block(*args_np, xh)
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= args.cpu_budget or n >= 50:
+                break
+        out["cpu_baseline"] = {"value": n * C0_T / el, "unit": "tokens/s", "cores": orc.num_threads(),
+                               "kind": "port", "sample": f"{n} blocks of 32 tokens of layer 0 in {el:.1f} s"}
+    del layers
+    torch.cuda.empty_cache()
+    return out
+
+
 def ar_sweep(group, world: int, dev, iters: int = 50) -> dict:
     """Hidden-state all-reduce over T x 3072 f32 (T = 1, 8, 64, 512, 2048): the peer exchange of
     this library (rank-ordered sum, residual fused) and NCCL's all_reduce for comparison.
@@ -567,6 +642,7 @@ def main():
     torch.cuda.empty_cache()
     prefill = None if args.no_prefill else run_prefill(pkg, synth, dev, args, rank, world, group)
     allreduce = ar_sweep(group, world, dev) if world > 1 and not args.no_ar_sweep else None
+    config0 = run_config0(pkg, synth, dev, args) if world == 1 and not args.no_prefill else None
 
     if rank == 0:
         out = {
@@ -593,6 +669,7 @@ def main():
             "cpu_baseline": cpu,
             "prefill": prefill,
             "allreduce_sweep": allreduce,
+            "config0": config0,
         }
         print(json.dumps(out), flush=True)
     if world > 1:
