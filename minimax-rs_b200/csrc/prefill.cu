@@ -503,7 +503,7 @@ int pf_reduce_topk(const float *dn, const float *residual, int T, int H, float *
 //      warp 1      one thread issues the chunk's 8 MMAs (M=128, N=routes rounded to 16, K=32),
 //                  one per 32-block, each into its own accumulator of the chunk's TMEM group
 //                  (8 x N columns), then one commit for the group
-//      warps 6-13  epilogue: 4 TMEM lane quarters x 2 halves of the route columns; per 32-block
+//      warps 6-21  epilogue: 4 TMEM lane quarters x 4 units of 8 route columns; per 32-block
 //                  sum = fma(dmx * d8, C, sum); sum = fma(dmy, s8, sum) in K order (the MMQ combine
 //                  of mmq_gguf.cuh vec_dot_q8_1_q8_1_mma, or with the generic numerics' scales the
 //                  vec_dot_q*_K_q8_1 combine), then the route rows are written (times the route
@@ -520,7 +520,7 @@ constexpr int kPfEpiWarp0 = 2 + kPfUnpackWarps;
 constexpr int kPfGroupCols = 8 * kPfNT;         // 256: the 8 block accumulators of one chunk
 constexpr int kPfTmemCols = kPfGroups * kPfGroupCols;
 static_assert(kPfTmemCols == 512, "two chunk groups fill the tensor memory");
-static_assert(kPfNT == 32 && kPfEpiWarps == 8, "epilogue geometry: 4 lane quarters x 2 x 16 route columns");
+static_assert(kPfNT == 32 && kPfEpiWarps == 16, "epilogue geometry: 4 lane quarters x 4 x 8 route columns");
 
 // Raw stage (TMA / bulk copies): weights, activations and their scales of one chunk.
 // Operand stage: what the unpack warps derive from a raw stage for the MMAs and the epilogue.
@@ -868,23 +868,21 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
             if (!ok) break;
         }
     } else {
-        // ---------------- epilogue (8 warps) ----------------
-        // warp = (TMEM lane quarter qd, route half h): route columns [16 h, 16 h + 16) of the rows
-        // 32 qd .. 32 qd + 31, read in units of 8 columns (only units holding a route); per chunk
-        // one group wait, then four passes of two 32-blocks.
-        const int qd = warp & 3, h = (warp - kPfEpiWarp0) >> 2;
+        // ---------------- epilogue (16 warps) ----------------
+        // warp = (TMEM lane quarter qd, route unit u): route columns [8 u, 8 u + 8) of the rows
+        // 32 qd .. 32 qd + 31 (units without a route only keep the barriers); per chunk one group
+        // wait, then four passes of two 32-blocks.
+        const int qd = warp & 3, u = (warp - kPfEpiWarp0) >> 2;
         const int r = qd * 32 + lane;
         const uint32_t tq = tmem + ((uint32_t)(qd * 32) << 16);
         uint32_t c = 0;
         for (int item = blockIdx.x; item < total && !pf_aborted(sm); item += gridDim.x) {
             const PfItem it = pf_item(p, sm.tiles, item);
             const int n16 = pad_to(it.nvalid, 16);
-            const bool has0 = 16 * h < it.nvalid, has1 = 16 * h + 8 < it.nvalid;
-            float2 acc[2][4];
+            const bool has = 8 * u < it.nvalid;
+            float2 acc[4];
 #pragma unroll
-            for (int u = 0; u < 2; ++u)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) acc[u][i] = make_float2(0.0f, 0.0f);
+            for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.0f, 0.0f);
             bool ok = true;
             for (int kc = 0; kc < nkc; ++kc, ++c) {
                 const int o = c % kPfOpStages, g = c % kPfGroups;
@@ -894,29 +892,27 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                     break;
                 }
                 tc_fence_after();
-                const uint32_t gbase = tq + g * kPfGroupCols + 16 * h;
+                const uint32_t gbase = tq + g * kPfGroupCols + 8 * u;
 #pragma unroll
                 for (int pass = 0; pass < 4; ++pass) {
-                    uint32_t v[2][2][8];  // [32-block][unit][column]
-#pragma unroll
-                    for (int b = 0; b < 2; ++b) {
-                        if (has0) tc_ld8(gbase + (2 * pass + b) * n16, v[b][0]);
-                        if (has1) tc_ld8(gbase + (2 * pass + b) * n16 + 8, v[b][1]);
+                    uint32_t v[2][8];  // [32-block][column]
+                    if (has) {
+                        tc_ld8(gbase + (2 * pass) * n16, v[0]);
+                        tc_ld8(gbase + (2 * pass + 1) * n16, v[1]);
+                        tc_wait_ld();
                     }
-                    if (has0) tc_wait_ld();
                     if (pass == 3) {
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&sm.gfree[g]);  // the group's values are in registers
                     }
+                    if (has) {
 #pragma unroll
-                    for (int b = 0; b < 2; ++b) {
-                        const int j = 2 * pass + b;
-                        const float2 scr = sm.sc[o][j * kPfMT + r];
-                        if (has0) pf_accumulate8(acc[0], v[b][0], scr, &sm.dst[o][0][j][16 * h], &sm.dst[o][1][j][16 * h]);
-                        if (has1)
-                            pf_accumulate8(acc[1], v[b][1], scr, &sm.dst[o][0][j][16 * h + 8],
-                                           &sm.dst[o][1][j][16 * h + 8]);
+                        for (int b = 0; b < 2; ++b) {
+                            const int j = 2 * pass + b;
+                            pf_accumulate8(acc, v[b], sm.sc[o][j * kPfMT + r], &sm.dst[o][0][j][8 * u],
+                                           &sm.dst[o][1][j][8 * u]);
+                        }
                     }
                 }
                 __syncwarp();
@@ -924,14 +920,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
             }
             if (!ok) break;
             const int row = it.m0 + r;
-            if (has0 && row < p.N) {
+            if (has && row < p.N) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int col = 16 * h + i;
+                for (int i = 0; i < 8; ++i) {
+                    const int col = 8 * u + i;
                     if (col < it.nvalid) {
                         const int route = p.plan.row_route[it.p0 + col];
-                        const float2 a2 = acc[i >> 3][(i & 7) >> 1];
-                        const float v = (i & 1) ? a2.y : a2.x;
+                        const float v = (i & 1) ? acc[i >> 1].y : acc[i >> 1].x;
                         p.out[(size_t)route * p.N + row] = p.route_scale ? __fmul_rn(v, p.route_scale[route]) : v;
                     }
                 }

@@ -14,7 +14,7 @@ constexpr int kPfSegAlign = 16;     // each expert's route segment is padded to 
 constexpr int kPfRawStages = 3;     // raw GGUF weight tiles in flight (TMA)
 constexpr int kPfOpStages = 3;      // unpacked operand stages (A int8, scales)
 constexpr int kPfGroups = 2;        // TMEM groups: the 8 block accumulators of one chunk each
-constexpr int kPfEpiWarps = 8;      // epilogue warps: 4 TMEM lane quarters x 2 halves of the routes
+constexpr int kPfEpiWarps = 16;     // epilogue warps: 4 TMEM lane quarters x 4 units of 8 routes
 constexpr int kPfUnpackWarps = 4;   // one thread per weight row
 constexpr int kPfThreads = 32 * (2 + kPfUnpackWarps + kPfEpiWarps);  // TMA, MMA, unpack, epilogue
 constexpr int kPfMaxExperts = 1024;
