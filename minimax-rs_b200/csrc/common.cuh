@@ -27,31 +27,6 @@ __host__ __device__ inline int kq_block_bytes(int t) { return t == MMRS_Q5K ? Q5
 __host__ __device__ inline size_t kq_row_bytes(int t, int k) { return (size_t)(k / QK_K) * kq_block_bytes(t); }
 __host__ __device__ inline int pad_to(int v, int p) { return (v + p - 1) / p * p; }
 
-// ------------------------------------------------------------------------------------------
-// Scale / min unpacking: get_scale_min_k4 (quantized.cu:926-933) for sub-blocks 2j and 2j+1
-// from the 12 packed bytes, read as three little-endian 32-bit words w0,w1,w2.
-// ------------------------------------------------------------------------------------------
-__device__ __forceinline__ void kq_scale_min_pair(uint32_t w0, uint32_t w1, uint32_t w2, int j,
-                                                  int &sc0, int &m0, int &sc1, int &m1) {
-    // byte(q, i): byte i of the 12-byte array
-    auto byte_of = [&](int i) -> uint32_t {
-        const uint32_t w = i < 4 ? w0 : (i < 8 ? w1 : w2);
-        return (w >> (8 * (i & 3))) & 0xffu;
-    };
-    const int a = 2 * j, b = 2 * j + 1;
-    if (a < 4) {
-        sc0 = byte_of(a) & 63;
-        m0 = byte_of(a + 4) & 63;
-        sc1 = byte_of(b) & 63;
-        m1 = byte_of(b + 4) & 63;
-    } else {
-        sc0 = (byte_of(a + 4) & 0xF) | ((byte_of(a - 4) >> 6) << 4);
-        m0 = (byte_of(a + 4) >> 4) | ((byte_of(a) >> 6) << 4);
-        sc1 = (byte_of(b + 4) & 0xF) | ((byte_of(b - 4) >> 6) << 4);
-        m1 = (byte_of(b + 4) >> 4) | ((byte_of(b) >> 6) << 4);
-    }
-}
-
 __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
     return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xffffu)));
 }
@@ -159,6 +134,9 @@ __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
 // Named barrier `id` over `nthreads` threads of the CTA.
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+__device__ __forceinline__ void named_arrive(int id, int nthreads) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // Control block at the start of every workspace: a status word, a grid-arrival counter and one

@@ -384,43 +384,71 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     if (tid == 0 && p.trace) p.trace[cta * 16 + 2] = globaltimer_ns();
     if (p.internal_routing) {
         if (ok) {
-            for (int e = tid; e < E; e += kThreads) {
-                const float l = __ldcg(p.logits + e);
-                const float sg = __fdiv_rn(1.0f, 1.0f + expf(-l));
-                s.sig[e] = sg;
-                s.part[e] = sg + p.bias[e];  // selection score
-            }
-            __syncthreads();
-            // rank_e = #{j : sel_j > sel_e} + #{j < e : sel_j == sel_e}  (stable descending order)
-            for (int e = tid; e < E; e += kThreads) {
-                const float me = s.part[e];
-                int r0 = 0, r1 = 0, r2 = 0, r3 = 0;
-                const float4 *sel4 = reinterpret_cast<const float4 *>(s.part);
-                for (int j4 = 0; j4 < E / 4; ++j4) {
-                    const float4 o = sel4[j4];
-                    const int j = 4 * j4;
-                    r0 += (o.x > me) | ((o.x == me) & (j + 0 < e));
-                    r1 += (o.y > me) | ((o.y == me) & (j + 1 < e));
-                    r2 += (o.z > me) | ((o.z == me) & (j + 2 < e));
-                    r3 += (o.w > me) | ((o.w == me) & (j + 3 < e));
+            // Selection score sigmoid(l) + bias as an order-preserving 32-bit key (-0 as +0); the
+            // stable descending order is "larger key first, lower expert id on equal keys".
+            // Warp w holds experts [32 w, 32 w + 32) and extracts its top 8 by rounds of redux max
+            // (key) and redux min (id among the lanes holding that key); warp 0 merges the
+            // candidates the same way.  Candidates (key, id) reuse the score array.
+            const int nw = (E + 31) / 32;
+            uint32_t *cand = reinterpret_cast<uint32_t *>(s.part);  // [2][8 nw] <= max(E, 16) words
+            if (warp < nw) {
+                const int e = tid;
+                uint32_t key = 0u;  // experts >= E: never selected (E >= 8 real keys are > 0)
+                if (e < E) {
+                    const float l = __ldcg(p.logits + e);
+                    const float sg = __fdiv_rn(1.0f, 1.0f + expf(-l));
+                    s.sig[e] = sg;
+                    float sv = sg + p.bias[e];
+                    if (sv == 0.0f) sv = 0.0f;
+                    const uint32_t u = __float_as_uint(sv);
+                    key = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
                 }
-                const int rank = (r0 + r1) + (r2 + r3);
-                if (rank < kTopK) s.ids[rank] = e;
+                bool taken = false;
+#pragma unroll
+                for (int k = 0; k < kTopK; ++k) {
+                    const uint32_t mk = __reduce_max_sync(0xffffffffu, taken ? 0u : key);
+                    const uint32_t me =
+                        __reduce_min_sync(0xffffffffu, (!taken && key == mk) ? (uint32_t)e : 0xffffffffu);
+                    taken |= (uint32_t)e == me;
+                    if (lane == 0) {
+                        cand[warp * kTopK + k] = mk;
+                        cand[8 * nw + warp * kTopK + k] = me;
+                    }
+                }
             }
             __syncthreads();
             if (warp == 0) {
-                __syncwarp();
-                if (lane == 0) {
-                    float v[kTopK];
-                    for (int k = 0; k < kTopK; ++k) v[k] = s.sig[s.ids[k]];
-                    const float denom = ((v[0] + v[4]) + (v[2] + v[6])) + ((v[1] + v[5]) + (v[3] + v[7]));
-                    for (int k = 0; k < kTopK; ++k) s.w[k] = __fdiv_rn(v[k], denom);
+                const int nc = 8 * nw;
+                const uint32_t ka = lane < nc ? cand[lane] : 0u, ia = lane < nc ? cand[nc + lane] : 0xffffffffu;
+                const uint32_t kb = lane + 32 < nc ? cand[lane + 32] : 0u;
+                const uint32_t ib = lane + 32 < nc ? cand[nc + lane + 32] : 0xffffffffu;
+                bool ta = false, tb = false;
+                int myid = 0;
+#pragma unroll
+                for (int k = 0; k < kTopK; ++k) {
+                    const uint32_t mk = __reduce_max_sync(0xffffffffu, max(ta ? 0u : ka, tb ? 0u : kb));
+                    const uint32_t ca = (!ta && ka == mk) ? ia : 0xffffffffu;
+                    const uint32_t cb = (!tb && kb == mk) ? ib : 0xffffffffu;
+                    const uint32_t me = __reduce_min_sync(0xffffffffu, min(ca, cb));
+                    if (ca == me) ta = true;
+                    else if (cb == me) tb = true;
+                    if (lane == k) myid = (int)me;
                 }
-            }
-            __syncthreads();
-            if (cta == 0 && tid < kTopK) {
-                if (p.topk_ids_out) p.topk_ids_out[tid] = (uint32_t)s.ids[tid];
-                if (p.topk_w_out) p.topk_w_out[tid] = s.w[tid];
+                // weights: sig / ((v0+v4)+(v2+v6))+((v1+v5)+(v3+v7)) on every lane, lane k keeps w_k
+                const float vk = lane < kTopK ? s.sig[myid] : 0.0f;
+                float v[kTopK];
+#pragma unroll
+                for (int k = 0; k < kTopK; ++k) v[k] = __shfl_sync(0xffffffffu, vk, k);
+                const float denom = ((v[0] + v[4]) + (v[2] + v[6])) + ((v[1] + v[5]) + (v[3] + v[7]));
+                if (lane < kTopK) {
+                    const float wk = __fdiv_rn(vk, denom);
+                    s.ids[lane] = myid;
+                    s.w[lane] = wk;
+                    if (cta == 0) {
+                        if (p.topk_ids_out) p.topk_ids_out[lane] = (uint32_t)myid;
+                        if (p.topk_w_out) p.topk_w_out[lane] = wk;
+                    }
+                }
             }
         }
     } else {
@@ -439,24 +467,27 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
                 s.w[slot] = p.ext_w[slot];
             }
         }
-        __syncthreads();
     }
     // Gate/up position space: the (slot, row) pairs of the computed experts, partitioned evenly
     // over the CTAs.  Single GPU and TP: all 8 slots in order.  Expert parallel: experts owned by
     // other ranks contribute nothing here and their slots are left out, so this rank's CTAs share
-    // only its own experts' rows.
+    // only its own experts' rows.  Warp 0 (whose lanes 0..7 wrote ids in both routing paths).
     const bool compact = p.world > 1 && p.ep;
-    __syncthreads();
-    if (compact && tid < kTopK && s.ids[tid] >= 0 && s.ids[tid] % p.world != p.rank) s.ids[tid] = -1;
-    __syncthreads();
-    if (tid == 0) {
-        int nv = 0;
-        for (int k = 0; k < kTopK; ++k)
-            if (!compact || s.ids[k] >= 0) s.vslot[nv++] = k;
-        s.n_gu[2] = nv;
-        for (int k = 0, m = nv; k < kTopK; ++k)
-            if (compact && s.ids[k] < 0) s.vslot[m++] = k;
-        for (int k = 0; k < kTopK; ++k) s.vpos[s.vslot[k]] = k;
+    if (warp == 0) {
+        __syncwarp();
+        int id = lane < kTopK ? s.ids[lane] : -1;
+        if (compact && id >= 0 && id % p.world != p.rank) id = -1;
+        const bool keep = lane < kTopK && (!compact || id >= 0);
+        const uint32_t kept = __ballot_sync(0xffffffffu, keep);
+        const int nv = __popc(kept);
+        if (lane < kTopK) {
+            const uint32_t below = (1u << lane) - 1u;
+            const int pos = keep ? __popc(kept & below) : nv + __popc(~kept & 0xFFu & below);
+            s.ids[lane] = id;
+            s.vslot[pos] = lane;
+            s.vpos[lane] = pos;
+        }
+        if (lane == 0) s.n_gu[2] = nv;
     }
     __syncthreads();
     const int nvs = s.n_gu[2];
@@ -472,80 +503,88 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     // first row, rows); for gate/up the offset of the first row in the CTA's (slot,row) range is
     // row-offset field .w >> 8 ... stored separately in gu_off.
     const int U_gu = p.gu_unit_rows, U_dn = p.dn_unit_rows;
-    if (tid == 0) {
-        int n = 0;
-        for (int q = gu_p0; q < gu_p1 && n + 2 <= kMaxUnits;) {
-            const GuUnit u = gu_unit_at(q, gu_p1, I, U_gu);
-            const int slot = s.vslot[u.slot];
-            s.units[n] = make_int4(0, slot, u.row0, u.n);
-            s.unit_off[n++] = q - gu_p0;
-            s.units[n] = make_int4(1, slot, u.row0, u.n);
-            s.unit_off[n++] = q - gu_p0;
-            q += u.n;
-        }
-        s.n_gu[0] = n;
-        for (int r = dn_r0; r < dn_r1 && n < kMaxUnits; r += U_dn) {
-            s.units[n] = make_int4(2, 0, r, min(U_dn, dn_r1 - r));
-            s.unit_off[n++] = r - dn_r0;
-        }
-        s.n_gu[1] = n;
-    }
-    __syncthreads();
-    const int n_gu = s.n_gu[0];
-    const int n_units = s.n_gu[1];
-
     if (warp == kConsumerWarps) {
         // ---------------------------- producer --------------------------------------------
-        if (lane == 0) {
-            auto unit_src = [&](int k, uint32_t &bytes) -> const uint8_t * {
-                const int4 u = s.units[k];
-                const int e = s.ids[u.y];
-                if (e < 0) return nullptr;
-                if (u.x < 2) {
-                    bytes = (uint32_t)(gu_row_bytes * u.w);
-                    return (u.x == 0 ? p.gate : p.up) + (size_t)e * gu_expert_bytes + (size_t)u.z * gu_row_bytes;
-                }
-                bytes = (uint32_t)(dn_row_bytes * u.w);
-                return p.down + (size_t)e * dn_expert_bytes + (size_t)u.z * dn_row_bytes;
-            };
-            int k = 0;
-            for (; k < n_units; ++k) {
-                const int st = k % p.stages;
-                if (!mbar_wait_bounded(&s.empty[st], ((uint32_t)(k / p.stages) & 1u) ^ 1u, deadline)) {
-                    atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
-                    break;
-                }
-                if (k == 0 && p.trace) p.trace[cta * 16 + 8] = globaltimer_ns();
-                if (k == n_gu && p.trace) p.trace[cta * 16 + 10] = globaltimer_ns();
-                // Publish which unit this stage now holds.  Consumer groups take interleaved units,
-                // so a group can reach unit k before unit k - stages (another group's) has landed;
-                // waiting for the ticket first keeps the parity wait from aliasing onto that phase.
-                *reinterpret_cast<volatile int *>(&s.ticket[st]) = k;
-                const int4 u = s.units[k];
-                uint8_t *dst = s.stages + (size_t)st * p.stage_bytes;
-                if (u.x == 2) {
-                    // rows [u.z, u.z + u.w) of all routed experts, expert q at dst + q * U_dn rows
-                    const uint32_t bytes = (uint32_t)(dn_row_bytes * u.w);
-                    uint32_t tx = 0;
-                    for (int q = 0; q < kTopK; ++q) tx += s.ids[q] >= 0 ? bytes : 0;
-                    mbar_arrive_expect_tx(&s.full[st], tx);
-                    for (int q = 0; q < kTopK; ++q) {
-                        const int e = s.ids[q];
-                        if (e < 0) continue;
-                        bulk_g2s(dst + (size_t)q * dn_row_bytes * U_dn,
-                                 p.down + (size_t)e * dn_expert_bytes + (size_t)u.z * dn_row_bytes, bytes, &s.full[st]);
-                    }
-                    continue;
-                }
-                uint32_t bytes = 0;
-                const uint8_t *src = unit_src(k, bytes);
-                if (!src) {
-                    mbar_arrive(&s.full[st]);
-                    continue;
-                }
-                mbar_arrive_expect_tx(&s.full[st], bytes);
-                bulk_g2s(dst, src, bytes, &s.full[st]);
+        // Lane 0 builds the unit table and issues each of the first ring's worth of units as soon
+        // as its entry exists; the consumers wait for the complete table on named barrier 3.
+        int n = 0, k = 0;
+        bool live = true;
+        int n_gu = 0x7fffffff;  // no "first down unit" stamp while the table grows
+        auto unit_src = [&](int k, uint32_t &bytes) -> const uint8_t * {
+            const int4 u = s.units[k];
+            const int e = s.ids[u.y];
+            if (e < 0) return nullptr;
+            if (u.x < 2) {
+                bytes = (uint32_t)(gu_row_bytes * u.w);
+                return (u.x == 0 ? p.gate : p.up) + (size_t)e * gu_expert_bytes + (size_t)u.z * gu_row_bytes;
             }
+            bytes = (uint32_t)(dn_row_bytes * u.w);
+            return p.down + (size_t)e * dn_expert_bytes + (size_t)u.z * dn_row_bytes;
+        };
+        // issue unit k into ring stage k % stages; false when the stage wait expired
+        auto issue = [&](int k) -> bool {
+            const int st = k % p.stages;
+            if (!mbar_wait_bounded(&s.empty[st], ((uint32_t)(k / p.stages) & 1u) ^ 1u, deadline)) {
+                atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
+                return false;
+            }
+            if (k == 0 && p.trace) p.trace[cta * 16 + 8] = globaltimer_ns();
+            if (k == n_gu && p.trace) p.trace[cta * 16 + 10] = globaltimer_ns();
+            // Publish which unit this stage now holds.  Consumer groups take interleaved units,
+            // so a group can reach unit k before unit k - stages (another group's) has landed;
+            // waiting for the ticket first keeps the parity wait from aliasing onto that phase.
+            *reinterpret_cast<volatile int *>(&s.ticket[st]) = k;
+            const int4 u = s.units[k];
+            uint8_t *dst = s.stages + (size_t)st * p.stage_bytes;
+            if (u.x == 2) {
+                // rows [u.z, u.z + u.w) of all routed experts, expert q at dst + q * U_dn rows
+                const uint32_t bytes = (uint32_t)(dn_row_bytes * u.w);
+                uint32_t tx = 0;
+                for (int q = 0; q < kTopK; ++q) tx += s.ids[q] >= 0 ? bytes : 0;
+                mbar_arrive_expect_tx(&s.full[st], tx);
+                for (int q = 0; q < kTopK; ++q) {
+                    const int e = s.ids[q];
+                    if (e < 0) continue;
+                    bulk_g2s(dst + (size_t)q * dn_row_bytes * U_dn,
+                             p.down + (size_t)e * dn_expert_bytes + (size_t)u.z * dn_row_bytes, bytes, &s.full[st]);
+                }
+                return true;
+            }
+            uint32_t bytes = 0;
+            const uint8_t *src = unit_src(k, bytes);
+            if (!src) {
+                mbar_arrive(&s.full[st]);
+                return true;
+            }
+            mbar_arrive_expect_tx(&s.full[st], bytes);
+            bulk_g2s(dst, src, bytes, &s.full[st]);
+            return true;
+        };
+        if (lane == 0) {
+            // the table (each entry is written before its unit is issued)
+            for (int q = gu_p0; q < gu_p1 && n + 2 <= kMaxUnits;) {
+                const GuUnit u = gu_unit_at(q, gu_p1, I, U_gu);
+                const int slot = s.vslot[u.slot];
+                s.units[n] = make_int4(0, slot, u.row0, u.n);
+                s.unit_off[n++] = q - gu_p0;
+                s.units[n] = make_int4(1, slot, u.row0, u.n);
+                s.unit_off[n++] = q - gu_p0;
+                q += u.n;
+                for (; live && k < n && k < p.stages; ++k) live = issue(k);
+            }
+            s.n_gu[0] = n;
+            for (int r = dn_r0; r < dn_r1 && n < kMaxUnits; r += U_dn) {
+                s.units[n] = make_int4(2, 0, r, min(U_dn, dn_r1 - r));
+                s.unit_off[n++] = r - dn_r0;
+            }
+            s.n_gu[1] = n;
+        }
+        __threadfence_block();
+        __syncwarp();
+        named_arrive(3, kThreads);  // the table is complete
+        if (lane == 0) {
+            n_gu = s.n_gu[0];
+            for (; live && k < n; ++k) live = issue(k);
             if (p.trace) p.trace[cta * 16 + 9] = globaltimer_ns();
             // Drain: no copy may still be landing in shared memory when the CTA retires.
             const int first = k > p.stages ? k - p.stages : 0;
@@ -554,6 +593,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         }
         return;
     }
+    named_sync(3, kThreads);
+    const int n_gu = s.n_gu[0];
+    const int n_units = s.n_gu[1];
 
     // ------------------------------- consumers ----------------------------------------------
     const int grp = warp / kGroupWarps, gw = warp % kGroupWarps;

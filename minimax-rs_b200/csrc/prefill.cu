@@ -19,19 +19,46 @@ namespace mmrs {
 //    l+32, l+64 of the slice with fmaf; the 32 lane partials are combined by an xor butterfly
 //    (16, 8, 4, 2, 1) and the slices by ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7)).
 //    Block: 8 warps = 8 slices, 8 experts per warp (weights in registers), 32 tokens per block.
+//    Each warp streams its slice of the token rows through a kRtDepth-deep cp.async ring in
+//    shared memory (a lane reads back exactly the 16-byte groups it copied), so the L2 latency
+//    of token t+kRtDepth overlaps the arithmetic of token t.
 //    The 8 butterflies of a warp are folded into one transposed reduction that produces the
 //    same sums (each step adds the same two operands as the plain butterfly).
 // ==========================================================================================
-constexpr int kRtExperts = 8, kRtTokens = 32, kRtMaxIter = 3;  // H <= 3072
+constexpr int kRtExperts = 8, kRtTokens = 32, kRtMaxIter = 3, kRtDepth = 3;  // H <= 3072
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 template <int ITER>
 __global__ void __launch_bounds__(256) router_logits_kernel(const float *__restrict__ x,
                                                             const float *__restrict__ wr, int T, int E, int H,
                                                             float *__restrict__ logits) {
     __shared__ float part[kRtTokens][kRtExperts][8];
+    __shared__ __align__(16) float4 ring[8][kRtDepth][32 * ITER];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e0 = blockIdx.x * kRtExperts, t0 = blockIdx.y * kRtTokens;
     const int slice = H / 8, groups = slice / 4;
+    const int tn = min(kRtTokens, T - t0);
+    // token rows are only read through the ring; start the first kRtDepth copies before the
+    // weight loads so both latencies overlap
+    auto issue = [&](int tt) {
+        if (tt < tn) {
+            const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)(t0 + tt) * H + warp * slice);
+#pragma unroll
+            for (int it = 0; it < ITER; ++it) {
+                const int g = lane + 32 * it;
+                if (g < groups) cp_async16(&ring[warp][tt % kRtDepth][g], src + g);
+            }
+        }
+        cp_async_commit();  // one group per token slot, empty past the end
+    };
+#pragma unroll
+    for (int d = 0; d < kRtDepth; ++d) issue(d);
     float4 w[kRtExperts][ITER];
 #pragma unroll
     for (int e = 0; e < kRtExperts; ++e)
@@ -42,14 +69,13 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const float *__restr
                            ? __ldg(reinterpret_cast<const float4 *>(wr + (size_t)(e0 + e) * H + warp * slice) + g)
                            : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-    const int tn = min(kRtTokens, T - t0);
     for (int tt = 0; tt < tn; ++tt) {
-        const float *xs = x + (size_t)(t0 + tt) * H + warp * slice;
+        cp_async_wait<kRtDepth - 1>();  // this lane's copies of token tt have landed
         float4 xv[ITER];
 #pragma unroll
         for (int it = 0; it < ITER; ++it) {
             const int g = lane + 32 * it;
-            xv[it] = g < groups ? __ldg(reinterpret_cast<const float4 *>(xs) + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+            xv[it] = g < groups ? ring[warp][tt % kRtDepth][g] : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         float v[kRtExperts];
 #pragma unroll
@@ -92,7 +118,9 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const float *__restr
         d = d + __shfl_xor_sync(0xffffffffu, d, 2);
         d = d + __shfl_xor_sync(0xffffffffu, d, 1);
         if ((lane & 3) == 0) part[tt][4 * b4 + 2 * b3 + b2][warp] = d;
+        issue(tt + kRtDepth);  // the slot's values are consumed (d depends on them)
     }
+    cp_async_wait<0>();
     __syncthreads();
     for (int i = threadIdx.x; i < tn * kRtExperts; i += blockDim.x) {
         const int tt = i / kRtExperts, e = i % kRtExperts;
@@ -121,13 +149,13 @@ int pf_router_logits(const float *x, const float *router, int T, int E, int H, f
 //    selection by s + bias in stable descending order (lower expert id first on ties),
 //    weights s / tree-sum (strides 4, 2, 1).  One warp per token.
 // ==========================================================================================
+template <int kPer>  // experts per lane: E <= 32 * kPer
 __global__ void __launch_bounds__(256) route_topk_kernel(const float *__restrict__ logits,
                                                          const float *__restrict__ bias, int T, int E,
                                                          uint32_t *__restrict__ ids, float *__restrict__ wts) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * 8 + warp;
     if (t >= T) return;
-    constexpr int kPer = kPfMaxExperts / 32;
     float sel[kPer], sig[kPer];
     const int per = (E + 31) / 32;
 #pragma unroll
@@ -197,7 +225,11 @@ __global__ void __launch_bounds__(256) route_topk_kernel(const float *__restrict
 int pf_route_topk(const float *logits, const float *bias, int T, int E, uint32_t *ids, float *w, cudaStream_t s) {
     if (T <= 0) return MMRS_OK;
     if (E < 8 || E > kPfMaxExperts) return MMRS_ERR_UNSUPPORTED;
-    route_topk_kernel<<<(T + 7) / 8, 256, 0, s>>>(logits, bias, T, E, ids, w);
+    const unsigned blocks = (T + 7) / 8;
+    if (E <= 256)
+        route_topk_kernel<8><<<blocks, 256, 0, s>>>(logits, bias, T, E, ids, w);
+    else
+        route_topk_kernel<kPfMaxExperts / 32><<<blocks, 256, 0, s>>>(logits, bias, T, E, ids, w);
     return cudaGetLastError() == cudaSuccess ? MMRS_OK : MMRS_ERR_LAUNCH;
 }
 
@@ -495,42 +527,53 @@ int pf_reduce_topk(const float *dn, const float *residual, int T, int H, float *
 //
 //    Work item = (expert e, route tile of <= 32 routes, 128 weight rows).  Per 256-column chunk
 //    (one GGUF super-block of every row):
-//      warp 0      TMA: the raw weight tile (tensor map, 128 rows x one super-block), the route
-//                  tile's int8 activations (B operand) and their block scales, into a 4-deep ring
+//      warp 0      TMA: the raw weight tile (tensor map, 128 rows x one super-block) and the route
+//                  tile's block scales into the raw ring; the route tile's int8 activations
+//                  (B operand) into the operand stage
 //      warps 2-5   unpack (one thread per row): nibbles (+ high bits) -> int8 A operand in the
 //                  canonical no-swizzle K-major shared-memory layout; per 32-block and row the
 //                  scales (dmx, dmy); the route tile's (d8, s8) planes for the epilogue
 //      warp 1      one thread issues the chunk's 8 MMAs (M=128, N=routes rounded to 16, K=32),
 //                  one per 32-block, each into its own accumulator of the chunk's TMEM group
-//                  (8 x N columns), then one commit for the group
+//                  (8 x 32 columns), then one commit for the group
 //      warps 6-21  epilogue: 4 TMEM lane quarters x 4 units of 8 route columns; per 32-block
 //                  sum = fma(dmx * d8, C, sum); sum = fma(dmy, s8, sum) in K order (the MMQ combine
 //                  of mmq_gguf.cuh vec_dot_q8_1_q8_1_mma, or with the generic numerics' scales the
 //                  vec_dot_q*_K_q8_1 combine), then the route rows are written (times the route
 //                  weight when given).
+//    Integer accumulators without a conversion: every accumulator column holds the bit pattern
+//    of 1.5 * 2^23 (0x4B400000) before its MMA, which adds the block's integer dot product C
+//    (|C| <= 32 * 31 * 127 < 2^22) to it, so the column reads as the float 12582912 + C and one
+//    exact subtraction gives C.  The epilogue writes the pattern back after reading a column.
 //    Every wait is bounded by a %globaltimer deadline; on expiry the CTA records
 //    MMRS_ERR_TIMEOUT, stops, waits (bounded) for its own copies and MMAs and frees its TMEM.
 // ==========================================================================================
 constexpr int kPfRawW = kPfMT * Q5K_BYTES;      // 22528: raw weight tile
 constexpr int kPfRawQ = kPfNT * QK_K;           // 8192: int8 activations of the route tile (B operand)
 constexpr int kPfRawD = kPfNT * 8 * 8;          // 2048: d8 and s8 planes of the route tile
-constexpr int kPfRawBytes = kPfRawW + kPfRawQ + kPfRawD;
+constexpr int kPfRawBytes = kPfRawW + kPfRawD;
 constexpr int kPfABytes = kPfMT * QK_K;         // 32768
 constexpr int kPfEpiWarp0 = 2 + kPfUnpackWarps;
 constexpr int kPfGroupCols = 8 * kPfNT;         // 256: the 8 block accumulators of one chunk
 constexpr int kPfTmemCols = kPfGroups * kPfGroupCols;
 static_assert(kPfTmemCols == 512, "two chunk groups fill the tensor memory");
 static_assert(kPfNT == 32 && kPfEpiWarps == 16, "epilogue geometry: 4 lane quarters x 4 x 8 route columns");
+constexpr int kPfPrefetch = 6;                  // weight tiles prefetched to L2 ahead of the loads
+constexpr uint32_t kPfAccBias = 0x4B400000u;  // float 12582912 = 1.5 * 2^23
+constexpr float kPfAccBiasF = 12582912.0f;
 
-// Raw stage (TMA / bulk copies): weights, activations and their scales of one chunk.
-// Operand stage: what the unpack warps derive from a raw stage for the MMAs and the epilogue.
+// Raw stage (TMA / bulk copies): the weights and the activation block scales of one chunk; it is
+// free again as soon as the unpack warps have read it.
+// Operand stage: the MMA operands (A from the unpack warps, B by a bulk copy; free when the
+// chunk's MMAs complete) and the epilogue's scales (free when the epilogue has used them).
 struct PfSmem {
     uint8_t raw[kPfRawStages][kPfRawBytes];
     uint8_t a[kPfOpStages][kPfABytes];
+    uint8_t b[kPfOpStages][kPfRawQ];
     float2 sc[kPfOpStages][8 * kPfMT];       // (dmx, dmy) per 32-block and row
     float dst[kPfOpStages][2][8][kPfNT];     // [d8 | s8][32-block][route]
     uint64_t rfull[kPfRawStages], rempty[kPfRawStages];
-    uint64_t oempty[kPfOpStages], aready[kPfOpStages];
+    uint64_t bfull[kPfOpStages], abempty[kPfOpStages], sdempty[kPfOpStages], aready[kPfOpStages];
     uint64_t gfull[kPfGroups], gfree[kPfGroups];
     uint64_t mdone;
     int tiles[kPfMaxExperts + 1];            // route-tile prefix of the plan (item decoding)
@@ -538,6 +581,7 @@ struct PfSmem {
     int abort;
 };
 
+static_assert(sizeof(PfSmem) + 128 <= 232448, "PfSmem exceeds the 227 KB a CTA can opt in to");
 size_t pf_gemm_smem_bytes() { return sizeof(PfSmem) + 128; }
 
 __device__ __forceinline__ uint64_t umma_smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -578,12 +622,24 @@ __device__ __forceinline__ void tc_ld8(uint32_t taddr, uint32_t (&v)[8]) {
                  : "r"(taddr));
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tc_st8_const(uint32_t taddr, uint32_t v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(v)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
             smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap *map, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y)
+                 : "memory");
 }
 
 struct PfItem {
@@ -606,48 +662,35 @@ __device__ __forceinline__ PfItem pf_item(const PfGemmParams &p, const int *tile
     return it;
 }
 
-// Unpack half hh (sub-block pairs 2hh, 2hh+1) of one raw GGUF super-block row into the int8 A tile
-// (canonical no-swizzle K-major layout: 8-row groups 2048 B apart, 16-byte K slices 128 B apart,
-// rows 16 B apart) and its 4 scale pairs.
+// Small non-negative integer (< 2^23) to float without the conversion pipe: the integer is
+// placed in the mantissa of 2^23 and 2^23 is subtracted (exact).
+__device__ __forceinline__ float small_uint_to_float(uint32_t v) {
+    return __uint_as_float(0x4B000000u | v) - 8388608.0f;
+}
+
+// Unpack one raw GGUF super-block row into the int8 A tile (canonical no-swizzle K-major layout:
+// 8-row groups 2048 B apart, 16-byte K slices 128 B apart, rows 16 B apart) and its 8 scale
+// pairs.  Every 16-byte load of the row is issued before the first store, so the loads are in
+// flight together instead of each waiting behind the previous store.
 template <int GT, int MODE>
-__device__ __forceinline__ void pf_unpack_row(const uint8_t *blk, uint8_t *a_tile, float2 *sc_col, int r, int hh) {
+__device__ __forceinline__ void pf_unpack_row(const uint8_t *__restrict__ blk, uint8_t *__restrict__ a_tile,
+                                              float2 *__restrict__ sc_col, int r) {
+    constexpr int kQs = GT == MMRS_Q5K ? 48 : 16;
     const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
-    const float dall = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
-    const uint32_t w0 = hdr.y, w1 = hdr.z, w2 = hdr.w;  // the 12 packed scale bytes
-#pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-        const int j = 4 * hh + jj;
-        // get_scale_min_k4 (quantized.cu:926-933) on bytes of w0..w2
-        const auto byte = [&](int i) -> uint32_t {
-            const uint32_t w = i < 4 ? w0 : (i < 8 ? w1 : w2);
-            return (w >> (8 * (i & 3))) & 0xffu;
-        };
-        int sc, mn;
-        if (j < 4) {
-            sc = byte(j) & 63;
-            mn = byte(j + 4) & 63;
-        } else {
-            sc = (byte(j + 4) & 0xF) | ((byte(j - 4) >> 6) << 4);
-            mn = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
-        }
-        float dmx = __fmul_rn(dall, (float)sc), dmy = __fmul_rn(-dmin, (float)mn);
-        if (MODE == kPfModeMmq) {  // the MMQ tile loader rounds both products to half
-            dmx = __half2float(__float2half_rn(dmx));
-            dmy = __half2float(__float2half_rn(dmy));
-        }
-        sc_col[j * kPfMT] = make_float2(dmx, dmy);
-    }
-    const uint8_t *qs = blk + (GT == MMRS_Q5K ? 48 : 16);
     uint4 qh0 = make_uint4(0, 0, 0, 0), qh1 = make_uint4(0, 0, 0, 0);
     if (GT == MMRS_Q5K) {
         qh0 = *reinterpret_cast<const uint4 *>(blk + 16);
         qh1 = *reinterpret_cast<const uint4 *>(blk + 32);
     }
+    uint4 qv[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) qv[q] = *reinterpret_cast<const uint4 *>(blk + kQs + 16 * q);
+
     uint8_t *arow = a_tile + (r >> 3) * 2048 + (r & 7) * 16;
 #pragma unroll
-    for (int qq = 0; qq < 4; ++qq) {
-        const int q = 4 * hh + qq, jp = q >> 1, hf = q & 1;
-        const uint4 v = *reinterpret_cast<const uint4 *>(qs + 16 * q);
+    for (int q = 0; q < 8; ++q) {
+        const int jp = q >> 1, hf = q & 1;
+        const uint4 v = qv[q];
         uint4 lo, hi;
         lo.x = v.x & 0x0F0F0F0Fu;
         lo.y = v.y & 0x0F0F0F0Fu;
@@ -671,6 +714,31 @@ __device__ __forceinline__ void pf_unpack_row(const uint8_t *blk, uint8_t *a_til
         }
         *reinterpret_cast<uint4 *>(arow + (4 * jp + hf) * 128) = lo;
         *reinterpret_cast<uint4 *>(arow + (4 * jp + 2 + hf) * 128) = hi;
+    }
+    const float dall = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
+    const uint32_t w0 = hdr.y, w1 = hdr.z, w2 = hdr.w;  // the 12 packed scale bytes
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        // get_scale_min_k4 (quantized.cu:926-933) on bytes of w0..w2
+        const auto byte = [&](int i) -> uint32_t {
+            const uint32_t w = i < 4 ? w0 : (i < 8 ? w1 : w2);
+            return (w >> (8 * (i & 3))) & 0xffu;
+        };
+        uint32_t sc, mn;
+        if (j < 4) {
+            sc = byte(j) & 63;
+            mn = byte(j + 4) & 63;
+        } else {
+            sc = (byte(j + 4) & 0xF) | ((byte(j - 4) >> 6) << 4);
+            mn = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
+        }
+        float dmx = __fmul_rn(dall, small_uint_to_float(sc)), dmy = __fmul_rn(-dmin, small_uint_to_float(mn));
+        if (MODE == kPfModeMmq) {  // the MMQ tile loader rounds both products to half
+            const float2 h = __half22float2(__floats2half2_rn(dmx, dmy));
+            dmx = h.x;
+            dmy = h.y;
+        }
+        sc_col[j * kPfMT] = make_float2(dmx, dmy);
     }
 }
 
@@ -708,27 +776,46 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
     return bits_f2(r);
 }
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    unsigned long long r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return bits_f2(r);
+}
 __device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
     unsigned long long r;
     asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
     return bits_f2(r);
 }
 
+// Scales of one 32-block for 8 route columns: (dmx, dmy) of the row, d8 and s8 of the routes.
+struct PfScales8 {
+    float2 row;
+    float4 d[2], s[2];
+};
+__device__ __forceinline__ PfScales8 pf_scales8(float2 row, const float *dcol, const float *scol) {
+    PfScales8 z;
+    z.row = row;
+    z.d[0] = *reinterpret_cast<const float4 *>(dcol);
+    z.d[1] = *reinterpret_cast<const float4 *>(dcol + 4);
+    z.s[0] = *reinterpret_cast<const float4 *>(scol);
+    z.s[1] = *reinterpret_cast<const float4 *>(scol + 4);
+    return z;
+}
+
 // Scale-and-accumulate 8 route columns of one 32-block: per column
 // sum = fma(dmx * d8, C, sum); sum = fma(dmy, s8, sum).
-__device__ __forceinline__ void pf_accumulate8(float2 (&acc)[4], const uint32_t (&v)[8], float2 scr, const float *dcol,
-                                               const float *scol) {
-    const float2 dmx = make_float2(scr.x, scr.x), dmy = make_float2(scr.y, scr.y);
+__device__ __forceinline__ void pf_accumulate8(float2 (&acc)[4], const uint32_t (&v)[8], const PfScales8 &z) {
+    const float2 dmx = make_float2(z.row.x, z.row.x), dmy = make_float2(z.row.y, z.row.y);
 #pragma unroll
     for (int h4 = 0; h4 < 2; ++h4) {
-        const float4 d4 = *reinterpret_cast<const float4 *>(dcol + 4 * h4);
-        const float4 s4 = *reinterpret_cast<const float4 *>(scol + 4 * h4);
-        const float2 dp[2] = {make_float2(d4.x, d4.y), make_float2(d4.z, d4.w)};
-        const float2 sp[2] = {make_float2(s4.x, s4.y), make_float2(s4.z, s4.w)};
+        const float2 dp[2] = {make_float2(z.d[h4].x, z.d[h4].y), make_float2(z.d[h4].z, z.d[h4].w)};
+        const float2 sp[2] = {make_float2(z.s[h4].x, z.s[h4].y), make_float2(z.s[h4].z, z.s[h4].w)};
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
             const int i = 2 * h4 + u;
-            const float2 cf = make_float2(__int2float_rn((int)v[2 * i]), __int2float_rn((int)v[2 * i + 1]));
+            // exact C from the biased accumulator (see the bias note above the kernel)
+            const float2 cf = fadd2(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])),
+                                    make_float2(-kPfAccBiasF, -kPfAccBiasF));
             acc[i] = ffma2(fmul2(dmx, dp[u]), cf, acc[i]);
             acc[i] = ffma2(dmy, sp[u], acc[i]);
         }
@@ -749,10 +836,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
     if (tid == 0) {
         for (int i = 0; i < kPfRawStages; ++i) {
             mbar_init(&sm.rfull[i], 1);
-            mbar_init(&sm.rempty[i], kPfUnpackWarps + 1);  // unpack warps + MMA commit
+            mbar_init(&sm.rempty[i], kPfUnpackWarps);
         }
         for (int i = 0; i < kPfOpStages; ++i) {
-            mbar_init(&sm.oempty[i], 1 + kPfEpiWarps);
+            mbar_init(&sm.bfull[i], 1);
+            mbar_init(&sm.abempty[i], 1);              // MMA commit
+            mbar_init(&sm.sdempty[i], kPfEpiWarps);
             mbar_init(&sm.aready[i], kPfUnpackWarps);
         }
         for (int i = 0; i < kPfGroups; ++i) {
@@ -773,67 +862,110 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
+    if (warp >= kPfEpiWarp0) {
+        // every accumulator column starts at the bias pattern (each epilogue warp: its lane
+        // quarter and route unit, all 8 blocks of both groups)
+        const int qd = warp & 3, u = (warp - kPfEpiWarp0) >> 2;
+        const uint32_t tq = tmem + ((uint32_t)(qd * 32) << 16) + 8 * u;
+#pragma unroll
+        for (int gj = 0; gj < kPfGroups * 8; ++gj) tc_st8_const(tq + gj * kPfNT, kPfAccBias);
+        tc_wait_st();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
-            uint32_t c = 0;
+            uint32_t c = 0, raw_extra = 0;
+            // L2 prefetch cursor kPfPrefetch chunks ahead of the loads: the strided weight tile
+            // (128 rows of one super-block) has a long DRAM latency that the raw ring alone
+            // cannot cover
+            int pitem = blockIdx.x, pkc = 0, prow0 = -1;
+            const auto prefetch_next = [&]() {
+                if (pitem >= total) return;
+                if (pkc == 0) {
+                    const PfItem pi = pf_item(p, sm.tiles, pitem);
+                    prow0 = pi.e * p.N + pi.m0;
+                }
+                tma_prefetch_2d(&wmap, pkc * (bb / 4), prow0);
+                if (++pkc == nkc) {
+                    pkc = 0;
+                    pitem += gridDim.x;
+                }
+            };
+            for (int i = 0; i < kPfPrefetch; ++i) prefetch_next();
             for (int item = blockIdx.x; item < total && !pf_aborted(sm); item += gridDim.x) {
                 const PfItem it = pf_item(p, sm.tiles, item);
                 const int row0 = it.e * p.N + it.m0;
                 const int n16 = pad_to(it.nvalid, 16);
                 const uint32_t qb = (uint32_t)n16 * QK_K, db = (uint32_t)n16 * 64;
+                bool ok = true;
                 for (int kc = 0; kc < nkc; ++kc, ++c) {
-                    const int s = c % kPfRawStages;
-                    if (!pf_wait(&sm.rempty[s], ((c / kPfRawStages) & 1) ^ 1, deadline, sm, p.status)) break;
-                    mbar_arrive_expect_tx(&sm.rfull[s], (uint32_t)(kPfMT * bb) + qb + db);
-                    tma_load_2d(sm.raw[s], &wmap, kc * (bb / 4), row0, &sm.rfull[s]);
-                    bulk_g2s(sm.raw[s] + kPfRawW, p.aq + (size_t)kc * p.plan.ppad * QK_K + (size_t)it.p0 * QK_K, qb,
-                             &sm.rfull[s]);
-                    bulk_g2s(sm.raw[s] + kPfRawW + kPfRawQ,
-                             p.ads + ((size_t)kc * (p.plan.ppad / 16) + it.p0 / 16) * 256, db, &sm.rfull[s]);
-                }
-            }
-            // drain: every issued copy lands before the CTA can exit
-            const uint32_t issued = c;
-            for (uint32_t k = issued > kPfRawStages ? issued - kPfRawStages : 0; k < issued; ++k)
-                mbar_wait_bounded(&sm.rfull[k % kPfRawStages], (k / kPfRawStages) & 1, deadline + p.timeout_ns);
-        }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            uint32_t c = 0;
-            bool ok = true;
-            for (int item = blockIdx.x; item < total && ok && !pf_aborted(sm); item += gridDim.x) {
-                const PfItem it = pf_item(p, sm.tiles, item);
-                const int n16 = pad_to(it.nvalid, 16);
-                const uint32_t idesc = umma_idesc_i8(kPfMT, n16);
-                for (int kc = 0; kc < nkc; ++kc, ++c) {
-                    const int o = c % kPfOpStages, s = c % kPfRawStages, g = c % kPfGroups;
-                    if (!pf_wait(&sm.aready[o], (c / kPfOpStages) & 1, deadline, sm, p.status) ||
-                        !pf_wait(&sm.rfull[s], (c / kPfRawStages) & 1, deadline, sm, p.status) ||
-                        !pf_wait(&sm.gfree[g], ((c / kPfGroups) & 1) ^ 1, deadline, sm, p.status)) {
+                    const int s = c % kPfRawStages, o = c % kPfOpStages;
+                    if (!pf_wait(&sm.rempty[s], ((c / kPfRawStages) & 1) ^ 1, deadline, sm, p.status)) {
                         ok = false;
                         break;
                     }
-                    tc_fence_after();
-                    const uint32_t abase = smem_u32(sm.a[o]), bbase = smem_u32(sm.raw[s] + kPfRawW);
-                    const uint32_t dbase = tmem + g * kPfGroupCols;
+                    mbar_arrive_expect_tx(&sm.rfull[s], (uint32_t)(kPfMT * bb) + db);
+                    tma_load_2d(sm.raw[s], &wmap, kc * (bb / 4), row0, &sm.rfull[s]);
+                    prefetch_next();
+                    bulk_g2s(sm.raw[s] + kPfRawW, p.ads + ((size_t)kc * (p.plan.ppad / 16) + it.p0 / 16) * 256, db,
+                             &sm.rfull[s]);
+                    if (!pf_wait(&sm.abempty[o], ((c / kPfOpStages) & 1) ^ 1, deadline, sm, p.status)) {
+                        raw_extra = 1;  // this chunk's raw copies are in flight, its operand copy is not
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&sm.bfull[o], qb);
+                    bulk_g2s(sm.b[o], p.aq + (size_t)kc * p.plan.ppad * QK_K + (size_t)it.p0 * QK_K, qb, &sm.bfull[o]);
+                }
+                if (!ok) break;
+            }
+            // drain: every issued copy lands before the CTA can exit
+            const uint32_t raw_issued = c + raw_extra, b_issued = c;
+            for (uint32_t k = raw_issued > kPfRawStages ? raw_issued - kPfRawStages : 0; k < raw_issued; ++k)
+                mbar_wait_bounded(&sm.rfull[k % kPfRawStages], (k / kPfRawStages) & 1, deadline + p.timeout_ns);
+            for (uint32_t k = b_issued > kPfOpStages ? b_issued - kPfOpStages : 0; k < b_issued; ++k)
+                mbar_wait_bounded(&sm.bfull[k % kPfOpStages], (k / kPfOpStages) & 1, deadline + p.timeout_ns);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (the warp waits and derives the descriptors; lane 0 issues) ----------------
+        uint32_t c = 0;
+        bool ok = true;
+        for (int item = blockIdx.x; item < total && ok && !pf_aborted(sm); item += gridDim.x) {
+            const PfItem it = pf_item(p, sm.tiles, item);
+            const int n16 = pad_to(it.nvalid, 16);
+            const uint32_t idesc = umma_idesc_i8(kPfMT, n16);
+            for (int kc = 0; kc < nkc; ++kc, ++c) {
+                const int o = c % kPfOpStages, g = c % kPfGroups;
+                if (!pf_wait(&sm.aready[o], (c / kPfOpStages) & 1, deadline, sm, p.status) ||
+                    !pf_wait(&sm.bfull[o], (c / kPfOpStages) & 1, deadline, sm, p.status) ||
+                    !pf_wait(&sm.gfree[g], ((c / kPfGroups) & 1) ^ 1, deadline, sm, p.status)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t abase = smem_u32(sm.a[o]), bbase = smem_u32(sm.b[o]);
+                const uint32_t dbase = tmem + g * kPfGroupCols;
+                if (lane == 0) {
 #pragma unroll
                     for (int j = 0; j < 8; ++j)
-                        tc_mma_i8(dbase + j * n16, umma_smem_desc(abase + j * 256, 128, 2048),
-                                  umma_smem_desc(bbase + j * 256, 128, 2048), idesc, 0);
+                        tc_mma_i8(dbase + j * kPfNT, umma_smem_desc(abase + j * 256, 128, 2048),
+                                  umma_smem_desc(bbase + j * 256, 128, 2048), idesc, 1);
                     tc_commit(&sm.gfull[g]);
-                    tc_commit(&sm.rempty[s]);
-                    tc_commit(&sm.oempty[o]);
+                    tc_commit(&sm.abempty[o]);
                 }
-            }
-            // all MMAs issued by this thread complete before TMEM is released
-            if (c > 0) {
-                tc_commit(&sm.mdone);
-                mbar_wait_bounded(&sm.mdone, 0, deadline + p.timeout_ns);
+                __syncwarp();
             }
         }
+        // all MMAs issued by lane 0 complete before TMEM is released
+        if (c > 0 && lane == 0) {
+            tc_commit(&sm.mdone);
+            mbar_wait_bounded(&sm.mdone, 0, deadline + p.timeout_ns);
+        }
+        __syncwarp();
     } else if (warp < kPfEpiWarp0) {
         // ---------------- unpack (128 threads, one weight row each) ----------------
         const int t = tid - 64, r = t;
@@ -844,15 +976,16 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
             bool ok = true;
             for (int kc = 0; kc < nkc; ++kc, ++c) {
                 const int s = c % kPfRawStages, o = c % kPfOpStages;
-                if (!pf_wait(&sm.oempty[o], ((c / kPfOpStages) & 1) ^ 1, deadline, sm, p.status) ||
+                const uint32_t op = ((c / kPfOpStages) & 1) ^ 1;
+                if (!pf_wait(&sm.abempty[o], op, deadline, sm, p.status) ||
+                    !pf_wait(&sm.sdempty[o], op, deadline, sm, p.status) ||
                     !pf_wait(&sm.rfull[s], (c / kPfRawStages) & 1, deadline, sm, p.status)) {
                     ok = false;
                     break;
                 }
-                pf_unpack_row<GT, MODE>(sm.raw[s] + r * bb, sm.a[o], &sm.sc[o][r], r, 0);
-                pf_unpack_row<GT, MODE>(sm.raw[s] + r * bb, sm.a[o], &sm.sc[o][r], r, 1);
+                pf_unpack_row<GT, MODE>(sm.raw[s] + r * bb, sm.a[o], &sm.sc[o][r], r);
                 // block scales of the route tile: 16-route records [d8 plane | s8 plane][32-block][16]
-                const float *dsraw = reinterpret_cast<const float *>(sm.raw[s] + kPfRawW + kPfRawQ);
+                const float *dsraw = reinterpret_cast<const float *>(sm.raw[s] + kPfRawW);
                 if (t < n16 * 4) {  // float4 t of the records -> dst[plane][j][route]
                     const int b = t >> 6, plane = (t >> 5) & 1, j = (t >> 2) & 7, c4 = t & 3;
                     *reinterpret_cast<float4 *>(&sm.dst[o][plane][j][b * 16 + c4 * 4]) =
@@ -879,7 +1012,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
         for (int item = blockIdx.x; item < total && !pf_aborted(sm); item += gridDim.x) {
             const PfItem it = pf_item(p, sm.tiles, item);
             const int n16 = pad_to(it.nvalid, 16);
-            const bool has = 8 * u < it.nvalid;
+            const bool has = 8 * u < it.nvalid, written = 8 * u < n16;  // read / reset this unit
             float2 acc[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.0f, 0.0f);
@@ -894,29 +1027,26 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                 tc_fence_after();
                 const uint32_t gbase = tq + g * kPfGroupCols + 8 * u;
 #pragma unroll
-                for (int pass = 0; pass < 4; ++pass) {
-                    uint32_t v[2][8];  // [32-block][column]
+                for (int j = 0; j < 8; ++j) {
+                    uint32_t v[8];  // the unit's 8 route columns of 32-block j
+                    PfScales8 z;
                     if (has) {
-                        tc_ld8(gbase + (2 * pass) * n16, v[0]);
-                        tc_ld8(gbase + (2 * pass + 1) * n16, v[1]);
+                        // scales first: their shared-memory latency overlaps the TMEM load
+                        z = pf_scales8(sm.sc[o][j * kPfMT + r], &sm.dst[o][0][j][8 * u], &sm.dst[o][1][j][8 * u]);
+                        tc_ld8(gbase + j * kPfNT, v);
                         tc_wait_ld();
                     }
-                    if (pass == 3) {
+                    if (written) tc_st8_const(gbase + j * kPfNT, kPfAccBias);
+                    if (j == 7) {
+                        if (written) tc_wait_st();
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&sm.gfree[g]);  // the group's values are in registers
                     }
-                    if (has) {
-#pragma unroll
-                        for (int b = 0; b < 2; ++b) {
-                            const int j = 2 * pass + b;
-                            pf_accumulate8(acc, v[b], sm.sc[o][j * kPfMT + r], &sm.dst[o][0][j][8 * u],
-                                           &sm.dst[o][1][j][8 * u]);
-                        }
-                    }
+                    if (has) pf_accumulate8(acc, v, z);
                 }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&sm.oempty[o]);
+                if (lane == 0) mbar_arrive(&sm.sdempty[o]);
             }
             if (!ok) break;
             const int row = it.m0 + r;
