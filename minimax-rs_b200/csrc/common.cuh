@@ -27,6 +27,16 @@ __host__ __device__ inline int kq_block_bytes(int t) { return t == MMRS_Q5K ? Q5
 __host__ __device__ inline size_t kq_row_bytes(int t, int k) { return (size_t)(k / QK_K) * kq_block_bytes(t); }
 __host__ __device__ inline int pad_to(int v, int p) { return (v + p - 1) / p * p; }
 
+// Exact integer -> float conversions that stay off the conversion pipe (a quarter-rate unit):
+// the integer is placed in the mantissa of a power of two and that power is subtracted.
+// small_uint_to_float: 0 <= v < 2^23.  int22_to_float: -2^22 <= v < 2^22.
+__device__ __forceinline__ float small_uint_to_float(uint32_t v) {
+    return __uint_as_float(0x4B000000u | v) - 8388608.0f;
+}
+__device__ __forceinline__ float int22_to_float(int v) {
+    return __int_as_float(0x4B400000 + v) - 12582912.0f;
+}
+
 __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
     return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xffffu)));
 }

@@ -135,8 +135,12 @@ __device__ __forceinline__ float task_dot(const uint8_t *row, int tau, const Tas
     const int dlo = d[0] + d[1], dhi = d[2];
     uint32_t scp, mp;
     scale_pair(hdr, j, scp, mp);
-    const float sd = a.ts.x * (float)(dlo * (int)(scp & 0xffu)) + a.ts.y * (float)(dhi * (int)(scp >> 8));
-    const float sm = a.ts.z * (float)(mp & 0xffu) + a.ts.w * (float)(mp >> 8);
+    // |d * sc| < 2^22 for Q4_K (32 * 15 * 127 * 63); Q5_K products reach 2^23 and use the plain conversion
+    const int plo = dlo * (int)(scp & 0xffu), phi = dhi * (int)(scp >> 8);
+    const float flo = TYPE == MMRS_Q5K ? (float)plo : int22_to_float(plo);
+    const float fhi = TYPE == MMRS_Q5K ? (float)phi : int22_to_float(phi);
+    const float sd = a.ts.x * flo + a.ts.y * fhi;
+    const float sm = a.ts.z * small_uint_to_float(mp & 0xffu) + a.ts.w * small_uint_to_float(mp >> 8);
     const float2 dm = __half22float2(*reinterpret_cast<const __half2 *>(&hdr.x));
     return dm.x * sd - dm.y * sm;
 }
@@ -505,8 +509,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     const int U_gu = p.gu_unit_rows, U_dn = p.dn_unit_rows;
     if (warp == kConsumerWarps) {
         // ---------------------------- producer --------------------------------------------
-        // Lane 0 builds the unit table and issues each of the first ring's worth of units as soon
-        // as its entry exists; the consumers wait for the complete table on named barrier 3.
+        // Lane 0 builds the unit table and releases the consumers (named barrier 3) before it
+        // issues the first copy: an issue can block on the copy engine, the consumers must not.
         int n = 0, k = 0;
         bool live = true;
         int n_gu = 0x7fffffff;  // no "first down unit" stamp while the table grows
@@ -570,7 +574,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
                 s.units[n] = make_int4(1, slot, u.row0, u.n);
                 s.unit_off[n++] = q - gu_p0;
                 q += u.n;
-                for (; live && k < n && k < p.stages; ++k) live = issue(k);
             }
             s.n_gu[0] = n;
             for (int r = dn_r0; r < dn_r1 && n < kMaxUnits; r += U_dn) {

@@ -662,12 +662,6 @@ __device__ __forceinline__ PfItem pf_item(const PfGemmParams &p, const int *tile
     return it;
 }
 
-// Small non-negative integer (< 2^23) to float without the conversion pipe: the integer is
-// placed in the mantissa of 2^23 and 2^23 is subtracted (exact).
-__device__ __forceinline__ float small_uint_to_float(uint32_t v) {
-    return __uint_as_float(0x4B000000u | v) - 8388608.0f;
-}
-
 // Unpack one raw GGUF super-block row into the int8 A tile (canonical no-swizzle K-major layout:
 // 8-row groups 2048 B apart, 16-byte K slices 128 B apart, rows 16 B apart) and its 8 scale
 // pairs.  Every 16-byte load of the row is issued before the first store, so the loads are in
