@@ -9,6 +9,10 @@
 
 namespace mmrs {
 
+// Messages of at least this many floats (2 MiB) use the two-shot all-reduce on 4 or more ranks
+// (measured on 4 B200s: one round of flags is cheaper below, two-shot ties or beats NCCL above).
+constexpr size_t kTwoShotMin = size_t(1) << 19;
+
 // ------------------------------------------------------------------------------------------
 // Multi-rank all-reduce: y[i] = (p_0[i] + p_1[i] + ... + p_{W-1}[i]) (+ residual[i]), summed in
 // rank order on every rank, so all ranks hold bit-identical results.  p_r is rank r's partial in
@@ -18,8 +22,9 @@ namespace mmrs {
 // ------------------------------------------------------------------------------------------
 struct PeerArParams {
     const float *part[kMaxRanks];
-    uint32_t *my_flags;
-    const uint32_t *peer_flags[kMaxRanks];
+    uint32_t *my_flags, *my_flags2;
+    const uint32_t *peer_flags[kMaxRanks], *peer_flags2[kMaxRanks];
+    float *my_part;  // this rank's partial (the two-shot kernel writes its reduced chunk there)
     uint32_t *status;
     const float *residual;
     float *y;
@@ -86,6 +91,95 @@ __global__ void __launch_bounds__(256) peer_allreduce_kernel(const PeerArParams 
     }
 }
 
+// ------------------------------------------------------------------------------------------
+// Two-shot all-reduce for large messages (W >= 4): chunk r = [r * cs, (r + 1) * cs) is reduced
+// by rank r alone (reduce-scatter: the same rank-ordered sum + residual as the one-shot kernel,
+// so every rank still ends with bit-identical values), written back over rank r's own partial
+// chunk (no other rank reads that chunk of rank r's partial) and published with a second flag;
+// then every rank copies the other ranks' reduced chunks (all-gather).  Each rank reads
+// 2 (W - 1) / W of the message over NVLink instead of (W - 1) times it.  CTA b owns sub-range b
+// of every chunk, so all waits pair CTA b with CTA b of the peers.
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ bool peer_wait_all(const PeerArParams &p, const uint32_t *const *flags, int b,
+                                              uint64_t deadline) {
+    for (int r = 0; r < p.world; ++r) {
+        if (r == p.rank) continue;
+        if (!wait_flag_sys(flags[r] + b, p.token, deadline)) {
+            atomicExch(p.status, (uint32_t)MMRS_ERR_TIMEOUT);
+            return false;
+        }
+    }
+    return true;
+}
+
+__global__ void __launch_bounds__(256) peer_allreduce2_kernel(const PeerArParams p, size_t cs, size_t per) {
+    __shared__ int ok;
+    const int b = blockIdx.x;
+    const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
+    auto sub = [&](int r, size_t &lo, size_t &hi) {  // sub-range b of chunk r
+        const size_t c0 = (size_t)r * cs, c1 = c0 + cs < p.count ? c0 + cs : p.count;
+        lo = c0 + (size_t)b * per < c1 ? c0 + (size_t)b * per : c1;
+        hi = lo + per < c1 ? lo + per : c1;
+    };
+    // phase 1: reduce this rank's chunk
+    if (threadIdx.x == 0) {
+        st_release_sys(p.my_flags + b, p.token);  // the local partial is ready
+        ok = peer_wait_all(p, p.peer_flags, b, deadline) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!ok) return;
+    size_t lo, hi;
+    sub(p.rank, lo, hi);
+    for (size_t i = lo + 4 * threadIdx.x; i + 4 <= hi; i += 4 * blockDim.x) {
+        float4 v[kMaxRanks];
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r)
+            if (r < p.world)
+                v[r] = r == p.rank ? *reinterpret_cast<const float4 *>(p.part[r] + i)
+                                   : ld_relaxed_sys_f4(reinterpret_cast<const float4 *>(p.part[r] + i));
+        float4 a = v[0];
+#pragma unroll
+        for (int r = 1; r < kMaxRanks; ++r)
+            if (r < p.world) {
+                a.x = a.x + v[r].x;
+                a.y = a.y + v[r].y;
+                a.z = a.z + v[r].z;
+                a.w = a.w + v[r].w;
+            }
+        if (p.residual) {
+            const float4 rr = *reinterpret_cast<const float4 *>(p.residual + i);
+            a.x = a.x + rr.x;
+            a.y = a.y + rr.y;
+            a.z = a.z + rr.z;
+            a.w = a.w + rr.w;
+        }
+        *reinterpret_cast<float4 *>(p.my_part + i) = a;
+        *reinterpret_cast<float4 *>(p.y + i) = a;
+    }
+    for (size_t i = hi - (hi - lo) % 4 + threadIdx.x; i < hi; i += blockDim.x) {
+        float v = p.rank == 0 ? p.part[0][i] : ld_relaxed_sys_f32(p.part[0] + i);
+        for (int r = 1; r < p.world; ++r) v = v + (r == p.rank ? p.part[r][i] : ld_relaxed_sys_f32(p.part[r] + i));
+        if (p.residual) v = v + p.residual[i];
+        p.my_part[i] = v;
+        p.y[i] = v;
+    }
+    __syncthreads();
+    // phase 2: publish the reduced sub-range, gather the peers'
+    if (threadIdx.x == 0) {
+        st_release_sys(p.my_flags2 + b, p.token);
+        ok = peer_wait_all(p, p.peer_flags2, b, deadline) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!ok) return;
+    for (int r = 0; r < p.world; ++r) {
+        if (r == p.rank) continue;
+        sub(r, lo, hi);
+        for (size_t i = lo + 4 * threadIdx.x; i + 4 <= hi; i += 4 * blockDim.x)
+            *reinterpret_cast<float4 *>(p.y + i) = ld_relaxed_sys_f4(reinterpret_cast<const float4 *>(p.part[r] + i));
+        for (size_t i = hi - (hi - lo) % 4 + threadIdx.x; i < hi; i += blockDim.x) p.y[i] = ld_relaxed_sys_f32(p.part[r] + i);
+    }
+}
+
 int peer_all_reduce(const PeerView &g, const float *residual, float *y, size_t count, uint32_t token,
                     uint64_t timeout_ns, cudaStream_t stream) {
     if (count == 0) return MMRS_OK;
@@ -98,8 +192,11 @@ int peer_all_reduce(const PeerView &g, const float *residual, float *y, size_t c
         if (!g.peers[r]) return MMRS_ERR_ARG;
         p.part[r] = reinterpret_cast<const float *>(g.peers[r] + kXchAPart) + (size_t)(token & 1u) * g.ar_capacity;
         p.peer_flags[r] = reinterpret_cast<const uint32_t *>(g.peers[r] + kXchAFlags);
+        p.peer_flags2[r] = reinterpret_cast<const uint32_t *>(g.peers[r] + kXchA2Flags);
     }
     p.my_flags = reinterpret_cast<uint32_t *>(g.mine + kXchAFlags);
+    p.my_flags2 = reinterpret_cast<uint32_t *>(g.mine + kXchA2Flags);
+    p.my_part = reinterpret_cast<float *>(g.mine + kXchAPart) + (size_t)(token & 1u) * g.ar_capacity;
     p.status = reinterpret_cast<uint32_t *>(g.mine + kXchStatus);
     p.residual = residual;
     p.y = y;
@@ -108,6 +205,15 @@ int peer_all_reduce(const PeerView &g, const float *residual, float *y, size_t c
     p.rank = g.rank;
     p.token = token;
     p.timeout_ns = timeout_ns;
+    if (g.world >= 4 && count >= kTwoShotMin) {
+        // chunks of a multiple of 4 floats; ~2K floats of every chunk per CTA
+        const size_t cs = ((count + g.world - 1) / g.world + 3) / 4 * 4;
+        size_t ctas = (cs + 2047) / 2048;
+        if (ctas > 592) ctas = 592;
+        const size_t per = ((cs + ctas - 1) / ctas + 3) / 4 * 4;
+        peer_allreduce2_kernel<<<(unsigned)ctas, 256, 0, stream>>>(p, cs, per);
+        return cudaGetLastError() == cudaSuccess ? MMRS_OK : MMRS_ERR_LAUNCH;
+    }
     // one CTA per ~4K floats, at most one wave of the flag array
     size_t ctas = (count + 4095) / 4096;
     if (ctas > (size_t)kXchMaxCtas) ctas = kXchMaxCtas;

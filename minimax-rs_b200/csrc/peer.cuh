@@ -19,7 +19,8 @@ constexpr int kXchMaxCtas = 1024;
 constexpr size_t kXchStatus = 0;       // u32: MMRS_ERR_TIMEOUT after an expired wait
 constexpr size_t kXchDFlags = 4096;    // u32[kXchMaxCtas]: fused decode kernel, one per CTA
 constexpr size_t kXchAFlags = 8192;    // u32[kXchMaxCtas]: all-reduce kernel, one per CTA
-constexpr size_t kXchDPart = 12288;    // f32[2][kXchMaxHidden]: decode partial y
+constexpr size_t kXchA2Flags = 12288;  // u32[kXchMaxCtas]: two-shot all-reduce, reduced chunk ready
+constexpr size_t kXchDPart = 16384;    // f32[2][kXchMaxHidden]: decode partial y
 constexpr size_t kXchAPart = kXchDPart + 2 * sizeof(float) * kXchMaxHidden;  // f32[2][cap]
 
 __host__ __device__ inline size_t xch_bytes(size_t ar_capacity) {

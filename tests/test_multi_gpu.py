@@ -117,11 +117,13 @@ def test_group_decode_repeated_tokens(pkg, synth, orc):
 
 
 @needs2
-def test_peer_all_reduce(pkg, synth):
+@pytest.mark.parametrize("count", [3 * 4096 + 17, 512 * 3072 + 13], ids=["one_shot", "two_shot"])
+def test_peer_all_reduce(pkg, synth, count):
+    """Rank-ordered sum + residual, bit-identical on every rank.  Messages of 512K floats or more
+    take the two-shot path (reduce-scatter + all-gather) on 4 or more ranks."""
     import torch
     gm = _group_mod(pkg)
     world = min(_ngpu(), 4)
-    count = 3 * 4096 + 17
     groups = gm.PeerGroup.local(list(range(world)), ar_capacity=(count + 3) // 4 * 4, expert_parallel=False)
     res = synth.normal_f32(count, 77, 9, 1.0)
     parts = [synth.normal_f32(count, 77, 10 + r, 1.0) for r in range(world)]
