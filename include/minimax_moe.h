@@ -141,6 +141,17 @@ MMRS_API int mmrs_moe_block_forward(const MmrsMoeWeights *w, const float *x, con
                            float *y, int num_tokens, uint32_t *topk_ids, float *topk_weights,
                            void *workspace, size_t workspace_bytes, mmrs_stream_t stream);
 
+/* No counterpart in the reference (its MoE input already lives on the device).  The same block
+ * as mmrs_moe_block_forward for a caller holding x and y in host memory, num_tokens * hidden
+ * floats each way, enqueued on `stream` in one call.  Pinned (mapped) host buffers are read by a
+ * small kernel into x_dev and written by the block's final stores directly; other host buffers
+ * go through copy-engine transfers via x_dev / y_dev.  residual, topk_ids and topk_weights are
+ * device pointers as in mmrs_moe_block_forward; x_dev / y_dev 16-byte aligned. */
+MMRS_API int mmrs_moe_block_forward_host(const MmrsMoeWeights *w, const float *x_host, const float *residual,
+                                         float *y_host, int num_tokens, float *x_dev, float *y_dev,
+                                         uint32_t *topk_ids, float *topk_weights, void *workspace,
+                                         size_t workspace_bytes, mmrs_stream_t stream);
+
 /* Copies the per-CTA phase timestamps (globaltimer ns, 16 slots per CTA: 0 start, 1 router done,
  * 2 routing barrier, 3 routing done, 4 gate/up done, 5 second barrier, 6 activation quantised,
  * 7 end, 8 first weight copy issued, 9 last copy issued, 10 first down copy issued) of the last

@@ -71,6 +71,8 @@ PROTOTYPES = {
                                           _VP, _VP, _VP, _SZ, _U32, _VP]),
     "mmrs_moe_workspace_bytes": (_SZ, [C.POINTER(MmrsMoeWeights), _I]),
     "mmrs_moe_block_forward": (_I, [C.POINTER(MmrsMoeWeights), _VP, _VP, _VP, _I, _VP, _VP, _VP, _SZ, _VP]),
+    "mmrs_moe_block_forward_host": (_I, [C.POINTER(MmrsMoeWeights), _VP, _VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _SZ,
+                                         _VP]),
     "mmrs_moe_workspace_status": (_I, [_VP, _VP]),
     "mmrs_moe_block_decode_static": (_I, [C.POINTER(MmrsMoeWeights), _VP, _VP, _VP, _VP, _VP, _VP]),
     "mmrs_moe_workspace_trace": (_I, [_VP, _VP, _I, _VP]),
@@ -154,6 +156,18 @@ class MoeLayer:
                                           _ptr(topk_ids), _ptr(topk_w), ws.data_ptr(), ws.numel(), _stream(stream))
         check(rc, "mmrs_moe_block_forward")
         return y
+
+    def forward_host(self, x_host, y_host, x_dev, y_dev, residual=None, topk_ids=None, topk_w=None, stream=None):
+        """y_host = MoE(x_host) (+ residual) in one library call: the copy of x_host [T, hidden]
+        (pinned host memory) into x_dev, the block into y_dev and the copy back into y_host are
+        enqueued on `stream`; residual / topk_* are CUDA tensors as in forward()."""
+        T = x_host.shape[0]
+        ws = self.workspace(T)
+        rc = lib().mmrs_moe_block_forward_host(C.byref(self.c), x_host.data_ptr(), _ptr(residual), y_host.data_ptr(),
+                                               T, x_dev.data_ptr(), y_dev.data_ptr(), _ptr(topk_ids), _ptr(topk_w),
+                                               ws.data_ptr(), ws.numel(), _stream(stream))
+        check(rc, "mmrs_moe_block_forward_host")
+        return y_host
 
     def trace(self, stream=None):
         """Per-CTA phase timestamps (ns) of the last single-token launch: array [256, 16]."""

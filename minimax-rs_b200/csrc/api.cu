@@ -2,6 +2,7 @@
 #include <cstdio>
 #include <cstring>
 
+#include <algorithm>
 #include "common.cuh"
 #include "decode.cuh"
 #include "peer.cuh"
@@ -457,6 +458,51 @@ extern "C" int mmrs_moe_block_forward(const MmrsMoeWeights *w, const float *x, c
     rc = decode_configure(p, device_sms(), device_max_smem());
     if (rc != MMRS_OK) return rc;
     return decode_launch(p, (cudaStream_t)stream);
+}
+
+// Device view of pinned host memory (UVA), or null when the memory is not mapped (the failed
+// query's error is cleared so that later launch checks do not see it).
+static void *mapped_host(const void *h) {
+    void *d = nullptr;
+    if (cudaHostGetDevicePointer(&d, const_cast<void *>(h), 0) == cudaSuccess) return d;
+    (void)cudaGetLastError();
+    return nullptr;
+}
+
+// Reads n floats (n % 4 == 0, 16-byte aligned) from mapped host memory into device memory:
+// for small messages the loads' PCIe round trip is shorter than a copy-engine transfer.
+__global__ void __launch_bounds__(256) host_in_kernel(const float4 *__restrict__ src, float4 *__restrict__ dst,
+                                                      size_t n4) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x)
+        dst[i] = src[i];
+}
+
+extern "C" int mmrs_moe_block_forward_host(const MmrsMoeWeights *w, const float *x_host, const float *residual,
+                                           float *y_host, int num_tokens, float *x_dev, float *y_dev,
+                                           uint32_t *topk_ids, float *topk_weights, void *workspace,
+                                           size_t workspace_bytes, mmrs_stream_t stream) {
+    int rc = validate_weights(w);
+    if (rc != MMRS_OK) return rc;
+    if (!x_host || !y_host || !x_dev || !y_dev || num_tokens < 0) return MMRS_ERR_ARG;
+    if (num_tokens == 0) return MMRS_OK;
+    const size_t n = (size_t)num_tokens * w->hidden, bytes = n * sizeof(float);
+    cudaStream_t s = (cudaStream_t)stream;
+    // input: loads from the mapped pinned buffer, else a copy-engine transfer
+    const void *xm = aligned16(x_host) ? mapped_host(x_host) : nullptr;
+    if (xm) {
+        const size_t n4 = n / 4;  // hidden is a multiple of 256
+        const unsigned blocks = (unsigned)std::min<size_t>((n4 + 255) / 256, 1184);
+        host_in_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const float4 *>(xm), reinterpret_cast<float4 *>(x_dev), n4);
+        if (cudaGetLastError() != cudaSuccess) return MMRS_ERR_LAUNCH;
+    } else if (cudaMemcpyAsync(x_dev, x_host, bytes, cudaMemcpyHostToDevice, s) != cudaSuccess) {
+        return MMRS_ERR_LAUNCH;
+    }
+    // output: the block's final stores go straight to the mapped pinned buffer, else via y_dev
+    void *ym = aligned16(y_host) ? mapped_host(y_host) : nullptr;
+    rc = mmrs_moe_block_forward(w, x_dev, residual, ym ? static_cast<float *>(ym) : y_dev, num_tokens, topk_ids,
+                                topk_weights, workspace, workspace_bytes, stream);
+    if (rc != MMRS_OK || ym) return rc;
+    return cudaMemcpyAsync(y_host, y_dev, bytes, cudaMemcpyDeviceToHost, s) == cudaSuccess ? MMRS_OK : MMRS_ERR_LAUNCH;
 }
 
 extern "C" int mmrs_moe_workspace_status(void *workspace, mmrs_stream_t stream) {

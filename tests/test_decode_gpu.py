@@ -106,3 +106,26 @@ def test_fused_block_decode_repeatable_and_many_tokens(pkg, orc, synth, dev):
     for t in range(6):
         ref_y, _, _, _ = oracle_decode(orc, pkg, L, L["x"].cpu().numpy()[t])
         assert rel_l2(outs[t].cpu().numpy()[0], ref_y) < TOL
+
+
+@pytest.mark.parametrize("T", [1, 40])
+def test_block_forward_host_matches_device_call(pkg, synth, dev, T):
+    """mmrs_moe_block_forward_host (copy in, block, copy out in one call) gives the bytes of
+    mmrs_moe_block_forward on the same input."""
+    import torch
+    E, H, I = 32, 1024, 512
+    L = make_layer(pkg, synth, dev, E, H, I, 1, 4, seed=51, T=T, x_scale=0.05)
+    layer = pkg.MoeLayer(L["router"], L["bias"], L["gate"], L["up"], L["down"], 1, 4)
+    x = L["x"].reshape(T, H)
+    res = L["residual"].reshape(T, H)
+    y_ref = layer.forward(x, residual=res)
+    x_host = torch.empty(T, H, dtype=torch.float32, pin_memory=True)
+    x_host.copy_(x.cpu())
+    y_host = torch.zeros(T, H, dtype=torch.float32, pin_memory=True)
+    x_dev = torch.empty_like(x)
+    y_dev = torch.empty_like(x)
+    s = torch.cuda.Stream()
+    layer.forward_host(x_host, y_host, x_dev, y_dev, residual=res, stream=s)
+    s.synchronize()
+    assert layer.status() == 0
+    assert torch.equal(y_host, y_ref.cpu())
