@@ -107,6 +107,22 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     }
     return true;
 }
+// Bounded wait that lets the waiting warp sleep in hardware (try_wait with a suspend-time hint)
+// instead of spinning on issue slots the working warps need.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint64_t deadline) {
+    for (;;) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
+            : "memory");
+        if (ok) return true;
+        if (globaltimer_ns() > deadline) return false;
+    }
+}
+
 // 1-D bulk copy global -> shared, completion counted on an mbarrier (bytes % 16 == 0,
 // both addresses 16-byte aligned).
 __device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, uint32_t bytes,

@@ -196,9 +196,11 @@ __device__ __forceinline__ bool wait_unit(uint64_t *full, const int *ticket, int
                                           uint64_t deadline) {
     uint32_t spins = 0;
     while (*reinterpret_cast<const volatile int *>(&ticket[st]) != k) {
+        __nanosleep(64);
         if ((++spins & 255u) == 0 && globaltimer_ns() > deadline) return false;
     }
-    return mbar_wait_bounded(&full[st], (uint32_t)(k / stages) & 1u, deadline);
+    // sleeping wait: a group waiting for its data leaves the issue slots to the groups computing
+    return mbar_wait_sleep(&full[st], (uint32_t)(k / stages) & 1u, deadline);
 }
 
 // Unit enumeration shared by producer and consumers (identical sequences).
@@ -528,7 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         // issue unit k into ring stage k % stages; false when the stage wait expired
         auto issue = [&](int k) -> bool {
             const int st = k % p.stages;
-            if (!mbar_wait_bounded(&s.empty[st], ((uint32_t)(k / p.stages) & 1u) ^ 1u, deadline)) {
+            if (!mbar_wait_sleep(&s.empty[st], ((uint32_t)(k / p.stages) & 1u) ^ 1u, deadline)) {
                 atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
                 return false;
             }

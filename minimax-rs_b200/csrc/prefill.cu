@@ -738,22 +738,6 @@ __device__ __forceinline__ void pf_unpack_row(const uint8_t *__restrict__ blk, u
 
 __device__ __forceinline__ bool pf_aborted(PfSmem &sm) { return *reinterpret_cast<volatile int *>(&sm.abort) != 0; }
 
-// Bounded wait that lets the waiting warp sleep in hardware (try_wait with a suspend-time hint)
-// instead of spinning on issue slots the working warps need.
-__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint64_t deadline) {
-    for (;;) {
-        uint32_t ok;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(ok)
-            : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
-            : "memory");
-        if (ok) return true;
-        if (globaltimer_ns() > deadline) return false;
-    }
-}
-
 __device__ __forceinline__ bool pf_wait(uint64_t *bar, uint32_t parity, uint64_t deadline, PfSmem &sm,
                                         uint32_t *status) {
     if (mbar_wait_sleep(bar, parity, deadline)) return true;
