@@ -92,6 +92,32 @@ def kquant(gguf_type: int, seed: int, stream: int, experts: int, rows: int, k: i
     return words.view(np.uint8).reshape(experts, nrows, nkblk * BLOCK_BYTES[gguf_type])
 
 
+def q8_0_blocks(seed: int, stream: int, rows: int, k: int) -> np.ndarray:
+    """Synthetic GGUF Q8_0 matrix [rows][k/32] x 34 bytes (half d = |N(0,1)| * 0.01, then 32
+    uniform int8 quants), as uint8 [rows, k/32 * 34]."""
+    nb = k // 32
+    key, key_d = stream_key(seed, stream), stream_key(seed, stream + 0x10000)
+    blk = np.arange(rows * nb, dtype=np.uint64)
+    q = rand64(key, (blk[:, None] * np.uint64(4) + np.arange(4, dtype=np.uint64)).ravel()).view(np.uint8)
+    d = (np.abs(normal(key_d, blk)) * np.float32(0.01)).astype(np.float16)
+    out = np.empty((rows * nb, 34), dtype=np.uint8)
+    out[:, :2] = d.view(np.uint8).reshape(-1, 2)
+    out[:, 2:] = q.reshape(-1, 32)
+    return out.reshape(rows, nb * 34)
+
+
+def normal_f16(n: int, seed: int, stream: int, scale: float = 1.0) -> np.ndarray:
+    """scale * N(0,1) rounded to half (round to nearest even)."""
+    return normal_f32(n, seed, stream, scale).astype(np.float16)
+
+
+def rope_tables(max_pos: int, rope_dim: int, theta: float = 5.0e6):
+    """cos / sin [max_pos][rope_dim / 2] f32 of the rotary embedding: angle(p, i) = p * theta^(-2i/rope_dim)."""
+    inv = theta ** (-np.arange(0, rope_dim, 2, dtype=np.float64) / rope_dim)
+    ang = np.arange(max_pos, dtype=np.float64)[:, None] * inv[None, :]
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
 def layer_streams(layer: int) -> dict:
     base = 16 * layer
     return dict(x=base + 0, router=base + 1, bias=base + 2, gate=base + 3, up=base + 4,

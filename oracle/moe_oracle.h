@@ -110,6 +110,16 @@ void orc_moe_block(const OrcMoeWeights *w, const float *x, const float *residual
 /* Number of OpenMP threads the oracle uses (for the CPU-baseline report). */
 int orc_num_threads(void);
 
+/* ---- decode attention (attn_oracle.c) ---- */
+uint16_t orc_double_to_half(double v);
+void orc_q8_0_matvec(const uint8_t *w, int rows, int k, const float *x, float *y);
+void orc_qkv_rmsnorm_f16(const float *proj, const float *q_alpha, const float *k_alpha, int q_rows,
+                         int k_rows, int v_rows, float eps, uint16_t *dst);
+void orc_partial_rope_f16(const uint16_t *q, const uint16_t *k, const float *cosv, const float *sinv, int q_rows,
+                          int k_rows, int head_dim, int rope_dim, int position, uint16_t *dst);
+void orc_gqa_decode_f16(const uint16_t *q, const uint16_t *k, const uint16_t *v, int seq_len, int q_heads,
+                        int kv_heads, int head_dim, int64_t kv_head_stride, float scale, uint16_t *out);
+
 #ifdef __cplusplus
 }
 #endif

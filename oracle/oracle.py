@@ -19,7 +19,7 @@ BLOCK_BYTES = {Q4K: 144, Q5K: 176}
 
 
 def build() -> Path:
-    src = [HERE / "moe_oracle.c", HERE / "moe_oracle.h", HERE / "Makefile"]
+    src = [HERE / "moe_oracle.c", HERE / "attn_oracle.c", HERE / "moe_oracle.h", HERE / "Makefile"]
     if not LIB_PATH.exists() or any(s.stat().st_mtime > LIB_PATH.stat().st_mtime for s in src):
         subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
     return LIB_PATH
@@ -170,3 +170,43 @@ def moe_block(router, bias, gate, up, down, gate_up_type, down_type, x, residual
     res = None if residual is None else _c(residual, np.float32).reshape(T, H)
     lib().orc_moe_block(C.byref(w), _p(x), _p(res), C.c_int(T), C.c_int(mmq_min_tokens), _p(y), _p(ids), _p(tw))
     return y, ids, tw
+
+
+# ---- decode attention (attn_oracle.c) ----------------------------------------------------
+def q8_0_matvec(w: np.ndarray, rows: int, k: int, x: np.ndarray) -> np.ndarray:
+    """y = W x for a Q8_0 matrix (rows x k/32 blocks of 34 bytes), x quantised to Q8_1."""
+    w, x = _c(w, np.uint8), _c(x, np.float32)
+    y = np.zeros(rows, dtype=np.float32)
+    lib().orc_q8_0_matvec(_p(w), C.c_int(rows), C.c_int(k), _p(x), _p(y))
+    return y
+
+
+def qkv_rmsnorm_f16(proj, q_alpha, k_alpha, q_rows: int, k_rows: int, v_rows: int, eps: float = 1e-6):
+    """f16 bits (uint16) of [RMSNorm(q) * q_alpha | RMSNorm(k) * k_alpha | v]."""
+    proj, qa, ka = _c(proj, np.float32), _c(q_alpha, np.float32), _c(k_alpha, np.float32)
+    out = np.zeros(q_rows + k_rows + v_rows, dtype=np.uint16)
+    lib().orc_qkv_rmsnorm_f16(_p(proj), _p(qa), _p(ka), C.c_int(q_rows), C.c_int(k_rows), C.c_int(v_rows),
+                              C.c_float(eps), _p(out))
+    return out
+
+
+def partial_rope_f16(q, k, cos, sin, head_dim: int, rope_dim: int, position: int):
+    """f16 bits of [rotated q | rotated k]; q / k given as float16 or uint16 bit arrays."""
+    q, k = _c(np.asarray(q).view(np.uint16), np.uint16), _c(np.asarray(k).view(np.uint16), np.uint16)
+    cos, sin = _c(cos, np.float32), _c(sin, np.float32)
+    out = np.zeros(q.size + k.size, dtype=np.uint16)
+    lib().orc_partial_rope_f16(_p(q), _p(k), _p(cos), _p(sin), C.c_int(q.size), C.c_int(k.size), C.c_int(head_dim),
+                               C.c_int(rope_dim), C.c_int(position), _p(out))
+    return out
+
+
+def gqa_decode_f16(q, k, v, seq_len: int, q_heads: int, kv_heads: int, head_dim: int, kv_head_stride: int,
+                   scale: float):
+    """f16 bits [q_heads * head_dim] of softmax(scale q.k) v over positions [0, seq_len)."""
+    q = _c(np.asarray(q).view(np.uint16), np.uint16)
+    k = _c(np.asarray(k).view(np.uint16), np.uint16)
+    v = _c(np.asarray(v).view(np.uint16), np.uint16)
+    out = np.zeros(q_heads * head_dim, dtype=np.uint16)
+    lib().orc_gqa_decode_f16(_p(q), _p(k), _p(v), C.c_int(seq_len), C.c_int(q_heads), C.c_int(kv_heads),
+                             C.c_int(head_dim), C.c_int64(kv_head_stride), C.c_float(scale), _p(out))
+    return out

@@ -125,3 +125,48 @@ def mmq_layout_to_logical(vy: np.ndarray, rows: int, kpad: int):
     d = ds[..., 0].transpose(1, 0, 2).reshape(rows, nb * 4)
     s = ds[..., 1].transpose(1, 0, 2).reshape(rows, nb * 4)
     return q, d, s
+
+
+# ------------------------------------------------------------------------------------------
+# Decode attention (tests/golden/ref_attn.npz): MiniMax's fixed head geometry (48 query heads,
+# 8 KV heads, head dim 128, rotary dims 64, theta 5e6) at the model's hidden size.
+# ------------------------------------------------------------------------------------------
+ATTN_H, QH, KVH, HD, ROT = 3072, 48, 8, 128, 64
+Q_ROWS, K_ROWS, V_ROWS = QH * HD, KVH * HD, KVH * HD
+ROPE_POS = (0, 7, 4095)
+ROPE_MAX_POS = 4096
+KV_CAP = 4096  # cache capacity (positions per KV head)
+GQA_CASES = ((1, 1), (129, 4), (1000, 16), (4096, 32))  # (seq_len, num_splits)
+
+
+def qkv_inputs():
+    x = S.normal_f32(ATTN_H, 701, 1, 1.0)
+    wq = S.q8_0_blocks(701, 2, Q_ROWS, ATTN_H)
+    wk = S.q8_0_blocks(701, 3, K_ROWS, ATTN_H)
+    wv = S.q8_0_blocks(701, 4, V_ROWS, ATTN_H)
+    qa = (1.0 + S.normal_f32(Q_ROWS, 701, 5, 0.1)).astype(np.float32)
+    ka = (1.0 + S.normal_f32(K_ROWS, 701, 6, 0.1)).astype(np.float32)
+    return x, wq, wk, wv, qa, ka
+
+
+def rope_inputs():
+    q = S.normal_f16(Q_ROWS, 702, 1, 1.0)
+    k = S.normal_f16(K_ROWS, 702, 2, 1.0)
+    cos, sin = S.rope_tables(ROPE_MAX_POS, ROT)
+    return q, k, cos, sin
+
+
+def gqa_inputs(seq_len: int):
+    """q [48][128] and K / V caches [8][KV_CAP][128] (positions >= seq_len are zero), half."""
+    q = S.normal_f16(QH * HD, 703, 1, 1.0).reshape(QH, HD)
+    k = np.zeros((KVH, KV_CAP, HD), dtype=np.float16)
+    v = np.zeros((KVH, KV_CAP, HD), dtype=np.float16)
+    k[:, :seq_len] = S.normal_f16(KVH * KV_CAP * HD, 703, 2, 1.0).reshape(KVH, KV_CAP, HD)[:, :seq_len]
+    v[:, :seq_len] = S.normal_f16(KVH * KV_CAP * HD, 703, 3, 1.0).reshape(KVH, KV_CAP, HD)[:, :seq_len]
+    return q, k, v
+
+
+def oproj_inputs():
+    a = S.normal_f16(Q_ROWS, 704, 1, 1.0).astype(np.float32)  # attention output, widened
+    wo = S.q8_0_blocks(704, 2, ATTN_H, Q_ROWS)
+    return a, wo
