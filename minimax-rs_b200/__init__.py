@@ -47,6 +47,14 @@ class MmrsPeerGroup(C.Structure):
 _VP, _I, _U32, _U64, _I64, _F = C.c_void_p, C.c_int, C.c_uint32, C.c_uint64, C.c_int64, C.c_float
 _SZ = C.c_size_t
 
+
+class MmrsAttnWeights(C.Structure):
+    """include/minimax_attn.h: MmrsAttnWeights."""
+    _fields_ = [("wq", C.c_void_p), ("wk", C.c_void_p), ("wv", C.c_void_p), ("wo", C.c_void_p),
+                ("q_norm", C.c_void_p), ("k_norm", C.c_void_p), ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
+                ("hidden", C.c_int), ("query_heads", C.c_int), ("kv_heads", C.c_int), ("rope_dim", C.c_int),
+                ("max_positions", C.c_int), ("eps", C.c_float)]
+
 # name -> (restype, argtypes)
 PROTOTYPES = {
     "minimax_moe_decode_topk": (None, [_VP] * 7),
@@ -55,6 +63,15 @@ PROTOTYPES = {
     "moe_gemm_mmq_gguf": (None, [_VP] * 6 + [_I] * 6 + [_VP]),
     "moe_sort_routes": (None, [_VP] * 3 + [_I] * 2 + [_VP]),
     "mmrs_last_error": (_I, []),
+    # decode attention (include/minimax_attn.h)
+    "launch_mmvq_gguf_quantize_q8_1_f32": (None, [_VP, _VP, _I, _I, _I, _VP]),
+    "launch_mmvq_gguf_q8_0_f32_plain": (None, [_VP] * 3 + [_I] * 5 + [_VP]),
+    "launch_mmvq_gguf_qkv_q8_0_f32": (None, [_VP] * 6 + [_I] * 5 + [_VP]),
+    "launch_mmvq_gguf_qkv_q8_0_f32_rmsnorm_f16": (None, [_VP] * 9 + [_I] * 5 + [_F, _VP]),
+    "launch_partial_rope_f16": (None, [_VP] * 5 + [_I] * 5 + [_VP]),
+    "launch_gqa_decode_mma_f16_128": (None, [_VP] * 5 + [_I] * 7 + [_F, _I, _VP]),
+    "mmrs_attn_workspace_bytes": (_SZ, [C.POINTER(MmrsAttnWeights)]),
+    "mmrs_attn_decode_forward": (_I, [C.POINTER(MmrsAttnWeights), _VP, _VP, _I, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "launch_tp2_peer_all_reduce_f32": (None, [_VP] * 8 + [C.c_uint, _I, _F, _VP]),
     "launch_tp2_peer_broadcast_f32": (None, [_VP] * 4 + [C.c_uint, _I, _I, _VP]),
     "mmrs_xch_bytes": (_SZ, [_SZ]),
@@ -216,3 +233,35 @@ def synth_kquant(t, gguf_type: int, seed: int, stream_id: int, experts: int, row
     check(lib().mmrs_synth_kquant(t.data_ptr(), gguf_type, seed, stream_id, experts, rows, k, row0, nrows, kblk0,
                                   nkblk, _stream(stream)), "mmrs_synth_kquant")
     return t
+
+
+class AttnLayer:
+    """Single-token attention half of a layer (Attention::forward, src/model.rs:79-162, T = 1):
+    device-resident Q8_0 weights, RMSNorm weights, rotary tables and the f16 KV cache
+    [kv_heads][max_positions][128], with the C struct that points at them."""
+
+    def __init__(self, wq, wk, wv, wo, q_norm, k_norm, rope_cos, rope_sin, hidden: int, query_heads: int = 48,
+                 kv_heads: int = 8, rope_dim: int = 64, eps: float = 1e-6):
+        import torch
+        self.t = (wq, wk, wv, wo, q_norm, k_norm, rope_cos, rope_sin)
+        self.max_positions = rope_cos.shape[0]
+        self.c = MmrsAttnWeights(wq.data_ptr(), wk.data_ptr(), wv.data_ptr(), wo.data_ptr(), q_norm.data_ptr(),
+                                 k_norm.data_ptr(), rope_cos.data_ptr(), rope_sin.data_ptr(), hidden, query_heads,
+                                 kv_heads, rope_dim, self.max_positions, eps)
+        dev = wq.device
+        self.k_cache = torch.zeros(kv_heads, self.max_positions, 128, dtype=torch.float16, device=dev)
+        self.v_cache = torch.zeros_like(self.k_cache)
+        self.ws = torch.zeros(lib().mmrs_attn_workspace_bytes(C.byref(self.c)), dtype=torch.uint8, device=dev)
+        if self.ws.numel() == 0:
+            raise MoeError(MMRS_ERR_UNSUPPORTED, "mmrs_attn_workspace_bytes")
+
+    def forward(self, x, position: int, residual=None, y=None, stream=None):
+        """y [hidden] f32 = Wo . attention(x) (+ residual); appends the token's K / V at `position`."""
+        import torch
+        if y is None:
+            y = torch.empty_like(x)
+        rc = lib().mmrs_attn_decode_forward(C.byref(self.c), x.data_ptr(), _ptr(residual), position,
+                                            self.k_cache.data_ptr(), self.v_cache.data_ptr(), y.data_ptr(),
+                                            self.ws.data_ptr(), self.ws.numel(), _stream(stream))
+        check(rc, "mmrs_attn_decode_forward")
+        return y
