@@ -372,6 +372,104 @@ def run_config0(pkg, synth, dev, args) -> dict:
     return out
 
 
+C3_POS = 8191  # configs[3]: the token attends to an 8192-position KV cache
+C3_SEED = 3001
+
+
+def run_config3(pkg, synth, dev, args) -> dict:
+    """one T = 1 decoder layer: attn_norm -> attention (Q8_0 Q/K/V/O, Q/K RMSNorm,
+    partial RoPE, GQA over an 8192-position f16 KV cache) + residual -> ffn_norm -> MoE block
+    (configs[1] weights) + residual.  Four layers rotate (4 x ~152 MB per step, larger than L2);
+    steps are replayed from CUDA graphs.  The attention half is also timed alone."""
+    import torch
+    NL, qr, kr = 4, 48 * 128, 8 * 128
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(C3_SEED)
+
+    def q8_0(rows, k):  # GGUF Q8_0 blocks: half d = |N(0,1)| * 0.01, 32 uniform int8
+        nb = k // 32
+        b = torch.randint(-128, 128, (rows, nb, 34), dtype=torch.int16, device=dev, generator=gen)
+        b = b.to(torch.int8).view(torch.uint8)
+        d = (torch.randn(rows, nb, device=dev, generator=gen).abs() * 0.01).half()
+        b[:, :, :2] = d.view(torch.uint8).reshape(rows, nb, 2)
+        return b.reshape(-1).contiguous()
+
+    def normw(n):
+        return (1.0 + 0.1 * torch.randn(n, device=dev, generator=gen)).float()
+
+    cos, sin = synth.rope_tables(C3_POS + 1, 64)
+    cos_t, sin_t = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
+    attn, an, fn = [], [], []
+    for _ in range(NL):
+        L = pkg.AttnLayer(q8_0(qr, H), q8_0(kr, H), q8_0(kr, H), q8_0(H, qr), normw(qr), normw(kr), cos_t, sin_t, H)
+        L.k_cache.normal_(generator=gen)
+        L.v_cache.normal_(generator=gen)
+        attn.append(L)
+        an.append(normw(H))
+        fn.append(normw(H))
+    moe = build_layers(pkg, synth, dev, NL)
+    for m in moe:
+        m.workspace(1)
+    xs = torch.randn(NL, H, device=dev, generator=gen)
+    n1, h, n2, y = (torch.empty(H, device=dev) for _ in range(4))
+    stream = torch.cuda.Stream(device=dev)
+
+    def layer_step(i):
+        l = i % NL
+        pkg.rmsnorm(xs[l], an[l], y=n1, stream=stream)
+        attn[l].forward(n1, C3_POS, residual=xs[l], y=h, stream=stream)
+        pkg.rmsnorm(h, fn[l], y=n2, stream=stream)
+        moe[l].forward(n2.view(1, H), residual=h.view(1, H), y=y.view(1, H), stream=stream)
+
+    def attn_step(i):
+        l = i % NL
+        attn[l].forward(n1, C3_POS, residual=xs[l], y=h, stream=stream)
+
+    def timed(step, reps=25, per_graph=8):
+        with torch.cuda.stream(stream):
+            for i in range(per_graph):
+                step(i)
+            stream.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(per_graph):
+                    step(i)
+            for _ in range(3):
+                g.replay()
+            stream.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+            e1.synchronize()
+        del g
+        return e0.elapsed_time(e1) / (reps * per_graph)
+
+    ms_attn = timed(attn_step)
+    with ClockSampler(0) as clk:
+        ms = timed(layer_step)
+    for m in moe:
+        assert m.status() == 0, "device-side timeout in configs[3]"
+    peaks = measured_peaks()
+    attn_w = (qr * H + 2 * kr * H + H * qr) * 34 // 32  # Q8_0: 34 bytes per 32 weights
+    kv = 2 * 8 * (C3_POS + 1) * 128 * 2
+    alg = attn_w + kv + algorithmic_bytes() + 4 * H * 4  # + the two norms' reads and writes
+    out = {"metric": "decoder_layer_decode_tokens_per_s", "value": 1.0 / (ms / 1e3), "unit": "tokens/s",
+           "ms_per_step": ms, "attention_ms_per_step": ms_attn,
+           "config": {"workload": "T=1 decoder layer (BASELINE configs[3]): attn_norm, Q8_0 attention over an 8192-"
+                                  "position f16 KV cache, ffn_norm, configs[1] MoE block", "layers_rotated": NL,
+                      "kv_positions": C3_POS + 1, "graph_steps": 8, "data": "synthetic (seeded torch generator)"},
+           "roofline": {"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                        "frac": alg / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], "algorithmic_bytes_per_step": alg,
+                        "attention_bytes_per_step": attn_w + kv,
+                        "attention_frac": (attn_w + kv) / (ms_attn / 1e3) / 1e9 / peaks["hbm_gbs"]},
+           "clocks": clk.summary()}
+    del attn, moe
+    torch.cuda.empty_cache()
+    return out
+
+
 def ar_sweep(group, world: int, dev, iters: int = 50) -> dict:
     """Hidden-state all-reduce over T x 3072 f32 (T = 1, 8, 64, 512, 2048): the peer exchange of
     this library (rank-ordered sum, residual fused) and NCCL's all_reduce for comparison.
@@ -470,6 +568,7 @@ def main():
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=2000)
+    ap.add_argument("--no-config3", action="store_true", help="skip the configs[3] decoder-layer line")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill-steps", type=int, default=40)
@@ -647,6 +746,7 @@ def main():
     prefill = None if args.no_prefill else run_prefill(pkg, synth, dev, args, rank, world, group)
     allreduce = ar_sweep(group, world, dev) if world > 1 and not args.no_ar_sweep else None
     config0 = run_config0(pkg, synth, dev, args) if world == 1 and not args.no_prefill else None
+    config3 = run_config3(pkg, synth, dev, args) if world == 1 and not args.no_config3 else None
 
     if rank == 0:
         out = {
@@ -674,6 +774,7 @@ def main():
             "prefill": prefill,
             "allreduce_sweep": allreduce,
             "config0": config0,
+            "config3": config3,
         }
         print(json.dumps(out), flush=True)
     if world > 1:

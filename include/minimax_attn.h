@@ -61,6 +61,12 @@ MMRS_API void launch_gqa_decode_mma_f16_128(const void *q, const void *k, const 
                                             int num_splits, int query_heads, int kv_heads, float scale,
                                             int device_ordinal, void *stream);
 
+/* No counterpart as a launcher in the reference (candle-nn RmsNorm, used for attn_norm / ffn_norm,
+ * src/model.rs:198-210): y[r] = x[r] / sqrt(mean(x[r]^2) + eps) * weight for `rows` rows of n
+ * floats.  Returns an MMRS status. */
+MMRS_API int mmrs_rmsnorm_f32(const float *x, const float *weight, float *y, int n, int rows, float eps,
+                              mmrs_stream_t stream);
+
 /* ---- fused single-token attention half of a layer --------------------------------------- */
 
 typedef struct {

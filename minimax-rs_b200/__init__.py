@@ -71,6 +71,7 @@ PROTOTYPES = {
     "launch_partial_rope_f16": (None, [_VP] * 5 + [_I] * 5 + [_VP]),
     "launch_gqa_decode_mma_f16_128": (None, [_VP] * 5 + [_I] * 7 + [_F, _I, _VP]),
     "mmrs_attn_workspace_bytes": (_SZ, [C.POINTER(MmrsAttnWeights)]),
+    "mmrs_rmsnorm_f32": (_I, [_VP, _VP, _VP, _I, _I, _F, _VP]),
     "mmrs_attn_decode_forward": (_I, [C.POINTER(MmrsAttnWeights), _VP, _VP, _I, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "launch_tp2_peer_all_reduce_f32": (None, [_VP] * 8 + [C.c_uint, _I, _F, _VP]),
     "launch_tp2_peer_broadcast_f32": (None, [_VP] * 4 + [C.c_uint, _I, _I, _VP]),
@@ -265,3 +266,14 @@ class AttnLayer:
                                             self.ws.data_ptr(), self.ws.numel(), _stream(stream))
         check(rc, "mmrs_attn_decode_forward")
         return y
+
+
+def rmsnorm(x, weight, y=None, eps: float = 1e-6, stream=None):
+    """y = x / sqrt(mean(x^2) + eps) * weight over the last dimension (CUDA f32 tensors)."""
+    import torch
+    if y is None:
+        y = torch.empty_like(x)
+    n = x.shape[-1]
+    check(lib().mmrs_rmsnorm_f32(x.data_ptr(), weight.data_ptr(), y.data_ptr(), n, x.numel() // n, eps,
+                                 _stream(stream)), "mmrs_rmsnorm_f32")
+    return y

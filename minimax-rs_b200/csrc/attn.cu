@@ -301,10 +301,14 @@ __global__ void __launch_bounds__(128) gqa_decode_kernel(const GqaParams p) {
 #pragma unroll
             for (int h = 0; h < kAttnGroup; ++h) s2[h] = make_float2(0.0f, 0.0f);
             if (valid) {
+                // the lane's whole K row in flight at once (16 x 16 B)
                 const uint4 *kr = reinterpret_cast<const uint4 *>(kh + (long)(base + lane) * kAttnHeadDim);
-#pragma unroll 4
+                uint4 krow[kAttnHeadDim / 8];
+#pragma unroll
+                for (int i = 0; i < kAttnHeadDim / 8; ++i) krow[i] = __ldg(kr + i);
+#pragma unroll
                 for (int i = 0; i < kAttnHeadDim / 8; ++i) {
-                    const uint4 kv = __ldg(kr + i);
+                    const uint4 kv = krow[i];
                     const float2 k01 = h2f2(kv.x), k23 = h2f2(kv.y), k45 = h2f2(kv.z), k67 = h2f2(kv.w);
 #pragma unroll
                     for (int h = 0; h < kAttnGroup; ++h) {
@@ -341,16 +345,25 @@ __global__ void __launch_bounds__(128) gqa_decode_kernel(const GqaParams p) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) acc[h][j] *= alpha;
         }
-        for (int j = 0; j < nvalid; ++j) {
-            const uint2 vv = __ldg(reinterpret_cast<const uint2 *>(vh + (long)(base + j) * kAttnHeadDim) + lane);
-            const float2 v01 = h2f2(vv.x), v23 = h2f2(vv.y);
+        // P.V in batches of 8 keys, the batch's V loads issued before its arithmetic
+        for (int j0 = 0; j0 < nvalid; j0 += 8) {
+            uint2 vv[8];
 #pragma unroll
-            for (int h = 0; h < kAttnGroup; ++h) {
-                const float pj = __shfl_sync(0xffffffffu, pr[h], j);
-                acc[h][0] = fmaf(pj, v01.x, acc[h][0]);
-                acc[h][1] = fmaf(pj, v01.y, acc[h][1]);
-                acc[h][2] = fmaf(pj, v23.x, acc[h][2]);
-                acc[h][3] = fmaf(pj, v23.y, acc[h][3]);
+            for (int u = 0; u < 8; ++u)
+                vv[u] = j0 + u < nvalid
+                            ? __ldg(reinterpret_cast<const uint2 *>(vh + (long)(base + j0 + u) * kAttnHeadDim) + lane)
+                            : make_uint2(0u, 0u);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float2 v01 = h2f2(vv[u].x), v23 = h2f2(vv[u].y);
+#pragma unroll
+                for (int h = 0; h < kAttnGroup; ++h) {
+                    const float pj = __shfl_sync(0xffffffffu, pr[h], (j0 + u) & 31);  // 0 past nvalid
+                    acc[h][0] = fmaf(pj, v01.x, acc[h][0]);
+                    acc[h][1] = fmaf(pj, v01.y, acc[h][1]);
+                    acc[h][2] = fmaf(pj, v23.x, acc[h][2]);
+                    acc[h][3] = fmaf(pj, v23.y, acc[h][3]);
+                }
             }
         }
     }
@@ -476,9 +489,36 @@ static int qkv_launch(const void *x, void *vy, const void *vq, const void *vk, c
     return mv_launch<float>(p, s);
 }
 
+// Row RMSNorm of the hidden state (candle-nn RmsNorm, src/model.rs:198-210: attn_norm / ffn_norm):
+// y = x / sqrt(mean(x^2) + eps) * w, one CTA per row, fixed reduction order.
+__global__ void __launch_bounds__(1024) rmsnorm_rows_kernel(const float *__restrict__ x, const float *__restrict__ w,
+                                                            float *__restrict__ y, int n, float eps) {
+    __shared__ float ws[32];
+    const float *xr = x + (long)blockIdx.x * n;
+    float *yr = y + (long)blockIdx.x * n;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+    if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float t = (int)(threadIdx.x & 31) < (int)(blockDim.x >> 5) ? ws[threadIdx.x & 31] : 0.0f;
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) t += __shfl_xor_sync(0xffffffffu, t, m);
+    const float scale = rsqrtf(__fdiv_rn(t, (float)n) + eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) yr[i] = __fmul_rn(__fmul_rn(xr[i], scale), w[i]);
+}
+
 }  // namespace mmrs
 
 using namespace mmrs;
+
+extern "C" int mmrs_rmsnorm_f32(const float *x, const float *weight, float *y, int n, int rows, float eps,
+                                mmrs_stream_t stream) {
+    if (!x || !weight || !y || n <= 0 || rows <= 0) return MMRS_ERR_ARG;
+    rmsnorm_rows_kernel<<<rows, 1024, 0, (cudaStream_t)stream>>>(x, weight, y, n, eps);
+    return cudaGetLastError() == cudaSuccess ? MMRS_OK : MMRS_ERR_LAUNCH;
+}
 
 // ------------------------------------------------------------------------------------------
 // C ABI
@@ -665,13 +705,9 @@ extern "C" int mmrs_attn_decode_forward(const MmrsAttnWeights *w, const float *x
     r.kv_stride = head_stride;
     rc = rope_launch(r, s);
     if (rc != MMRS_OK) return rc;
-    // 3. attention over positions [0, position]: splits of >= 256 keys, about two CTAs per SM
+    // 3. attention over positions [0, position]: splits of 128 keys (one 32-key chunk per warp)
     const int seq = position + 1;
-    int sms = 148, dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int splits = std::max(1, std::min({(seq + 255) / 256, (2 * sms + w->kv_heads - 1) / w->kv_heads,
-                                             kAttnMaxSplits}));
+    const int splits = std::max(1, std::min((seq + 127) / 128, kAttnMaxSplits));
     GqaParams g = {};
     g.q = qrot;
     g.k = static_cast<const __half *>(k_cache);

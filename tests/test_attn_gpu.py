@@ -183,3 +183,14 @@ def test_fused_decode_steps_match_oracle(pkg, orc, dev):
         # the caches hold the rotated K and the V of every step so far
         assert _ulps(layer.k_cache[:, pos].cpu().numpy().view(np.uint16), kc[:, pos]).max() <= 2
         assert _ulps(layer.v_cache[:, pos].cpu().numpy().view(np.uint16), vc[:, pos]).max() <= 1
+
+
+def test_rmsnorm_rows(pkg, synth, dev):
+    import torch
+    x = synth.normal_f32(3 * 3072, 901, 1, 2.0).reshape(3, 3072)
+    w = (1.0 + synth.normal_f32(3072, 901, 2, 0.1)).astype(np.float32)
+    y = pkg.rmsnorm(torch.from_numpy(x).to(dev), torch.from_numpy(w).to(dev), eps=1e-6)
+    torch.cuda.synchronize()
+    x64 = x.astype(np.float64)
+    ref = x64 / np.sqrt(np.mean(x64 * x64, axis=1, keepdims=True) + 1e-6) * w
+    assert _rel(y.cpu().numpy(), ref) < 1e-6
