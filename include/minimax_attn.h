@@ -84,8 +84,13 @@ typedef struct {
     float eps;                /* RMSNorm epsilon (1e-6)                                        */
 } MmrsAttnWeights;
 
-/* Workspace bytes of mmrs_attn_decode_forward (caller-owned, no alignment beyond 256 needed). */
+/* Workspace bytes of mmrs_attn_decode_forward (caller-owned, 256-byte aligned, zero before first
+ * use: it holds per-KV-head split counters that every call leaves at zero, and a status word). */
 MMRS_API size_t mmrs_attn_workspace_bytes(const MmrsAttnWeights *w);
+
+/* Status word of a workspace after its calls completed (synchronous read): MMRS_OK, or
+ * MMRS_ERR_TIMEOUT when a bounded wait inside the attention kernel expired. */
+MMRS_API int mmrs_attn_workspace_status(const void *workspace);
 
 /* No single counterpart in the reference: Attention::forward for one token (src/model.rs:79-162)
  * as one call.  x f32 [hidden] (the attn_norm output); the token's rotated K and its V are

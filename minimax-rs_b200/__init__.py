@@ -71,6 +71,7 @@ PROTOTYPES = {
     "launch_partial_rope_f16": (None, [_VP] * 5 + [_I] * 5 + [_VP]),
     "launch_gqa_decode_mma_f16_128": (None, [_VP] * 5 + [_I] * 7 + [_F, _I, _VP]),
     "mmrs_attn_workspace_bytes": (_SZ, [C.POINTER(MmrsAttnWeights)]),
+    "mmrs_attn_workspace_status": (_I, [_VP]),
     "mmrs_rmsnorm_f32": (_I, [_VP, _VP, _VP, _I, _I, _F, _VP]),
     "mmrs_attn_decode_forward": (_I, [C.POINTER(MmrsAttnWeights), _VP, _VP, _I, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "launch_tp2_peer_all_reduce_f32": (None, [_VP] * 8 + [C.c_uint, _I, _F, _VP]),
@@ -255,6 +256,10 @@ class AttnLayer:
         self.ws = torch.zeros(lib().mmrs_attn_workspace_bytes(C.byref(self.c)), dtype=torch.uint8, device=dev)
         if self.ws.numel() == 0:
             raise MoeError(MMRS_ERR_UNSUPPORTED, "mmrs_attn_workspace_bytes")
+
+    def status(self) -> int:
+        """MMRS_OK, or MMRS_ERR_TIMEOUT when a bounded wait in the attention kernel expired."""
+        return lib().mmrs_attn_workspace_status(self.ws.data_ptr())
 
     def forward(self, x, position: int, residual=None, y=None, stream=None):
         """y [hidden] f32 = Wo . attention(x) (+ residual); appends the token's K / V at `position`."""

@@ -6,22 +6,29 @@
 // decode_attention.cu:311-918) and the Q8_0 output projection (QMatMul: quantize_q8_1 +
 // mmvq, mmvq_gguf.cu:1137-1200).
 //
-// All of it is memory-bound (Q8_0 weights 46.8 MB and the f16 KV cache per token), so the kernels
-// are dp4a / packed-f32 CUDA-core kernels that keep every byte moving once:
-//   * matvec: each CTA quantises the activation into shared memory, a warp owns a row and its
-//     lanes stride over the 34-byte Q8_0 blocks, read as aligned 32-bit words and realigned with
-//     funnel shifts (k % 64 == 0 keeps the last word of every block inside its row);
-//   * attention: CTA = (key split, KV head); a lane owns a key for Q.K (its 256-byte K row against
-//     the 6 query heads in shared memory), online softmax per warp, then a lane owns 4 dims for
-//     P.V (coalesced V rows); warps merge in shared memory; a combine kernel merges the splits.
+// All of it is memory-bound (Q8_0 weights 46.8 MB and the f16 KV cache per token).  The fused
+// forward is three launches chained by programmatic dependent launch:
+//   * Q8_0 matvec (dp4a): each CTA quantises the activation into shared memory (8 threads per
+//     32-block) and owns a contiguous range of rows, which it asks L2 to fetch before waiting for
+//     the previous kernel; a warp takes a row, its lanes stride over the 34-byte blocks read as
+//     aligned 32-bit words and realigned with funnel shifts (k % 64 == 0 keeps the last word of
+//     every block inside its row);
+//   * GQA decode on the tensor cores: CTA = (key split, KV head), K / V chunks streamed by TMA into
+//     128-byte-swizzled shared tiles, Q K^T and P V as mma.m16n8k16 with the 6 query heads as M;
+//     its prologue does the Q / K RMSNorm, RoPE and the KV append, the last CTA of a KV head merges
+//     the splits and writes the Q8_1 blocks the output projection reads;
+//   * the output projection (the matvec on ready Q8_1 blocks, + residual).
+// The reference-named launchers run the same kernels one operation at a time.
 #include <cuda_fp16.h>
 
 #include <algorithm>
 #include <cfloat>
 #include <mutex>
+#include <type_traits>
 
 #include "../../include/minimax_attn.h"
 #include "common.cuh"
+#include "tma.cuh"
 #include "workspace.cuh"
 
 namespace mmrs {
@@ -56,56 +63,91 @@ struct MvAct {
     float *d;
 };
 
-// Quantise x (f32 or f16) into shared memory (all threads of the CTA); optionally also store the
-// Q8_1 blocks in the reference's 36-byte layout (vy, zero-padded to kpad).
+// Quantise x (f32 or f16, zero past k) into shared memory, 8 threads per 32-block with 4 values
+// each; optionally also store the Q8_1 blocks in the reference's 36-byte layout (vy, kpad / 32
+// blocks).  amax and d are those of quantize_q8_1; the block sum pairs elements at distances 16,
+// 8, 4 (threads xor 4, 2, 1) then 2 and 1 (inside the thread), the order of lane 0 of the
+// reference's 32-lane butterfly, so the stored half sum is bit-identical.
 template <typename T>
-__device__ void mv_quantize(const T *__restrict__ x, int k, MvAct a, uint8_t *vy, int kpad) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int b = warp; b < kpad / 32; b += nw) {
-        const int i = b * 32 + lane;
-        const float v = i < k ? (float)x[i] : 0.0f;
-        float d, sum;
-        const int8_t q = q81_lane(v, d, sum);
-        if (b < k / 32) {  // k % 32 == 0: blocks past k are only padding of vy
-            a.q[i] = q;
-            if (lane == 0) a.d[b] = __half2float(__float2half_rn(d));
+__device__ void mv_quantize(const T *__restrict__ x, int k, int kpad, MvAct a, uint8_t *vy, int tid, int nthreads) {
+    const int nb = kpad / 32;
+    for (int base = 0; base < nb * 8; base += nthreads) {  // uniform trip count: shuffles stay converged
+        const int t = base + tid, b = t >> 3, j = t & 7, i0 = 32 * b + 4 * j;
+        float v[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) v[c] = (t < nb * 8 && i0 + c < k) ? (float)x[i0 + c] : 0.0f;
+        float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        const float d = __fdiv_rn(amax, 127.0f);
+        uint32_t packed = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int q = amax == 0.0f ? 0 : (int)roundf(__fdiv_rn(v[c], d));
+            packed |= (uint32_t)(q & 0xFF) << (8 * c);
         }
+        float sm[4] = {v[0], v[1], v[2], v[3]};
         if (vy) {
-            uint8_t *blk = vy + (size_t)b * 36;
-            blk[4 + lane] = (uint8_t)q;
-            if (lane == 0) {
-                const __half hd = __float2half_rn(d), hs = __float2half_rn(sum);
-                *reinterpret_cast<__half *>(blk) = hd;
-                *reinterpret_cast<__half *>(blk + 2) = hs;
+#pragma unroll
+            for (int m = 4; m > 0; m >>= 1)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) sm[c] += __shfl_xor_sync(0xffffffffu, sm[c], m);
+            sm[0] += sm[2];
+            sm[1] += sm[3];
+            sm[0] += sm[1];
+        }
+        if (t < nb * 8) {
+            *reinterpret_cast<uint32_t *>(a.q + i0) = packed;
+            if (j == 0) a.d[b] = __half2float(__float2half_rn(d));
+            if (vy) {
+                uint8_t *blk = vy + (size_t)b * 36;
+                *reinterpret_cast<uint32_t *>(blk + 4 + 4 * j) = packed;
+                if (j == 0)
+                    *reinterpret_cast<uint32_t *>(blk) =
+                        (uint32_t)__half_as_ushort(__float2half_rn(d)) |
+                        ((uint32_t)__half_as_ushort(__float2half_rn(sm[0])) << 16);
             }
         }
     }
 }
 
-// Dot of Q8_0 row `row` (nb blocks of 34 bytes, nb even) with the shared-memory activation; the
-// lanes of a warp stride over the blocks, the result is returned on every lane.
+// Dot of Q8_0 row `row` (nb blocks of 34 bytes, nb even) with the shared-memory activation; lane
+// l takes blocks l, l + 32, l + 64, ... (three blocks' words in flight before any arithmetic); the
+// result is returned on every lane.
+template <bool kShared = false>
 __device__ __forceinline__ float mv_row_dot(const uint8_t *__restrict__ row, int nb, MvAct a, int lane) {
     float acc = 0.0f;
-    for (int b = lane; b < nb; b += 32) {
-        // the block's 34 bytes from 9 aligned words: even b starts on a word, odd b two bytes in
-        const uint32_t *w = reinterpret_cast<const uint32_t *>(row + ((34 * b) & ~3));
-        uint32_t W[9];
+    for (int b0 = lane; b0 < nb; b0 += 96) {
+        // each block's 34 bytes from 9 aligned words: even b starts on a word, odd b two bytes in
+        uint32_t W[3][9];
 #pragma unroll
-        for (int i = 0; i < 9; ++i) W[i] = __ldg(w + i);
-        const bool odd = b & 1;
-        const uint32_t sh = odd ? 32u : 16u;
-        const float dw = __half2float(__ushort_as_half((unsigned short)((odd ? W[0] >> 16 : W[0]) & 0xFFFFu)));
-        const int4 *xq = reinterpret_cast<const int4 *>(a.q + 32 * b);
-        const int4 x0 = xq[0], x1 = xq[1];
-        const int xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-        int s0 = 0, s1 = 0;
+        for (int u = 0; u < 3; ++u) {
+            const int b = b0 + 32 * u;
+            const uint32_t *w = reinterpret_cast<const uint32_t *>(row + ((34 * b) & ~3));
 #pragma unroll
-        for (int i = 0; i < 8; i += 2) {
-            s0 = __dp4a((int)__funnelshift_rc(W[i], W[i + 1], sh), xv[i], s0);
-            s1 = __dp4a((int)__funnelshift_rc(W[i + 1], W[i + 2], sh), xv[i + 1], s1);
+            for (int i = 0; i < 9; ++i) W[u][i] = b < nb ? (kShared ? w[i] : __ldg(w + i)) : 0u;
         }
-        // vec_dot_q8_0_q8_1_impl (mmvq_gguf.cu:282-290): sumi * d_w * d_x
-        acc += __fmul_rn(__fmul_rn((float)(s0 + s1), dw), a.d[b]);
+#pragma unroll
+        for (int u = 0; u < 3; ++u) {
+            const int b = b0 + 32 * u;
+            if (b >= nb) break;
+            const bool odd = b & 1;
+            const uint32_t sh = odd ? 32u : 16u;
+            const float dw =
+                __half2float(__ushort_as_half((unsigned short)((odd ? W[u][0] >> 16 : W[u][0]) & 0xFFFFu)));
+            const int4 *xq = reinterpret_cast<const int4 *>(a.q + 32 * b);
+            const int4 x0 = xq[0], x1 = xq[1];
+            const int xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            int s0 = 0, s1 = 0;
+#pragma unroll
+            for (int i = 0; i < 8; i += 2) {
+                s0 = __dp4a((int)__funnelshift_rc(W[u][i], W[u][i + 1], sh), xv[i], s0);
+                s1 = __dp4a((int)__funnelshift_rc(W[u][i + 1], W[u][i + 2], sh), xv[i + 1], s1);
+            }
+            // vec_dot_q8_0_q8_1_impl (mmvq_gguf.cu:282-290): sumi * d_w * d_x
+            acc += __fmul_rn(__fmul_rn((float)(s0 + s1), dw), a.d[b]);
+        }
     }
 #pragma unroll
     for (int m = 16; m > 0; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
@@ -114,7 +156,10 @@ __device__ __forceinline__ float mv_row_dot(const uint8_t *__restrict__ row, int
 
 // One or more Q8_0 matrices sharing one activation: rows [0, n0) of w0, then n1 rows of w1, then
 // n2 rows of w2, into dst [n0 + n1 + n2] (+ residual when given).  The activation is x (f32 or
-// f16, quantised per CTA) or, with x == nullptr, ready Q8_1 blocks in vy_in.
+// f16, quantised per CTA) or, with x == nullptr, ready Q8_1 blocks in vy_in.  CTA i owns the
+// contiguous rows [i * total / grid, (i + 1) * total / grid), warps take every 8th of them.
+// Before waiting for the previous kernel (programmatic dependent launch) the CTA asks L2 to fetch
+// its weight rows, which do not depend on that kernel.
 struct MvParams {
     const uint8_t *w[3];
     int n[3];
@@ -125,31 +170,61 @@ struct MvParams {
     int kpad;
     const float *residual;
     float *dst;
+    uint32_t *status;  // optional: MMRS_ERR_TIMEOUT when a wait of the streaming kernel expired
 };
+
+__device__ __forceinline__ void mv_prefetch_rows(const uint8_t *w, long r0, long r1, size_t row_bytes) {
+    if (!w || r1 <= r0) return;
+    const uint8_t *p = w + r0 * row_bytes;
+    size_t bytes = (size_t)(r1 - r0) * row_bytes;
+    while (bytes >= 16) {
+        const uint32_t n = (uint32_t)std::min<size_t>(bytes, (size_t)1 << 20) & ~15u;
+        prefetch_l2_bulk(p, n);
+        p += n;
+        bytes -= n;
+    }
+}
+
+// Ready Q8_1 blocks (36 bytes, 4-byte aligned) into the shared activation.
+__device__ __forceinline__ void mv_copy_q81(const uint8_t *__restrict__ vy, int nb, MvAct a, int tid, int nthreads) {
+    for (int b = tid; b < nb; b += nthreads) {
+        const uint8_t *blk = vy + (size_t)b * 36;
+        a.d[b] = __half2float(*reinterpret_cast<const __half *>(blk));
+        const int *s32 = reinterpret_cast<const int *>(blk + 4);
+        int *d32 = reinterpret_cast<int *>(a.q + 32 * b);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) d32[i] = s32[i];
+    }
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kMvThreads) q8_0_matvec_kernel(const MvParams p) {
     extern __shared__ __align__(16) uint8_t mv_smem[];
     MvAct a{reinterpret_cast<int8_t *>(mv_smem), reinterpret_cast<float *>(mv_smem + p.kpad)};
     const int nb = p.k / 32;
+    const int total = p.n[0] + p.n[1] + p.n[2];
+    const int r0 = (int)((long)blockIdx.x * total / gridDim.x), r1 = (int)((long)(blockIdx.x + 1) * total / gridDim.x);
+    const size_t row_bytes = (size_t)nb * 34;
+    if (threadIdx.x == 0 && row_bytes % 16 == 0) {
+        // rows of matrix m inside [r0, r1), when the matrix base allows 16-byte bulk requests
+        const int e1 = p.n[0], e2 = p.n[0] + p.n[1];
+        if (!((uintptr_t)p.w[0] & 15u)) mv_prefetch_rows(p.w[0], r0, std::min(r1, e1), row_bytes);
+        if (p.n[1] && !((uintptr_t)p.w[1] & 15u))
+            mv_prefetch_rows(p.w[1], std::max(r0, e1) - e1, std::min(r1, e2) - e1, row_bytes);
+        if (p.n[2] && !((uintptr_t)p.w[2] & 15u))
+            mv_prefetch_rows(p.w[2], std::max(r0, e2) - e2, r1 - e2, row_bytes);
+    }
+    grid_dependency_wait();
+    launch_dependents();
     if (p.x) {
-        mv_quantize<T>(static_cast<const T *>(p.x), p.k, a, blockIdx.x == 0 ? p.vy_out : nullptr, p.kpad);
+        mv_quantize<T>(static_cast<const T *>(p.x), p.k, p.kpad, a, blockIdx.x == 0 ? p.vy_out : nullptr, threadIdx.x,
+                       blockDim.x);
     } else {
-        for (int b = threadIdx.x; b < nb; b += blockDim.x) {
-            const uint8_t *blk = p.vy_in + (size_t)b * 36;
-            a.d[b] = __half2float(*reinterpret_cast<const __half *>(blk));
-            // 36-byte blocks keep 4-byte alignment only: copy the quants as words
-            const int *s32 = reinterpret_cast<const int *>(blk + 4);
-            int *d32 = reinterpret_cast<int *>(a.q + 32 * b);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) d32[i] = s32[i];
-        }
+        mv_copy_q81(p.vy_in, nb, a, threadIdx.x, blockDim.x);
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int total = p.n[0] + p.n[1] + p.n[2];
-    const size_t row_bytes = (size_t)nb * 34;
-    for (int r = blockIdx.x * (kMvThreads / 32) + warp; r < total; r += gridDim.x * (kMvThreads / 32)) {
+    for (int r = r0 + warp; r < r1; r += kMvThreads / 32) {
         // matrix by comparison (indexing the parameter arrays would copy them to local memory)
         const bool m0 = r < p.n[0], m1 = !m0 && r < p.n[0] + p.n[1];
         const uint8_t *wm = m0 ? p.w[0] : (m1 ? p.w[1] : p.w[2]);
@@ -158,8 +233,228 @@ __global__ void __launch_bounds__(kMvThreads) q8_0_matvec_kernel(const MvParams 
         if (lane == 0) p.dst[r] = p.residual ? v + p.residual[r] : v;
     }
 }
+__host__ __device__ inline size_t mv_smem_bytes(int kpad) { return (size_t)kpad + (size_t)(kpad / 32) * sizeof(float); }
 
-static size_t mv_smem_bytes(int kpad) { return (size_t)kpad + (size_t)(kpad / 32) * sizeof(float); }
+// ------------------------------------------------------------------------------------------
+// Streaming matvec on a ready Q8_1 activation (rows of 16-byte multiple length, 16-byte aligned
+// matrices): one CTA per SM owns a contiguous range of rows, cut into groups of whole rows of one
+// matrix (<= 16 KB each).  A producer warp streams the groups through a ring of 12 shared-memory
+// slots with bulk copies, the first 12 issued before waiting for the previous kernel, so the CTA's
+// bytes (about 180 KB for the Q / K / V projection) are requested at once.  NC consumer warps
+// load their lanes' activation blocks (lane + 32u) straight into registers, then take group j
+// when j % NC is theirs and dot its rows out of shared memory.
+// ------------------------------------------------------------------------------------------
+constexpr int kMsSlots = 12;
+constexpr int kMsSlotBytes = 16384;
+constexpr int kMsMaxGroups = 96;
+
+struct MsGroup {
+    const uint8_t *src;
+    int row0, rows;
+};
+
+static size_t ms_smem_bytes() {
+    return (size_t)kMsSlots * kMsSlotBytes + sizeof(MsGroup) * kMsMaxGroups + sizeof(uint64_t) * 2 * kMsSlots + 16;
+}
+
+// One row of a group in shared memory against the register activation; lane l takes blocks
+// l + 32u; the per-lane block order and the final butterfly are those of mv_row_dot.
+template <int NBL, bool kFull>
+__device__ __forceinline__ float ms_row_dot(const uint8_t *row, int nb, const int4 (&xa)[NBL][2],
+                                            const float (&xd)[NBL], int lane) {
+    uint32_t W[NBL][9];
+#pragma unroll
+    for (int u = 0; u < NBL; ++u) {
+        const int b = lane + 32 * u;
+        const uint32_t *w = reinterpret_cast<const uint32_t *>(row + ((34 * b) & ~3));
+#pragma unroll
+        for (int i = 0; i < 9; ++i) W[u][i] = (kFull || b < nb) ? w[i] : 0u;
+    }
+    float acc = 0.0f;
+#pragma unroll
+    for (int u = 0; u < NBL; ++u) {
+        const int b = lane + 32 * u;
+        if (!kFull && b >= nb) break;
+        const bool odd = b & 1;
+        const uint32_t sh = odd ? 32u : 16u;
+        const float dw = __half2float(__ushort_as_half((unsigned short)((odd ? W[u][0] >> 16 : W[u][0]) & 0xFFFFu)));
+        const int xv[8] = {xa[u][0].x, xa[u][0].y, xa[u][0].z, xa[u][0].w, xa[u][1].x, xa[u][1].y, xa[u][1].z, xa[u][1].w};
+        int s0 = 0, s1 = 0;
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+            s0 = __dp4a((int)__funnelshift_rc(W[u][i], W[u][i + 1], sh), xv[i], s0);
+            s1 = __dp4a((int)__funnelshift_rc(W[u][i + 1], W[u][i + 2], sh), xv[i + 1], s1);
+        }
+        acc += __fmul_rn(__fmul_rn((float)(s0 + s1), dw), xd[u]);
+    }
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+    return acc;
+}
+
+template <int NBL, int NC, bool kFull>
+__global__ void __launch_bounds__(32 * (NC + 1), 1) q8_0_matvec_stream_kernel(const MvParams p) {
+    extern __shared__ __align__(128) uint8_t ms_smem[];
+    uint8_t *slots = ms_smem;
+    MsGroup *groups = reinterpret_cast<MsGroup *>(ms_smem + (size_t)kMsSlots * kMsSlotBytes);
+    uint64_t *full = reinterpret_cast<uint64_t *>(groups + kMsMaxGroups);
+    uint64_t *empty = full + kMsSlots;
+    int *ngroups = reinterpret_cast<int *>(empty + kMsSlots);
+    const int nb = p.k / 32, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int total = p.n[0] + p.n[1] + p.n[2];
+    const int r0 = (int)((long)blockIdx.x * total / gridDim.x), r1 = (int)((long)(blockIdx.x + 1) * total / gridDim.x);
+    const size_t row_bytes = (size_t)nb * 34;
+    const int per = std::max(1, (int)(kMsSlotBytes / row_bytes));
+    const uint64_t deadline = globaltimer_ns() + 2000000000ull;
+    if (threadIdx.x == NC * 32) {
+        // groups: whole rows of one matrix, at most `per` of them
+        const int e1 = p.n[0], e2 = p.n[0] + p.n[1];
+        int ng = 0;
+        for (int r = r0; r < r1 && ng < kMsMaxGroups;) {
+            const int m = r < e1 ? 0 : (r < e2 ? 1 : 2);
+            const int base = m == 0 ? 0 : (m == 1 ? e1 : e2), lim = m == 0 ? e1 : (m == 1 ? e2 : total);
+            const int end = std::min({r + per, r1, lim});
+            groups[ng].src = (m == 0 ? p.w[0] : (m == 1 ? p.w[1] : p.w[2])) + (size_t)(r - base) * row_bytes;
+            groups[ng].row0 = r;
+            groups[ng].rows = end - r;
+            ++ng;
+            r = end;
+        }
+        *ngroups = ng;
+        for (int i = 0; i < kMsSlots; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        fence_mbar_init();
+        for (int j = 0; j < ng && j < kMsSlots; ++j) {
+            const uint32_t bytes = (uint32_t)(groups[j].rows * row_bytes);
+            mbar_arrive_expect_tx(&full[j], bytes);
+            bulk_g2s(slots + (size_t)j * kMsSlotBytes, groups[j].src, bytes, &full[j]);
+        }
+    }
+    __syncthreads();
+    grid_dependency_wait();
+    launch_dependents();
+    const int ng = *ngroups;
+    if (warp == NC) {  // producer: refill slots as their groups are consumed
+        if (lane == 0) {
+            for (int j = kMsSlots; j < ng; ++j) {
+                const int st = j % kMsSlots;
+                if (!mbar_wait_sleep(&empty[st], (uint32_t)(((j / kMsSlots) - 1) & 1), deadline)) {
+                    if (p.status) atomicExch(p.status, (uint32_t)MMRS_ERR_TIMEOUT);
+                    break;
+                }
+                const uint32_t bytes = (uint32_t)(groups[j].rows * row_bytes);
+                mbar_arrive_expect_tx(&full[st], bytes);
+                bulk_g2s(slots + (size_t)st * kMsSlotBytes, groups[j].src, bytes, &full[st]);
+            }
+        }
+        return;
+    }
+    // this lane's activation blocks (lane + 32u), Q8_1 (half d, half sum, 32 int8), in registers
+    int4 xa[NBL][2];
+    float xd[NBL];
+#pragma unroll
+    for (int u = 0; u < NBL; ++u) {
+        const int b = lane + 32 * u;
+        const uint32_t *blk = reinterpret_cast<const uint32_t *>(p.vy_in + (size_t)b * 36);
+        uint32_t v[9];
+#pragma unroll
+        for (int i = 0; i < 9; ++i) v[i] = (kFull || b < nb) ? blk[i] : 0u;
+        xd[u] = __half2float(__ushort_as_half((unsigned short)(v[0] & 0xFFFFu)));
+        xa[u][0] = make_int4((int)v[1], (int)v[2], (int)v[3], (int)v[4]);
+        xa[u][1] = make_int4((int)v[5], (int)v[6], (int)v[7], (int)v[8]);
+    }
+    for (int j = warp; j < ng; j += NC) {
+        const int st = j % kMsSlots;
+        if (!mbar_wait_sleep(&full[st], (uint32_t)((j / kMsSlots) & 1), deadline)) {
+            if (lane == 0 && p.status) atomicExch(p.status, (uint32_t)MMRS_ERR_TIMEOUT);
+            break;
+        }
+        const uint8_t *g = slots + (size_t)st * kMsSlotBytes;
+        const MsGroup gr = groups[j];
+        for (int i = 0; i < gr.rows; ++i) {
+            const float v = ms_row_dot<NBL, kFull>(g + (size_t)i * row_bytes, nb, xa, xd, lane);
+            const int r = gr.row0 + i;
+            if (lane == 0) p.dst[r] = p.residual ? v + p.residual[r] : v;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+    }
+}
+
+// Q8_1 blocks of num_rows rows (mmvq_gguf.cu:1137-1169): warp per 32-block.  Runs after the
+// previous kernel completed (ordinary launch) and lets the next kernel, which streams weights that
+// do not depend on it, start at once.
+__global__ void __launch_bounds__(256) quantize_q8_1_rows_kernel(const float *__restrict__ x, uint8_t *__restrict__ vy,
+                                                                 int kx, int kx_padded, int num_rows) {
+    launch_dependents();
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int nb = kx_padded / 32;
+    if (warp >= nb * num_rows) return;
+    const int row = warp / nb, b = warp % nb, i = b * 32 + lane;
+    const float v = i < kx ? x[(long)row * kx + i] : 0.0f;
+    float d, sum;
+    const int8_t q = q81_lane(v, d, sum);
+    uint8_t *blk = vy + ((long)row * nb + b) * 36;
+    blk[4 + lane] = (uint8_t)q;
+    if (lane == 0) {
+        *reinterpret_cast<__half *>(blk) = __float2half_rn(d);
+        *reinterpret_cast<__half *>(blk + 2) = __float2half_rn(sum);
+    }
+}
+
+// Launch with the programmatic-serialization attribute: the kernel may start while the previous
+// kernel of the stream finishes (it waits for it before reading the activation).
+template <typename K, typename... Args>
+static cudaError_t launch_pdl(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+static int sm_count() {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+
+template <int NBL, int NC, bool kFull>
+static cudaError_t ms_launch(const MvParams &p, int grid, cudaStream_t s) {
+    static std::once_flag once[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::call_once(once[dev & 63], [] {
+        cudaFuncSetAttribute(q8_0_matvec_stream_kernel<NBL, NC, kFull>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)ms_smem_bytes());
+    });
+    return launch_pdl(q8_0_matvec_stream_kernel<NBL, NC, kFull>, dim3(grid), dim3(32 * (NC + 1)), ms_smem_bytes(), s, p);
+}
+
+// Blocks per lane 1..8 (k <= 8192); 16 consumer warps up to 3 blocks per lane (6 when every lane
+// has all its blocks), 8 above.
+template <bool kFull>
+static cudaError_t ms_dispatch(const MvParams &p, int grid, cudaStream_t s) {
+    switch ((p.k / 32 + 31) / 32) {
+        case 1: return ms_launch<1, 16, kFull>(p, grid, s);
+        case 2: return ms_launch<2, 16, kFull>(p, grid, s);
+        case 3: return ms_launch<3, 16, kFull>(p, grid, s);
+        case 4: return ms_launch<4, kFull ? 16 : 8, kFull>(p, grid, s);
+        case 5: return ms_launch<5, kFull ? 16 : 8, kFull>(p, grid, s);
+        case 6: return ms_launch<6, kFull ? 16 : 8, kFull>(p, grid, s);
+        case 7: return ms_launch<7, 8, kFull>(p, grid, s);
+        default: return ms_launch<8, 8, kFull>(p, grid, s);
+    }
+}
 
 template <typename T>
 static int mv_launch(const MvParams &p, cudaStream_t s) {
@@ -167,13 +462,32 @@ static int mv_launch(const MvParams &p, cudaStream_t s) {
     if (p.k <= 0 || p.k % 64 || p.k > kMvMaxK || p.kpad < p.k || p.kpad % 32 || total <= 0) return MMRS_ERR_ARG;
     for (int m = 0; m < 3; ++m)
         if (p.n[m] > 0 && (!p.w[m] || ((uintptr_t)p.w[m] & 3u))) return MMRS_ERR_ARG;
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int rows_per_cta = kMvThreads / 32;
-    const int blocks = std::min((total + rows_per_cta - 1) / rows_per_cta, sms * 8);
-    q8_0_matvec_kernel<T><<<blocks, kMvThreads, mv_smem_bytes(p.kpad), s>>>(p);
-    return cudaGetLastError() == cudaSuccess ? MMRS_OK : MMRS_ERR_LAUNCH;
+    const int sms = sm_count();
+    const size_t row_bytes = (size_t)(p.k / 32) * 34;
+    // the streaming kernel reads a ready Q8_1 activation: vy_in, or x quantised into vy_out first
+    bool stream = row_bytes % 16 == 0 && row_bytes <= (size_t)kMsSlotBytes && (p.vy_in || (p.x && p.vy_out)) &&
+                  (p.vy_in ? !((uintptr_t)p.vy_in & 3u) : !((uintptr_t)p.vy_out & 3u));
+    for (int m = 0; m < 3; ++m) stream = stream && (p.n[m] == 0 || !((uintptr_t)p.w[m] & 15u));
+    const int grid = std::min(sms, total);
+    const int per = stream ? std::max(1, (int)(kMsSlotBytes / row_bytes)) : 1;
+    stream = stream && (total / grid + 1 + per - 1) / per + 3 <= kMsMaxGroups;
+    cudaError_t e;
+    if (stream) {
+        MvParams q = p;
+        if (p.x) {  // activation -> Q8_1 once, then the matrices stream against it
+            const int nbp = p.kpad / 32;
+            quantize_q8_1_rows_kernel<<<(nbp * 32 + 255) / 256, 256, 0, s>>>(static_cast<const float *>(p.x), p.vy_out,
+                                                                            p.k, p.kpad, 1);
+            q.x = nullptr;
+            q.vy_in = p.vy_out;
+        }
+        e = (p.k / 32) % 32 == 0 ? ms_dispatch<true>(q, grid, s) : ms_dispatch<false>(q, grid, s);
+    } else {
+        const int rows_per_cta = kMvThreads / 32;
+        const int blocks = std::min((total + rows_per_cta - 1) / rows_per_cta, sms * 4);
+        e = launch_pdl(q8_0_matvec_kernel<T>, dim3(blocks), dim3(kMvThreads), mv_smem_bytes(p.kpad), s, p);
+    }
+    return e == cudaSuccess ? MMRS_OK : MMRS_ERR_LAUNCH;
 }
 
 // ------------------------------------------------------------------------------------------
@@ -252,155 +566,473 @@ __global__ void __launch_bounds__(256) partial_rope_kernel(const RopeParams p) {
 }
 
 // ------------------------------------------------------------------------------------------
-// Split-K GQA decode.  CTA = (split, KV head g), 4 warps; the split's keys [k0, k1) are walked
-// in 32-key chunks, chunk c by warp c % 4.  Q.K: lane = key, its K row (16 x 16 B) against the
-// 6 query heads held in shared memory (packed f32 FMAs); online softmax per warp and head; P.V:
-// lane = 4 dims, each key's probability broadcast by shuffle, V rows read coalesced.  The warps'
-// (max, sum, values) merge in shared memory into the split's partial per query head.
+// Split-K GQA decode on the tensor cores.  CTA = (split, KV head g), 4 warps; the split's keys are
+// 32-key chunks, chunk i of the split handled by warp i % 4 from stage i % 8 (two chunks in flight
+// per warp).  A stage holds the chunk's K and V rows as four TMA tiles of 32 keys x 64 dims (f16,
+// 128-byte rows, 128-byte swizzle: 16-byte column c of key r sits at column c ^ (r & 7)), so the
+// ldmatrix reads below are free of bank conflicts.  Rows past seq_len arrive as zeros.
+//   S = Q K^T: mma.m16n8k16 (f16 in, f32 accumulate) with the 6 query heads as M (rows 6-15 zero,
+//   Q in registers) and 8 keys as N, K fragments by ldmatrix;
+//   online softmax per head over the chunk; the probabilities, split into f16 hi + lo parts, are
+//   reused in registers as the A operands of
+//   O += P V: mma.m16n8k16 with keys as K and 8 dims as N, V fragments by ldmatrix.trans (the
+//   reference's tensor-core kernel rounds P to f16; the split keeps about 22 bits).
+// The warps' (max, sum, O) merge in shared memory into the split's partial per query head.
+// Fused mode (single-token layer forward): the prologue computes the Q / K RMSNorm scales from the
+// f32 projection, the group's 6 query heads normalised and rotated, and, in the split that holds
+// the new position, its rotated K and its V (written to the caches, and into the stage in place of
+// the row the TMA read); the last CTA of each KV head merges the splits and writes the attention
+// output in f16 and as Q8_1 blocks for the output projection.
 // ------------------------------------------------------------------------------------------
+constexpr int kGqWarps = 4;
+constexpr int kGqThreads = 32 * kGqWarps;
+constexpr int kGqStages = 2 * kGqWarps;
+constexpr int kGqTile = 32 * 128;  // bytes of one 32-key x 64-dim f16 tile
+constexpr int kGqStageBytes = 4 * kGqTile;  // K dims 0-63 | K dims 64-127 | V dims 0-63 | V dims 64-127
+
+struct GqSmem {
+    uint8_t stage[kGqStages][kGqStageBytes];
+    float wacc[kGqWarps][kAttnGroup][kAttnHeadDim];
+    __half qh[kAttnGroup][kAttnHeadDim];
+    __half qn[kAttnGroup][kAttnHeadDim];
+    __half newk[kAttnHeadDim], newkn[kAttnHeadDim], newv[kAttnHeadDim];
+    float wm[kGqWarps][8], wl[kGqWarps][8];
+    float red[2][kGqWarps];
+    float wts[kAttnGroup][kAttnMaxSplits];
+    float den[kAttnGroup];
+    uint64_t full[kGqStages];
+    uint64_t cbar;  // the combining CTA's bulk read of the split records
+    int last;
+};
+// Split record: plain mode [num_splits][query_heads][130] (max, sum, 128 values: the reference's
+// layout); fused mode [kv_heads][num_splits][6][132] (max, sum, 2 pad, 128 values), so that one
+// KV head's records are one contiguous, 16-byte aligned range for the combining CTA.
+constexpr int kGqRec = 132;
+constexpr int kGqMaxFusedSplits = kGqStages * kGqStageBytes / (kAttnGroup * kGqRec * 4);  // records fit the stages
+constexpr size_t kGqSmemBytes = sizeof(GqSmem) + 1024;  // + alignment of the swizzled stages
+
 struct GqaParams {
-    const __half *q, *k, *v;
-    float *partials;
-    int seq_len, q_head_stride, num_splits, query_heads;
-    long k_head_stride, v_head_stride;
+    // plain mode: q f16 [query_heads][q_head_stride] (normalised and rotated already)
+    const __half *q;
+    int q_head_stride;
+    // fused mode
+    const float *proj;  // f32 [q_rows + 2 k_rows] = [Wq x | Wk x | Wv x]
+    const float *q_norm, *k_norm, *cos, *sin;
+    float eps;
+    int rope_dim;
+    __half *k_cache, *v_cache;  // append target: head g at g * cache_head_stride, position at + pos * 128
+    long cache_head_stride;
+    uint32_t *tickets;  // [kv_heads], zero before first use, left zero
+    uint32_t *status;   // MMRS_ERR_TIMEOUT when a wait expired
+    __half *out;        // fused: attention output f16 [query_heads][128]
+    uint8_t *vy;        // fused: the same as Q8_1 blocks [query_heads * 4]
+    float *partials;    // [num_splits][query_heads][130]
+    int seq_len, num_splits, query_heads;
     float scale;
 };
 
-__device__ __forceinline__ float2 h2f2(uint32_t h) {
-    return __half22float2(*reinterpret_cast<const __half2 *>(&h));
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr)
+                 : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr)
+                 : "memory");
+}
+// D = A B + D, m16n8k16, A rows 8-15 zero (a1 = a3 = 0): only d0, d1 (row lane / 4) are carried.
+__device__ __forceinline__ void mma_rows8(float &d0, float &d1, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+    float e2 = 0.0f, e3 = 0.0f;
+    asm(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d0), "+f"(d1), "+f"(e2), "+f"(e3)
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+// Byte offset of 16-byte column c (0-15 over the 128 dims) of key r inside a K or V stage half.
+__device__ __forceinline__ uint32_t gq_swz(int r, int c) {
+    return (uint32_t)((c >> 3) * kGqTile + r * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
-__global__ void __launch_bounds__(128) gqa_decode_kernel(const GqaParams p) {
-    __shared__ __align__(16) float qs[kAttnGroup][kAttnHeadDim];
-    __shared__ float wm[4][kAttnGroup], wl[4][kAttnGroup];
-    __shared__ __align__(16) float wacc[4][kAttnGroup][kAttnHeadDim];
+template <bool kFused>
+__global__ void __launch_bounds__(kGqThreads, 1)
+    gqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                  const GqaParams p) {
+    extern __shared__ uint8_t gq_raw[];
+    GqSmem &sm = *reinterpret_cast<GqSmem *>((reinterpret_cast<uintptr_t>(gq_raw) + 1023) & ~uintptr_t(1023));
     const int split = blockIdx.x, g = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int k0 = (int)((long)p.seq_len * split / p.num_splits);
-    const int k1 = (int)((long)p.seq_len * (split + 1) / p.num_splits);
-    for (int i = tid; i < kAttnGroup * kAttnHeadDim; i += blockDim.x) {
-        const int h = i / kAttnHeadDim, d = i % kAttnHeadDim;
-        qs[h][d] = __half2float(p.q[(long)(g * kAttnGroup + h) * p.q_head_stride + d]);
+    const int seq = p.seq_len, pos = seq - 1;
+    const int nch = (seq + 31) / 32;
+    const int c0 = (int)((long)split * nch / p.num_splits), c1 = (int)((long)(split + 1) * nch / p.num_splits);
+    const int mine = c1 - c0;
+    const bool holds_pos = kFused && pos / 32 >= c0 && pos / 32 < c1;
+    auto issue = [&](int i) {
+        const int st = i % kGqStages, key0 = (c0 + i) * 32;
+        uint8_t *dst = sm.stage[st];
+        mbar_arrive_expect_tx(&sm.full[st], kGqStageBytes);
+        tma_load_3d(dst, &kmap, 0, key0, g, &sm.full[st]);
+        tma_load_3d(dst + kGqTile, &kmap, 64, key0, g, &sm.full[st]);
+        tma_load_3d(dst + 2 * kGqTile, &vmap, 0, key0, g, &sm.full[st]);
+        tma_load_3d(dst + 3 * kGqTile, &vmap, 64, key0, g, &sm.full[st]);
+    };
+    if (tid == 0) {
+        for (int i = 0; i < kGqStages; ++i) mbar_init(&sm.full[i], 1);
+        mbar_init(&sm.cbar, 1);
+        fence_mbar_init();
+        // the cached keys come from earlier launches: their loads start before the wait below
+        for (int i = 0; i < mine && i < kGqStages; ++i) issue(i);
+    }
+    grid_dependency_wait();
+    launch_dependents();
+    if constexpr (kFused) {
+        // every global value the prologue needs is requested before any arithmetic: the Q and K
+        // rows for the RMSNorm sums (q_rows <= 8192: at most 16 float4 per thread), the group's
+        // 6 heads with their norm weights and rotary entries, and head g's K / V row
+        const int qr = p.query_heads * kAttnHeadDim, kr = qr / kAttnGroup, half_rope = p.rope_dim / 2;
+        const float4 *p4 = reinterpret_cast<const float4 *>(p.proj);
+        float4 vq[16], vk[3];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+            const int i = tid + u * kGqThreads;
+            vq[u] = i < qr / 4 ? p4[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+#pragma unroll
+        for (int u = 0; u < 3; ++u) {
+            const int i = tid + u * kGqThreads;
+            vk[u] = i < kr / 4 ? p4[qr / 4 + i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        float pq[kAttnGroup], aq[kAttnGroup], cq6[kAttnGroup], sq6[kAttnGroup];
+#pragma unroll
+        for (int u = 0; u < kAttnGroup; ++u) {
+            const int e = tid + u * kGqThreads, col = e % kAttnHeadDim;
+            const int qi = g * kAttnGroup * kAttnHeadDim + e;
+            pq[u] = p.proj[qi];
+            aq[u] = p.q_norm[qi];
+            const int freq = col < half_rope ? col : col - half_rope;
+            const bool rot = col < p.rope_dim;
+            cq6[u] = rot ? p.cos[(long)pos * half_rope + freq] : 0.0f;
+            sq6[u] = rot ? p.sin[(long)pos * half_rope + freq] : 0.0f;
+        }
+        float pk = 0.0f, ak = 0.0f, pv = 0.0f, ck = 0.0f, sk1 = 0.0f;
+        if (holds_pos) {
+            const int ki = g * kAttnHeadDim + tid, freq = tid < half_rope ? tid : tid - half_rope;
+            pk = p.proj[qr + ki];
+            ak = p.k_norm[ki];
+            pv = p.proj[qr + kr + ki];
+            if (tid < p.rope_dim) {
+                ck = p.cos[(long)pos * half_rope + freq];
+                sk1 = p.sin[(long)pos * half_rope + freq];
+            }
+        }
+        // RMSNorm scales of all Q rows and all K rows (fixed order: per-thread chain, butterfly, warps)
+        float sq = 0.0f, sk = 0.0f;
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+            sq = fmaf(vq[u].x, vq[u].x, sq);
+            sq = fmaf(vq[u].y, vq[u].y, sq);
+            sq = fmaf(vq[u].z, vq[u].z, sq);
+            sq = fmaf(vq[u].w, vq[u].w, sq);
+        }
+#pragma unroll
+        for (int u = 0; u < 3; ++u) {
+            sk = fmaf(vk[u].x, vk[u].x, sk);
+            sk = fmaf(vk[u].y, vk[u].y, sk);
+            sk = fmaf(vk[u].z, vk[u].z, sk);
+            sk = fmaf(vk[u].w, vk[u].w, sk);
+        }
+#pragma unroll
+        for (int m = 16; m > 0; m >>= 1) {
+            sq += __shfl_xor_sync(0xffffffffu, sq, m);
+            sk += __shfl_xor_sync(0xffffffffu, sk, m);
+        }
+        if (lane == 0) {
+            sm.red[0][warp] = sq;
+            sm.red[1][warp] = sk;
+        }
+        __syncthreads();
+        const float tq = ((sm.red[0][0] + sm.red[0][1]) + sm.red[0][2]) + sm.red[0][3];
+        const float tk = ((sm.red[1][0] + sm.red[1][1]) + sm.red[1][2]) + sm.red[1][3];
+        const float scq = rsqrtf(__fdiv_rn(tq, (float)qr) + p.eps), sck = rsqrtf(__fdiv_rn(tk, (float)kr) + p.eps);
+        // qkv_rmsnorm_f16: f16(scale * v * alpha) for the group's 6 heads (and head g of K, V)
+#pragma unroll
+        for (int u = 0; u < kAttnGroup; ++u)
+            (&sm.qn[0][0])[tid + u * kGqThreads] = __float2half_rn(__fmul_rn(__fmul_rn(scq, pq[u]), aq[u]));
+        if (holds_pos) {
+            sm.newkn[tid] = __float2half_rn(__fmul_rn(__fmul_rn(sck, pk), ak));
+            sm.newv[tid] = __float2half_rn(pv);
+        }
+        __syncthreads();
+        // RoPE (partial_rope_kernel arithmetic) with the rotary entries already in registers
+#pragma unroll
+        for (int u = 0; u < kAttnGroup; ++u) {
+            const int e = tid + u * kGqThreads, h = e / kAttnHeadDim, col = e % kAttnHeadDim;
+            __half r = sm.qn[h][col];
+            if (col < p.rope_dim) {
+                const bool first = col < half_rope;
+                const __half c = __float2half_rn(cq6[u]), sn = __float2half_rn(sq6[u]);
+                const __half x = sm.qn[h][col], xp = sm.qn[h][first ? col + half_rope : col - half_rope];
+                r = first ? __hfma(x, c, __hneg(__hmul_rn(xp, sn))) : __hfma(xp, sn, __hmul_rn(x, c));
+            }
+            sm.qh[h][col] = r;
+        }
+        if (holds_pos) {
+            __half kv = sm.newkn[tid];
+            if (tid < p.rope_dim) {
+                const bool first = tid < half_rope;
+                const __half c = __float2half_rn(ck), sn = __float2half_rn(sk1);
+                const __half x = sm.newkn[tid], xp = sm.newkn[first ? tid + half_rope : tid - half_rope];
+                kv = first ? __hfma(x, c, __hneg(__hmul_rn(xp, sn))) : __hfma(xp, sn, __hmul_rn(x, c));
+            }
+            sm.newk[tid] = kv;
+            const long at = (long)g * p.cache_head_stride + (long)pos * kAttnHeadDim + tid;
+            p.k_cache[at] = kv;
+            p.v_cache[at] = sm.newv[tid];
+        }
+    } else {
+        for (int e = tid; e < kAttnGroup * kAttnHeadDim; e += kGqThreads) {
+            const int h = e / kAttnHeadDim, col = e % kAttnHeadDim;
+            sm.qh[h][col] = p.q[(long)(g * kAttnGroup + h) * p.q_head_stride + col];
+        }
     }
     __syncthreads();
-    const __half *kh = p.k + (long)g * p.k_head_stride, *vh = p.v + (long)g * p.v_head_stride;
-    float m[kAttnGroup], l[kAttnGroup], acc[kAttnGroup][4];
+    // Q as the A operand: row lane / 4 (query head of the group; rows 6-15 zero), dims of k-step s
+    const int gq = lane >> 2, cq = 2 * (lane & 3);
+    uint32_t qa0[8], qa2[8];
 #pragma unroll
-    for (int h = 0; h < kAttnGroup; ++h) {
-        m[h] = -INFINITY;
-        l[h] = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[h][j] = 0.0f;
+    for (int s8 = 0; s8 < 8; ++s8) {
+        qa0[s8] = gq < kAttnGroup ? *reinterpret_cast<const uint32_t *>(&sm.qh[gq][16 * s8 + cq]) : 0u;
+        qa2[s8] = gq < kAttnGroup ? *reinterpret_cast<const uint32_t *>(&sm.qh[gq][16 * s8 + 8 + cq]) : 0u;
     }
-    const int nchunks = (k1 - k0 + 31) / 32;
-    for (int c = warp; c < nchunks; c += 4) {
-        const int base = k0 + 32 * c, nvalid = min(32, k1 - base);
-        const bool valid = lane < nvalid;
-        float sc[kAttnGroup];
-        {
-            float2 s2[kAttnGroup];
+    float m_run = -INFINITY, l_run = 0.0f;
+    float o[16][2];
 #pragma unroll
-            for (int h = 0; h < kAttnGroup; ++h) s2[h] = make_float2(0.0f, 0.0f);
-            if (valid) {
-                // the lane's whole K row in flight at once (16 x 16 B)
-                const uint4 *kr = reinterpret_cast<const uint4 *>(kh + (long)(base + lane) * kAttnHeadDim);
-                uint4 krow[kAttnHeadDim / 8];
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = 0.0f;
+    const uint64_t deadline = globaltimer_ns() + 2000000000ull;
+    bool ok = true;
+    for (int i = warp; i < mine; i += kGqWarps) {
+        const int st = i % kGqStages;
+        if (!mbar_wait_sleep(&sm.full[st], (uint32_t)((i / kGqStages) & 1), deadline)) {
+            ok = false;
+            break;
+        }
+        uint8_t *sb = sm.stage[st];
+        const int key0 = (c0 + i) * 32, nvalid = min(32, seq - key0);
+        if (kFused && pos >= key0 && pos < key0 + 32) {  // the new position replaces the cached row
+            const uint32_t off = gq_swz(pos - key0, lane >> 1) + (lane & 1) * 8;
+            *reinterpret_cast<uint2 *>(sb + off) = *reinterpret_cast<const uint2 *>(&sm.newk[4 * lane]);
+            *reinterpret_cast<uint2 *>(sb + 2 * kGqTile + off) = *reinterpret_cast<const uint2 *>(&sm.newv[4 * lane]);
+            __syncwarp();
+        }
+        const uint32_t sbase = smem_u32(sb);
+        // S = Q K^T: n-tile t = keys 8t..8t+7; the lane holds head gq, keys 8t + cq + {0, 1}
+        float sc[4][2];
 #pragma unroll
-                for (int i = 0; i < kAttnHeadDim / 8; ++i) krow[i] = __ldg(kr + i);
+        for (int t = 0; t < 4; ++t) sc[t][0] = sc[t][1] = 0.0f;
 #pragma unroll
-                for (int i = 0; i < kAttnHeadDim / 8; ++i) {
-                    const uint4 kv = krow[i];
-                    const float2 k01 = h2f2(kv.x), k23 = h2f2(kv.y), k45 = h2f2(kv.z), k67 = h2f2(kv.w);
+        for (int kk = 0; kk < 4; ++kk) {  // k-steps 2kk, 2kk + 1 of the four n-tiles, independent mmas adjacent
+            uint32_t b[4][4];
 #pragma unroll
-                    for (int h = 0; h < kAttnGroup; ++h) {
-                        const float4 qa = *reinterpret_cast<const float4 *>(&qs[h][8 * i]);
-                        const float4 qb = *reinterpret_cast<const float4 *>(&qs[h][8 * i + 4]);
-                        s2[h].x = fmaf(k01.x, qa.x, s2[h].x);
-                        s2[h].y = fmaf(k01.y, qa.y, s2[h].y);
-                        s2[h].x = fmaf(k23.x, qa.z, s2[h].x);
-                        s2[h].y = fmaf(k23.y, qa.w, s2[h].y);
-                        s2[h].x = fmaf(k45.x, qb.x, s2[h].x);
-                        s2[h].y = fmaf(k45.y, qb.y, s2[h].y);
-                        s2[h].x = fmaf(k67.x, qb.z, s2[h].x);
-                        s2[h].y = fmaf(k67.y, qb.w, s2[h].y);
-                    }
-                }
+            for (int t = 0; t < 4; ++t)
+                ldsm_x4(sbase + gq_swz(8 * t + (lane & 7), 4 * kk + (lane >> 3)), b[t][0], b[t][1], b[t][2], b[t][3]);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) mma_rows8(sc[t][0], sc[t][1], qa0[2 * kk], qa2[2 * kk], b[t][0], b[t][1]);
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+                mma_rows8(sc[t][0], sc[t][1], qa0[2 * kk + 1], qa2[2 * kk + 1], b[t][2], b[t][3]);
+        }
+        // online softmax of head gq over the chunk (its 32 keys sit on the 4 lanes of the quad)
+        float mx = -INFINITY;
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                const float v = 8 * t + cq + c < nvalid ? sc[t][c] * p.scale : -INFINITY;
+                sc[t][c] = v;
+                mx = fmaxf(mx, v);
             }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float mn = fmaxf(m_run, mx);  // finite: key 0 of every chunk is valid
+        const float alpha = m_run == -INFINITY ? 0.0f : expf(m_run - mn);
+        // probabilities as f16 pairs hi + lo (hi = f16(p), lo = f16(p - hi)): two tensor-core
+        // products carry p to about 22 bits
+        uint32_t pa[4], pb[4];
+        float ps = 0.0f;
 #pragma unroll
-            for (int h = 0; h < kAttnGroup; ++h) sc[h] = valid ? (s2[h].x + s2[h].y) * p.scale : -INFINITY;
+        for (int t = 0; t < 4; ++t) {
+            const float p0 = expf(sc[t][0] - mn), p1 = expf(sc[t][1] - mn);
+            const __half2 ph = __floats2half2_rn(p0, p1);
+            const float2 pf = __half22float2(ph);
+            const __half2 pl = __floats2half2_rn(p0 - pf.x, p1 - pf.y);
+            pa[t] = *reinterpret_cast<const uint32_t *>(&ph);
+            pb[t] = *reinterpret_cast<const uint32_t *>(&pl);
+            ps += p0 + p1;
         }
-        float pr[kAttnGroup];
+        ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+        l_run = fmaf(l_run, alpha, ps);
+        m_run = mn;
 #pragma unroll
-        for (int h = 0; h < kAttnGroup; ++h) {
-            float cm = sc[h];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
-            const float mn = fmaxf(m[h], cm);  // finite: every chunk holds a valid key
-            const float alpha = m[h] == -INFINITY ? 0.0f : expf(m[h] - mn);
-            pr[h] = valid ? expf(sc[h] - mn) : 0.0f;
-            float ps = pr[h];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-            l[h] = l[h] * alpha + ps;
-            m[h] = mn;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) acc[h][j] *= alpha;
+        for (int n = 0; n < 16; ++n) {
+            o[n][0] *= alpha;
+            o[n][1] *= alpha;
         }
-        // P.V in batches of 8 keys, the batch's V loads issued before its arithmetic
-        for (int j0 = 0; j0 < nvalid; j0 += 8) {
-            uint2 vv[8];
+        // O += P V: k-step j = keys 16j..16j+15 (A = probabilities of n-tiles 2j, 2j + 1), n-tile = 8 dims
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
-                vv[u] = j0 + u < nvalid
-                            ? __ldg(reinterpret_cast<const uint2 *>(vh + (long)(base + j0 + u) * kAttnHeadDim) + lane)
-                            : make_uint2(0u, 0u);
+        for (int j = 0; j < 2; ++j) {
+            const int r = 16 * j + ((lane >> 3) & 1) * 8 + (lane & 7);
+            uint32_t b[8][4];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const float2 v01 = h2f2(vv[u].x), v23 = h2f2(vv[u].y);
+            for (int dp = 0; dp < 8; ++dp)
+                ldsm_x4_t(sbase + 2 * kGqTile + gq_swz(r, 2 * dp + (lane >> 4)), b[dp][0], b[dp][1], b[dp][2], b[dp][3]);
 #pragma unroll
-                for (int h = 0; h < kAttnGroup; ++h) {
-                    const float pj = __shfl_sync(0xffffffffu, pr[h], (j0 + u) & 31);  // 0 past nvalid
-                    acc[h][0] = fmaf(pj, v01.x, acc[h][0]);
-                    acc[h][1] = fmaf(pj, v01.y, acc[h][1]);
-                    acc[h][2] = fmaf(pj, v23.x, acc[h][2]);
-                    acc[h][3] = fmaf(pj, v23.y, acc[h][3]);
-                }
-            }
+            for (int n = 0; n < 16; ++n)
+                mma_rows8(o[n][0], o[n][1], pa[2 * j], pa[2 * j + 1], b[n >> 1][2 * (n & 1)], b[n >> 1][2 * (n & 1) + 1]);
+#pragma unroll
+            for (int n = 0; n < 16; ++n)
+                mma_rows8(o[n][0], o[n][1], pb[2 * j], pb[2 * j + 1], b[n >> 1][2 * (n & 1)], b[n >> 1][2 * (n & 1) + 1]);
         }
-    }
-    // merge the 4 warps: each publishes (m, l, acc), thread d combines dim d of every head
-    if (lane == 0) {
-#pragma unroll
-        for (int h = 0; h < kAttnGroup; ++h) {
-            wm[warp][h] = m[h];
-            wl[warp][h] = l[h];
+        __syncwarp();
+        if (i + kGqStages < mine && lane == 0) {  // refill the stage this warp just read
+            fence_proxy_async_smem();
+            issue(i + kGqStages);
         }
     }
+    if (!ok && p.status) atomicExch(p.status, (uint32_t)MMRS_ERR_TIMEOUT);
+    // merge the 4 warps: each publishes (m, l, O), thread d combines dim d of every head
+    if ((lane & 3) == 0 && gq < kAttnGroup) {
+        sm.wm[warp][gq] = m_run;
+        sm.wl[warp][gq] = l_run;
+    }
+    if (gq < kAttnGroup) {
 #pragma unroll
-    for (int h = 0; h < kAttnGroup; ++h)
-        *reinterpret_cast<float4 *>(&wacc[warp][h][4 * lane]) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+        for (int n = 0; n < 16; ++n)
+            *reinterpret_cast<float2 *>(&sm.wacc[warp][gq][8 * n + cq]) = make_float2(o[n][0], o[n][1]);
+    }
     __syncthreads();
-    const int d = tid;  // 128 threads = 128 dims
+    {
+        const int d = tid;  // 128 threads = 128 dims
 #pragma unroll
-    for (int h = 0; h < kAttnGroup; ++h) {
-        float M = -INFINITY;
+        for (int h = 0; h < kAttnGroup; ++h) {
+            float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w][h]);
-        float L = 0.0f, A = 0.0f;
-        if (M != -INFINITY) {
+            for (int w = 0; w < kGqWarps; ++w) M = fmaxf(M, sm.wm[w][h]);
+            float L = 0.0f, A = 0.0f;
+            if (M != -INFINITY) {
 #pragma unroll
-            for (int w = 0; w < 4; ++w) {
-                if (wm[w][h] == -INFINITY) continue;
-                const float e = expf(wm[w][h] - M);
-                L = fmaf(wl[w][h], e, L);
-                A = fmaf(wacc[w][h][d], e, A);
+                for (int w = 0; w < kGqWarps; ++w) {
+                    if (sm.wm[w][h] == -INFINITY) continue;
+                    const float e = expf(sm.wm[w][h] - M);
+                    L = fmaf(sm.wl[w][h], e, L);
+                    A = fmaf(sm.wacc[w][h][d], e, A);
+                }
             }
+            float *rec = kFused ? p.partials + ((long)(g * p.num_splits + split) * kAttnGroup + h) * kGqRec
+                                : p.partials + ((long)split * p.query_heads + g * kAttnGroup + h) * kAttnPartial;
+            if (d == 0) {
+                rec[0] = M == -INFINITY ? -FLT_MAX : M;
+                rec[1] = L;
+            }
+            rec[(kFused ? 4 : 2) + d] = A;
         }
-        float *rec = p.partials + ((long)split * p.query_heads + g * kAttnGroup + h) * kAttnPartial;
-        if (d == 0) {
-            rec[0] = M == -INFINITY ? -FLT_MAX : M;
-            rec[1] = L;
+    }
+    if constexpr (kFused) {
+        // the last CTA of KV head g merges the splits (gqa_combine_f16_128 arithmetic)
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            sm.last = atomicAdd(&p.tickets[g], 1u) == (uint32_t)(p.num_splits - 1);
         }
-        rec[2 + d] = A;
+        __syncthreads();
+        if (!sm.last) return;
+        __threadfence();
+        // the bulk read below sees the other CTAs' records and follows this CTA's reads of the stages
+        asm volatile("fence.proxy.async;" ::: "memory");
+        const int S = p.num_splits;
+        const float *cs = reinterpret_cast<const float *>(sm.stage[0]);
+        if (tid == 0) {
+            p.tickets[g] = 0u;
+            const uint32_t bytes = (uint32_t)(S * kAttnGroup * kGqRec * 4);
+            mbar_arrive_expect_tx(&sm.cbar, bytes);
+            bulk_g2s(sm.stage[0], p.partials + (long)g * S * kAttnGroup * kGqRec, bytes, &sm.cbar);
+        }
+        if (!mbar_wait_sleep(&sm.cbar, 0u, deadline)) {
+            if (tid == 0 && p.status) atomicExch(p.status, (uint32_t)MMRS_ERR_TIMEOUT);
+            return;
+        }
+        // weights exp(max_s - max) of the splits with a non-zero sum, and the denominator, per head
+        for (int h = warp; h < kAttnGroup; h += kGqWarps) {
+            float M = -FLT_MAX;
+            for (int s2 = lane; s2 < S; s2 += 32) M = fmaxf(M, cs[(s2 * kAttnGroup + h) * kGqRec]);
+#pragma unroll
+            for (int m = 16; m > 0; m >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, m));
+            float den = 0.0f;
+            for (int s2 = lane; s2 < S; s2 += 32) {
+                const float *rec = cs + (s2 * kAttnGroup + h) * kGqRec;
+                const float w = rec[1] == 0.0f ? 0.0f : expf(rec[0] - M);
+                sm.wts[h][s2] = w;
+                den = fmaf(rec[1], w, den);
+            }
+#pragma unroll
+            for (int m = 16; m > 0; m >>= 1) den += __shfl_xor_sync(0xffffffffu, den, m);
+            if (lane == 0) sm.den[h] = den;
+        }
+        __syncthreads();
+        // 6 heads x 32 four-dim items over 128 threads (warps 0-1 take a second item)
+        for (int idx = tid; idx < kAttnGroup * 32; idx += kGqThreads) {
+            const int h = idx >> 5, d4 = idx & 31, qh = g * kAttnGroup + h;
+            float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            for (int s2 = 0; s2 < S; ++s2) {
+                const float4 v = reinterpret_cast<const float4 *>(cs + (s2 * kAttnGroup + h) * kGqRec + 4)[d4];
+                const float w = sm.wts[h][s2];
+                acc.x = fmaf(v.x, w, acc.x);
+                acc.y = fmaf(v.y, w, acc.y);
+                acc.z = fmaf(v.z, w, acc.z);
+                acc.w = fmaf(v.w, w, acc.w);
+            }
+            const float dn = sm.den[h];
+            const __half2 h01 = __floats2half2_rn(__fdiv_rn(acc.x, dn), __fdiv_rn(acc.y, dn));
+            const __half2 h23 = __floats2half2_rn(__fdiv_rn(acc.z, dn), __fdiv_rn(acc.w, dn));
+            const long e = (long)qh * kAttnHeadDim + 4 * d4;
+            uint2 packed_h;
+            packed_h.x = *reinterpret_cast<const uint32_t *>(&h01);
+            packed_h.y = *reinterpret_cast<const uint32_t *>(&h23);
+            *reinterpret_cast<uint2 *>(p.out + e) = packed_h;
+            // Q8_1 of the f16 output for the output projection: 8 lanes hold one 32-block; amax / d /
+            // q as quantize_q8_1, the sum in the order of its lane-0 butterfly
+            const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+            float v[4] = {f01.x, f01.y, f23.x, f23.y};
+            float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+            float sm4[4] = {v[0], v[1], v[2], v[3]};
+#pragma unroll
+            for (int m = 4; m > 0; m >>= 1) {
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+#pragma unroll
+                for (int c = 0; c < 4; ++c) sm4[c] += __shfl_xor_sync(0xffffffffu, sm4[c], m);
+            }
+            sm4[0] += sm4[2];
+            sm4[1] += sm4[3];
+            sm4[0] += sm4[1];
+            const float d = __fdiv_rn(amax, 127.0f);
+            uint32_t packed = 0;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int q = amax == 0.0f ? 0 : (int)roundf(__fdiv_rn(v[c], d));
+                packed |= (uint32_t)(q & 0xFF) << (8 * c);
+            }
+            uint8_t *blk = p.vy + (e / 32) * 36;
+            *reinterpret_cast<uint32_t *>(blk + 4 + (e % 32)) = packed;
+            if ((d4 & 7) == 0)
+                *reinterpret_cast<uint32_t *>(blk) = (uint32_t)__half_as_ushort(__float2half_rn(d)) |
+                                                     ((uint32_t)__half_as_ushort(__float2half_rn(sm4[0])) << 16);
+        }
     }
 }
 
@@ -431,23 +1063,6 @@ __global__ void __launch_bounds__(128) gqa_combine_kernel(const float *__restric
     out[(long)qh * kAttnHeadDim + d] = __float2half_rn(__fdiv_rn(v, den));
 }
 
-// Q8_1 blocks of num_rows rows (mmvq_gguf.cu:1137-1169): warp per 32-block.
-__global__ void __launch_bounds__(256) quantize_q8_1_rows_kernel(const float *__restrict__ x, uint8_t *__restrict__ vy,
-                                                                 int kx, int kx_padded, int num_rows) {
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    const int nb = kx_padded / 32;
-    if (warp >= nb * num_rows) return;
-    const int row = warp / nb, b = warp % nb, i = b * 32 + lane;
-    const float v = i < kx ? x[(long)row * kx + i] : 0.0f;
-    float d, sum;
-    const int8_t q = q81_lane(v, d, sum);
-    uint8_t *blk = vy + ((long)row * nb + b) * 36;
-    blk[4 + lane] = (uint8_t)q;
-    if (lane == 0) {
-        *reinterpret_cast<__half *>(blk) = __float2half_rn(d);
-        *reinterpret_cast<__half *>(blk + 2) = __float2half_rn(sum);
-    }
-}
 
 static int rope_launch(const RopeParams &r, cudaStream_t s) {
     if (r.q_rows < 0 || r.k_rows < 0 || r.head_dim <= 0 || r.rope_dim < 0 || r.rope_dim > r.head_dim ||
@@ -459,20 +1074,54 @@ static int rope_launch(const RopeParams &r, cudaStream_t s) {
     return cudaGetLastError() == cudaSuccess ? MMRS_OK : MMRS_ERR_LAUNCH;
 }
 
-static int gqa_launch(const GqaParams &g, int kv_heads, __half *out, cudaStream_t s) {
-    if (!g.q || !g.k || !g.v || !g.partials || !out || g.seq_len < 1 || g.num_splits < 1 ||
+// Tensor map over an f16 KV cache: [heads][rows][128], head h at h * head_stride elements; box =
+// 64 dims x 32 positions of one head, 128-byte swizzle; rows past `rows` read as zeros.
+static int make_kv_map(CUtensorMap *map, const void *base, int rows, int heads, long head_stride) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return MMRS_ERR_LAUNCH;
+    cuuint64_t dims[3] = {(cuuint64_t)kAttnHeadDim, (cuuint64_t)rows, (cuuint64_t)heads};
+    cuuint64_t strides[2] = {(cuuint64_t)kAttnHeadDim * 2, (cuuint64_t)head_stride * 2};
+    cuuint32_t box[3] = {64, 32, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? MMRS_OK : MMRS_ERR_ARG;
+}
+
+static void gqa_smem_setup() {
+    static std::once_flag once[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::call_once(once[dev & 63], [] {
+        cudaFuncSetAttribute(gqa_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGqSmemBytes);
+        cudaFuncSetAttribute(gqa_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGqSmemBytes);
+    });
+}
+
+// Plain mode (launch_gqa_decode_mma_f16_128): the split kernel, then the combine kernel.
+static int gqa_launch(const GqaParams &g, int kv_heads, const __half *k, const __half *v, long k_head_stride,
+                      long v_head_stride, __half *out, cudaStream_t s) {
+    if (!g.q || !k || !v || !g.partials || !out || g.seq_len < 1 || g.num_splits < 1 ||
         g.num_splits > kAttnMaxSplits || kv_heads < 1 || g.query_heads != kAttnGroup * kv_heads ||
-        g.q_head_stride < kAttnHeadDim || g.k_head_stride < (long)g.seq_len * kAttnHeadDim ||
-        g.v_head_stride < (long)g.seq_len * kAttnHeadDim || ((uintptr_t)g.k & 15u) || ((uintptr_t)g.v & 15u) ||
-        (g.k_head_stride % 8) || (g.v_head_stride % 8))
+        g.q_head_stride < kAttnHeadDim || k_head_stride < (long)g.seq_len * kAttnHeadDim ||
+        v_head_stride < (long)g.seq_len * kAttnHeadDim || ((uintptr_t)k & 15u) || ((uintptr_t)v & 15u) ||
+        (k_head_stride % 8) || (v_head_stride % 8) || ((uintptr_t)g.q & 3u) || (g.q_head_stride % 2))
         return MMRS_ERR_ARG;
-    gqa_decode_kernel<<<dim3(g.num_splits, kv_heads), 128, 0, s>>>(g);
+    CUtensorMap kmap, vmap;
+    int rc = make_kv_map(&kmap, k, g.seq_len, kv_heads, k_head_stride);
+    if (rc == MMRS_OK) rc = make_kv_map(&vmap, v, g.seq_len, kv_heads, v_head_stride);
+    if (rc != MMRS_OK) return rc;
+    gqa_smem_setup();
+    if (launch_pdl(gqa_tc_kernel<false>, dim3(g.num_splits, kv_heads), dim3(kGqThreads), kGqSmemBytes, s, kmap, vmap,
+                   g) != cudaSuccess)
+        return MMRS_ERR_LAUNCH;
     gqa_combine_kernel<<<g.query_heads, 128, 0, s>>>(g.partials, out, g.num_splits, g.query_heads);
     return cudaGetLastError() == cudaSuccess ? MMRS_OK : MMRS_ERR_LAUNCH;
 }
 
 static int qkv_launch(const void *x, void *vy, const void *vq, const void *vk, const void *vv, float *proj, int kx,
-                      int kx_padded, int q_rows, int k_rows, int v_rows, cudaStream_t s) {
+                      int kx_padded, int q_rows, int k_rows, int v_rows, cudaStream_t s, uint32_t *status = nullptr) {
     if (!x || q_rows < 0 || k_rows < 0 || v_rows < 0) return MMRS_ERR_ARG;
     MvParams p = {};
     p.w[0] = static_cast<const uint8_t *>(vq);
@@ -486,6 +1135,7 @@ static int qkv_launch(const void *x, void *vy, const void *vq, const void *vk, c
     p.x = x;
     p.vy_out = static_cast<uint8_t *>(vy);
     p.dst = proj;
+    p.status = status;
     return mv_launch<float>(p, s);
 }
 
@@ -614,17 +1264,14 @@ extern "C" void launch_gqa_decode_mma_f16_128(const void *q, const void *k, cons
     (void)device_ordinal;  // no per-device kernel configuration is needed here
     GqaParams g = {};
     g.q = static_cast<const __half *>(q);
-    g.k = static_cast<const __half *>(k);
-    g.v = static_cast<const __half *>(v);
+    g.q_head_stride = q_head_stride;
     g.partials = static_cast<float *>(partials);
     g.seq_len = seq_len;
-    g.q_head_stride = q_head_stride;
-    g.k_head_stride = k_head_stride;
-    g.v_head_stride = v_head_stride;
     g.num_splits = num_splits;
     g.query_heads = query_heads;
     g.scale = scale;
-    record_error(gqa_launch(g, kv_heads, static_cast<__half *>(output), (cudaStream_t)stream));
+    record_error(gqa_launch(g, kv_heads, static_cast<const __half *>(k), static_cast<const __half *>(v), k_head_stride,
+                            v_head_stride, static_cast<__half *>(output), (cudaStream_t)stream));
 }
 
 // ------------------------------------------------------------------------------------------
@@ -632,7 +1279,7 @@ extern "C" void launch_gqa_decode_mma_f16_128(const void *q, const void *k, cons
 // ------------------------------------------------------------------------------------------
 namespace {
 struct AttnLayout {
-    size_t proj, qkv, qrot, part, out, total;
+    size_t proj, part, out, vy, xq, tickets, total;
 };
 AttnLayout attn_layout(const MmrsAttnWeights *w) {
     const size_t qr = (size_t)w->query_heads * kAttnHeadDim, kr = (size_t)w->kv_heads * kAttnHeadDim;
@@ -643,19 +1290,21 @@ AttnLayout attn_layout(const MmrsAttnWeights *w) {
         o = (o + b + 255) / 256 * 256;
         return at;
     };
+    l.tickets = take(sizeof(uint32_t) * (2 + (size_t)w->kv_heads));  // [0] status, [1] pad, then one per KV head
     l.proj = take(sizeof(float) * (qr + 2 * kr));
-    l.qkv = take(sizeof(__half) * (qr + 2 * kr));
-    l.qrot = take(sizeof(__half) * qr);
     l.part = take(sizeof(float) * kAttnMaxSplits * w->query_heads * kAttnPartial);
     l.out = take(sizeof(__half) * qr);
+    l.vy = take((qr / 32) * 36);
+    l.xq = take(((size_t)w->hidden / 32) * 36);
     l.total = o;
     return l;
 }
 int attn_validate(const MmrsAttnWeights *w) {
     if (!w || !w->wq || !w->wk || !w->wv || !w->wo || !w->q_norm || !w->k_norm || !w->rope_cos || !w->rope_sin)
         return MMRS_ERR_ARG;
-    if (w->hidden <= 0 || w->hidden % 64 || w->kv_heads < 1 || w->query_heads != kAttnGroup * w->kv_heads ||
-        w->rope_dim < 0 || w->rope_dim > kAttnHeadDim || w->rope_dim % 2 || w->max_positions < 1)
+    if (w->hidden <= 0 || w->hidden % 64 || w->hidden > kMvMaxK || w->kv_heads < 1 ||
+        w->query_heads != kAttnGroup * w->kv_heads || w->query_heads * kAttnHeadDim > kMvMaxK || w->rope_dim < 0 ||
+        w->rope_dim > kAttnHeadDim || w->rope_dim % 2 || w->max_positions < 1)
         return MMRS_ERR_UNSUPPORTED;
     return MMRS_OK;
 }
@@ -665,6 +1314,18 @@ extern "C" size_t mmrs_attn_workspace_bytes(const MmrsAttnWeights *w) {
     return attn_validate(w) == MMRS_OK ? attn_layout(w).total : 0;
 }
 
+extern "C" int mmrs_attn_workspace_status(const void *workspace) {
+    if (!workspace) return MMRS_ERR_ARG;
+    uint32_t st = 0;
+    if (cudaMemcpy(&st, workspace, sizeof(st), cudaMemcpyDeviceToHost) != cudaSuccess) return MMRS_ERR_LAUNCH;
+    return (int)st;
+}
+
+// Four launches, the last three allowed to start while their predecessor drains (programmatic
+// dependent launch): the activation to Q8_1; the Q / K / V matvec (its weights streamed into
+// shared memory before the wait); the GQA kernel in fused mode (cached K / V tiles requested
+// before the wait; norm, RoPE, append, split merge and the Q8_1 output inside); the output
+// projection on those Q8_1 blocks (+ residual).
 extern "C" int mmrs_attn_decode_forward(const MmrsAttnWeights *w, const float *x, const float *residual, int position,
                                         void *k_cache, void *v_cache, float *y, void *workspace,
                                         size_t workspace_bytes, mmrs_stream_t stream) {
@@ -679,57 +1340,52 @@ extern "C" int mmrs_attn_decode_forward(const MmrsAttnWeights *w, const float *x
     cudaStream_t s = (cudaStream_t)stream;
     uint8_t *ws = static_cast<uint8_t *>(workspace);
     float *proj = reinterpret_cast<float *>(ws + l.proj);
-    __half *qkv = reinterpret_cast<__half *>(ws + l.qkv), *qrot = reinterpret_cast<__half *>(ws + l.qrot);
-    __half *att = reinterpret_cast<__half *>(ws + l.out);
     const int qr = w->query_heads * kAttnHeadDim, kr = w->kv_heads * kAttnHeadDim;
     const long head_stride = (long)w->max_positions * kAttnHeadDim;
-    // 1. Q / K / V projection (one launch for the three matrices) and Q / K RMSNorm to f16
-    rc = qkv_launch(x, nullptr, w->wq, w->wk, w->wv, proj, w->hidden, w->hidden, qr, kr, kr, s);
+    // 1. Q / K / V projection (one launch for the three matrices)
+    uint32_t *status = reinterpret_cast<uint32_t *>(ws + l.tickets);
+    rc = qkv_launch(x, ws + l.xq, w->wq, w->wk, w->wv, proj, w->hidden, w->hidden, qr, kr, kr, s, status);
     if (rc != MMRS_OK) return rc;
-    qkv_rmsnorm_f16_kernel<<<3, 1024, 0, s>>>(proj, w->q_norm, w->k_norm, qkv, qr, kr, kr, w->eps);
-    // 2. rotary embedding of Q (into qrot) and K, K and V appended to the caches at `position`
-    RopeParams r = {};
-    r.q = qkv;
-    r.k = qkv + qr;
-    r.v = qkv + qr + kr;
-    r.cos = w->rope_cos;
-    r.sin = w->rope_sin;
-    r.q_out = qrot;
-    r.k_out = static_cast<__half *>(k_cache) + (long)position * kAttnHeadDim;
-    r.v_out = static_cast<__half *>(v_cache) + (long)position * kAttnHeadDim;
-    r.q_rows = qr;
-    r.k_rows = kr;
-    r.head_dim = kAttnHeadDim;
-    r.rope_dim = w->rope_dim;
-    r.position = position;
-    r.kv_stride = head_stride;
-    rc = rope_launch(r, s);
+    // 2. attention over positions [0, position]: about one CTA per SM, at least 4 chunks per split
+    const int seq = position + 1, nch = (seq + 31) / 32;
+    const int splits = std::max(1, std::min({sm_count() / w->kv_heads, (nch + 3) / 4, kGqMaxFusedSplits}));
+    CUtensorMap kmap, vmap;
+    rc = make_kv_map(&kmap, k_cache, seq, w->kv_heads, head_stride);
+    if (rc == MMRS_OK) rc = make_kv_map(&vmap, v_cache, seq, w->kv_heads, head_stride);
     if (rc != MMRS_OK) return rc;
-    // 3. attention over positions [0, position]: splits of 128 keys (one 32-key chunk per warp)
-    const int seq = position + 1;
-    const int splits = std::max(1, std::min((seq + 127) / 128, kAttnMaxSplits));
     GqaParams g = {};
-    g.q = qrot;
-    g.k = static_cast<const __half *>(k_cache);
-    g.v = static_cast<const __half *>(v_cache);
+    g.proj = proj;
+    g.q_norm = w->q_norm;
+    g.k_norm = w->k_norm;
+    g.cos = w->rope_cos;
+    g.sin = w->rope_sin;
+    g.eps = w->eps;
+    g.rope_dim = w->rope_dim;
+    g.k_cache = static_cast<__half *>(k_cache);
+    g.v_cache = static_cast<__half *>(v_cache);
+    g.cache_head_stride = head_stride;
+    g.status = status;
+    g.tickets = status + 2;
+    g.out = reinterpret_cast<__half *>(ws + l.out);
+    g.vy = ws + l.vy;
     g.partials = reinterpret_cast<float *>(ws + l.part);
     g.seq_len = seq;
-    g.q_head_stride = kAttnHeadDim;
-    g.k_head_stride = head_stride;
-    g.v_head_stride = head_stride;
     g.num_splits = splits;
     g.query_heads = w->query_heads;
     g.scale = 1.0f / sqrtf((float)kAttnHeadDim);
-    rc = gqa_launch(g, w->kv_heads, att, s);
-    if (rc != MMRS_OK) return rc;
-    // 4. output projection of the f16 attention output (+ residual)
+    gqa_smem_setup();
+    if (launch_pdl(gqa_tc_kernel<true>, dim3(splits, w->kv_heads), dim3(kGqThreads), kGqSmemBytes, s, kmap, vmap, g) !=
+        cudaSuccess)
+        return MMRS_ERR_LAUNCH;
+    // 3. output projection of the attention output's Q8_1 blocks (+ residual)
     MvParams o = {};
     o.w[0] = static_cast<const uint8_t *>(w->wo);
     o.n[0] = w->hidden;
     o.k = qr;
     o.kpad = qr;
-    o.x = att;
+    o.vy_in = ws + l.vy;
     o.residual = residual;
     o.dst = y;
-    return mv_launch<__half>(o, s);
+    o.status = status;
+    return mv_launch<float>(o, s);
 }

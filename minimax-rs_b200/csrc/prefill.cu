@@ -10,6 +10,7 @@
 #include <mutex>
 
 #include "prefill.cuh"
+#include "tma.cuh"
 
 namespace mmrs {
 
@@ -1052,18 +1053,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
 
 // Tensor map over the expert weights viewed as a 2-D array of 32-bit words:
 // [E * N rows][row_bytes / 4], box = one super-block (bb / 4 words) x 128 rows.
-static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *ptr = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-    });
-    return fn;
-}
 
 static int make_weight_map(CUtensorMap *map, const void *w, int gtype, long rows, int K) {
     auto enc = tensor_map_encoder();

@@ -140,7 +140,7 @@ def test_unsupported_batch_is_reported(pkg, dev):
     assert pkg.last_error() == pkg.MMRS_ERR_UNSUPPORTED
 
 
-def _layer(pkg, dev, hidden, seed):
+def _layer(pkg, dev, hidden, seed, max_pos=64):
     import torch
     S = G.S
     qr, kr = G.Q_ROWS, G.K_ROWS
@@ -148,7 +148,7 @@ def _layer(pkg, dev, hidden, seed):
              wv=S.q8_0_blocks(seed, 4, kr, hidden), wo=S.q8_0_blocks(seed, 5, hidden, qr),
              qn=(1.0 + S.normal_f32(qr, seed, 6, 0.1)).astype(np.float32),
              kn=(1.0 + S.normal_f32(kr, seed, 7, 0.1)).astype(np.float32))
-    cos, sin = S.rope_tables(64, G.ROT)
+    cos, sin = S.rope_tables(max_pos, G.ROT)
     t = {k: torch.from_numpy(v).to(dev) for k, v in w.items()}
     layer = pkg.AttnLayer(t["wq"], t["wk"], t["wv"], t["wo"], t["qn"], t["kn"], torch.from_numpy(cos).to(dev),
                           torch.from_numpy(sin).to(dev), hidden)
@@ -183,6 +183,49 @@ def test_fused_decode_steps_match_oracle(pkg, orc, dev):
         # the caches hold the rotated K and the V of every step so far
         assert _ulps(layer.k_cache[:, pos].cpu().numpy().view(np.uint16), kc[:, pos]).max() <= 2
         assert _ulps(layer.v_cache[:, pos].cpu().numpy().view(np.uint16), vc[:, pos]).max() <= 1
+
+
+def _oracle_step(orc, w, x, res, kc, vc, cos, sin, pos, hidden):
+    qr, kr = G.Q_ROWS, G.K_ROWS
+    proj = np.concatenate([orc.q8_0_matvec(w["wq"], qr, hidden, x), orc.q8_0_matvec(w["wk"], kr, hidden, x),
+                           orc.q8_0_matvec(w["wv"], kr, hidden, x)])
+    nrm = orc.qkv_rmsnorm_f16(proj, w["qn"], w["kn"], qr, kr, kr, 1e-6)
+    rot = orc.partial_rope_f16(nrm[:qr], nrm[qr:qr + kr], cos, sin, G.HD, G.ROT, pos)
+    kc[:, pos] = rot[qr:].reshape(G.KVH, G.HD)
+    vc[:, pos] = nrm[qr + kr:].reshape(G.KVH, G.HD)
+    att = orc.gqa_decode_f16(rot[:qr], kc, vc, pos + 1, G.QH, G.KVH, G.HD, kc.shape[1] * G.HD, 1.0 / math.sqrt(G.HD))
+    return orc.q8_0_matvec(w["wo"], hidden, qr, _f16(att).astype(np.float32)) + res
+
+
+@pytest.mark.parametrize("pos", [700, 1023])
+def test_fused_decode_long_cache(pkg, orc, dev, pos):
+    """A step at a late position over a filled cache: several key splits merged by the last CTA of
+    each KV head, the new position inside a chunk (700) or closing the cache (1023).  The step runs
+    twice: the split counters return to zero, so the second result is identical."""
+    import torch
+    hidden, seed, cap = G.ATTN_H, 811, 1024
+    layer, w, cos, sin = _layer(pkg, dev, hidden, seed, max_pos=cap)
+    kc = G.S.normal_f16(G.KVH * cap * G.HD, seed, 10, 1.0).reshape(G.KVH, cap, G.HD).view(np.uint16).copy()
+    vc = G.S.normal_f16(G.KVH * cap * G.HD, seed, 11, 1.0).reshape(G.KVH, cap, G.HD).view(np.uint16).copy()
+    layer.k_cache.copy_(torch.from_numpy(kc.view(np.float16)))
+    layer.v_cache.copy_(torch.from_numpy(vc.view(np.float16)))
+    x = G.S.normal_f32(hidden, seed, 8, 1.0)
+    res = G.S.normal_f32(hidden, seed, 9, 1.0)
+    xd, rd = torch.from_numpy(x).to(dev), torch.from_numpy(res).to(dev)
+    y1 = layer.forward(xd, pos, residual=rd).cpu().numpy()
+    y2 = layer.forward(xd, pos, residual=rd).cpu().numpy()
+    torch.cuda.synchronize()
+    assert layer.status() == 0
+    assert np.array_equal(y1, y2)
+    ref = _oracle_step(orc, w, x, res, kc, vc, cos, sin, pos, hidden)
+    assert _rel(y1 - res, ref - res) < 5e-3
+    assert _ulps(layer.k_cache[:, pos].cpu().numpy().view(np.uint16), kc[:, pos]).max() <= 2
+    assert _ulps(layer.v_cache[:, pos].cpu().numpy().view(np.uint16), vc[:, pos]).max() <= 1
+    # positions other than `pos` are untouched
+    got_k = layer.k_cache.cpu().numpy().view(np.uint16)
+    keep = np.ones(cap, bool)
+    keep[pos] = False
+    assert np.array_equal(got_k[:, keep], kc[:, keep])
 
 
 def test_rmsnorm_rows(pkg, synth, dev):
