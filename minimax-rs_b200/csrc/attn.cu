@@ -171,6 +171,7 @@ struct MvParams {
     const float *residual;
     float *dst;
     uint32_t *status;  // optional: MMRS_ERR_TIMEOUT when a wait of the streaming kernel expired
+    int pre;           // streaming kernel: groups requested before the dependency wait (0: default)
 };
 
 __device__ __forceinline__ void mv_prefetch_rows(const uint8_t *w, long r0, long r1, size_t row_bytes) {
@@ -239,13 +240,19 @@ __host__ __device__ inline size_t mv_smem_bytes(int kpad) { return (size_t)kpad 
 // Streaming matvec on a ready Q8_1 activation (rows of 16-byte multiple length, 16-byte aligned
 // matrices): one CTA per SM owns a contiguous range of rows, cut into groups of whole rows of one
 // matrix (<= 16 KB each).  A producer warp streams the groups through a ring of 12 shared-memory
-// slots with bulk copies, the first 12 issued before waiting for the previous kernel, so the CTA's
-// bytes (about 180 KB for the Q / K / V projection) are requested at once.  NC consumer warps
-// load their lanes' activation blocks (lane + 32u) straight into registers, then take group j
-// when j % NC is theirs and dot its rows out of shared memory.
+// slots with bulk copies (about 180 KB per CTA for the Q / K / V projection): the
+// first groups are requested before waiting for the previous kernel and the rest of the ring once
+// the consumers hold their activation.  NC consumer warps load their lanes' activation blocks
+// (lane + 32u) straight into registers, then take group j when j % NC is theirs and dot its rows
+// out of shared memory.
 // ------------------------------------------------------------------------------------------
 constexpr int kMsSlots = 12;
 constexpr int kMsSlotBytes = 16384;
+// Slots requested before the dependency wait by default.  Everything in flight at once would queue
+// the consumers' activation loads behind the whole stream (about 4 us for 27 MB) when the previous
+// kernel is short; a few slots per SM already keep HBM busy meanwhile.  After a long kernel (the
+// output projection after attention) the whole ring is requested early (MvParams::pre).
+constexpr int kMsPre = 3;
 constexpr int kMsMaxGroups = 96;
 
 struct MsGroup {
@@ -305,6 +312,7 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) q8_0_matvec_stream_kernel(co
     const int r0 = (int)((long)blockIdx.x * total / gridDim.x), r1 = (int)((long)(blockIdx.x + 1) * total / gridDim.x);
     const size_t row_bytes = (size_t)nb * 34;
     const int per = std::max(1, (int)(kMsSlotBytes / row_bytes));
+    const int pre = p.pre <= 0 ? kMsPre : (p.pre < kMsSlots ? p.pre : kMsSlots);
     const uint64_t deadline = globaltimer_ns() + 2000000000ull;
     if (threadIdx.x == NC * 32) {
         // groups: whole rows of one matrix, at most `per` of them
@@ -326,7 +334,7 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) q8_0_matvec_stream_kernel(co
             mbar_init(&empty[i], 1);
         }
         fence_mbar_init();
-        for (int j = 0; j < ng && j < kMsSlots; ++j) {
+        for (int j = 0; j < ng && j < pre; ++j) {
             const uint32_t bytes = (uint32_t)(groups[j].rows * row_bytes);
             mbar_arrive_expect_tx(&full[j], bytes);
             bulk_g2s(slots + (size_t)j * kMsSlotBytes, groups[j].src, bytes, &full[j]);
@@ -336,11 +344,12 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) q8_0_matvec_stream_kernel(co
     grid_dependency_wait();
     launch_dependents();
     const int ng = *ngroups;
-    if (warp == NC) {  // producer: refill slots as their groups are consumed
+    if (warp == NC) {  // producer: the rest of the ring once the consumers hold their activation, then refills
+        named_sync(2, 32 * (NC + 1));
         if (lane == 0) {
-            for (int j = kMsSlots; j < ng; ++j) {
+            for (int j = pre; j < ng; ++j) {
                 const int st = j % kMsSlots;
-                if (!mbar_wait_sleep(&empty[st], (uint32_t)(((j / kMsSlots) - 1) & 1), deadline)) {
+                if (j >= kMsSlots && !mbar_wait_sleep(&empty[st], (uint32_t)(((j / kMsSlots) - 1) & 1), deadline)) {
                     if (p.status) atomicExch(p.status, (uint32_t)MMRS_ERR_TIMEOUT);
                     break;
                 }
@@ -365,6 +374,7 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) q8_0_matvec_stream_kernel(co
         xa[u][0] = make_int4((int)v[1], (int)v[2], (int)v[3], (int)v[4]);
         xa[u][1] = make_int4((int)v[5], (int)v[6], (int)v[7], (int)v[8]);
     }
+    named_arrive(2, 32 * (NC + 1));  // xd is in use: the loads have landed
     for (int j = warp; j < ng; j += NC) {
         const int st = j % kMsSlots;
         if (!mbar_wait_sleep(&full[st], (uint32_t)((j / kMsSlots) & 1), deadline)) {
@@ -566,9 +576,9 @@ __global__ void __launch_bounds__(256) partial_rope_kernel(const RopeParams p) {
 }
 
 // ------------------------------------------------------------------------------------------
-// Split-K GQA decode on the tensor cores.  CTA = (split, KV head g), 4 warps; the split's keys are
-// 32-key chunks, chunk i of the split handled by warp i % 4 from stage i % 8 (two chunks in flight
-// per warp).  A stage holds the chunk's K and V rows as four TMA tiles of 32 keys x 64 dims (f16,
+// Split-K GQA decode on the tensor cores.  CTA = (split, KV head g), 8 warps; the split's keys are
+// 16-key chunks, chunk i of the split handled by warp i % 8 from stage i % 16 (two chunks in
+// flight per warp).  A stage holds the chunk's K and V rows as four TMA tiles of 16 keys x 64 dims (f16,
 // 128-byte rows, 128-byte swizzle: 16-byte column c of key r sits at column c ^ (r & 7)), so the
 // ldmatrix reads below are free of bank conflicts.  Rows past seq_len arrive as zeros.
 //   S = Q K^T: mma.m16n8k16 (f16 in, f32 accumulate) with the 6 query heads as M (rows 6-15 zero,
@@ -584,10 +594,12 @@ __global__ void __launch_bounds__(256) partial_rope_kernel(const RopeParams p) {
 // the row the TMA read); the last CTA of each KV head merges the splits and writes the attention
 // output in f16 and as Q8_1 blocks for the output projection.
 // ------------------------------------------------------------------------------------------
-constexpr int kGqWarps = 4;
+constexpr int kGqWarps = 8;
 constexpr int kGqThreads = 32 * kGqWarps;
-constexpr int kGqStages = 2 * kGqWarps;
-constexpr int kGqTile = 32 * 128;  // bytes of one 32-key x 64-dim f16 tile
+constexpr int kGqKeys = 16;               // keys per chunk
+constexpr int kGqStages = 2 * kGqWarps;    // two chunks in flight per warp
+constexpr int kGqPre = 8;                  // stages requested before the dependency wait
+constexpr int kGqTile = kGqKeys * 128;  // bytes of one 16-key x 64-dim f16 tile
 constexpr int kGqStageBytes = 4 * kGqTile;  // K dims 0-63 | K dims 64-127 | V dims 0-63 | V dims 64-127
 
 struct GqSmem {
@@ -609,6 +621,8 @@ struct GqSmem {
 // KV head's records are one contiguous, 16-byte aligned range for the combining CTA.
 constexpr int kGqRec = 132;
 constexpr int kGqMaxFusedSplits = kGqStages * kGqStageBytes / (kAttnGroup * kGqRec * 4);  // records fit the stages
+static_assert(kGqThreads == 2 * kAttnHeadDim && (kAttnGroup * kAttnHeadDim) % kGqThreads == 0,
+              "the prologue and the split merge assume 256 threads");
 constexpr size_t kGqSmemBytes = sizeof(GqSmem) + 1024;  // + alignment of the swizzled stages
 
 struct GqaParams {
@@ -669,12 +683,12 @@ __global__ void __launch_bounds__(kGqThreads, 1)
     GqSmem &sm = *reinterpret_cast<GqSmem *>((reinterpret_cast<uintptr_t>(gq_raw) + 1023) & ~uintptr_t(1023));
     const int split = blockIdx.x, g = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int seq = p.seq_len, pos = seq - 1;
-    const int nch = (seq + 31) / 32;
+    const int nch = (seq + kGqKeys - 1) / kGqKeys;
     const int c0 = (int)((long)split * nch / p.num_splits), c1 = (int)((long)(split + 1) * nch / p.num_splits);
     const int mine = c1 - c0;
-    const bool holds_pos = kFused && pos / 32 >= c0 && pos / 32 < c1;
+    const bool holds_pos = kFused && pos / kGqKeys >= c0 && pos / kGqKeys < c1;
     auto issue = [&](int i) {
-        const int st = i % kGqStages, key0 = (c0 + i) * 32;
+        const int st = i % kGqStages, key0 = (c0 + i) * kGqKeys;
         uint8_t *dst = sm.stage[st];
         mbar_arrive_expect_tx(&sm.full[st], kGqStageBytes);
         tma_load_3d(dst, &kmap, 0, key0, g, &sm.full[st]);
@@ -686,31 +700,35 @@ __global__ void __launch_bounds__(kGqThreads, 1)
         for (int i = 0; i < kGqStages; ++i) mbar_init(&sm.full[i], 1);
         mbar_init(&sm.cbar, 1);
         fence_mbar_init();
-        // the cached keys come from earlier launches: their loads start before the wait below
-        for (int i = 0; i < mine && i < kGqStages; ++i) issue(i);
+        // the cached keys come from earlier launches: the first loads start before the wait below,
+        // the rest once the prologue's own loads have landed (so they do not queue behind them)
+        for (int i = 0; i < mine && i < kGqPre; ++i) issue(i);
     }
     grid_dependency_wait();
     launch_dependents();
     if constexpr (kFused) {
         // every global value the prologue needs is requested before any arithmetic: the Q and K
-        // rows for the RMSNorm sums (q_rows <= 8192: at most 16 float4 per thread), the group's
-        // 6 heads with their norm weights and rotary entries, and head g's K / V row
+        // rows for the RMSNorm sums (q_rows <= 8192: at most 8 float4 per thread), the group's
+        // 6 heads with their norm weights and rotary entries (3 values per thread), and head g's
+        // K / V row (threads 0-127)
         const int qr = p.query_heads * kAttnHeadDim, kr = qr / kAttnGroup, half_rope = p.rope_dim / 2;
         const float4 *p4 = reinterpret_cast<const float4 *>(p.proj);
-        float4 vq[16], vk[3];
+        constexpr int kQ4 = kMvMaxK / 4 / kGqThreads, kK4 = (kMvMaxK / kAttnGroup / 4 + kGqThreads - 1) / kGqThreads;
+        constexpr int kQe = kAttnGroup * kAttnHeadDim / kGqThreads;
+        float4 vq[kQ4], vk[kK4];
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
+        for (int u = 0; u < kQ4; ++u) {
             const int i = tid + u * kGqThreads;
             vq[u] = i < qr / 4 ? p4[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
 #pragma unroll
-        for (int u = 0; u < 3; ++u) {
+        for (int u = 0; u < kK4; ++u) {
             const int i = tid + u * kGqThreads;
             vk[u] = i < kr / 4 ? p4[qr / 4 + i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
-        float pq[kAttnGroup], aq[kAttnGroup], cq6[kAttnGroup], sq6[kAttnGroup];
+        float pq[kQe], aq[kQe], cq6[kQe], sq6[kQe];
 #pragma unroll
-        for (int u = 0; u < kAttnGroup; ++u) {
+        for (int u = 0; u < kQe; ++u) {
             const int e = tid + u * kGqThreads, col = e % kAttnHeadDim;
             const int qi = g * kAttnGroup * kAttnHeadDim + e;
             pq[u] = p.proj[qi];
@@ -721,7 +739,8 @@ __global__ void __launch_bounds__(kGqThreads, 1)
             sq6[u] = rot ? p.sin[(long)pos * half_rope + freq] : 0.0f;
         }
         float pk = 0.0f, ak = 0.0f, pv = 0.0f, ck = 0.0f, sk1 = 0.0f;
-        if (holds_pos) {
+        const bool krow = holds_pos && tid < kAttnHeadDim;
+        if (krow) {
             const int ki = g * kAttnHeadDim + tid, freq = tid < half_rope ? tid : tid - half_rope;
             pk = p.proj[qr + ki];
             ak = p.k_norm[ki];
@@ -734,14 +753,14 @@ __global__ void __launch_bounds__(kGqThreads, 1)
         // RMSNorm scales of all Q rows and all K rows (fixed order: per-thread chain, butterfly, warps)
         float sq = 0.0f, sk = 0.0f;
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
+        for (int u = 0; u < kQ4; ++u) {
             sq = fmaf(vq[u].x, vq[u].x, sq);
             sq = fmaf(vq[u].y, vq[u].y, sq);
             sq = fmaf(vq[u].z, vq[u].z, sq);
             sq = fmaf(vq[u].w, vq[u].w, sq);
         }
 #pragma unroll
-        for (int u = 0; u < 3; ++u) {
+        for (int u = 0; u < kK4; ++u) {
             sk = fmaf(vk[u].x, vk[u].x, sk);
             sk = fmaf(vk[u].y, vk[u].y, sk);
             sk = fmaf(vk[u].z, vk[u].z, sk);
@@ -757,21 +776,27 @@ __global__ void __launch_bounds__(kGqThreads, 1)
             sm.red[1][warp] = sk;
         }
         __syncthreads();
-        const float tq = ((sm.red[0][0] + sm.red[0][1]) + sm.red[0][2]) + sm.red[0][3];
-        const float tk = ((sm.red[1][0] + sm.red[1][1]) + sm.red[1][2]) + sm.red[1][3];
+        if (tid == 0)
+            for (int i = kGqPre; i < mine && i < kGqStages; ++i) issue(i);
+        float tq = 0.0f, tk = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kGqWarps; ++w) {
+            tq += sm.red[0][w];
+            tk += sm.red[1][w];
+        }
         const float scq = rsqrtf(__fdiv_rn(tq, (float)qr) + p.eps), sck = rsqrtf(__fdiv_rn(tk, (float)kr) + p.eps);
         // qkv_rmsnorm_f16: f16(scale * v * alpha) for the group's 6 heads (and head g of K, V)
 #pragma unroll
-        for (int u = 0; u < kAttnGroup; ++u)
+        for (int u = 0; u < kQe; ++u)
             (&sm.qn[0][0])[tid + u * kGqThreads] = __float2half_rn(__fmul_rn(__fmul_rn(scq, pq[u]), aq[u]));
-        if (holds_pos) {
+        if (krow) {
             sm.newkn[tid] = __float2half_rn(__fmul_rn(__fmul_rn(sck, pk), ak));
             sm.newv[tid] = __float2half_rn(pv);
         }
         __syncthreads();
         // RoPE (partial_rope_kernel arithmetic) with the rotary entries already in registers
 #pragma unroll
-        for (int u = 0; u < kAttnGroup; ++u) {
+        for (int u = 0; u < kQe; ++u) {
             const int e = tid + u * kGqThreads, h = e / kAttnHeadDim, col = e % kAttnHeadDim;
             __half r = sm.qn[h][col];
             if (col < p.rope_dim) {
@@ -782,7 +807,7 @@ __global__ void __launch_bounds__(kGqThreads, 1)
             }
             sm.qh[h][col] = r;
         }
-        if (holds_pos) {
+        if (krow) {
             __half kv = sm.newkn[tid];
             if (tid < p.rope_dim) {
                 const bool first = tid < half_rope;
@@ -800,6 +825,9 @@ __global__ void __launch_bounds__(kGqThreads, 1)
             const int h = e / kAttnHeadDim, col = e % kAttnHeadDim;
             sm.qh[h][col] = p.q[(long)(g * kAttnGroup + h) * p.q_head_stride + col];
         }
+        __syncthreads();
+        if (tid == 0)
+            for (int i = kGqPre; i < mine && i < kGqStages; ++i) issue(i);
     }
     __syncthreads();
     // Q as the A operand: row lane / 4 (query head of the group; rows 6-15 zero), dims of k-step s
@@ -823,8 +851,8 @@ __global__ void __launch_bounds__(kGqThreads, 1)
             break;
         }
         uint8_t *sb = sm.stage[st];
-        const int key0 = (c0 + i) * 32, nvalid = min(32, seq - key0);
-        if (kFused && pos >= key0 && pos < key0 + 32) {  // the new position replaces the cached row
+        const int key0 = (c0 + i) * kGqKeys, nvalid = min(kGqKeys, seq - key0);
+        if (kFused && pos >= key0 && pos < key0 + kGqKeys) {  // the new position replaces the cached row
             const uint32_t off = gq_swz(pos - key0, lane >> 1) + (lane & 1) * 8;
             *reinterpret_cast<uint2 *>(sb + off) = *reinterpret_cast<const uint2 *>(&sm.newk[4 * lane]);
             *reinterpret_cast<uint2 *>(sb + 2 * kGqTile + off) = *reinterpret_cast<const uint2 *>(&sm.newv[4 * lane]);
@@ -832,25 +860,26 @@ __global__ void __launch_bounds__(kGqThreads, 1)
         }
         const uint32_t sbase = smem_u32(sb);
         // S = Q K^T: n-tile t = keys 8t..8t+7; the lane holds head gq, keys 8t + cq + {0, 1}
-        float sc[4][2];
+        constexpr int NT = kGqKeys / 8;  // n-tiles of 8 keys
+        float sc[NT][2];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) sc[t][0] = sc[t][1] = 0.0f;
+        for (int t = 0; t < NT; ++t) sc[t][0] = sc[t][1] = 0.0f;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {  // k-steps 2kk, 2kk + 1 of the four n-tiles, independent mmas adjacent
-            uint32_t b[4][4];
+            uint32_t b[NT][4];
 #pragma unroll
-            for (int t = 0; t < 4; ++t)
+            for (int t = 0; t < NT; ++t)
                 ldsm_x4(sbase + gq_swz(8 * t + (lane & 7), 4 * kk + (lane >> 3)), b[t][0], b[t][1], b[t][2], b[t][3]);
 #pragma unroll
-            for (int t = 0; t < 4; ++t) mma_rows8(sc[t][0], sc[t][1], qa0[2 * kk], qa2[2 * kk], b[t][0], b[t][1]);
+            for (int t = 0; t < NT; ++t) mma_rows8(sc[t][0], sc[t][1], qa0[2 * kk], qa2[2 * kk], b[t][0], b[t][1]);
 #pragma unroll
-            for (int t = 0; t < 4; ++t)
+            for (int t = 0; t < NT; ++t)
                 mma_rows8(sc[t][0], sc[t][1], qa0[2 * kk + 1], qa2[2 * kk + 1], b[t][2], b[t][3]);
         }
-        // online softmax of head gq over the chunk (its 32 keys sit on the 4 lanes of the quad)
+        // online softmax of head gq over the chunk (its 16 keys sit on the 4 lanes of the quad)
         float mx = -INFINITY;
 #pragma unroll
-        for (int t = 0; t < 4; ++t)
+        for (int t = 0; t < NT; ++t)
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 const float v = 8 * t + cq + c < nvalid ? sc[t][c] * p.scale : -INFINITY;
@@ -863,10 +892,10 @@ __global__ void __launch_bounds__(kGqThreads, 1)
         const float alpha = m_run == -INFINITY ? 0.0f : expf(m_run - mn);
         // probabilities as f16 pairs hi + lo (hi = f16(p), lo = f16(p - hi)): two tensor-core
         // products carry p to about 22 bits
-        uint32_t pa[4], pb[4];
+        uint32_t pa[NT], pb[NT];
         float ps = 0.0f;
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
+        for (int t = 0; t < NT; ++t) {
             const float p0 = expf(sc[t][0] - mn), p1 = expf(sc[t][1] - mn);
             const __half2 ph = __floats2half2_rn(p0, p1);
             const float2 pf = __half22float2(ph);
@@ -886,7 +915,7 @@ __global__ void __launch_bounds__(kGqThreads, 1)
         }
         // O += P V: k-step j = keys 16j..16j+15 (A = probabilities of n-tiles 2j, 2j + 1), n-tile = 8 dims
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
+        for (int j = 0; j < NT / 2; ++j) {
             const int r = 16 * j + ((lane >> 3) & 1) * 8 + (lane & 7);
             uint32_t b[8][4];
 #pragma unroll
@@ -918,9 +947,9 @@ __global__ void __launch_bounds__(kGqThreads, 1)
     }
     __syncthreads();
     {
-        const int d = tid;  // 128 threads = 128 dims
+        const int d = tid % kAttnHeadDim, h0 = tid / kAttnHeadDim * (kAttnGroup / 2);  // 256 threads: 2 x 3 heads
 #pragma unroll
-        for (int h = 0; h < kAttnGroup; ++h) {
+        for (int h = h0; h < h0 + kAttnGroup / 2; ++h) {
             float M = -INFINITY;
 #pragma unroll
             for (int w = 0; w < kGqWarps; ++w) M = fmaxf(M, sm.wm[w][h]);
@@ -1075,13 +1104,13 @@ static int rope_launch(const RopeParams &r, cudaStream_t s) {
 }
 
 // Tensor map over an f16 KV cache: [heads][rows][128], head h at h * head_stride elements; box =
-// 64 dims x 32 positions of one head, 128-byte swizzle; rows past `rows` read as zeros.
+// 64 dims x 16 positions of one head, 128-byte swizzle; rows past `rows` read as zeros.
 static int make_kv_map(CUtensorMap *map, const void *base, int rows, int heads, long head_stride) {
     auto enc = tensor_map_encoder();
     if (!enc) return MMRS_ERR_LAUNCH;
     cuuint64_t dims[3] = {(cuuint64_t)kAttnHeadDim, (cuuint64_t)rows, (cuuint64_t)heads};
     cuuint64_t strides[2] = {(cuuint64_t)kAttnHeadDim * 2, (cuuint64_t)head_stride * 2};
-    cuuint32_t box[3] = {64, 32, 1};
+    cuuint32_t box[3] = {64, (cuuint32_t)kGqKeys, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -1347,8 +1376,8 @@ extern "C" int mmrs_attn_decode_forward(const MmrsAttnWeights *w, const float *x
     rc = qkv_launch(x, ws + l.xq, w->wq, w->wk, w->wv, proj, w->hidden, w->hidden, qr, kr, kr, s, status);
     if (rc != MMRS_OK) return rc;
     // 2. attention over positions [0, position]: about one CTA per SM, at least 4 chunks per split
-    const int seq = position + 1, nch = (seq + 31) / 32;
-    const int splits = std::max(1, std::min({sm_count() / w->kv_heads, (nch + 3) / 4, kGqMaxFusedSplits}));
+    const int seq = position + 1, nch = (seq + kGqKeys - 1) / kGqKeys;
+    const int splits = std::max(1, std::min({sm_count() / w->kv_heads, (nch + 7) / 8, kGqMaxFusedSplits}));
     CUtensorMap kmap, vmap;
     rc = make_kv_map(&kmap, k_cache, seq, w->kv_heads, head_stride);
     if (rc == MMRS_OK) rc = make_kv_map(&vmap, v_cache, seq, w->kv_heads, head_stride);
@@ -1387,5 +1416,6 @@ extern "C" int mmrs_attn_decode_forward(const MmrsAttnWeights *w, const float *x
     o.residual = residual;
     o.dst = y;
     o.status = status;
+    o.pre = kMsSlots;  // Wo does not depend on the attention kernel: stream it while that runs
     return mv_launch<float>(o, s);
 }
