@@ -569,6 +569,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=2000)
     ap.add_argument("--no-config3", action="store_true", help="skip the configs[3] decoder-layer line")
+    ap.add_argument("--only-config3", action="store_true",
+                    help="run only the configs[3] decoder-layer measurement and print its object (profiling)")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill-steps", type=int, default=40)
@@ -595,6 +597,9 @@ def main():
         dist.init_process_group("nccl", device_id=dev)
 
     pkg, synth = ge.load_package(), ge.load_synth()
+    if args.only_config3:
+        print(json.dumps(run_config3(pkg, synth, dev, args)))
+        return
     group = None
     if world > 1:
         # TP = 2 (the reference layout) at two GPUs, expert parallel (e % W) at four and eight

@@ -260,8 +260,11 @@ struct MsGroup {
     int row0, rows;
 };
 
+constexpr int kMsActBytes = kMvMaxK / 32 * 36;  // the Q8_1 activation (at most 256 blocks)
+
 static size_t ms_smem_bytes() {
-    return (size_t)kMsSlots * kMsSlotBytes + sizeof(MsGroup) * kMsMaxGroups + sizeof(uint64_t) * 2 * kMsSlots + 16;
+    return (size_t)kMsSlots * kMsSlotBytes + kMsActBytes + sizeof(MsGroup) * kMsMaxGroups +
+           sizeof(uint64_t) * (2 * kMsSlots + 1) + 16;
 }
 
 // One row of a group in shared memory against the register activation; lane l takes blocks
@@ -303,11 +306,16 @@ template <int NBL, int NC, bool kFull>
 __global__ void __launch_bounds__(32 * (NC + 1), 1) q8_0_matvec_stream_kernel(const MvParams p) {
     extern __shared__ __align__(128) uint8_t ms_smem[];
     uint8_t *slots = ms_smem;
-    MsGroup *groups = reinterpret_cast<MsGroup *>(ms_smem + (size_t)kMsSlots * kMsSlotBytes);
+    uint8_t *act = ms_smem + (size_t)kMsSlots * kMsSlotBytes;
+    MsGroup *groups = reinterpret_cast<MsGroup *>(act + kMsActBytes);
     uint64_t *full = reinterpret_cast<uint64_t *>(groups + kMsMaxGroups);
     uint64_t *empty = full + kMsSlots;
-    int *ngroups = reinterpret_cast<int *>(empty + kMsSlots);
+    uint64_t *abar = empty + kMsSlots;
+    int *ngroups = reinterpret_cast<int *>(abar + 1);
     const int nb = p.k / 32, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // the activation by one bulk copy when its size is a multiple of 16 bytes (nb % 4 == 0) and
+    // it is 16-byte aligned; otherwise each lane loads its blocks
+    const bool act_bulk = (nb % 4) == 0 && !((uintptr_t)p.vy_in & 15u);
     const int total = p.n[0] + p.n[1] + p.n[2];
     const int r0 = (int)((long)blockIdx.x * total / gridDim.x), r1 = (int)((long)(blockIdx.x + 1) * total / gridDim.x);
     const size_t row_bytes = (size_t)nb * 34;
@@ -333,6 +341,7 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) q8_0_matvec_stream_kernel(co
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
+        mbar_init(abar, 1);
         fence_mbar_init();
         for (int j = 0; j < ng && j < pre; ++j) {
             const uint32_t bytes = (uint32_t)(groups[j].rows * row_bytes);
@@ -344,7 +353,11 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) q8_0_matvec_stream_kernel(co
     grid_dependency_wait();
     launch_dependents();
     const int ng = *ngroups;
-    if (warp == NC) {  // producer: the rest of the ring once the consumers hold their activation, then refills
+    if (warp == NC) {  // producer: the activation, the rest of the ring once the consumers hold it, refills
+        if (lane == 0 && act_bulk) {
+            mbar_arrive_expect_tx(abar, (uint32_t)(nb * 36));
+            bulk_g2s(act, p.vy_in, (uint32_t)(nb * 36), abar);
+        }
         named_sync(2, 32 * (NC + 1));
         if (lane == 0) {
             for (int j = pre; j < ng; ++j) {
@@ -363,10 +376,13 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) q8_0_matvec_stream_kernel(co
     // this lane's activation blocks (lane + 32u), Q8_1 (half d, half sum, 32 int8), in registers
     int4 xa[NBL][2];
     float xd[NBL];
+    if (act_bulk && !mbar_wait_sleep(abar, 0u, deadline) && lane == 0 && p.status)
+        atomicExch(p.status, (uint32_t)MMRS_ERR_TIMEOUT);
+    const uint8_t *asrc = act_bulk ? act : p.vy_in;
 #pragma unroll
     for (int u = 0; u < NBL; ++u) {
         const int b = lane + 32 * u;
-        const uint32_t *blk = reinterpret_cast<const uint32_t *>(p.vy_in + (size_t)b * 36);
+        const uint32_t *blk = reinterpret_cast<const uint32_t *>(asrc + (size_t)b * 36);
         uint32_t v[9];
 #pragma unroll
         for (int i = 0; i < 9; ++i) v[i] = (kFull || b < nb) ? blk[i] : 0u;
