@@ -374,6 +374,7 @@ def run_config0(pkg, synth, dev, args) -> dict:
 
 C3_POS = 8191  # configs[3]: the token attends to an 8192-position KV cache
 C3_SEED = 3001
+LM_SEED = 4001  # the LM head line (configs[4]'s end-of-stack projection)
 
 
 def run_config3(pkg, synth, dev, args) -> dict:
@@ -466,6 +467,63 @@ def run_config3(pkg, synth, dev, args) -> dict:
                         "attention_frac": (attn_w + kv) / (ms_attn / 1e3) / 1e9 / peaks["hbm_gbs"]},
            "clocks": clk.summary()}
     del attn, moe
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_lm_head(pkg, dev, args) -> dict:
+    """The output projection of a decode step at the model's size: output_norm, the Q6_K `output`
+    matrix [200064][3072] (504 MB, larger than L2), greedy token; replayed from CUDA graphs of 8
+    steps.  Weights: random ql / qh bytes, int8 scales in [-64, 63], half d = |N(0,1)| * 0.002."""
+    import torch
+    vocab, hidden = 200064, H
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(LM_SEED)
+    nsb = hidden // 256
+    w = torch.randint(0, 256, (vocab, nsb, 210), dtype=torch.int16, device=dev, generator=gen).to(torch.uint8)
+    w[:, :, 192:208] = (torch.randint(-64, 64, (vocab, nsb, 16), dtype=torch.int16, device=dev, generator=gen)
+                        .to(torch.int8).view(torch.uint8))
+    d = (torch.randn(vocab, nsb, device=dev, generator=gen).abs() * 0.002).half()
+    w[:, :, 208:] = d.view(torch.uint8).reshape(vocab, nsb, 2)
+    w = w.reshape(-1).contiguous()
+    nw = (1.0 + 0.1 * torch.randn(hidden, device=dev, generator=gen)).float()
+    x = torch.randn(hidden, device=dev, generator=gen)
+    head = pkg.LmHead(w, nw, vocab, hidden)
+    stream = torch.cuda.Stream(device=dev)
+    per, reps = 8, 12
+    with torch.cuda.stream(stream):
+        for _ in range(per):
+            head.forward(x, stream=stream)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for _ in range(per):
+                head.forward(x, stream=stream)
+        for _ in range(3):
+            g.replay()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(0) as clk:
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+            e1.synchronize()
+    assert head.status() == 0, "device-side timeout in the LM head"
+    tok = int(head.token.item())
+    assert tok == int(torch.argmax(head.logits).item()), "greedy token differs from the logits' argmax"
+    del g
+    ms = e0.elapsed_time(e1) / (reps * per)
+    alg = vocab * nsb * 210 + hidden * 4 * 2 + vocab * 4  # weights + x and norm weight + logits written
+    peaks = measured_peaks()
+    out = {"metric": "lm_head_tokens_per_s", "value": 1.0 / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+           "config": {"workload": "output_norm + Q6_K output projection [200064 x 3072] + greedy token (T = 1)",
+                      "graph_steps": per, "l2": "504 MB of weights per step (> L2)",
+                      "data": "synthetic (seeded torch generator)"},
+           "roofline": {"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                        "frac": alg / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], "algorithmic_bytes_per_step": alg},
+           "clocks": clk.summary()}
+    del head, w
     torch.cuda.empty_cache()
     return out
 
@@ -569,6 +627,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=2000)
     ap.add_argument("--no-config3", action="store_true", help="skip the configs[3] decoder-layer line")
+    ap.add_argument("--no-lm-head", action="store_true", help="skip the LM head line")
+    ap.add_argument("--only-lm-head", action="store_true", help="run only the LM head measurement (profiling)")
     ap.add_argument("--only-config3", action="store_true",
                     help="run only the configs[3] decoder-layer measurement and print its object (profiling)")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
@@ -599,6 +659,9 @@ def main():
     pkg, synth = ge.load_package(), ge.load_synth()
     if args.only_config3:
         print(json.dumps(run_config3(pkg, synth, dev, args)))
+        return
+    if args.only_lm_head:
+        print(json.dumps(run_lm_head(pkg, dev, args)))
         return
     group = None
     if world > 1:
@@ -752,6 +815,7 @@ def main():
     allreduce = ar_sweep(group, world, dev) if world > 1 and not args.no_ar_sweep else None
     config0 = run_config0(pkg, synth, dev, args) if world == 1 and not args.no_prefill else None
     config3 = run_config3(pkg, synth, dev, args) if world == 1 and not args.no_config3 else None
+    lm_head = run_lm_head(pkg, dev, args) if world == 1 and not args.no_lm_head else None
 
     if rank == 0:
         out = {
@@ -780,6 +844,7 @@ def main():
             "allreduce_sweep": allreduce,
             "config0": config0,
             "config3": config3,
+            "lm_head": lm_head,
         }
         print(json.dumps(out), flush=True)
     if world > 1:

@@ -48,6 +48,11 @@ _VP, _I, _U32, _U64, _I64, _F = C.c_void_p, C.c_int, C.c_uint32, C.c_uint64, C.c
 _SZ = C.c_size_t
 
 
+class MmrsLmHead(C.Structure):
+    _fields_ = [("weight", C.c_void_p), ("norm_weight", C.c_void_p), ("vocab", C.c_int), ("hidden", C.c_int),
+                ("eps", C.c_float)]
+
+
 class MmrsAttnWeights(C.Structure):
     """include/minimax_attn.h: MmrsAttnWeights."""
     _fields_ = [("wq", C.c_void_p), ("wk", C.c_void_p), ("wv", C.c_void_p), ("wo", C.c_void_p),
@@ -72,6 +77,10 @@ PROTOTYPES = {
     "launch_gqa_decode_mma_f16_128": (None, [_VP] * 5 + [_I] * 7 + [_F, _I, _VP]),
     "mmrs_attn_workspace_bytes": (_SZ, [C.POINTER(MmrsAttnWeights)]),
     "mmrs_attn_workspace_status": (_I, [_VP]),
+    "launch_mmvq_gguf_q6_k_f32_plain": (None, [_VP] * 3 + [_I] * 5 + [_VP]),
+    "mmrs_lm_head_workspace_bytes": (_SZ, [C.POINTER(MmrsLmHead)]),
+    "mmrs_lm_head_workspace_status": (_I, [_VP]),
+    "mmrs_lm_head_forward": (_I, [C.POINTER(MmrsLmHead), _VP, _VP, _VP, _VP, _SZ, _VP]),
     "mmrs_rmsnorm_f32": (_I, [_VP, _VP, _VP, _I, _I, _F, _VP]),
     "mmrs_attn_decode_forward": (_I, [C.POINTER(MmrsAttnWeights), _VP, _VP, _I, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "launch_tp2_peer_all_reduce_f32": (None, [_VP] * 8 + [C.c_uint, _I, _F, _VP]),
@@ -271,6 +280,33 @@ class AttnLayer:
                                             self.ws.data_ptr(), self.ws.numel(), _stream(stream))
         check(rc, "mmrs_attn_decode_forward")
         return y
+
+
+class LmHead:
+    """Output projection of a decode step (TensorParallelModel::logits, src/tensor_parallel_model.rs:871-880,
+    and greedy sampling, src/sampling.rs:84-88): device-resident Q6_K `output.weight` [vocab][hidden]
+    and `output_norm.weight` (or None), with the C struct that points at them."""
+
+    def __init__(self, weight, norm_weight, vocab: int, hidden: int, eps: float = 1e-6):
+        import torch
+        self.t = (weight, norm_weight)
+        self.c = MmrsLmHead(weight.data_ptr(), _ptr(norm_weight), vocab, hidden, eps)
+        n = lib().mmrs_lm_head_workspace_bytes(C.byref(self.c))
+        if n == 0:
+            raise MoeError(MMRS_ERR_UNSUPPORTED, "mmrs_lm_head_workspace_bytes")
+        self.ws = torch.zeros(n, dtype=torch.uint8, device=weight.device)
+        self.logits = torch.empty(vocab, dtype=torch.float32, device=weight.device)
+        self.token = torch.zeros(1, dtype=torch.int32, device=weight.device)
+
+    def status(self) -> int:
+        return lib().mmrs_lm_head_workspace_status(self.ws.data_ptr())
+
+    def forward(self, x, stream=None):
+        """(logits [vocab] f32, token [1] int32) for the final hidden state x [hidden] f32."""
+        rc = lib().mmrs_lm_head_forward(C.byref(self.c), x.data_ptr(), self.logits.data_ptr(), self.token.data_ptr(),
+                                        self.ws.data_ptr(), self.ws.numel(), _stream(stream))
+        check(rc, "mmrs_lm_head_forward")
+        return self.logits, self.token
 
 
 def rmsnorm(x, weight, y=None, eps: float = 1e-6, stream=None):

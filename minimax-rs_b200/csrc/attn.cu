@@ -264,7 +264,7 @@ constexpr int kMsActBytes = kMvMaxK / 32 * 36;  // the Q8_1 activation (at most 
 
 static size_t ms_smem_bytes() {
     return (size_t)kMsSlots * kMsSlotBytes + kMsActBytes + sizeof(MsGroup) * kMsMaxGroups +
-           sizeof(uint64_t) * (2 * kMsSlots + 1) + 16;
+           sizeof(uint64_t) * (2 * kMsSlots + 1) + sizeof(int) * (kMsSlots + 1) + 16;
 }
 
 // One row of a group in shared memory against the register activation; lane l takes blocks
@@ -312,6 +312,7 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) q8_0_matvec_stream_kernel(co
     uint64_t *empty = full + kMsSlots;
     uint64_t *abar = empty + kMsSlots;
     int *ngroups = reinterpret_cast<int *>(abar + 1);
+    int *ticket = ngroups + 1;  // [kMsSlots]
     const int nb = p.k / 32, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // the activation by one bulk copy when its size is a multiple of 16 bytes (nb % 4 == 0) and
     // it is 16-byte aligned; otherwise each lane loads its blocks
@@ -340,11 +341,13 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) q8_0_matvec_stream_kernel(co
         for (int i = 0; i < kMsSlots; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
+            ticket[i] = -1;
         }
         mbar_init(abar, 1);
         fence_mbar_init();
         for (int j = 0; j < ng && j < pre; ++j) {
             const uint32_t bytes = (uint32_t)(groups[j].rows * row_bytes);
+            ticket[j] = j;
             mbar_arrive_expect_tx(&full[j], bytes);
             bulk_g2s(slots + (size_t)j * kMsSlotBytes, groups[j].src, bytes, &full[j]);
         }
@@ -367,6 +370,7 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) q8_0_matvec_stream_kernel(co
                     break;
                 }
                 const uint32_t bytes = (uint32_t)(groups[j].rows * row_bytes);
+                *reinterpret_cast<volatile int *>(&ticket[st]) = j;
                 mbar_arrive_expect_tx(&full[st], bytes);
                 bulk_g2s(slots + (size_t)st * kMsSlotBytes, groups[j].src, bytes, &full[st]);
             }
@@ -393,7 +397,7 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) q8_0_matvec_stream_kernel(co
     named_arrive(2, 32 * (NC + 1));  // xd is in use: the loads have landed
     for (int j = warp; j < ng; j += NC) {
         const int st = j % kMsSlots;
-        if (!mbar_wait_sleep(&full[st], (uint32_t)((j / kMsSlots) & 1), deadline)) {
+        if (!ring_wait(full, ticket, st, j, kMsSlots, deadline)) {
             if (lane == 0 && p.status) atomicExch(p.status, (uint32_t)MMRS_ERR_TIMEOUT);
             break;
         }

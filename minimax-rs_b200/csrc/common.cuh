@@ -123,6 +123,20 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, 
     }
 }
 
+// Ring slot hand-over for consumers that may run more than one fill ahead of a slot: the
+// producer stores the index of the fill it is about to issue into ticket[slot]; a consumer waits
+// for its fill's index there before the parity wait, which could otherwise match the completed
+// phase of an older fill with the same parity.  Bounded by the deadline.
+__device__ __forceinline__ bool ring_wait(uint64_t *full, const int *ticket, int slot, int fill, int slots,
+                                          uint64_t deadline) {
+    uint32_t spins = 0;
+    while (*reinterpret_cast<const volatile int *>(&ticket[slot]) != fill) {
+        __nanosleep(32);
+        if ((++spins & 255u) == 0 && globaltimer_ns() > deadline) return false;
+    }
+    return mbar_wait_sleep(&full[slot], (uint32_t)(fill / slots) & 1u, deadline);
+}
+
 // 1-D bulk copy global -> shared, completion counted on an mbarrier (bytes % 16 == 0,
 // both addresses 16-byte aligned).
 __device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, uint32_t bytes,

@@ -106,6 +106,22 @@ def q8_0_blocks(seed: int, stream: int, rows: int, k: int) -> np.ndarray:
     return out.reshape(rows, nb * 34)
 
 
+def q6k_blocks(seed: int, stream: int, rows: int, k: int) -> np.ndarray:
+    """Synthetic GGUF Q6_K matrix [rows][k/256] x 210 bytes: ql (128 B) and qh (64 B) uniform
+    bytes, 16 int8 scales uniform in [-64, 63], half d = |N(0,1)| * 0.002, as uint8 [rows, k/256 * 210]."""
+    nb = k // 256
+    key, key_d = stream_key(seed, stream), stream_key(seed, stream + 0x10000)
+    blk = np.arange(rows * nb, dtype=np.uint64)
+    q = rand64(key, (blk[:, None] * np.uint64(26) + np.arange(26, dtype=np.uint64)).ravel()).view(np.uint8)
+    q = q.reshape(-1, 208)
+    d = (np.abs(normal(key_d, blk)) * np.float32(0.002)).astype(np.float16)
+    out = np.empty((rows * nb, 210), dtype=np.uint8)
+    out[:, :192] = q[:, :192]
+    out[:, 192:208] = ((q[:, 192:208].astype(np.int16) & 127) - 64).astype(np.int8).view(np.uint8)
+    out[:, 208:] = d.view(np.uint8).reshape(-1, 2)
+    return out.reshape(rows, nb * 210)
+
+
 def normal_f16(n: int, seed: int, stream: int, scale: float = 1.0) -> np.ndarray:
     """scale * N(0,1) rounded to half (round to nearest even)."""
     return normal_f32(n, seed, stream, scale).astype(np.float16)

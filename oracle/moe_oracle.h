@@ -113,6 +113,11 @@ int orc_num_threads(void);
 /* ---- decode attention (attn_oracle.c) ---- */
 uint16_t orc_double_to_half(double v);
 void orc_q8_0_matvec(const uint8_t *w, int rows, int k, const float *x, float *y);
+
+/* ---- LM head (lmhead_oracle.c) ---- */
+void orc_q6k_dequant_row(const uint8_t *row, int k, float *out);
+void orc_q6k_matvec(const uint8_t *w, int rows, int k, const float *x, float *y);
+int orc_argmax_f32(const float *v, int n);
 void orc_qkv_rmsnorm_f16(const float *proj, const float *q_alpha, const float *k_alpha, int q_rows,
                          int k_rows, int v_rows, float eps, uint16_t *dst);
 void orc_partial_rope_f16(const uint16_t *q, const uint16_t *k, const float *cosv, const float *sinv, int q_rows,

@@ -47,6 +47,7 @@ def lib() -> C.CDLL:
         _lib.orc_dot_q5k_q81.restype = C.c_float
         _lib.orc_dot_kq_mmq.restype = C.c_float
         _lib.orc_num_threads.restype = C.c_int
+        _lib.orc_argmax_f32.restype = C.c_int
     return _lib
 
 
@@ -179,6 +180,27 @@ def q8_0_matvec(w: np.ndarray, rows: int, k: int, x: np.ndarray) -> np.ndarray:
     y = np.zeros(rows, dtype=np.float32)
     lib().orc_q8_0_matvec(_p(w), C.c_int(rows), C.c_int(k), _p(x), _p(y))
     return y
+
+
+def q6k_matvec(w: np.ndarray, rows: int, k: int, x: np.ndarray) -> np.ndarray:
+    """y = W x for a Q6_K matrix (rows x k/256 blocks of 210 bytes), x quantised to Q8_1
+    (lmhead_oracle.c; exact up to the final rounding)."""
+    w, x = _c(w, np.uint8), _c(x, np.float32)
+    y = np.zeros(rows, dtype=np.float32)
+    lib().orc_q6k_matvec(_p(w), C.c_int(rows), C.c_int(k), _p(x), _p(y))
+    return y
+
+
+def q6k_dequant_row(row: np.ndarray, k: int) -> np.ndarray:
+    out = np.zeros(k, dtype=np.float32)
+    lib().orc_q6k_dequant_row(_p(_c(row, np.uint8)), C.c_int(k), _p(out))
+    return out
+
+
+def argmax_f32(v: np.ndarray) -> int:
+    """First index of the maximum (the reference's greedy choice)."""
+    v = _c(v, np.float32)
+    return int(lib().orc_argmax_f32(_p(v), C.c_int(v.size)))
 
 
 def qkv_rmsnorm_f16(proj, q_alpha, k_alpha, q_rows: int, k_rows: int, v_rows: int, eps: float = 1e-6):

@@ -170,3 +170,14 @@ def oproj_inputs():
     a = S.normal_f16(Q_ROWS, 704, 1, 1.0).astype(np.float32)  # attention output, widened
     wo = S.q8_0_blocks(704, 2, ATTN_H, Q_ROWS)
     return a, wo
+
+
+# ---- LM head (output projection, Q6_K) -------------------------------------------------------
+LM_ROWS, LM_K = 4096, 3072  # a slice of the 200064-row vocabulary at the model's hidden size
+
+
+def lm_inputs():
+    """x [3072] f32 (the normed final hidden state) and a Q6_K matrix [4096][12 x 210 B]."""
+    x = S.normal_f32(LM_K, 901, 1, 1.0)
+    w = S.q6k_blocks(901, 2, LM_ROWS, LM_K)
+    return x, w

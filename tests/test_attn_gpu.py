@@ -237,3 +237,26 @@ def test_rmsnorm_rows(pkg, synth, dev):
     x64 = x.astype(np.float64)
     ref = x64 / np.sqrt(np.mean(x64 * x64, axis=1, keepdims=True) + 1e-6) * w
     assert _rel(y.cpu().numpy(), ref) < 1e-6
+
+
+def test_streaming_matvec_refills_the_ring(pkg, orc, synth, dev):
+    """A Q8_0 matrix of 24576 x 3072 (about 33 groups of rows per CTA, so every slot of the
+    12-slot ring is refilled): against the oracle, and bit-identical across repeated calls."""
+    import torch
+    L = pkg.lib()
+    rows, k = 24576, 3072
+    w = synth.q8_0_blocks(931, 2, rows, k)
+    x = synth.normal_f32(k, 931, 3, 1.0)
+    wd, xd = torch.from_numpy(np.ascontiguousarray(w)).to(dev), torch.from_numpy(x).to(dev)
+    vy = torch.zeros(k // 32 * 36, dtype=torch.uint8, device=dev)
+    L.launch_mmvq_gguf_quantize_q8_1_f32(C.c_void_p(xd.data_ptr()), C.c_void_p(vy.data_ptr()), k, k, 1, _s())
+    outs = []
+    for _ in range(3):
+        y = torch.zeros(rows, dtype=torch.float32, device=dev)
+        L.launch_mmvq_gguf_q8_0_f32_plain(C.c_void_p(wd.data_ptr()), C.c_void_p(vy.data_ptr()),
+                                          C.c_void_p(y.data_ptr()), k, rows, k // 32, rows, 1, _s())
+        torch.cuda.synchronize()
+        assert pkg.last_error() == 0
+        outs.append(y.cpu().numpy())
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
+    assert _rel(outs[0], orc.q8_0_matvec(w, rows, k, x)) < 1e-6
