@@ -471,16 +471,19 @@ static cudaError_t ms_launch(const MvParams &p, int grid, cudaStream_t s) {
 }
 
 // Blocks per lane 1..8 (k <= 8192); 16 consumer warps up to 3 blocks per lane (6 when every lane
-// has all its blocks), 8 above.
+// has all its blocks), 8 above.  The two shapes of the attention half (3 and 6 blocks, every lane
+// full) take 11: with the producer that is 12 warps, 3 per scheduler, so a thread may use up to
+// 168 registers instead of the 96 that 17 warps leave (the per-scheduler register file bounds
+// the busiest scheduler).
 template <bool kFull>
 static cudaError_t ms_dispatch(const MvParams &p, int grid, cudaStream_t s) {
     switch ((p.k / 32 + 31) / 32) {
         case 1: return ms_launch<1, 16, kFull>(p, grid, s);
         case 2: return ms_launch<2, 16, kFull>(p, grid, s);
-        case 3: return ms_launch<3, 16, kFull>(p, grid, s);
+        case 3: return ms_launch<3, kFull ? 11 : 16, kFull>(p, grid, s);
         case 4: return ms_launch<4, kFull ? 16 : 8, kFull>(p, grid, s);
         case 5: return ms_launch<5, kFull ? 16 : 8, kFull>(p, grid, s);
-        case 6: return ms_launch<6, kFull ? 16 : 8, kFull>(p, grid, s);
+        case 6: return ms_launch<6, kFull ? 11 : 8, kFull>(p, grid, s);
         case 7: return ms_launch<7, 8, kFull>(p, grid, s);
         default: return ms_launch<8, 8, kFull>(p, grid, s);
     }

@@ -8,9 +8,9 @@
 // HBM-bound (504 MB of Q6_K weights per token at the model's 200064 x 3072), so one streaming
 // kernel: one CTA per SM owns a contiguous range of rows (even-aligned: a Q6_K row is 2520
 // bytes, 16-byte aligned every second row), streamed in groups of 6 rows through a ring of 12
-// shared-memory slots by bulk copies from a producer warp; 16 consumer warps take a row per
-// step with lane = the reference's iqs (8 of a super-block's 256 weights), the lane's Q8_1
-// activation words and their -32 offsets in registers.  Logits go to global memory; each CTA
+// shared-memory slots by bulk copies from a producer warp; 11 consumer warps take a group at a
+// time with lane = the reference's iqs (8 of a super-block's 256 weights) and three rows a step,
+// the lane's Q8_1 activation words in registers.  Logits go to global memory; each CTA
 // folds its best (value, lowest index) into one 64-bit atomic maximum and the last CTA to finish
 // writes the token.
 #include <cuda_fp16.h>
@@ -26,11 +26,15 @@
 namespace mmrs {
 
 constexpr int kQ6Bytes = 210;       // ql[128] | qh[64] | int8 scales[16] | half d
-constexpr int kLmConsumers = 16;
+// 11 consumer warps + the producer = 12 warps, 3 per scheduler: 168 registers a thread are
+// available (144 used), enough for three rows in flight per warp; 17 warps capped the kernel at
+// 96 registers (measured 101 us per token against 129 us at 16 warps x 2 rows).
+constexpr int kLmConsumers = 11;
 constexpr int kLmThreads = 32 * (kLmConsumers + 1);
 constexpr int kLmSlots = 12;
 constexpr int kLmSlotBytes = 16384;
 constexpr int kLmGroupRows = 6;     // 15120 bytes: a multiple of 16
+constexpr int kLmRowsPerStep = 3;   // independent rows per warp step
 constexpr int kLmMaxK = 8192;
 constexpr int kLmMaxGroups = 512;
 
@@ -55,48 +59,49 @@ __device__ __forceinline__ unsigned long long lm_key(float v, int idx) {
     return ((unsigned long long)o << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
 }
 
-// dp4a with unsigned bytes in a (the 6-bit values 0..63) and signed bytes in b.
-__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
-    int d;
-    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
-
 // 32-bit word at byte offset `off` (2-byte aligned) of a row in shared memory.
 __device__ __forceinline__ uint32_t lm_word(const uint8_t *row, int off) {
     const uint32_t *w = reinterpret_cast<const uint32_t *>(row + (off & ~3));
     return (off & 3) ? __funnelshift_r(w[0], w[1], 16) : w[0];
 }
 
-// One row: lane = iqs.  Per super-block, the lane's 4 low-nibble and 4 high-nibble weights
-// (vl, vh as vec_dot_q6_K_q8_1 reads them), dotted with its two activation words u[s][i]
-// (offset -32 folded into c[s][i] = -32 * sum of u's bytes), scaled by the 16-weight scales and
-// the activation block scales d8, then by the super-block d: the reference's
-// d * (d8[0] * (dot0 * sc0) + d8[1] * (dot1 * sc1)) summed over the row, then the warp butterfly.
-template <int NSB>
-__device__ __forceinline__ float lm_row_dot(const uint8_t *row, int lane, const int (&u)[NSB][2],
-                                            const int (&c)[NSB][2], const float (&d8)[NSB][2]) {
+// R rows: lane = iqs.  Per super-block, the lane's 4 low-nibble and 4 high-nibble weights
+// (vl, vh as vec_dot_q6_K_q8_1 reads them) as signed bytes q - 32 (per byte (q + 0x60) ^ 0x80:
+// q <= 63, so no carry crosses a byte), dotted with the lane's two activation words u[s][i],
+// scaled by the 16-weight scales and the activation block scales d8, then by the super-block d:
+// the reference's d * (d8[0] * (dot0 * sc0) + d8[1] * (dot1 * sc1)) summed over the row, then the
+// warp butterfly.  The R rows are independent chains (more loads in flight per warp).
+template <int NSB, int R>
+__device__ __forceinline__ void lm_rows_dot(const uint8_t *rows, size_t row_bytes, int lane, const int (&u)[NSB][2],
+                                            const float (&d8)[NSB][2], float (&out)[R]) {
     const int qh_word = (lane / 16) * 8 + lane % 8, vh_shift = 2 * ((lane % 16) / 8);
     const int so = (lane / 16) * 8 + (lane % 16) / 4;
-    float acc = 0.0f;
+#pragma unroll
+    for (int q = 0; q < R; ++q) out[q] = 0.0f;
 #pragma unroll
     for (int s = 0; s < NSB; ++s) {
-        const int base = s * kQ6Bytes;
-        const uint32_t vl = lm_word(row, base + 4 * lane);
-        const uint32_t vh = lm_word(row, base + 128 + 4 * qh_word) >> vh_shift;
-        const int sc0 = (int8_t)row[base + 192 + so], sc1 = (int8_t)row[base + 192 + so + 4];
-        const float d = __half2float(*reinterpret_cast<const __half *>(row + base + 208));
-        const uint32_t v0 = (vl & 0x0F0F0F0Fu) | ((vh << 4) & 0x30303030u);
-        const uint32_t v1 = ((vl >> 4) & 0x0F0F0F0Fu) | (vh & 0x30303030u);
-        const int dot0 = dp4a_us(v0, u[s][0], c[s][0]), dot1 = dp4a_us(v1, u[s][1], c[s][1]);
-        float sumf = 0.0f;
-        sumf += d8[s][0] * (float)(dot0 * sc0);
-        sumf += d8[s][1] * (float)(dot1 * sc1);
-        acc += d * sumf;
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+            const uint8_t *row = rows + q * row_bytes;
+            const int base = s * kQ6Bytes;
+            const uint32_t vl = lm_word(row, base + 4 * lane);
+            const uint32_t vh = lm_word(row, base + 128 + 4 * qh_word) >> vh_shift;
+            const int sc0 = (int8_t)row[base + 192 + so], sc1 = (int8_t)row[base + 192 + so + 4];
+            const float d = __half2float(*reinterpret_cast<const __half *>(row + base + 208));
+            const uint32_t v0 = (((vl & 0x0F0F0F0Fu) | ((vh << 4) & 0x30303030u)) + 0x60606060u) ^ 0x80808080u;
+            const uint32_t v1 = ((((vl >> 4) & 0x0F0F0F0Fu) | (vh & 0x30303030u)) + 0x60606060u) ^ 0x80808080u;
+            const int dot0 = __dp4a((int)v0, u[s][0], 0), dot1 = __dp4a((int)v1, u[s][1], 0);
+            // |dot * sc| < 2^20: exact conversion on the integer / FP32 pipes (int22_to_float)
+            float sumf = 0.0f;
+            sumf += d8[s][0] * int22_to_float(dot0 * sc0);
+            sumf += d8[s][1] * int22_to_float(dot1 * sc1);
+            out[q] += d * sumf;
+        }
     }
 #pragma unroll
-    for (int m = 16; m > 0; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
-    return acc;
+    for (int m = 16; m > 0; m >>= 1)
+#pragma unroll
+        for (int q = 0; q < R; ++q) out[q] += __shfl_xor_sync(0xffffffffu, out[q], m);
 }
 
 template <int NSB>
@@ -156,7 +161,7 @@ __global__ void __launch_bounds__(kLmThreads, 1) lm_q6k_kernel(const LmParams p)
     }
     bool ok = mbar_wait_sleep(abar, 0u, deadline);
     // the lane's activation words: super-block s, part i -> Q8_1 block 8s + bq8_offset + 2i
-    int u[NSB][2], c[NSB][2];
+    int u[NSB][2];
     float d8[NSB][2];
     {
         const int bq8 = 4 * (lane / 16) + (lane % 16) / 8;
@@ -166,7 +171,6 @@ __global__ void __launch_bounds__(kLmThreads, 1) lm_q6k_kernel(const LmParams p)
             for (int i = 0; i < 2; ++i) {
                 const uint8_t *blk = act + (size_t)(8 * s + bq8 + 2 * i) * 36;
                 u[s][i] = reinterpret_cast<const int *>(blk + 4)[lane % 8];
-                c[s][i] = -32 * __dp4a(u[s][i], 0x01010101, 0);
                 d8[s][i] = __half2float(*reinterpret_cast<const __half *>(blk));
             }
     }
@@ -179,11 +183,25 @@ __global__ void __launch_bounds__(kLmThreads, 1) lm_q6k_kernel(const LmParams p)
         }
         const uint8_t *g = slots + (size_t)st * kLmSlotBytes;
         const int g0 = r0 + j * kLmGroupRows, n = min(kLmGroupRows, r1 - g0);
-        for (int i = 0; i < n; ++i) {
-            const float v = lm_row_dot<NSB>(g + (size_t)i * row_bytes, lane, u, c, d8);
+        int i = 0;
+        for (; i + kLmRowsPerStep <= n; i += kLmRowsPerStep) {
+            float v[kLmRowsPerStep];
+            lm_rows_dot<NSB, kLmRowsPerStep>(g + (size_t)i * row_bytes, row_bytes, lane, u, d8, v);
             if (lane == 0) {
-                p.logits[g0 + i] = v;
-                const unsigned long long key = lm_key(v, g0 + i);
+#pragma unroll
+                for (int q = 0; q < kLmRowsPerStep; ++q) {
+                    p.logits[g0 + i + q] = v[q];
+                    const unsigned long long key = lm_key(v[q], g0 + i + q);
+                    best = key > best ? key : best;
+                }
+            }
+        }
+        for (; i < n; ++i) {  // the last group of a CTA may be shorter
+            float v[1];
+            lm_rows_dot<NSB, 1>(g + (size_t)i * row_bytes, row_bytes, lane, u, d8, v);
+            if (lane == 0) {
+                p.logits[g0 + i] = v[0];
+                const unsigned long long key = lm_key(v[0], g0 + i);
                 best = key > best ? key : best;
             }
         }
@@ -192,10 +210,11 @@ __global__ void __launch_bounds__(kLmThreads, 1) lm_q6k_kernel(const LmParams p)
     }
     if (ok && (p.rows & 1) && blockIdx.x == gridDim.x - 1 && warp == 0) {  // odd last row, from global memory
         const int r = p.rows - 1;
-        const float v = lm_row_dot<NSB>(p.w + (size_t)r * row_bytes, lane, u, c, d8);
+        float v[1];
+        lm_rows_dot<NSB, 1>(p.w + (size_t)r * row_bytes, row_bytes, lane, u, d8, v);
         if (lane == 0) {
-            p.logits[r] = v;
-            const unsigned long long key = lm_key(v, r);
+            p.logits[r] = v[0];
+            const unsigned long long key = lm_key(v[0], r);
             best = key > best ? key : best;
         }
     }
