@@ -375,6 +375,7 @@ def run_config0(pkg, synth, dev, args) -> dict:
 C3_POS = 8191  # configs[3]: the token attends to an 8192-position KV cache
 C3_SEED = 3001
 LM_SEED = 4001  # the LM head line (configs[4]'s end-of-stack projection)
+C4_SEED = 4002
 
 
 def run_config3(pkg, synth, dev, args) -> dict:
@@ -528,6 +529,109 @@ def run_lm_head(pkg, dev, args) -> dict:
     return out
 
 
+def run_config4(pkg, synth, dev, args) -> dict:
+    """configs[4] on one GPU: a decode step of the whole 62-layer stack at context 32768 — per layer
+    attn_norm, the attention half over the layer's 32768-position f16 KV cache (filled with
+    synthetic values in place of the prefill), ffn_norm, the MoE block — then output_norm, the Q6_K
+    LM head and the greedy token.  The 62 layers have their own attention weights and caches; the
+    MoE weights are 16 distinct sets used in turn (62 x 2.2 GB would not fit one GPU; a token reads
+    62 x 73 MB of expert weights, 35 times L2, so no layer finds its set in L2).  One step is a CUDA
+    graph (~560 launches) replayed at position 32767."""
+    import torch
+    NL, NMOE, CTX = 62, 16, 32768
+    pos = CTX - 1
+    qr, kr = 48 * 128, 8 * 128
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(C4_SEED)
+
+    def q8_0(rows, k):
+        nb = k // 32
+        b = torch.randint(-128, 128, (rows, nb, 34), dtype=torch.int16, device=dev, generator=gen).to(torch.int8)
+        b = b.view(torch.uint8)
+        d = (torch.randn(rows, nb, device=dev, generator=gen).abs() * 0.01).half()
+        b[:, :, :2] = d.view(torch.uint8).reshape(rows, nb, 2)
+        return b.reshape(-1).contiguous()
+
+    def normw(n):
+        return (1.0 + 0.1 * torch.randn(n, device=dev, generator=gen)).float()
+
+    cos, sin = synth.rope_tables(CTX, 64)
+    cos_t, sin_t = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
+    attn, an, fn = [], [], []
+    for _ in range(NL):
+        L = pkg.AttnLayer(q8_0(qr, H), q8_0(kr, H), q8_0(kr, H), q8_0(H, qr), normw(qr), normw(kr), cos_t, sin_t, H)
+        L.k_cache.normal_(generator=gen)
+        L.v_cache.normal_(generator=gen)
+        attn.append(L)
+        an.append(normw(H))
+        fn.append(normw(H))
+    moe = build_layers(pkg, synth, dev, NMOE, seed=C4_SEED)
+    for m in moe:
+        m.workspace(1)
+    vocab, nsb = 200064, H // 256
+    w = torch.randint(0, 256, (vocab, nsb, 210), dtype=torch.int16, device=dev, generator=gen).to(torch.uint8)
+    w[:, :, 192:208] = (torch.randint(-64, 64, (vocab, nsb, 16), dtype=torch.int16, device=dev, generator=gen)
+                        .to(torch.int8).view(torch.uint8))
+    w[:, :, 208:] = (torch.randn(vocab, nsb, device=dev, generator=gen).abs() * 0.002).half().view(torch.uint8).reshape(
+        vocab, nsb, 2)
+    head = pkg.LmHead(w.reshape(-1).contiguous(), normw(H), vocab, H)
+    del w
+    x0 = torch.randn(H, device=dev, generator=gen)  # the step's input token embedding (synthetic)
+    h, h2, n1, n2 = (torch.empty(H, device=dev) for _ in range(4))
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        h.copy_(x0)
+        for l in range(NL):
+            pkg.rmsnorm(h, an[l], y=n1, stream=stream)
+            attn[l].forward(n1, pos, residual=h, y=h2, stream=stream)
+            pkg.rmsnorm(h2, fn[l], y=n2, stream=stream)
+            moe[l % NMOE].forward(n2.view(1, H), residual=h2.view(1, H), y=h.view(1, H), stream=stream)
+        head.forward(h, stream=stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step()
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step()
+        for _ in range(3):
+            g.replay()
+        stream.synchronize()
+        reps = 10
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(0) as clk:
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+            e1.synchronize()
+    ok = all(m.status() == 0 for m in moe) and all(a.status() == 0 for a in attn[:4]) and head.status() == 0
+    assert ok, "device-side timeout in configs[4]"
+    tok = int(head.token.item())
+    assert 0 <= tok < vocab and tok == int(torch.argmax(head.logits).item())
+    del g
+    ms = e0.elapsed_time(e1) / reps
+    kv = 2 * 8 * CTX * 128 * 2
+    attn_w = (qr * H + 2 * kr * H + H * qr) * 34 // 32
+    alg = NL * (attn_w + kv + algorithmic_bytes() + 4 * H * 4) + vocab * nsb * 210 + vocab * 4
+    peaks = measured_peaks()
+    out = {"metric": "stack_decode_tokens_per_s", "value": 1.0 / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+           "config": {"workload": "62-layer decode step at context 32768 (BASELINE configs[4], W = 1): per layer "
+                                  "attn_norm, Q8_0 attention over the layer's f16 KV cache, ffn_norm, MoE block; "
+                                  "output_norm, Q6_K LM head [200064 x 3072], greedy token",
+                      "layers": NL, "moe_weight_sets": NMOE, "kv_positions": CTX, "token": tok,
+                      "data": "synthetic (seeded torch generator; KV caches filled with N(0,1) f16 in place of "
+                              "the prefill)"},
+           "roofline": {"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                        "frac": alg / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], "algorithmic_bytes_per_step": alg},
+           "clocks": clk.summary()}
+    del attn, moe, head
+    torch.cuda.empty_cache()
+    return out
+
+
 def ar_sweep(group, world: int, dev, iters: int = 50) -> dict:
     """Hidden-state all-reduce over T x 3072 f32 (T = 1, 8, 64, 512, 2048): the peer exchange of
     this library (rank-ordered sum, residual fused) and NCCL's all_reduce for comparison.
@@ -628,6 +732,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=2000)
     ap.add_argument("--no-config3", action="store_true", help="skip the configs[3] decoder-layer line")
     ap.add_argument("--no-lm-head", action="store_true", help="skip the LM head line")
+    ap.add_argument("--no-config4", action="store_true", help="skip the configs[4] whole-stack decode line")
+    ap.add_argument("--only-config4", action="store_true", help="run only the configs[4] measurement")
     ap.add_argument("--only-lm-head", action="store_true", help="run only the LM head measurement (profiling)")
     ap.add_argument("--only-config3", action="store_true",
                     help="run only the configs[3] decoder-layer measurement and print its object (profiling)")
@@ -662,6 +768,9 @@ def main():
         return
     if args.only_lm_head:
         print(json.dumps(run_lm_head(pkg, dev, args)))
+        return
+    if args.only_config4:
+        print(json.dumps(run_config4(pkg, synth, dev, args)))
         return
     group = None
     if world > 1:
