@@ -925,6 +925,7 @@ def main():
     config0 = run_config0(pkg, synth, dev, args) if world == 1 and not args.no_prefill else None
     config3 = run_config3(pkg, synth, dev, args) if world == 1 and not args.no_config3 else None
     lm_head = run_lm_head(pkg, dev, args) if world == 1 and not args.no_lm_head else None
+    config4 = run_config4(pkg, synth, dev, args) if world == 1 and not args.no_config4 else None
 
     if rank == 0:
         out = {
@@ -954,6 +955,7 @@ def main():
             "config0": config0,
             "config3": config3,
             "lm_head": lm_head,
+            "config4": config4,
         }
         print(json.dumps(out), flush=True)
     if world > 1:
