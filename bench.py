@@ -607,8 +607,9 @@ def run_config4(pkg, synth, dev, args) -> dict:
                 g.replay()
             e1.record(stream)
             e1.synchronize()
-    ok = all(m.status() == 0 for m in moe) and all(a.status() == 0 for a in attn[:4]) and head.status() == 0
-    assert ok, "device-side timeout in configs[4]"
+    bad = {"moe": [i for i, m in enumerate(moe) if m.status() != 0],
+           "attn": [i for i, a in enumerate(attn) if a.status() != 0], "lm_head": head.status()}
+    assert not bad["moe"] and not bad["attn"] and bad["lm_head"] == 0, f"device-side timeout in configs[4]: {bad}"
     tok = int(head.token.item())
     assert 0 <= tok < vocab and tok == int(torch.argmax(head.logits).item())
     del g
