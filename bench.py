@@ -415,6 +415,8 @@ def run_config3(pkg, synth, dev, args) -> dict:
     xs = torch.randn(NL, H, device=dev, generator=gen)
     n1, h, n2, y = (torch.empty(H, device=dev) for _ in range(4))
     stream = torch.cuda.Stream(device=dev)
+    # weights and zeroed workspaces were made on the default stream; `stream` does not wait for it
+    torch.cuda.synchronize()
 
     def layer_step(i):
         l = i % NL
@@ -491,6 +493,8 @@ def run_lm_head(pkg, dev, args) -> dict:
     x = torch.randn(hidden, device=dev, generator=gen)
     head = pkg.LmHead(w, nw, vocab, hidden)
     stream = torch.cuda.Stream(device=dev)
+    # weights and the zeroed workspace were made on the default stream; `stream` does not wait for it
+    torch.cuda.synchronize()
     per, reps = 8, 12
     with torch.cuda.stream(stream):
         for _ in range(per):
@@ -579,6 +583,8 @@ def run_config4(pkg, synth, dev, args) -> dict:
     x0 = torch.randn(H, device=dev, generator=gen)  # the step's input token embedding (synthetic)
     h, h2, n1, n2 = (torch.empty(H, device=dev) for _ in range(4))
     stream = torch.cuda.Stream(device=dev)
+    # weights and zeroed workspaces were made on the default stream; `stream` does not wait for it
+    torch.cuda.synchronize()
 
     def step():
         h.copy_(x0)
@@ -607,7 +613,7 @@ def run_config4(pkg, synth, dev, args) -> dict:
                 g.replay()
             e1.record(stream)
             e1.synchronize()
-    bad = {"moe": [i for i, m in enumerate(moe) if m.status() != 0],
+    bad = {"moe": [(i, st) for i, m in enumerate(moe) for st in [m.status()] if st != 0],
            "attn": [i for i, a in enumerate(attn) if a.status() != 0], "lm_head": head.status()}
     assert not bad["moe"] and not bad["attn"] and bad["lm_head"] == 0, f"device-side timeout in configs[4]: {bad}"
     tok = int(head.token.item())
