@@ -5,10 +5,10 @@
 //   -> quantize_q8_1 -> moe_gate_up_decode_kernel -> quantize_silu_mul_q8_1
 //   -> moe_down_decode_kernel (moe_gguf.cu:200-343, 426-567) -> + residual (model.rs:218)
 //
-// One CTA per SM: 16 consumer warps (two groups of 8) + 1 producer warp.
-//   P0  router GEMV in the canonical order (8 K-slices; warp w computes slice w%8 of the CTA's
-//       expert w/8: 32 lane partials, butterfly, fixed slice tree); every CTA quantises x to Q8_1
-//       in shared memory.  Grid barrier #1.
+// One CTA per SM: 12 consumer warps (three groups of 4) + 1 producer warp.
+//   P0  router GEMV in the canonical order (8 K-slices; the CTA's two experts x 8 slices are 16
+//       (expert, slice) pairs, pair w + 12 r to consumer warp w: 32 lane partials, butterfly,
+//       fixed slice tree); every CTA quantises x to Q8_1 in shared memory.  Grid barrier #1.
 //   P1  every CTA selects the top-8 with warp-shuffle argmax rounds on 64-bit keys
 //       (score desc, expert id asc — the stable descending order) and renormalises the weights
 //       with the reference's fixed tree.
@@ -35,11 +35,14 @@
 namespace mmrs {
 
 constexpr int kGroupWarps = 4;
-constexpr int kGroups = 4;
+// 3 groups of 4 consumer warps + the producer = 13 warps (at most 4 on a scheduler): 128 registers
+// a thread; 4 groups (17 warps, 5 on one scheduler) capped the kernel at 96 with spills.
+constexpr int kGroups = 3;
 constexpr int kRowsPerLane = 2;   // rows a lane group computes per unit (same activation registers)
 constexpr int kMaxUnits = 96;
 constexpr int kConsumerWarps = kGroupWarps * kGroups;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kRouterRounds = (16 + kConsumerWarps - 1) / kConsumerWarps;  // 2 experts x 8 K-slices per CTA
 constexpr int kThreads = kConsumerThreads + 32;
 constexpr int kTopK = 8;
 constexpr int kTPL = 3;  // tasks (64-weight sub-block pairs) per lane
@@ -330,19 +333,23 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         float rv = 0.f;
         const int rrow = dn_r0 + tid;
         if (p.residual && rrow < dn_r1) rv = __ldg(p.residual + rrow);
-        const int slice = H / 8, groups = slice / 4, sl = warp & 7, le = warp >> 3;
-        const int e = cta + G * le;
-        const bool do_router = p.internal_routing && e < E;
-        float4 xx[4], wv[4];
-        if (do_router) {
-            const float4 *xs = reinterpret_cast<const float4 *>(p.x + sl * slice);
-            const float4 *wr = reinterpret_cast<const float4 *>(p.router + (size_t)e * H + sl * slice);
+        // router pairs (expert le of this CTA's two, K-slice sl): pair pi = warp + kConsumerWarps * r
+        const int slice = H / 8, groups = slice / 4;
+        float4 xx[kRouterRounds][4], wv[kRouterRounds][4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int g = lane + 32 * i;
-                if (g < groups) {
-                    xx[i] = __ldg(xs + g);
-                    wv[i] = __ldg(wr + g);
+        for (int r = 0; r < kRouterRounds; ++r) {
+            const int pi = warp + kConsumerWarps * r, sl = pi & 7, le = pi >> 3;
+            const int e = cta + G * le;
+            if (pi < 16 && p.internal_routing && e < E) {
+                const float4 *xs = reinterpret_cast<const float4 *>(p.x + sl * slice);
+                const float4 *wr = reinterpret_cast<const float4 *>(p.router + (size_t)e * H + sl * slice);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int g = lane + 32 * i;
+                    if (g < groups) {
+                        xx[r][i] = __ldg(xs + g);
+                        wv[r][i] = __ldg(wr + g);
+                    }
                 }
             }
         }
@@ -355,16 +362,19 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             if (c < nxc) quant128(xv[i], s.xq + c * 128, s.xd + c * 4, s.xS + c * 4, lane);
         }
         if (p.residual && rrow < dn_r1) s.res_s[tid] = rv;
-        if (do_router) {
+#pragma unroll
+        for (int r = 0; r < kRouterRounds; ++r) {
+            const int pi = warp + kConsumerWarps * r, sl = pi & 7, le = pi >> 3;
+            if (!(pi < 16 && p.internal_routing && cta + G * le < E)) continue;
             float acc = 0.f;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const int g = lane + 32 * i;
                 if (g < groups) {
-                    acc = fmaf(wv[i].x, xx[i].x, acc);
-                    acc = fmaf(wv[i].y, xx[i].y, acc);
-                    acc = fmaf(wv[i].z, xx[i].z, acc);
-                    acc = fmaf(wv[i].w, xx[i].w, acc);
+                    acc = fmaf(wv[r][i].x, xx[r][i].x, acc);
+                    acc = fmaf(wv[r][i].y, xx[r][i].y, acc);
+                    acc = fmaf(wv[r][i].z, xx[r][i].z, acc);
+                    acc = fmaf(wv[r][i].w, xx[r][i].w, acc);
                 }
             }
             acc = warp_sum_butterfly(acc);
