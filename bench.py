@@ -519,6 +519,41 @@ def run_lm_head(pkg, dev, args) -> dict:
     assert tok == int(torch.argmax(head.logits).item()), "greedy token differs from the logits' argmax"
     del g
     ms = e0.elapsed_time(e1) / (reps * per)
+    # token sampling over the logits just written (L2-resident, as right after the LM head):
+    # TokenSampler::sample at the reference's defaults, with no cut, greedy; and token_logprob
+    samp = {}
+    for name, (t, p, k) in (("default_t1_p095_k40", (1.0, 0.95, 40)), ("no_cut_t1", (1.0, 1.0, 0)),
+                            ("greedy", (0.0, 1.0, 0)), ("logprob", (1.0, 0.95, 40))):
+        sm = pkg.Sampler(vocab, dev, temperature=t, top_p=p, top_k=k)
+        call = ((lambda: sm.token_logprob(head.logits, 4321, stream=stream)) if name == "logprob"
+                else (lambda: sm.sample(head.logits, 0.37, stream=stream)))
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                call()
+            stream.synchronize()
+            gs = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gs, stream=stream):
+                for _ in range(per):
+                    call()
+            gs.replay()
+            stream.synchronize()
+            e0.record(stream)
+            for _ in range(reps):
+                gs.replay()
+            e1.record(stream)
+            e1.synchronize()
+        assert sm.status() == 0, f"sampling ({name}) status {sm.status()}"
+        samp[name + "_us"] = e0.elapsed_time(e1) / (reps * per) * 1e3
+        del gs, sm
+    host = torch.empty(vocab, dtype=torch.float32, pin_memory=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            host.copy_(head.logits, non_blocking=True)
+        e1.record(stream)
+        e1.synchronize()
+    samp["logits_d2h_us"] = e0.elapsed_time(e1) / reps * 1e3  # what the reference's stochastic path copies
     alg = vocab * nsb * 210 + hidden * 4 * 2 + vocab * 4  # weights + x and norm weight + logits written
     peaks = measured_peaks()
     out = {"metric": "lm_head_tokens_per_s", "value": 1.0 / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
@@ -527,6 +562,7 @@ def run_lm_head(pkg, dev, args) -> dict:
                       "data": "synthetic (seeded torch generator)"},
            "roofline": {"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                         "frac": alg / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], "algorithmic_bytes_per_step": alg},
+           "sampling": samp,
            "clocks": clk.summary()}
     del head, w
     torch.cuda.empty_cache()

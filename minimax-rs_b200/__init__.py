@@ -22,9 +22,10 @@ HEADER = PKG_DIR.parent / "include" / "minimax_moe.h"
 
 MMRS_OK, MMRS_ERR_ARG, MMRS_ERR_UNSUPPORTED, MMRS_ERR_LAUNCH, MMRS_ERR_TIMEOUT, MMRS_ERR_ALLOC = range(6)
 MMRS_ERR_SCRATCH_LIMIT = 6
+MMRS_ERR_NONFINITE = 7
 Q8_0, Q4K, Q2K, Q3K, Q5K, Q6K = 0, 1, 2, 3, 4, 5
 ERROR_NAMES = {0: "ok", 1: "invalid argument", 2: "unsupported", 3: "launch failure", 4: "device wait timed out",
-               5: "allocation failure", 6: "problem exceeds the fixed scratch"}
+               5: "allocation failure", 6: "problem exceeds the fixed scratch", 7: "non-finite value"}
 
 
 class MoeError(RuntimeError):
@@ -51,6 +52,11 @@ _SZ = C.c_size_t
 class MmrsLmHead(C.Structure):
     _fields_ = [("weight", C.c_void_p), ("norm_weight", C.c_void_p), ("vocab", C.c_int), ("hidden", C.c_int),
                 ("eps", C.c_float)]
+
+
+class MmrsSamplingParams(C.Structure):
+    """include/minimax_sample.h: SamplingParams (src/sampling.rs:13-17)."""
+    _fields_ = [("temperature", C.c_double), ("top_p", C.c_double), ("top_k", C.c_int)]
 
 
 class MmrsAttnWeights(C.Structure):
@@ -82,6 +88,11 @@ PROTOTYPES = {
     "mmrs_lm_head_workspace_status": (_I, [_VP]),
     "mmrs_lm_head_forward": (_I, [C.POINTER(MmrsLmHead), _VP, _VP, _VP, _VP, _SZ, _VP]),
     "mmrs_rmsnorm_f32": (_I, [_VP, _VP, _VP, _I, _I, _F, _VP]),
+    # token sampling (include/minimax_sample.h)
+    "mmrs_sample_workspace_bytes": (_SZ, [_I]),
+    "mmrs_sample_workspace_status": (_I, [_VP]),
+    "mmrs_sample_token": (_I, [_VP, _I, C.POINTER(MmrsSamplingParams), C.c_double, _VP, _VP, _SZ, _VP]),
+    "mmrs_token_logprob": (_I, [_VP, _I, _I, _VP, _VP, _SZ, _VP]),
     "mmrs_attn_decode_forward": (_I, [C.POINTER(MmrsAttnWeights), _VP, _VP, _I, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "launch_tp2_peer_all_reduce_f32": (None, [_VP] * 8 + [C.c_uint, _I, _F, _VP]),
     "launch_tp2_peer_broadcast_f32": (None, [_VP] * 4 + [C.c_uint, _I, _I, _VP]),
@@ -307,6 +318,58 @@ class LmHead:
                                         self.ws.data_ptr(), self.ws.numel(), _stream(stream))
         check(rc, "mmrs_lm_head_forward")
         return self.logits, self.token
+
+
+DEFAULT_TEMPERATURE, DEFAULT_TOP_P, DEFAULT_TOP_K = 1.0, 0.95, 40  # src/sampling.rs:6-8
+
+
+class Sampler:
+    """TokenSampler (src/sampling.rs:43-150) over device logits: greedy at temperature 0, else top-k,
+    top-p and temperature sampling, the choice made on the device (mmrs_sample_token).  The uniform
+    draw is the caller's: `sample(logits, u)` takes it, or draws it from this sampler's own
+    generator (numpy PCG64 seeded with `seed`; the reference draws from a per-request StdRng) only
+    when the temperature is positive, as the reference draws only then."""
+
+    def __init__(self, vocab: int, device, temperature: float = DEFAULT_TEMPERATURE, top_p: float = DEFAULT_TOP_P,
+                 top_k: int = DEFAULT_TOP_K, seed: int = 0):
+        import math
+
+        import numpy as np
+        import torch
+        # SamplingParams::validate (src/sampling.rs:31-39)
+        if not math.isfinite(temperature) or temperature < 0.0:
+            raise MoeError(MMRS_ERR_ARG, "temperature must be a finite number greater than or equal to 0")
+        if not math.isfinite(top_p) or not 0.0 <= top_p <= 1.0:
+            raise MoeError(MMRS_ERR_ARG, "top_p must be a finite number between 0 and 1")
+        self.params = MmrsSamplingParams(float(temperature), float(top_p), int(top_k))
+        self.vocab = vocab
+        n = lib().mmrs_sample_workspace_bytes(vocab)
+        if n == 0:
+            raise MoeError(MMRS_ERR_ARG, "mmrs_sample_workspace_bytes")
+        self.ws = torch.zeros(n, dtype=torch.uint8, device=device)
+        self.token = torch.full((1,), -1, dtype=torch.int32, device=device)
+        self.logprob = torch.zeros(1, dtype=torch.float32, device=device)
+        self.rng = np.random.default_rng(seed)
+
+    def status(self) -> int:
+        """Outcome of the last completed call (synchronous)."""
+        return lib().mmrs_sample_workspace_status(self.ws.data_ptr())
+
+    def sample(self, logits, u: float | None = None, stream=None):
+        """token [1] int32 on the device (-1 when status() is not MMRS_OK) for logits [vocab] f32."""
+        if u is None:
+            u = float(self.rng.random()) if self.params.temperature > 0.0 else 0.0
+        rc = lib().mmrs_sample_token(logits.data_ptr(), self.vocab, C.byref(self.params), float(u),
+                                     self.token.data_ptr(), self.ws.data_ptr(), self.ws.numel(), _stream(stream))
+        check(rc, "mmrs_sample_token")
+        return self.token
+
+    def token_logprob(self, logits, token_id: int, stream=None):
+        """ln softmax(logits)[token_id] as a [1] f32 device tensor (token_logprob, src/sampling.rs:60-75)."""
+        rc = lib().mmrs_token_logprob(logits.data_ptr(), self.vocab, int(token_id), self.logprob.data_ptr(),
+                                      self.ws.data_ptr(), self.ws.numel(), _stream(stream))
+        check(rc, "mmrs_token_logprob")
+        return self.logprob
 
 
 def rmsnorm(x, weight, y=None, eps: float = 1e-6, stream=None):

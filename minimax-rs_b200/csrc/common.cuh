@@ -171,6 +171,17 @@ __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// Greedy-choice key of a float (-0 == +0; NaN below every number) and the lowest index among
+// equal values: larger key = larger value, then smaller index.  The maximum over a vector is
+// its argmax (candle's argmax: the first index of the largest value).
+__device__ __forceinline__ unsigned long long lm_key(float v, int idx) {
+    v = v + 0.0f;  // -0 -> +0
+    uint32_t u = __float_as_uint(v);
+    uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    if (v != v) o = 0u;
+    return ((unsigned long long)o << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
+}
+
 // Named barrier `id` over `nthreads` threads of the CTA.
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

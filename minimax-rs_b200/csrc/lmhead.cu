@@ -49,15 +49,6 @@ struct LmParams {
     uint32_t *status;   // optional: MMRS_ERR_TIMEOUT when a wait expired
 };
 
-// Order-preserving key of a float (-0 == +0; NaN below every number) and the lowest index among
-// equal values: larger key = larger value, then smaller index.
-__device__ __forceinline__ unsigned long long lm_key(float v, int idx) {
-    v = v + 0.0f;  // -0 -> +0
-    uint32_t u = __float_as_uint(v);
-    uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-    if (v != v) o = 0u;
-    return ((unsigned long long)o << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
-}
 
 // 32-bit word at byte offset `off` (2-byte aligned) of a row in shared memory.
 __device__ __forceinline__ uint32_t lm_word(const uint8_t *row, int off) {

@@ -125,6 +125,13 @@ void orc_partial_rope_f16(const uint16_t *q, const uint16_t *k, const float *cos
 void orc_gqa_decode_f16(const uint16_t *q, const uint16_t *k, const uint16_t *v, int seq_len, int q_heads,
                         int kv_heads, int head_dim, int64_t kv_head_stride, float scale, uint16_t *out);
 
+/* ---- token sampling (sample_oracle.c); statuses as the CUDA path's ---- */
+#define MMRS_ERR_ARG_ORC 1
+#define MMRS_ERR_NONFINITE_ORC 7
+int orc_sample_token(const float *logits, int vocab, double temperature, double top_p, int top_k, double u,
+                     int32_t *token, double *margin);
+int orc_token_logprob(const float *logits, int vocab, int token_id, float *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -19,7 +19,8 @@ BLOCK_BYTES = {Q4K: 144, Q5K: 176}
 
 
 def build() -> Path:
-    src = [HERE / "moe_oracle.c", HERE / "attn_oracle.c", HERE / "moe_oracle.h", HERE / "Makefile"]
+    src = [HERE / n for n in ("moe_oracle.c", "attn_oracle.c", "lmhead_oracle.c", "sample_oracle.c", "moe_oracle.h",
+                              "Makefile")]
     if not LIB_PATH.exists() or any(s.stat().st_mtime > LIB_PATH.stat().st_mtime for s in src):
         subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
     return LIB_PATH
@@ -201,6 +202,25 @@ def argmax_f32(v: np.ndarray) -> int:
     """First index of the maximum (the reference's greedy choice)."""
     v = _c(v, np.float32)
     return int(lib().orc_argmax_f32(_p(v), C.c_int(v.size)))
+
+
+def sample_token(logits: np.ndarray, temperature: float, top_p: float, top_k: int, u: float):
+    """(status, token, margin) of TokenSampler::sample for the draw u (sample_oracle.c); status 0,
+    1 (invalid parameters) or 7 (non-finite logits)."""
+    v = _c(logits, np.float32)
+    tok = C.c_int32(-1)
+    margin = C.c_double(0.0)
+    st = lib().orc_sample_token(_p(v), C.c_int(v.size), C.c_double(temperature), C.c_double(top_p), C.c_int(top_k),
+                                C.c_double(u), C.byref(tok), C.byref(margin))
+    return int(st), int(tok.value), float(margin.value)
+
+
+def token_logprob(logits: np.ndarray, token_id: int):
+    """(status, ln softmax(logits)[token_id]) (sample_oracle.c); status 0, 1 or 7."""
+    v = _c(logits, np.float32)
+    out = C.c_float(0.0)
+    st = lib().orc_token_logprob(_p(v), C.c_int(v.size), C.c_int(token_id), C.byref(out))
+    return int(st), float(out.value)
 
 
 def qkv_rmsnorm_f16(proj, q_alpha, k_alpha, q_rows: int, k_rows: int, v_rows: int, eps: float = 1e-6):
