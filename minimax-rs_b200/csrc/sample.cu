@@ -11,18 +11,20 @@
 //            total-order bits << 20 | (2^20 - 1 - id), so a larger key is a larger logit, then a
 //            smaller id (the reference's compare_candidates); it notes non-finite values and its
 //            largest key, and histograms the keys' top 13 bits;
-//   rounds   radix selection of the k-th largest key, 13 bits a round (4 rounds, one grid barrier
-//            each): every CTA adds its shared-memory histogram into a global one, and after the
-//            barrier every CTA scans the same global histogram, so all agree on the next digit
-//            without another exchange.  Two ranks are selected side by side when needed (the
-//            list top-p sorts, and the whole candidate set when top_k is larger than the list);
-//   top-p    CTAs append the keys at or above the list's threshold (at most 1024) to a global
-//            list; the last CTA to finish sorts it (bitonic, shared memory), cuts it where the
-//            cumulative weight reaches top_p of the total and draws from what is left;
-//   no top-p every CTA sums the weights of its slice's candidates (ids ascending), one more
-//            barrier lets every CTA form the same prefix over CTAs, and the CTA whose range holds
-//            u * total walks its slice to the chosen id.
-// Weights and sums are double, as the reference's.  The grid barrier is the bounded software
+//   rounds   radix selection of the k-th largest key, 13 bits a round (at most 4 rounds, one
+//            grid barrier each): every CTA adds its shared-memory histogram into a global one, and
+//            after the barrier every CTA scans the same global histogram, so all agree on the next
+//            digit without another exchange.  When a list of at most 1024 keys will do (top-p, or
+//            top_k <= 1024), selection stops at the first round whose digit leaves at most 1024
+//            keys at or above it — usually the first round — and the list's owner sorts them;
+//   list     CTAs append those keys to a global list; the last CTA to finish sorts it (bitonic,
+//            shared memory), keeps the top_k, cuts them where the cumulative weight reaches top_p
+//            of the total (or orders them by id when there is no top-p cut) and draws;
+//   walk     top_k > 1024 (or none) without top-p: the exact k-th key is selected, every CTA sums
+//            its candidates' weights (ids ascending), one more barrier lets every CTA form the
+//            same prefix over CTAs, and the CTA whose range holds u * total walks its slice.
+// Weights and sums are double, as the reference's; the token-log-probability call is one barrier
+// and a sum of exp(l - max).  The grid barrier is the bounded software
 // barrier of common.cuh (epoch words in the workspace); nothing else waits.
 #include <cuda_runtime.h>
 #include <math.h>
@@ -48,7 +50,9 @@ constexpr uint64_t kSpTimeoutNs = 2000000000ull;
 static_assert(kSpMaxSorted == 2 * kSpThreads, "the sorted list is two entries per thread");
 static_assert(kSpBins % kSpThreads == 0, "whole bins per thread");
 
-enum SpMode : int { kGreedy = 0, kSorted = 1, kIdOrder = 2, kLogprob = 3 };
+// kList: the candidates end in one list of at most 1024 keys that the last CTA finishes (top-p, or
+// top_k <= 1024); kIdWalk: top_k > 1024 (or none) without top-p, walked across the CTAs by id.
+enum SpMode : int { kGreedy = 0, kList = 1, kIdWalk = 2, kLogprob = 3 };
 
 // Flags in SpMisc::flags (cleared by the last CTA of every call).
 constexpr uint32_t kFlagNonfinite = 1u;
@@ -83,8 +87,9 @@ struct SpParams {
     const float *logits;
     int V, chunk, mode;
     int kA, kB;           // ranks to select (0: no selection, every key qualifies)
-    int list_n;           // kSorted: length of the sorted list (min(top_k, 1024))
-    int s_from_partials;  // top-p total over a candidate set larger than the sorted list
+    int list_n;           // kList: entries kept (min(top_k, 1024))
+    int sorted;           // kList: top-p cut (candidates in sorted order), else ascending id
+    int s_from_partials;  // top-p total over a candidate set larger than the list
     int token_id;         // kLogprob
     double top_p, temperature, u;
     int32_t *token;
@@ -155,11 +160,15 @@ __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v)
 struct SpShared {
     double sw_d[kSpWarps + 1];
     uint32_t sw_u[kSpWarps + 1];
-    unsigned long long max_key;
-    double d[4];
-    int i[8];
+    unsigned long long max_key, gmax_key;
     int ok;
     uint32_t epoch;
+    uint32_t flags;              // the call's flags, as read after the first barrier
+    int digit, above, in_bin;    // sp_scan's answer
+    int first, last;             // smallest / largest index a search found
+    int is_last;                 // this CTA finished last
+    int status;
+    int last_nz;                 // last CTA with a positive partial sum
 };
 
 // Histogram of round r for the active searches over the CTA's keys, added into the global one.
@@ -167,7 +176,8 @@ __device__ void sp_histogram(const SpParams &p, const unsigned long long *keys, 
                              const unsigned long long *prefix, const bool *act) {
     const int tid = threadIdx.x;
     const int shift = (kSpRounds - 1 - r) * kSpDigitBits;
-    for (int b = tid; b < 2 * kSpBins; b += kSpThreads) sh[b] = 0u;
+    const int b0 = act[0] ? 0 : kSpBins, b1 = act[1] ? 2 * kSpBins : kSpBins;
+    for (int b = b0 + tid; b < b1; b += kSpThreads) sh[b] = 0u;
     __syncthreads();
     for (int i = tid; i < n; i += kSpThreads) {
         const unsigned long long key = keys[i];
@@ -178,24 +188,31 @@ __device__ void sp_histogram(const SpParams &p, const unsigned long long *keys, 
     }
     __syncthreads();
     uint32_t *gh = p.hist + (size_t)r * 2 * kSpBins;
-    for (int b = tid; b < 2 * kSpBins; b += kSpThreads)
-        if (act[b / kSpBins] && sh[b]) atomicAdd(&gh[b], sh[b]);
+    for (int b = b0 + tid; b < b1; b += kSpThreads)
+        if (sh[b]) atomicAdd(&gh[b], sh[b]);
 }
 
-// Digit of round r for search s: the largest d with (count in bins above d) < need; returns the
-// count above it through *above (-1 digit when the histogram holds fewer than `need` keys).
-__device__ int sp_scan(const SpParams &p, SpShared &s, int r, int srch, uint32_t need, uint32_t *above) {
+// Digit of round r for search `srch`: the largest d with (count in bins above d) < need.  Returns d
+// (-1 when the histogram holds fewer than `need` keys), the count above it and the count in it.
+__device__ int sp_scan(const SpParams &p, SpShared &s, int r, int srch, uint32_t need, uint32_t *above,
+                       uint32_t *in_bin) {
     const int tid = threadIdx.x;
     const uint32_t *gh = p.hist + ((size_t)r * 2 + srch) * kSpBins;
     const int top = kSpBins - 1 - tid * kSpBinsPerThread;  // this thread: digits top, top-1, ...
+    static_assert(kSpBinsPerThread == 16, "four 16-byte loads a thread");
+    uint4 v[4];
+    const uint4 *src = reinterpret_cast<const uint4 *>(gh + top - (kSpBinsPerThread - 1));
+#pragma unroll
+    for (int q = 0; q < 4; ++q) v[q] = __ldcg(src + q);
+    const uint32_t *flat = reinterpret_cast<const uint32_t *>(v);
     uint32_t c[kSpBinsPerThread];
     uint32_t sum = 0;
 #pragma unroll
     for (int j = 0; j < kSpBinsPerThread; ++j) {
-        c[j] = __ldcg(gh + top - j);
+        c[j] = flat[kSpBinsPerThread - 1 - j];
         sum += c[j];
     }
-    if (tid == 0) s.i[2] = -1;
+    if (tid == 0) s.digit = -1;
     uint32_t tot;
     const uint32_t ex = block_excl_scan(sum, s.sw_u, tot);  // (its barriers order the store above)
     if (ex < need && need <= ex + sum) {
@@ -203,17 +220,19 @@ __device__ int sp_scan(const SpParams &p, SpShared &s, int r, int srch, uint32_t
 #pragma unroll
         for (int j = 0; j < kSpBinsPerThread; ++j) {
             if (run + c[j] >= need) {
-                s.i[2] = top - j;
-                s.i[3] = (int)run;
+                s.digit = top - j;
+                s.above = (int)run;
+                s.in_bin = (int)c[j];
                 break;
             }
             run += c[j];
         }
     }
     __syncthreads();
-    const int d = s.i[2];
-    *above = (uint32_t)s.i[3];
-    __syncthreads();  // (the next scan resets s.i[2])
+    const int d = s.digit;
+    *above = (uint32_t)s.above;
+    *in_bin = (uint32_t)s.in_bin;
+    __syncthreads();  // (the next scan resets s.digit)
     return d;
 }
 
@@ -241,7 +260,41 @@ __device__ void sp_sort_desc(unsigned long long *k, int n2) {
     }
 }
 
-// Inclusive cumulative weights of the sorted list (two entries per thread: 2t, 2t + 1).
+// Sort of at most 64 keys into descending order by warp 0 in registers (lane l holds entries l
+// and l + 32); the other warps wait at the closing barrier.
+__device__ void sp_warp_sort64_desc(unsigned long long *k, int n) {
+    const int lane = threadIdx.x & 31;
+    if (threadIdx.x < 32) {
+        unsigned long long x[2] = {lane < n ? k[lane] : 0ull, lane + 32 < n ? k[lane + 32] : 0ull};
+#pragma unroll
+        for (int size = 2; size <= 64; size <<= 1) {
+#pragma unroll
+            for (int j = size >> 1; j > 0; j >>= 1) {
+                if (j == 32) {
+                    if (x[0] < x[1]) {  // entries l and l + 32 of the one block of 64: descending
+                        const unsigned long long t = x[0];
+                        x[0] = x[1];
+                        x[1] = t;
+                    }
+                } else {
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int i = lane + 32 * h;
+                        const unsigned long long y = __shfl_xor_sync(0xffffffffu, x[h], j);
+                        const bool lower = (i & j) == 0, desc = (i & size) == 0;
+                        const unsigned long long hi = x[h] > y ? x[h] : y, lo = x[h] > y ? y : x[h];
+                        x[h] = (desc == lower) ? hi : lo;
+                    }
+                }
+            }
+        }
+        k[lane] = x[0];
+        k[lane + 32] = x[1];
+    }
+    __syncthreads();
+}
+
+// Inclusive cumulative weights of a list of 1024 (two entries per thread: 2t, 2t + 1).
 __device__ void sp_cumulate(const double *w, double *cum, SpShared &s, double *total) {
     const int tid = threadIdx.x;
     const double a = w[2 * tid], b = w[2 * tid + 1];
@@ -253,64 +306,130 @@ __device__ void sp_cumulate(const double *w, double *cum, SpShared &s, double *t
     __syncthreads();
 }
 
-// The last CTA's part of a top-p call: sort, cut, draw.  Returns the status; writes *token.
-__device__ int sp_sorted_finish(const SpParams &p, SpShared &s, unsigned char *scratch) {
+// The CTAs' partial sums, loaded in parallel, and their running sum in CTA order (one thread, the
+// same additions in every CTA): pre[c] = the partials before CTA c, pre[G] = the total.  Also the
+// last CTA with a positive partial.
+__device__ void sp_cta_prefix(const SpParams &p, SpShared &s, double *vals, double *pre) {
+    const int tid = threadIdx.x, G = (int)gridDim.x;
+    for (int c = tid; c < G; c += kSpThreads) vals[c] = __ldcg(p.partial + c);
+    __syncthreads();
+    if (tid == 0) {
+        double run = 0.0;
+        int last_nz = -1;
+        for (int c = 0; c < G; ++c) {
+            pre[c] = run;
+            if (vals[c] > 0.0) last_nz = c;
+            run += vals[c];
+        }
+        pre[G] = run;
+        s.last_nz = last_nz;
+    }
+    __syncthreads();
+}
+
+// Scratch of the last CTA (the histogram space): sorted keys | weights | cumulative weights |
+// logits | ids | CTA partials | their prefix.
+struct SpScratch {
+    unsigned long long *sk;
+    double *w, *cum, *lg;
+    int *ids;
+    double *vals, *pre;
+    __device__ explicit SpScratch(unsigned char *b)
+        : sk(reinterpret_cast<unsigned long long *>(b)),
+          w(reinterpret_cast<double *>(b + 8 * kSpMaxSorted)),
+          cum(reinterpret_cast<double *>(b + 16 * kSpMaxSorted)),
+          lg(reinterpret_cast<double *>(b + 24 * kSpMaxSorted)),
+          ids(reinterpret_cast<int *>(b + 32 * kSpMaxSorted)),
+          vals(reinterpret_cast<double *>(b + 36 * kSpMaxSorted)),
+          pre(reinterpret_cast<double *>(b + 36 * kSpMaxSorted + 8 * kMaxGridCtas)) {}
+};
+constexpr size_t kSpScratchBytes = 36 * kSpMaxSorted + 8 * (2 * kMaxGridCtas + 1);
+static_assert(kSpScratchBytes <= 8 * kSpBins, "the last CTA's scratch fits the histogram space");
+
+// The last CTA's part of a list call: the (at most 1024) appended keys sorted, the top list_n
+// kept; with top-p, cut where the cumulative weight exp(l - max) reaches top_p of the total;
+// without, visited by ascending id; then one draw.  Returns the status; writes the token.
+__device__ int sp_list_finish(const SpParams &p, SpShared &s, unsigned char *scratch) {
     const int tid = threadIdx.x;
-    unsigned long long *sk = reinterpret_cast<unsigned long long *>(scratch);   // [1024]
-    double *w = reinterpret_cast<double *>(scratch + 8 * kSpMaxSorted);         // [1024]
-    double *cum = reinterpret_cast<double *>(scratch + 16 * kSpMaxSorted);      // [1024]
-    const int n = min((int)__ldcg(&p.misc->ncand), kSpMaxSorted);
-    if (n != p.list_n || n < 1) return MMRS_ERR_LAUNCH;  // the selection always yields list_n keys
+    SpScratch b(scratch);
+    const int n = (int)__ldcg(&p.misc->ncand), L = p.list_n;
+    if (n < L || n > kSpMaxSorted || L < 1) return MMRS_ERR_LAUNCH;  // the selection yields list_n..1024 keys
     int n2 = 2;
     while (n2 < n) n2 <<= 1;
-    for (int i = tid; i < kSpMaxSorted; i += kSpThreads) sk[i] = i < n ? __ldcg(p.cand + i) : 0ull;
+    for (int i = tid; i < kSpMaxSorted; i += kSpThreads) b.sk[i] = i < n ? __ldcg(p.cand + i) : 0ull;
     __syncthreads();
-    sp_sort_desc(sk, n2);
-    const double l0 = sp_logit(sk[0]);
-    // top-p over weights at temperature 1 (exponential_weights(&candidates, 1.0))
-    for (int i = tid; i < kSpMaxSorted; i += kSpThreads) w[i] = i < n ? exp(sp_logit(sk[i]) - l0) : 0.0;
-    __syncthreads();
-    double tot;
-    sp_cumulate(w, cum, s, &tot);
-    if (p.s_from_partials && tid == 0) {
-        double S = 0.0;
-        for (int c = 0; c < (int)gridDim.x; ++c) S += __ldcg(p.partial + c);
-        s.d[0] = S;
+    if (n2 <= 64)
+        sp_warp_sort64_desc(b.sk, n);
+    else
+        sp_sort_desc(b.sk, n2);
+    const double l0 = sp_logit(b.sk[0]);
+    int m = L;
+    if (p.sorted) {
+        // top-p over weights at temperature 1 (exponential_weights(&candidates, 1.0)), sorted order
+        for (int i = tid; i < kSpMaxSorted; i += kSpThreads) {
+            const bool in = i < L;
+            b.lg[i] = in ? sp_logit(b.sk[i]) : 0.0;
+            b.ids[i] = in ? sp_id(b.sk[i]) : 0;
+            b.w[i] = in ? exp(b.lg[i] - l0) : 0.0;
+        }
+        __syncthreads();
+        double tot;
+        sp_cumulate(b.w, b.cum, s, &tot);
+        if (p.s_from_partials) sp_cta_prefix(p, s, b.vals, b.pre);
+        const double S = p.s_from_partials ? b.pre[gridDim.x] : tot;
+        const double threshold = S * p.top_p;
+        if (tid == 0) s.first = kSpMaxSorted;
+        __syncthreads();
+        for (int i = tid; i < L; i += kSpThreads)
+            if (b.cum[i] >= threshold) atomicMin(&s.first, i);
+        __syncthreads();
+        if (s.first >= L) {
+            if (p.s_from_partials) return MMRS_ERR_UNSUPPORTED;  // the nucleus is longer than the list
+            m = L;  // (rounding between the two sums: the whole list is the nucleus)
+        } else {
+            m = s.first + 1;
+        }
+    } else {
+        // the top list_n by ascending id: sort (id << 32 | float bits), complemented, descending
+        for (int i = tid; i < n2; i += kSpThreads) {
+            const unsigned long long k = b.sk[i];
+            const uint32_t o = (uint32_t)(k >> kSpIdBits);
+            const uint32_t bits = (o & 0x80000000u) ? (o & 0x7FFFFFFFu) : ~o;
+            b.sk[i] = i < L ? ~(((unsigned long long)sp_id(k) << 32) | bits) : 0ull;
+        }
+        __syncthreads();
+        if (n2 <= 64)
+            sp_warp_sort64_desc(b.sk, L);
+        else
+            sp_sort_desc(b.sk, n2);
+        for (int i = tid; i < kSpMaxSorted; i += kSpThreads) {
+            const bool in = i < L;
+            const unsigned long long x = ~b.sk[i];
+            b.lg[i] = in ? (double)__uint_as_float((uint32_t)x) : 0.0;
+            b.ids[i] = in ? (int)(x >> 32) : 0;
+        }
+        __syncthreads();
     }
-    if (tid == 0) s.i[4] = kSpMaxSorted;
-    __syncthreads();
-    const double S = p.s_from_partials ? s.d[0] : tot;
-    const double threshold = S * p.top_p;
-    for (int i = tid; i < n; i += kSpThreads)
-        if (cum[i] >= threshold) atomicMin(&s.i[4], i);
-    __syncthreads();
-    int m = s.i[4] + 1;
-    if (s.i[4] >= n) {
-        if (p.s_from_partials) return MMRS_ERR_UNSUPPORTED;  // the nucleus is longer than the list
-        m = n;  // (rounding between the two sums; the whole list is the nucleus)
-    }
-    // draw over the nucleus at the requested temperature
-    __syncthreads();
-    for (int i = tid; i < kSpMaxSorted; i += kSpThreads)
-        w[i] = i < m ? exp((sp_logit(sk[i]) - l0) / p.temperature) : 0.0;
+    // one draw over the first m entries at the requested temperature
+    for (int i = tid; i < kSpMaxSorted; i += kSpThreads) b.w[i] = i < m ? exp((b.lg[i] - l0) / p.temperature) : 0.0;
     __syncthreads();
     double total;
-    sp_cumulate(w, cum, s, &total);
+    sp_cumulate(b.w, b.cum, s, &total);
     const double sample = p.u * total;
     if (tid == 0) {
-        s.i[5] = kSpMaxSorted;
-        s.i[6] = 0;
+        s.first = kSpMaxSorted;
+        s.last = 0;
     }
     __syncthreads();
     for (int i = tid; i < m; i += kSpThreads) {
-        if (w[i] > 0.0) {
-            if (sample < cum[i]) atomicMin(&s.i[5], i);
-            atomicMax(&s.i[6], i);
+        if (b.w[i] > 0.0) {
+            if (sample < b.cum[i]) atomicMin(&s.first, i);
+            atomicMax(&s.last, i);
         }
     }
     __syncthreads();
-    const int pick = s.i[5] < m ? s.i[5] : s.i[6];
-    if (tid == 0) p.token[0] = sp_id(sk[pick]);
+    const int pick = s.first < m ? s.first : s.last;
+    if (tid == 0) p.token[0] = b.ids[pick];
     return MMRS_OK;
 }
 
@@ -320,15 +439,18 @@ __global__ void __launch_bounds__(kSpThreads, 1) sample_kernel(const SpParams p)
     const int tid = threadIdx.x, lane = tid & 31, G = (int)gridDim.x, cta = (int)blockIdx.x;
     unsigned long long *keys = reinterpret_cast<unsigned long long *>(sp_smem);
     uint32_t *sh = reinterpret_cast<uint32_t *>(sp_smem + (size_t)8 * p.chunk);  // [2][kSpBins]
+    unsigned char *scratch = sp_smem + (size_t)8 * p.chunk;                       // the same space, later
     const uint64_t deadline = globaltimer_ns() + kSpTimeoutNs;
     const int lo = min(p.V, cta * p.chunk), n = min(p.V, lo + p.chunk) - lo;
     if (tid == 0) {
         s.ok = 1;
         s.epoch = __ldcg(&p.ctl->epoch[cta]);
         s.max_key = 0ull;
+        s.gmax_key = 0ull;
+        s.flags = 0u;
     }
-    int nsync = 0;
-    bool skip = false;
+    int nsync = 0, rounds = 0;
+    double gmax = 0.0;
 
     if (p.mode == kGreedy) {
         unsigned long long best = 0ull;
@@ -342,13 +464,14 @@ __global__ void __launch_bounds__(kSpThreads, 1) sample_kernel(const SpParams p)
         __syncthreads();
         if (tid == 0 && s.max_key) atomicMax(&p.misc->best, s.max_key);
     } else {
-        // ---- phase 0: keys, non-finite values, largest key, round-0 histogram --------------
-        const bool select = p.mode != kLogprob && (p.kA > 0 || p.kB > 0);
-        const bool act[2] = {p.kA > 0, p.kB > 0};
-        unsigned long long prefix[2] = {0ull, 0ull};
-        uint32_t need[2] = {(uint32_t)p.kA, (uint32_t)p.kB};
+        // ---- phase 0: keys, non-finite values, largest key, round-0 histogram ----------------
+        bool act[2] = {p.mode != kLogprob && p.kA > 0, p.mode != kLogprob && p.kB > 0};
+        const bool select = act[0] || act[1];
+        unsigned long long prefix[2] = {0ull, 0ull}, bound[2] = {0ull, 0ull};
+        uint32_t need[2] = {(uint32_t)p.kA, (uint32_t)p.kB}, gt[2] = {0u, 0u};
+        const int nb = act[1] ? 2 * kSpBins : kSpBins;  // (search B runs only beside A)
         if (select)
-            for (int b = tid; b < 2 * kSpBins; b += kSpThreads) sh[b] = 0u;
+            for (int b = tid; b < nb; b += kSpThreads) sh[b] = 0u;
         __syncthreads();
         int nonfin = 0;
         unsigned long long kmax = 0ull;
@@ -370,26 +493,26 @@ __global__ void __launch_bounds__(kSpThreads, 1) sample_kernel(const SpParams p)
         if (__syncthreads_or(nonfin) && tid == 0) atomicOr(&p.misc->flags, kFlagNonfinite);
         if (tid == 0) p.cta_max[cta] = s.max_key;
         if (select) {
-            for (int b = tid; b < 2 * kSpBins; b += kSpThreads)
-                if (act[b / kSpBins] && sh[b]) atomicAdd(&p.hist[b], sh[b]);
+            for (int b = tid; b < nb; b += kSpThreads)
+                if (sh[b]) atomicAdd(&p.hist[b], sh[b]);
+            rounds = 1;
         }
         if (!sp_grid_sync(p, s, nsync, deadline)) return;
 
-        // ---- global maximum and the call's flags (the same in every CTA) --------------------
-        if (tid == 0) s.max_key = 0ull;
-        __syncthreads();
+        // ---- global maximum and the call's flags (the same in every CTA) ----------------------
         {
+            if (tid == 0) s.flags = __ldcg(&p.misc->flags);
             unsigned long long m = 0ull;
             for (int c = tid; c < G; c += kSpThreads) {
                 const unsigned long long v = __ldcg(p.cta_max + c);
                 m = v > m ? v : m;
             }
             m = warp_max_u64(m);
-            if (lane == 0 && m) atomicMax(&s.max_key, m);
+            if (lane == 0 && m) atomicMax(&s.gmax_key, m);
         }
         __syncthreads();
-        const double gmax = sp_logit(s.max_key);
-        if (p.mode != kLogprob && (__ldcg(&p.misc->flags) & kFlagNonfinite)) skip = true;
+        gmax = sp_logit(s.gmax_key);
+        const bool skip = p.mode != kLogprob && (s.flags & kFlagNonfinite);
 
         if (p.mode == kLogprob) {
             double acc = 0.0;
@@ -398,51 +521,61 @@ __global__ void __launch_bounds__(kSpThreads, 1) sample_kernel(const SpParams p)
             block_excl_scan(acc, s.sw_d, tot);
             if (tid == 0) p.partial[cta] = tot;
         } else if (!skip) {
-            // ---- radix selection --------------------------------------------------------------
-            if (select) {
-                for (int r = 0; r < kSpRounds && !skip; ++r) {
-                    if (r > 0) {
-                        sp_histogram(p, keys, n, sh, r, prefix, act);
-                        if (!sp_grid_sync(p, s, nsync, deadline)) return;
-                        // every CTA has scanned round r - 1's histogram: clear this CTA's share
-                        uint32_t *prev = p.hist + (size_t)(r - 1) * 2 * kSpBins;
-                        const int per = (2 * kSpBins + G - 1) / G;
-                        for (int b = cta * per + tid; b < min(2 * kSpBins, (cta + 1) * per); b += kSpThreads)
-                            prev[b] = 0u;
+            // ---- radix selection ------------------------------------------------------------------
+            bool failed = false;
+            for (int r = 0; r < kSpRounds && (act[0] || act[1]); ++r) {
+                if (r > 0) {
+                    sp_histogram(p, keys, n, sh, r, prefix, act);
+                    if (!sp_grid_sync(p, s, nsync, deadline)) return;
+                    rounds = r + 1;
+                    // every CTA has scanned round r - 1's histogram: clear this CTA's share of it
+                    uint32_t *prev = p.hist + (size_t)(r - 1) * 2 * kSpBins;
+                    const int per = (2 * kSpBins + G - 1) / G;
+                    for (int b = cta * per + tid; b < min(2 * kSpBins, (cta + 1) * per); b += kSpThreads)
+                        prev[b] = 0u;
+                }
+                const int shift = (kSpRounds - 1 - r) * kSpDigitBits;
+                for (int q = 0; q < 2; ++q) {
+                    if (!act[q]) continue;
+                    uint32_t above = 0, in_bin = 0;
+                    const int d = sp_scan(p, s, r, q, need[q], &above, &in_bin);
+                    if (d < 0) {
+                        failed = true;
+                        act[0] = act[1] = false;
+                        if (tid == 0) atomicOr(&p.misc->flags, kFlagInternal);
+                        break;
                     }
-                    for (int q = 0; q < 2; ++q) {
-                        if (!act[q]) continue;
-                        uint32_t above = 0;
-                        const int d = sp_scan(p, s, r, q, need[q], &above);
-                        if (d < 0) {
-                            skip = true;
-                            if (tid == 0) atomicOr(&p.misc->flags, kFlagInternal);
-                            break;
-                        }
-                        prefix[q] = (prefix[q] << kSpDigitBits) | (unsigned long long)d;
-                        need[q] -= above;
+                    prefix[q] = (prefix[q] << kSpDigitBits) | (unsigned long long)d;
+                    gt[q] += above;
+                    need[q] -= above;
+                    if (shift == 0) {
+                        bound[q] = prefix[q];  // the exact key of rank k
+                        act[q] = false;
+                    } else if (q == 0 && p.mode == kList && gt[q] + in_bin <= (uint32_t)kSpMaxSorted) {
+                        bound[q] = prefix[q] << shift;  // at most 1024 keys at or above: the list sorts them
+                        act[q] = false;
                     }
                 }
             }
-            const unsigned long long tA = act[0] ? prefix[0] : 0ull, tB = act[1] ? prefix[1] : 0ull;
-            if (!skip && p.mode == kSorted) {
-                // ---- top-p: append the list's keys; sum the whole candidate set if needed ---------
+            if (!failed && p.mode == kList) {
+                // ---- append the list's keys; sum the whole candidate set when it is longer --------
                 double acc = 0.0;
                 for (int i = tid; i < n; i += kSpThreads) {
                     const unsigned long long key = keys[i];
-                    if (key >= tA) {
+                    if (key >= bound[0]) {
                         const uint32_t pos = atomicAdd(&p.misc->ncand, 1u);
                         if (pos < (uint32_t)kSpMaxSorted) p.cand[pos] = key;
                     }
-                    if (p.s_from_partials && key >= tB) acc += exp(sp_logit(key) - gmax);
+                    if (p.s_from_partials && key >= bound[1]) acc += exp(sp_logit(key) - gmax);
                 }
                 if (p.s_from_partials) {
                     double tot;
                     block_excl_scan(acc, s.sw_d, tot);
                     if (tid == 0) p.partial[cta] = tot;
                 }
-            } else if (!skip) {
-                // ---- no top-p: walk the candidates by ascending id -------------------------------
+            } else if (!failed) {
+                // ---- kIdWalk: walk the candidates by ascending id across the CTAs ------------------
+                const unsigned long long tA = bound[0];
                 const int per = (n + kSpThreads - 1) / kSpThreads;
                 const int i0 = min(n, tid * per), i1 = min(n, i0 + per);
                 double acc = 0.0;
@@ -452,26 +585,18 @@ __global__ void __launch_bounds__(kSpThreads, 1) sample_kernel(const SpParams p)
                 const double ex = block_excl_scan(acc, s.sw_d, mine);
                 if (tid == 0) p.partial[cta] = mine;
                 if (!sp_grid_sync(p, s, nsync, deadline)) return;
-                if (tid == 0) {
-                    double run = 0.0, before = 0.0;
-                    int last_nz = -1;
-                    for (int c = 0; c < G; ++c) {
-                        const double v = __ldcg(p.partial + c);
-                        if (c == cta) before = run;
-                        if (v > 0.0) last_nz = c;
-                        run += v;
-                    }
-                    s.d[0] = before;
-                    s.d[1] = run;
-                    s.i[0] = last_nz;
-                    s.i[5] = kSpMaxSlice;
-                    s.i[6] = -1;
-                }
-                __syncthreads();
-                const double before = s.d[0], total = s.d[1], sample = p.u * total;
-                const bool owner = mine > 0.0 && before <= sample && sample < before + mine;
-                const bool fallback = sample >= total && cta == s.i[0];
+                SpScratch b(scratch);
+                sp_cta_prefix(p, s, b.vals, b.pre);
+                const double before = b.pre[cta], after = b.pre[cta + 1], total = b.pre[G];
+                const double sample = p.u * total;
+                const bool owner = before <= sample && sample < after;
+                const bool fallback = sample >= total && cta == s.last_nz;
                 if (owner || fallback) {
+                    if (tid == 0) {
+                        s.first = kSpMaxSlice;
+                        s.last = -1;
+                    }
+                    __syncthreads();
                     double run = ex;
                     for (int i = i0; i < i1; ++i) {
                         if (keys[i] < tA) continue;
@@ -479,14 +604,14 @@ __global__ void __launch_bounds__(kSpThreads, 1) sample_kernel(const SpParams p)
                         run += wi;
                         if (wi > 0.0) {
                             if (owner && sample < before + run) {
-                                atomicMin(&s.i[5], i);
+                                atomicMin(&s.first, i);
                                 break;
                             }
-                            atomicMax(&s.i[6], i);
+                            atomicMax(&s.last, i);
                         }
                     }
                     __syncthreads();
-                    const int pick = s.i[5] < kSpMaxSlice ? s.i[5] : s.i[6];
+                    const int pick = s.first < kSpMaxSlice ? s.first : s.last;
                     if (tid == 0 && pick >= 0) p.token[0] = lo + pick;
                 }
             }
@@ -497,15 +622,17 @@ __global__ void __launch_bounds__(kSpThreads, 1) sample_kernel(const SpParams p)
     __syncthreads();
     if (tid == 0) {
         p.ctl->epoch[cta] = s.epoch + (uint32_t)nsync;  // read again only by this CTA's next launch
-        __threadfence();
-        s.i[7] = atomicAdd(&p.misc->ticket, 1u) == (uint32_t)G - 1u;
+        // release this CTA's writes (ordered before by the barrier), acquire the others'
+        uint32_t t;
+        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(t) : "l"(&p.misc->ticket) : "memory");
+        s.is_last = t == (uint32_t)G - 1u;
+        if (s.is_last) s.flags = __ldcg(&p.misc->flags);
     }
     __syncthreads();
-    if (!s.i[7]) return;
-    __threadfence();
+    if (!s.is_last) return;
+    __syncthreads();
+    const uint32_t flags = s.flags;
     int result = MMRS_OK;
-    const uint32_t flags = __ldcg(&p.misc->flags);
-    unsigned char *scratch = sp_smem + (size_t)8 * p.chunk;  // the histogram space, free now
     if (p.mode == kGreedy) {
         if (tid == 0) {
             const unsigned long long b = __ldcg(&p.misc->best);
@@ -514,32 +641,27 @@ __global__ void __launch_bounds__(kSpThreads, 1) sample_kernel(const SpParams p)
     } else if (flags & kFlagInternal) {
         result = MMRS_ERR_LAUNCH;
     } else if (p.mode == kLogprob) {
+        SpScratch b(scratch);
+        sp_cta_prefix(p, s, b.vals, b.pre);
         if (tid == 0) {
-            double S = 0.0;
-            for (int c = 0; c < G; ++c) S += __ldcg(p.partial + c);
-            unsigned long long m = 0ull;
-            for (int c = 0; c < G; ++c) {
-                const unsigned long long v = __ldcg(p.cta_max + c);
-                m = v > m ? v : m;
-            }
             const double lt = (double)__ldg(p.logits + p.token_id);
-            const float v = (float)(lt - sp_logit(m) - log(S));
+            const float v = (float)(lt - gmax - log(b.pre[G]));
             p.out[0] = v;
-            s.i[1] = isfinite(v) ? MMRS_OK : MMRS_ERR_NONFINITE;
+            s.status = isfinite(v) ? MMRS_OK : MMRS_ERR_NONFINITE;
         }
         __syncthreads();
-        result = s.i[1];
+        result = s.status;
     } else if (flags & kFlagNonfinite) {
         result = MMRS_ERR_NONFINITE;
-    } else if (p.mode == kSorted) {
-        result = sp_sorted_finish(p, s, scratch);
+    } else if (p.mode == kList) {
+        result = sp_list_finish(p, s, scratch);
     }
     if (result != MMRS_OK && p.token && tid == 0) p.token[0] = -1;
-    // leave the workspace clean: the histograms not cleared on the way (round 3's; all of them
-    // when the rounds stopped early), the list counter, flags, maximum, ticket
-    if ((p.mode == kSorted || p.mode == kIdOrder) && (p.kA > 0 || p.kB > 0)) {
-        const int r0 = flags ? 0 : kSpRounds - 1;
-        for (int b = r0 * 2 * kSpBins + tid; b < kSpRounds * 2 * kSpBins; b += kSpThreads) p.hist[b] = 0u;
+    // leave the workspace clean: the histogram rounds not cleared on the way (the last one run;
+    // all of them when the call stopped early), the list counter, flags, maximum, ticket
+    if (rounds > 0) {
+        const int r0 = flags ? 0 : rounds - 1, r1 = flags ? kSpRounds : rounds;
+        for (int b = r0 * 2 * kSpBins + tid; b < r1 * 2 * kSpBins; b += kSpThreads) p.hist[b] = 0u;
     }
     __syncthreads();
     if (tid == 0) {
@@ -547,8 +669,7 @@ __global__ void __launch_bounds__(kSpThreads, 1) sample_kernel(const SpParams p)
         p.misc->ncand = 0u;
         p.misc->flags = 0u;
         p.misc->result = (uint32_t)result;
-        __threadfence();
-        p.misc->ticket = 0u;
+        p.misc->ticket = 0u;  // (the next launch sees all of these: kernel boundary)
     }
 }
 
@@ -651,14 +772,16 @@ extern "C" int mmrs_sample_token(const float *logits, int vocab, const MmrsSampl
         p.mode = kGreedy;
     } else {
         const int k = (params->top_k > 0 && params->top_k < vocab) ? params->top_k : vocab;
-        if (top_p < 1.0 && k > 1) {
-            p.mode = kSorted;
+        const bool sorted = top_p < 1.0 && k > 1;
+        if (sorted || k <= kSpMaxSorted) {
+            p.mode = kList;
+            p.sorted = sorted;
             p.list_n = k < kSpMaxSorted ? k : kSpMaxSorted;
             p.kA = p.list_n < vocab ? p.list_n : 0;
-            p.s_from_partials = k > p.list_n;
-            p.kB = (k > p.list_n && k < vocab) ? k : 0;
+            p.s_from_partials = sorted && k > p.list_n;
+            p.kB = (p.s_from_partials && k < vocab) ? k : 0;
         } else {
-            p.mode = kIdOrder;
+            p.mode = kIdWalk;
             p.kA = k < vocab ? k : 0;
         }
     }
