@@ -126,3 +126,23 @@ def test_oracle_matches_python_restatement(orc, case):
     for u in rng.random(8):
         st, tok, _ = orc.sample_token(x, t, p, k, float(u))
         assert st == 0 and tok == _py_sample(x, t, p, k, float(u)), (t, p, k, u)
+
+
+def test_host_side_rejections_launch_nothing(pkg):
+    """mmrs_sample_token / mmrs_token_logprob check their arguments before any CUDA call
+    (SamplingParams::validate, src/sampling.rs:31-39; the draw in [0, 1)), so this runs without a GPU."""
+    import ctypes as C
+    lib = pkg.lib()
+    assert lib.mmrs_sample_workspace_bytes(0) == 0 and lib.mmrs_sample_workspace_bytes(1 << 20 | 1) == 0
+    assert lib.mmrs_sample_workspace_bytes(200064) > 0
+    fake = C.c_void_p(256)  # never dereferenced: every call below fails validation first
+    bad = [(-0.1, 0.95, 40, 0.5), (float("nan"), 0.95, 40, 0.5), (1.0, 1.5, 40, 0.5), (1.0, float("nan"), 40, 0.5),
+           (1.0, 0.95, 40, 1.0), (1.0, 0.95, 40, -0.1), (1.0, 0.95, 40, float("nan"))]
+    for t, p, k, u in bad:
+        prm = pkg.MmrsSamplingParams(t, p, k)
+        assert lib.mmrs_sample_token(fake, 200064, C.byref(prm), u, fake, fake, 1 << 20, None) == pkg.MMRS_ERR_ARG
+    ok = pkg.MmrsSamplingParams(1.0, 0.95, 40)
+    assert lib.mmrs_sample_token(None, 200064, C.byref(ok), 0.5, fake, fake, 1 << 20, None) == pkg.MMRS_ERR_ARG
+    assert lib.mmrs_sample_token(fake, 0, C.byref(ok), 0.5, fake, fake, 1 << 20, None) == pkg.MMRS_ERR_ARG
+    assert lib.mmrs_token_logprob(fake, 10, 10, fake, fake, 1 << 20, None) == pkg.MMRS_ERR_ARG
+    assert lib.mmrs_token_logprob(fake, 10, -1, fake, fake, 1 << 20, None) == pkg.MMRS_ERR_ARG
