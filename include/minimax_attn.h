@@ -45,6 +45,23 @@ MMRS_API void launch_mmvq_gguf_qkv_q8_0_f32_rmsnorm_f16(const void *x, void *vy,
                                                        const void *k_alpha, void *dst, int kx, int kx_padded,
                                                        int q_rows, int k_rows, int v_rows, float eps, void *stream);
 
+/* ffi.rs:529-536 (mmvq_gguf.cu:970-990, 1360-1366): tensor-parallel decode, before the Q/K
+ * statistics all-reduce: stats[0] = sum of q[i]^2 over this rank's q_rows, stats[1] = the same over
+ * k (f32, the reference's summation order: bit-identical statistics). */
+MMRS_API void launch_qkv_tp_sumsq_f32(const void *q, const void *k, void *stats, int q_rows, int k_rows,
+                                      void *stream);
+
+/* ffi.rs:537-557 (mmvq_gguf.cu:995-1034, 1368-1382): after the all-reduce, dst f16
+ * [q_rows + k_rows + v_rows] = [rope(RMSNorm_global(q) * q_alpha) | rope(RMSNorm_global(k) * k_alpha)
+ * | v]: scale = rsqrt(global_stats[0 or 1] / q_full_rows (k_full_rows) + eps) over the full,
+ * all-rank width; the first rope_dim columns of every head_dim-wide head rotated by the f32 tables
+ * cos / sin [positions][rope_dim / 2] at `position`, with launch_partial_rope_f16's arithmetic. */
+MMRS_API void launch_qkv_tp_rmsnorm_rope_f16(const void *q, const void *k, const void *v, const void *global_stats,
+                                             const void *q_alpha, const void *k_alpha, const void *cos,
+                                             const void *sin, void *dst, int q_rows, int k_rows, int v_rows,
+                                             int q_full_rows, int k_full_rows, int head_dim, int rope_dim,
+                                             int position, float eps, void *stream);
+
 /* ffi.rs:558-570 (mmvq_gguf.cu:1038-1066, 1385-1395): dst f16 [q_rows + k_rows] = q, k (f16) with
  * the first rope_dim columns of every head_dim-wide head rotated by the f32 tables
  * cos / sin [positions][rope_dim / 2] at `position`. */

@@ -80,6 +80,8 @@ PROTOTYPES = {
     "launch_mmvq_gguf_qkv_q8_0_f32": (None, [_VP] * 6 + [_I] * 5 + [_VP]),
     "launch_mmvq_gguf_qkv_q8_0_f32_rmsnorm_f16": (None, [_VP] * 9 + [_I] * 5 + [_F, _VP]),
     "launch_partial_rope_f16": (None, [_VP] * 5 + [_I] * 5 + [_VP]),
+    "launch_qkv_tp_sumsq_f32": (None, [_VP] * 3 + [_I] * 2 + [_VP]),
+    "launch_qkv_tp_rmsnorm_rope_f16": (None, [_VP] * 9 + [_I] * 8 + [_F, _VP]),
     "launch_gqa_decode_mma_f16_128": (None, [_VP] * 5 + [_I] * 7 + [_F, _I, _VP]),
     "mmrs_attn_workspace_bytes": (_SZ, [C.POINTER(MmrsAttnWeights)]),
     "mmrs_attn_workspace_status": (_I, [_VP]),

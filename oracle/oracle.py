@@ -242,6 +242,29 @@ def partial_rope_f16(q, k, cos, sin, head_dim: int, rope_dim: int, position: int
     return out
 
 
+def tp_qk_sumsq(q: np.ndarray, k: np.ndarray) -> np.ndarray:
+    """[sum q^2, sum k^2] of one tensor-parallel rank's projection (launch_qkv_tp_sumsq_f32,
+    mmvq_gguf.cu:970-990), accumulated in double."""
+    q, k = np.asarray(q, np.float64), np.asarray(k, np.float64)
+    return np.array([np.dot(q, q), np.dot(k, k)])
+
+
+def tp_qk_rmsnorm_rope_f16(q, k, v, global_stats, q_alpha, k_alpha, cos, sin, q_full: int, k_full: int,
+                           head_dim: int, rope_dim: int, position: int, eps: float = 1e-6) -> np.ndarray:
+    """f16 bits of [rope(q * s_q * q_alpha) | rope(k * s_k * k_alpha) | v] for one TP rank
+    (launch_qkv_tp_rmsnorm_rope_f16, mmvq_gguf.cu:995-1034): s = 1 / sqrt(global / full + eps) with
+    the global (all-rank) sums, computed here in double and rounded to f32 (the kernel's rsqrtf is
+    within 2 ulp of it); the products in f32, rounded to half; the rotation with the reference's
+    half arithmetic (partial_rope_f16); v rounded to half."""
+    g = np.asarray(global_stats, np.float32)
+    sq = np.float32(1.0 / np.sqrt(np.float64(np.float32(g[0] / np.float32(q_full)) + np.float32(eps))))
+    sk = np.float32(1.0 / np.sqrt(np.float64(np.float32(g[1] / np.float32(k_full)) + np.float32(eps))))
+    qh = ((sq * np.asarray(q, np.float32)) * np.asarray(q_alpha, np.float32)).astype(np.float16)
+    kh = ((sk * np.asarray(k, np.float32)) * np.asarray(k_alpha, np.float32)).astype(np.float16)
+    rot = partial_rope_f16(qh, kh, cos, sin, head_dim, rope_dim, position)
+    return np.concatenate([rot, np.asarray(v, np.float32).astype(np.float16).view(np.uint16)])
+
+
 def gqa_decode_f16(q, k, v, seq_len: int, q_heads: int, kv_heads: int, head_dim: int, kv_head_stride: int,
                    scale: float):
     """f16 bits [q_heads * head_dim] of softmax(scale q.k) v over positions [0, seq_len)."""

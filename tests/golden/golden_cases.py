@@ -181,3 +181,24 @@ def lm_inputs():
     x = S.normal_f32(LM_K, 901, 1, 1.0)
     w = S.q6k_blocks(901, 2, LM_ROWS, LM_K)
     return x, w
+
+
+# ---- tensor-parallel Q/K RMSNorm (TP = 2) ------------------------------------------------------
+TP_Q_LOCAL, TP_KV_LOCAL = 24 * 128, 4 * 128  # a rank's 24 query heads and 4 KV heads
+TP_Q_FULL, TP_K_FULL = 48 * 128, 8 * 128
+TP_POS = (0, 1234)
+
+
+def tp_qk_inputs(rank: int):
+    """A TP = 2 rank's f32 projection q / k / v (the rank's heads), its slices of the Q / K norm
+    weights, and the rotary tables.  Rank 1's q is scaled by 3 so the two ranks' sums differ."""
+    scale = 1.0 if rank == 0 else 3.0
+    q = (S.normal_f32(TP_Q_LOCAL, 911, 1 + 10 * rank, 1.0) * scale).astype(np.float32)
+    k = S.normal_f32(TP_KV_LOCAL, 911, 2 + 10 * rank, 2.0)
+    v = S.normal_f32(TP_KV_LOCAL, 911, 3 + 10 * rank, 1.0)
+    qa_full = (1.0 + S.normal_f32(TP_Q_FULL, 911, 4, 0.1)).astype(np.float32)
+    ka_full = (1.0 + S.normal_f32(TP_K_FULL, 911, 5, 0.1)).astype(np.float32)
+    qa = np.ascontiguousarray(qa_full[rank * TP_Q_LOCAL:(rank + 1) * TP_Q_LOCAL])
+    ka = np.ascontiguousarray(ka_full[rank * TP_KV_LOCAL:(rank + 1) * TP_KV_LOCAL])
+    cos, sin = S.rope_tables(ROPE_MAX_POS, ROT)
+    return q, k, v, qa, ka, cos, sin
