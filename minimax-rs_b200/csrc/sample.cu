@@ -346,6 +346,123 @@ struct SpScratch {
 constexpr size_t kSpScratchBytes = 36 * kSpMaxSorted + 8 * (2 * kMaxGridCtas + 1);
 static_assert(kSpScratchBytes <= 8 * kSpBins, "the last CTA's scratch fits the histogram space");
 
+// Inclusive prefix sum of the 64 entries a warp holds (lane l: entries l and l + 32).
+__device__ __forceinline__ void warp_cum64(const double (&w)[2], double (&cum)[2]) {
+    const int lane = threadIdx.x & 31;
+    cum[0] = warp_incl_scan(w[0], lane);
+    const double t0 = __shfl_sync(0xffffffffu, cum[0], 31);
+    cum[1] = warp_incl_scan(w[1], lane) + t0;
+}
+
+// First entry (of 64) whose flag is set, or 64.
+__device__ __forceinline__ int warp_first64(bool f0, bool f1) {
+    const unsigned b0 = __ballot_sync(0xffffffffu, f0), b1 = __ballot_sync(0xffffffffu, f1);
+    return b0 ? __ffs(b0) - 1 : (b1 ? 32 + __ffs(b1) - 1 : 64);
+}
+// Last entry (of 64) whose flag is set, or -1.
+__device__ __forceinline__ int warp_last64(bool f0, bool f1) {
+    const unsigned b0 = __ballot_sync(0xffffffffu, f0), b1 = __ballot_sync(0xffffffffu, f1);
+    return b1 ? 63 - __clz(b1) : (b0 ? 31 - __clz(b0) : -1);
+}
+
+// A list of at most 64 entries finished by warp 0 alone (no CTA barriers): the keys sorted in
+// descending order, the top-p cut, the id order when there is no cut, the draw.  Same arithmetic
+// as the CTA-wide finish (prefix sums in another order: differences at rounding level only).
+__device__ int sp_list_finish_warp(const SpParams &p, int n) {
+    const int lane = threadIdx.x & 31, L = p.list_n;
+    unsigned long long x[2] = {lane < n ? __ldcg(p.cand + lane) : 0ull, lane + 32 < n ? __ldcg(p.cand + lane + 32) : 0ull};
+    // bitonic sort of the 64 keys, descending (entry e = lane + 32 h)
+#pragma unroll
+    for (int size = 2; size <= 64; size <<= 1) {
+#pragma unroll
+        for (int j = size >> 1; j > 0; j >>= 1) {
+            if (j == 32) {
+                if (x[0] < x[1]) {
+                    const unsigned long long t = x[0];
+                    x[0] = x[1];
+                    x[1] = t;
+                }
+            } else {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int e = lane + 32 * h;
+                    const unsigned long long y = __shfl_xor_sync(0xffffffffu, x[h], j);
+                    const bool lower = (e & j) == 0, desc = (e & size) == 0;
+                    const unsigned long long hi = x[h] > y ? x[h] : y, lo = x[h] > y ? y : x[h];
+                    x[h] = (desc == lower) ? hi : lo;
+                }
+            }
+        }
+    }
+    const double l0 = __shfl_sync(0xffffffffu, sp_logit(x[0]), 0);
+    double lg[2];
+    int ids[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        lg[h] = sp_logit(x[h]);
+        ids[h] = sp_id(x[h]);
+    }
+    int m = L;
+    if (p.sorted) {
+        double w[2], cum[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) w[h] = lane + 32 * h < L ? exp(lg[h] - l0) : 0.0;
+        warp_cum64(w, cum);
+        const double S = __shfl_sync(0xffffffffu, cum[1], 31);
+        const double threshold = S * p.top_p;
+        const int first = warp_first64(lane < L && cum[0] >= threshold, lane + 32 < L && cum[1] >= threshold);
+        m = first < L ? first + 1 : L;
+    } else {
+        // the top L by ascending id: sort (id << 32 | float bits), complemented, descending
+        unsigned long long z[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t o = (uint32_t)(x[h] >> kSpIdBits);
+            const uint32_t bits = (o & 0x80000000u) ? (o & 0x7FFFFFFFu) : ~o;
+            z[h] = lane + 32 * h < L ? ~(((unsigned long long)ids[h] << 32) | bits) : 0ull;
+        }
+#pragma unroll
+        for (int size = 2; size <= 64; size <<= 1) {
+#pragma unroll
+            for (int j = size >> 1; j > 0; j >>= 1) {
+                if (j == 32) {
+                    if (z[0] < z[1]) {
+                        const unsigned long long t = z[0];
+                        z[0] = z[1];
+                        z[1] = t;
+                    }
+                } else {
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int e = lane + 32 * h;
+                        const unsigned long long y = __shfl_xor_sync(0xffffffffu, z[h], j);
+                        const bool lower = (e & j) == 0, desc = (e & size) == 0;
+                        const unsigned long long hi = z[h] > y ? z[h] : y, lo = z[h] > y ? y : z[h];
+                        z[h] = (desc == lower) ? hi : lo;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const unsigned long long v = ~z[h];
+            lg[h] = (double)__uint_as_float((uint32_t)v);
+            ids[h] = (int)(v >> 32);
+        }
+    }
+    double w[2], cum[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) w[h] = lane + 32 * h < m ? exp((lg[h] - l0) / p.temperature) : 0.0;
+    warp_cum64(w, cum);
+    const double total = __shfl_sync(0xffffffffu, cum[1], 31);
+    const double sample = p.u * total;
+    int pick = warp_first64(w[0] > 0.0 && sample < cum[0], w[1] > 0.0 && sample < cum[1]);
+    if (pick >= m) pick = warp_last64(w[0] > 0.0, w[1] > 0.0);
+    const int tok = pick < 32 ? __shfl_sync(0xffffffffu, ids[0], pick & 31) : __shfl_sync(0xffffffffu, ids[1], pick & 31);
+    if (lane == 0) p.token[0] = tok;
+    return MMRS_OK;
+}
+
 // The last CTA's part of a list call: the (at most 1024) appended keys sorted, the top list_n
 // kept; with top-p, cut where the cumulative weight exp(l - max) reaches top_p of the total;
 // without, visited by ascending id; then one draw.  Returns the status; writes the token.
@@ -654,7 +771,17 @@ __global__ void __launch_bounds__(kSpThreads, 1) sample_kernel(const SpParams p)
     } else if (flags & kFlagNonfinite) {
         result = MMRS_ERR_NONFINITE;
     } else if (p.mode == kList) {
-        result = sp_list_finish(p, s, scratch);
+        const int n = (int)__ldcg(&p.misc->ncand);
+        if (n <= 64 && n >= p.list_n && p.list_n >= 1) {
+            if (tid < 32) {
+                const int r = sp_list_finish_warp(p, n);
+                if (tid == 0) s.status = r;
+            }
+            __syncthreads();
+            result = s.status;
+        } else {
+            result = sp_list_finish(p, s, scratch);
+        }
     }
     if (result != MMRS_OK && p.token && tid == 0) p.token[0] = -1;
     // leave the workspace clean: the histogram rounds not cleared on the way (the last one run;
