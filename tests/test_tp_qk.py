@@ -75,3 +75,51 @@ def test_ranks_agree_with_full_width_normalisation(orc, gold):
         dq = _half_ulps(gq, fq[r * G.TP_Q_LOCAL:(r + 1) * G.TP_Q_LOCAL])
         dk = _half_ulps(gk, fk[r * G.TP_KV_LOCAL:(r + 1) * G.TP_KV_LOCAL])
         assert dq.max() <= 2 and dk.max() <= 2
+
+
+def _tp_rank_main(rank, world, port, q):
+    """One TP rank on CPU: its rank-local statistics (the reference kernel's, from the recording),
+    the two-float all-reduce over gloo (the collective of src/tensor_parallel_model.rs:407-410),
+    then the normalisation with the reduced statistics (oracle)."""
+    import os
+    import sys
+    root = Path(__file__).resolve().parents[1]
+    sys.path[:0] = [str(root / "oracle"), str(root / "tests" / "golden")]
+    import torch
+    import torch.distributed as dist
+
+    import golden_cases as Gc
+    import oracle
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    gold = np.load(GOLD)
+    stats = torch.from_numpy(np.array(gold["stats"][rank], dtype=np.float32))
+    dist.all_reduce(stats)
+    qq, k, v, qa, ka, cos, sin = Gc.tp_qk_inputs(rank)
+    dst = oracle.tp_qk_rmsnorm_rope_f16(qq, k, v, stats.numpy(), qa, ka, cos, sin, Gc.TP_Q_FULL, Gc.TP_K_FULL,
+                                        Gc.HD, Gc.ROT, Gc.TP_POS[1])
+    q.put((rank, stats.numpy().tobytes(), _half_ulps(dst, gold[f"dst_r{rank}_p{Gc.TP_POS[1]}"]).max()))
+    dist.destroy_process_group()
+
+
+def test_tp2_statistics_all_reduce_gloo(gold):
+    """world_size 2 on CPU: the all-reduced statistics equal the recorded global sums bit for bit,
+    and each rank's normalisation from them matches its recorded output."""
+    import socket
+
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_tp_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, stats, worst in results:
+        assert stats == np.asarray(gold["global"], np.float32).tobytes()
+        assert worst <= 2
