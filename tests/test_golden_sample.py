@@ -146,3 +146,18 @@ def test_host_side_rejections_launch_nothing(pkg):
     assert lib.mmrs_sample_token(fake, 0, C.byref(ok), 0.5, fake, fake, 1 << 20, None) == pkg.MMRS_ERR_ARG
     assert lib.mmrs_token_logprob(fake, 10, 10, fake, fake, 1 << 20, None) == pkg.MMRS_ERR_ARG
     assert lib.mmrs_token_logprob(fake, 10, -1, fake, fake, 1 << 20, None) == pkg.MMRS_ERR_ARG
+
+
+@pytest.mark.parametrize("x,t,p,k", [
+    ([1.5], 1.0, 0.9, 40),                       # one candidate
+    ([0.0, 2.0, 1.0], 1.0, 0.95, 10),            # top_k above the vocabulary
+    ([0.0, 2.0, 1.0, 2.0], 1e-30, 1.0, 0),       # weights underflow: only the maxima remain
+    ([0.0, 2.0, 1.0, 2.0], 1e-30, 0.5, 0),
+    ([-3.0, -1.0, -2.0], 0.5, 0.999999, 2),
+    ([5.0] * 9, 2.0, 0.3, 4),                    # all equal: lowest ids first
+])
+def test_oracle_edge_cases_match_python_restatement(orc, x, t, p, k):
+    x = np.array(x, np.float32)
+    for u in (0.0, 0.25, 0.5, 0.999, 1.0 - 2.0 ** -53):
+        st, tok, _ = orc.sample_token(x, t, p, k, u)
+        assert st == 0 and tok == _py_sample(x, t, p, k, u), (u, tok)
