@@ -137,10 +137,72 @@ def build_layers(pkg, synth, dev, n_layers: int, inter: int = I, experts: int = 
     return layers
 
 
+# Layers and groups of this process, for the per-rank diagnostics printed when a run fails.
+_LIVE = {"layers": [], "group": None}
+
+
+def check_status(objs, where: str):
+    """Raises with the rank, the object index and the device status word of every object whose
+    bounded device-side wait expired (MMRS_ERR_TIMEOUT = 4)."""
+    bad = [(i, st) for i, o in enumerate(objs) for st in [o.status()] if st != 0]
+    if bad:
+        raise RuntimeError(f"rank {os.environ.get('RANK', '0')}: device status in {where}: {bad}")
+
+
+def rel_l2(got, ref, base) -> float:
+    """||got - ref|| / ||ref - base|| in float64 (base: the residual the block adds)."""
+    import numpy as np
+    g, r, b = (np.asarray(v, dtype=np.float64) for v in (got, ref, base))
+    return float(np.linalg.norm(g - r) / max(np.linalg.norm(r - b), 1e-30))
+
+
+def ranks_identical(t, world: int) -> bool:
+    """True when every rank holds the same bits in tensor t (all_gather over the process group)."""
+    import torch
+    import torch.distributed as dist
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t.contiguous())
+    ok = all(torch.equal(parts[0].view(torch.int32), p.view(torch.int32)) for p in parts[1:])
+    flag = torch.tensor([1 if ok else 0], device=t.device)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    return bool(flag.item())
+
+
+PARITY_BOUND = 1e-4  # relative L2 of the group's block output against the single-GPU block
+
+
+def decode_parity(pkg, synth, dev, group, world, layers, xs, res, tp: bool) -> dict:
+    """Four decode tokens over two layers in turn through the group, each compared with the
+    single-GPU block of the full layer on this rank's GPU (TP: full layers generated for the
+    check; EP: the rank's layers are full) and across ranks bit for bit."""
+    import torch
+    import torch.distributed as dist
+    full = build_layers(pkg, synth, dev, 2) if tp else layers[:2]
+    for L in full:
+        L.workspace(1)
+    torch.cuda.synchronize()
+    dist.barrier()
+    worst, same = 0.0, True
+    for t in range(4):
+        l = t % 2
+        x, r = xs[t:t + 1], res[t:t + 1]
+        yg = group.forward(layers[l], x, residual=r)
+        y1 = full[l].forward(x, residual=r)
+        torch.cuda.synchronize()
+        worst = max(worst, rel_l2(yg.cpu().numpy(), y1.cpu().numpy(), r.cpu().numpy()))
+        same = ranks_identical(yg, world) and same
+    check_status(layers[:2] + (full if tp else []), "decode parity")
+    if tp:
+        del full
+        torch.cuda.empty_cache()
+    return {"decode_rel_l2": worst, "decode_tokens": 4, "decode_layers": 2, "decode_ranks_identical": same}
+
+
 def cpu_decode_sample(layer, xs_host, res_host, budget_s: float):
     """The CPU oracle (OpenMP, all host threads) on a bounded sample of decode tokens."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle as orc
+    orc.set_threads(0)
     router = layer.router.cpu().numpy()
     bias = layer.bias.cpu().numpy()
     gate, up, down = layer.gate.cpu().numpy(), layer.up.cpu().numpy(), layer.down.cpu().numpy()
@@ -192,13 +254,33 @@ def run_prefill(pkg, synth, dev, args, rank: int, world: int, group=None):
     for L in layers:
         L.workspace(PF_T)
     torch.cuda.synchronize()
+    parity = None
+    if group is not None:
+        # one T = 512 block through the group against the single-GPU block of the full layer, at
+        # x * 0.05 (the prescribed N(0, 1) overflows MMQ's half block sums, see config["x"])
+        full = build_prefill_layers(pkg, synth, dev, 1) if tp else layers[:1]
+        full[0].workspace(PF_T)
+        xp = xs[0] * 0.05
+        rp = torch.empty(PF_T, H, dtype=torch.float32, device=dev)
+        pkg.synth_normal(rp, PF_SEED, 201, 1.0)
+        torch.cuda.synchronize()
+        dist.barrier()
+        yg = group.forward(layers[0], xp, residual=rp)
+        y1 = full[0].forward(xp, residual=rp)
+        torch.cuda.synchronize()
+        check_status(layers[:1] + full, "prefill parity")
+        parity = {"prefill_rel_l2": rel_l2(yg.cpu().numpy(), y1.cpu().numpy(), rp.cpu().numpy()),
+                  "prefill_tokens": PF_T, "prefill_ranks_identical": ranks_identical(yg, world)}
+        del full, yg, y1
+        torch.cuda.empty_cache()
+    if world > 1:
+        dist.barrier()
     with torch.cuda.stream(stream):
         for i in range(max(3, args.warmup if args.warmup < 10 else 3)):
             L = i % 2
             fwd(layers[L], xs[L], y=ys, topk_ids=ids[L], topk_w=wts[L], stream=stream)
         stream.synchronize()
-    for L in layers:
-        assert L.status() == 0, "device-side timeout in prefill warm-up"
+    check_status(layers, "prefill warm-up")
     steps = args.prefill_steps
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
@@ -217,8 +299,7 @@ def run_prefill(pkg, synth, dev, args, rank: int, world: int, group=None):
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = float(ms.item())
-    for L in layers:
-        assert L.status() == 0, "device-side timeout in prefill"
+    check_status(layers, "prefill")
     # e2e through the public API: x from pinned host memory, y back to pinned host memory
     x_host = torch.empty(PF_T, H, dtype=torch.float32, pin_memory=True)
     x_host.copy_(xs[0].cpu())
@@ -274,10 +355,11 @@ def run_prefill(pkg, synth, dev, args, rank: int, world: int, group=None):
                         "int8_tops": ops / per_step_s / 1e12, "int8_frac_of_nominal_4500": ops / per_step_s / 4.5e15},
            "e2e": {"value": PF_T * e2e_steps / (e2e_ms / 1e3), "unit": "tokens/s",
                    "h2d_bytes_per_step": PF_T * H * 4, "d2h_bytes_per_step": PF_T * H * 4},
-           "gpu_launches": 10 * steps, "clocks": clk.summary()}
+           "gpu_launches": 10 * steps, "clocks": clk.summary(), "parity": parity}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sys.path.insert(0, str(ROOT / "oracle"))
         import oracle as orc
+        orc.set_threads(0)
         L = layers[0]
         router, bias = L.router.cpu().numpy(), L.bias.cpu().numpy()
         gate, up, down = L.gate.cpu().numpy(), L.up.cpu().numpy(), L.down.cpu().numpy()
@@ -339,8 +421,7 @@ def run_config0(pkg, synth, dev, args) -> dict:
         e1.record(stream)
         e1.synchronize()
     ms = e0.elapsed_time(e1) / steps
-    for L in layers:
-        assert L.status() == 0, "device-side timeout in configs[0]"
+    check_status(layers, "configs[0]")
     distinct = len(np.unique(ids[0].cpu().numpy()))
     eb = 3 * I * (H // 256) * 144  # all-Q4_K expert
     alg = distinct * eb + E * H * 4 + 2 * C0_T * H * 4
@@ -354,6 +435,7 @@ def run_config0(pkg, synth, dev, args) -> dict:
     if not args.no_cpu_baseline:
         sys.path.insert(0, str(ROOT / "oracle"))
         import oracle as orc
+        orc.set_threads(0)
         L = layers[0]
         args_np = (L.router.cpu().numpy(), L.bias.cpu().numpy(), L.gate.cpu().numpy(), L.up.cpu().numpy(),
                    L.down.cpu().numpy(), Q4K, Q4K)
@@ -689,6 +771,8 @@ def ar_sweep(group, world: int, dev, iters: int = 50) -> dict:
         nccl_buf = torch.ones(count, dtype=torch.float32, device=dev)
         row = {"T": T, "bytes": count * 4}
         for name in ("peer", "nccl"):
+            torch.cuda.synchronize()
+            dist.barrier()
             for i in range(5):  # warm-up
                 if name == "peer":
                     group.all_reduce(lambda ptr: None, count, residual=res, y=y)
@@ -714,51 +798,77 @@ def ar_sweep(group, world: int, dev, iters: int = 50) -> dict:
     return out
 
 
+def _load_synth_module():
+    """minimax-rs_b200/synth.py alone (numpy only): the reference arm loads no product library."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("mmrs_synth_np", ROOT / "minimax-rs_b200" / "synth.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def reference_inputs(n_tok: int = 16):
+    """Host copies of layer 0 of the decode bench and its first n_tok tokens, made by
+    the numpy mirror of the synthetic generator (bit-identical with the device generator); only
+    the experts the tokens route to are generated (the others stay zero and are never read)."""
+    import numpy as np
+    synth = _load_synth_module()
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as orc
+    st = synth.layer_streams(0)
+    router = synth.normal_f32(E * H, SEED, st["router"], 0.02).reshape(E, H)
+    bias = synth.normal_f32(E, SEED, st["bias"], 0.01)
+    xs = synth.normal_f32(n_tok * H, SEED, 100, 1.0, bf16=True).reshape(n_tok, H)
+    res = synth.normal_f32(n_tok * H, SEED, 101, 1.0).reshape(n_tok, H)
+    ids, _ = orc.route_topk(orc.router_logits(xs, router), bias)
+    used = sorted(set(int(e) for e in ids.reshape(-1)))
+    gb, db = (H // 256) * 144, (I // 256) * 176
+    gate = np.zeros((E, I, gb), dtype=np.uint8)
+    up = np.zeros_like(gate)
+    down = np.zeros((E, H, db), dtype=np.uint8)
+    for c in range(0, len(used), 16):
+        sub = used[c:c + 16]
+        gate[sub] = synth.kquant(Q4K, SEED, st["gate"], E, I, H, expert_ids=sub)
+        up[sub] = synth.kquant(Q4K, SEED, st["up"], E, I, H, expert_ids=sub)
+        down[sub] = synth.kquant(Q5K, SEED, st["down"], E, H, I, expert_ids=sub)
+    return router, bias, gate, up, down, xs, res, len(used)
+
+
 def run_reference(args):
     """Reference arm: the CPU restatement of the reference's MoE decode block (the reference's
-    own CPU path, Candle's quantized matmul, cannot be built here: no Rust toolchain), on all
-    host threads, same metric and config, each step one token."""
+    own CPU path, Candle's quantized matmul, cannot be built here: no Rust toolchain), on every
+    host thread (set explicitly: torchrun exports OMP_NUM_THREADS=1), same metric and config, one
+    token per step.  Inputs come from the numpy generator, so this arm loads no product library
+    and no CUDA context.  At least `--steps` tokens and at least 12 s are timed (60 s cap)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import torch
-    import __graft_entry__ as ge
-    pkg, synth = ge.load_package(), ge.load_synth()
-    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
-    layer = build_layers(pkg, synth, dev, 1)[0]
-    xs = torch.empty(16, H, dtype=torch.float32, device=dev)
-    pkg.synth_normal(xs, SEED, 100, 1.0, bf16=True)
-    res = torch.empty(16, H, dtype=torch.float32, device=dev)
-    pkg.synth_normal(res, SEED, 101, 1.0)
-    torch.cuda.synchronize()
-    xs_h, res_h = xs.cpu().numpy(), res.cpu().numpy()
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle as orc
-    router, bias = layer.router.cpu().numpy(), layer.bias.cpu().numpy()
-    gate, up, down = layer.gate.cpu().numpy(), layer.up.cpu().numpy(), layer.down.cpu().numpy()
-    del layer
-    torch.cuda.empty_cache()
-    for i in range(min(args.warmup, 3)):
+    cores = orc.set_threads(0)
+    router, bias, gate, up, down, xs_h, res_h, n_exp = reference_inputs()
+    warm = min(args.warmup, 3)
+    for i in range(warm):
         orc.moe_block(router, bias, gate, up, down, Q4K, Q5K, xs_h[i:i + 1], res_h[i:i + 1])
-    budget = 60.0
+    min_s, cap_s = 12.0, 60.0
     n, t0 = 0, time.perf_counter()
-    while n < args.steps:
+    while True:
         i = n % len(xs_h)
         orc.moe_block(router, bias, gate, up, down, Q4K, Q5K, xs_h[i:i + 1], res_h[i:i + 1])
         n += 1
-        if time.perf_counter() - t0 > budget:
+        el = time.perf_counter() - t0
+        if (n >= args.steps and el >= min_s) or el >= cap_s:
             break
-    el = time.perf_counter() - t0
     v = n / el
     out = {"metric": "moe_block_decode_tokens_per_s", "value": v, "unit": "tokens/s", "impl": "reference",
-           "n_gpus": args.gpus, "steps": n, "warmup": min(args.warmup, 3), "ms_per_step": 1e3 * el / n,
+           "n_gpus": args.gpus, "steps": n, "warmup": warm, "ms_per_step": 1e3 * el / n,
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xq4k/q5k->f32",
-           "data": "synthetic (seeded, device-generated, copied to host)",
-           "config": {"workload": "decode T=1 MoE block (BASELINE configs[1]), 1 layer, fresh token per step",
+           "data": "synthetic (seeded numpy generator, bit-identical with the device generator)",
+           "config": {"workload": "decode T=1 MoE block (BASELINE configs[1]), 1 layer, 16 tokens in turn",
                       "experts": E, "hidden": H, "inter": I, "topk": TOPK, "gate_up": "Q4_K", "down": "Q5_K"},
-           "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": orc.num_threads(), "kind": "port",
-                            "sample": f"{n} decode tokens (time-bounded at {budget:.0f} s of the requested "
-                                      f"{args.steps} steps)"},
+           "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                            "sample": f"{n} decode tokens in {el:.1f} s (16 tokens of layer 0 in turn, "
+                                      f"{n_exp} distinct experts; oracle/moe_oracle.c, OpenMP, {cores} threads)"},
            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
            "note": "CPU restatement (oracle/moe_oracle.c) of the reference's GGUF MoE arithmetic; the "
                    "reference's Candle CPU path is unavailable (no Rust toolchain on this box)"}
@@ -829,6 +939,8 @@ def main():
         group = gm.PeerGroup(world, rank, ar_capacity=2048 * H, expert_parallel=world > 2, allgather=allgather)
     tp = world == 2
     layers = build_layers(pkg, synth, dev, args.layers, tp_world=2 if tp else 1, tp_rank=rank if tp else 0)
+    _LIVE["layers"] = layers
+    _LIVE["group"] = group
     n_tok = 512
     xs = torch.empty(n_tok, H, dtype=torch.float32, device=dev)
     pkg.synth_normal(xs, SEED, 100, 1.0, bf16=True)  # the same tokens on every rank (TP / EP)
@@ -839,6 +951,15 @@ def main():
         L.workspace(1)
     stream = torch.cuda.Stream(device=dev)
     torch.cuda.synchronize()
+    parity = None
+    if world > 1:
+        # load the kernels on every rank first (the module loads lazily at the first launch), so
+        # no rank's first group launch waits on a peer that is still loading
+        layers[0].forward(xs[:1], residual=res[:1], y=ys[:1])
+        torch.cuda.synchronize()
+        check_status(layers[:1], "local warm-up")
+        parity = decode_parity(pkg, synth, dev, group, world, layers, xs, res, tp)
+        dist.barrier()
 
     def step(i, s):
         L = layers[i % len(layers)]
@@ -851,6 +972,8 @@ def main():
     # CUDA graph of G consecutive steps (G multiple of the layer count)
     G = max(len(layers), 64 // len(layers) * len(layers))
     graphs = []
+    if world > 1:
+        dist.barrier()
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
             step(i, stream)
@@ -866,8 +989,7 @@ def main():
             print(f"[bench] graph capture failed ({e}); timing direct launches", file=sys.stderr)
             graphs = []
     torch.cuda.synchronize()
-    for L in layers:
-        assert L.status() == 0, "device-side timeout during warm-up"
+    check_status(layers, "decode warm-up")
 
     n_graph_reps = (args.steps + G - 1) // G if graphs else 0
     steps = n_graph_reps * G if graphs else args.steps
@@ -890,8 +1012,7 @@ def main():
     if world > 1:
         dist.barrier()
     ms = start.elapsed_time(end)
-    for L in layers:
-        assert L.status() == 0, "device-side timeout in the timed region"
+    check_status(layers, "decode timed region")
     ms_t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
@@ -1000,7 +1121,16 @@ def main():
             "lm_head": lm_head,
             "config4": config4,
         }
+        if world > 1:
+            pf = (prefill or {}).get("parity") or {}
+            out["parity"] = dict(parity or {}, **pf, bound=PARITY_BOUND)
         print(json.dumps(out), flush=True)
+    if world > 1:
+        pf = (prefill or {}).get("parity") or {}
+        bad = (not parity or parity["decode_rel_l2"] > PARITY_BOUND or not parity["decode_ranks_identical"]
+               or (pf and (not pf["prefill_rel_l2"] <= PARITY_BOUND or not pf["prefill_ranks_identical"])))
+        if bad:
+            raise RuntimeError(f"multi-GPU parity failed: {parity} {pf}")
     if world > 1:
         torch.cuda.synchronize()
         dist.barrier()  # no peer still reads this rank's exchange region
@@ -1008,5 +1138,27 @@ def main():
         dist.destroy_process_group()
 
 
+def _report_failure():
+    """Prints the exception and the device status words of this rank's layers and group to
+    stdout, every line prefixed with the rank (a launcher's summary shows only exit codes)."""
+    import traceback
+    rank = os.environ.get("RANK", "0")
+    for line in traceback.format_exc().splitlines():
+        print(f"[rank {rank}] {line}", flush=True)
+    try:
+        st = [L.status() for L in _LIVE["layers"]]
+        print(f"[rank {rank}] layer status words: {st}", flush=True)
+        if _LIVE["group"] is not None:
+            print(f"[rank {rank}] group status word: {_LIVE['group'].status()}", flush=True)
+    except Exception as e:  # the status read itself failed (e.g. a lost context)
+        print(f"[rank {rank}] status read failed: {e!r}", flush=True)
+
+
 if __name__ == "__main__":
-    main()
+    try:
+        main()
+    except SystemExit:
+        raise
+    except BaseException:
+        _report_failure()
+        sys.exit(1)

@@ -174,6 +174,14 @@ MMRS_API int mmrs_moe_block_decode_static(const MmrsMoeWeights *w, const float *
                                           const float *residual, float *y, uint32_t *topk_ids,
                                           float *topk_weights, mmrs_stream_t stream);
 
+/* No counterpart in the reference.  Device-side status of the last mmrs_moe_block_decode_static
+ * call on the current device: synchronises `stream`, returns MMRS_OK or MMRS_ERR_TIMEOUT (a
+ * bounded wait of that call expired and y was not written) and clears the word.  Allocates
+ * nothing.  The next static call clears the word as well, so read it before that call.  The
+ * cached scratch address is tied to the device's current context: do not call the static entry
+ * points across a cudaDeviceReset in the same process. */
+MMRS_API int mmrs_moe_static_status(mmrs_stream_t stream);
+
 /* Reads back (synchronising `stream`) and clears the device-side status word of a workspace. */
 MMRS_API int mmrs_moe_workspace_status(void *workspace, mmrs_stream_t stream);
 
@@ -236,7 +244,10 @@ MMRS_API int mmrs_peer_status(const MmrsPeerGroup *g, mmrs_stream_t stream);
  * TensorParallelRankGroup::all_reduce_sum_with_residual, tensor_parallel.rs:786-812): y is the
  * full block output (+ residual) on every rank.  T == 1: the fused decode kernel exchanges the
  * ranks' partial rows over NVLink inside the same launch.  T > 1: the multi-token path on the
- * rank's shard, then mmrs_peer_all_reduce with `token` (same on all ranks, monotonic). */
+ * rank's shard, then mmrs_peer_all_reduce.  `token` is the group's operation counter for every T:
+ * the same value on all ranks, monotonic over all calls on the group (whatever the layer), never
+ * 0 (MMRS_ERR_ARG).  The exchange flags and partial buffers belong to the group, so layers that
+ * share a group must not reuse tokens. */
 MMRS_API int mmrs_moe_block_forward_group(const MmrsMoeWeights *w, const MmrsPeerGroup *g,
                                           const float *x, const float *residual, float *y,
                                           int num_tokens, uint32_t *topk_ids, float *topk_weights,

@@ -116,6 +116,7 @@ PROTOTYPES = {
                                          _VP]),
     "mmrs_moe_workspace_status": (_I, [_VP, _VP]),
     "mmrs_moe_block_decode_static": (_I, [C.POINTER(MmrsMoeWeights), _VP, _VP, _VP, _VP, _VP, _VP]),
+    "mmrs_moe_static_status": (_I, [_VP]),
     "mmrs_moe_workspace_trace": (_I, [_VP, _VP, _I, _VP]),
     "mmrs_synth_normal_f32": (_I, [_VP, _I64, _U64, _U32, _F, _I, _VP]),
     "mmrs_synth_kquant": (_I, [_VP, _I, _U64, _U32] + [_I] * 7 + [_VP]),

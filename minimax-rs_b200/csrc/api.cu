@@ -551,13 +551,14 @@ extern "C" int mmrs_moe_block_forward_group(const MmrsMoeWeights *w, const MmrsP
         !aligned16(y) || (residual && !aligned16(residual)))
         return MMRS_ERR_ARG;
     if (w->hidden > kXchMaxHidden) return MMRS_ERR_UNSUPPORTED;
+    if (token == 0) return MMRS_ERR_ARG;  // tokens start at 1 (flags are zero-initialised)
     uint8_t *ws = (uint8_t *)workspace;
     cudaStream_t s = (cudaStream_t)stream;
     const int ep = g->expert_parallel ? 1 : 0;
     if (num_tokens > 1) {
         // rank-local block into this rank's all-reduce buffer, then the peer all-reduce (+ residual)
         const size_t count = (size_t)num_tokens * w->hidden;
-        if (count > g->ar_capacity || token == 0) return MMRS_ERR_ARG;
+        if (count > g->ar_capacity) return MMRS_ERR_ARG;
         float *partial = mmrs_xch_ar_buffer(g, token);
         rc = block_forward_multi(w, x, nullptr, partial, num_tokens, topk_ids, topk_weights, ws, s,
                                  ep ? g->world : 1, ep ? g->rank : 0);
@@ -589,6 +590,7 @@ extern "C" int mmrs_moe_block_forward_group(const MmrsMoeWeights *w, const MmrsP
     p.world = g->world;
     p.rank = g->rank;
     p.ep = ep;
+    p.token = token;
     rc = decode_configure(p, device_sms(), device_max_smem());
     if (rc != MMRS_OK) return rc;
     return decode_launch(p, s);

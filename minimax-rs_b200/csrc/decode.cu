@@ -28,6 +28,8 @@
 // (gguf.cuh:727-750, 783-813): dall * sum d8*(dot*sc) - dmin * sum d8*sum(q8)*m.
 // Every wait is bounded by a globaltimer deadline; on expiry the kernel records MMRS_ERR_TIMEOUT in
 // the workspace status word, keeps every named barrier matched, drains its copies and returns.
+#include <mutex>
+
 #include "common.cuh"
 #include "decode.cuh"
 #include "peer.cuh"
@@ -797,7 +799,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             // (bounded) for the same CTA's flag on every peer, then sum the ranks' rows in rank
             // order (bit-identical on all ranks) and add the residual
             // (TensorParallelRankGroup::all_reduce_sum_with_residual, tensor_parallel.rs:786-812).
-            const uint32_t token = epoch / 2u + 1u;
+            // The token is the group's operation counter: every layer sharing the group draws a
+            // fresh one, so a flag raised for another layer's exchange never satisfies this wait.
+            const uint32_t token = p.token;
             const size_t part_off = kXchDPart + sizeof(float) * (size_t)(token & 1u) * kXchMaxHidden;
             float *mine = reinterpret_cast<float *>(p.xch + part_off);
             for (int r = tid; r < dn_r1 - dn_r0; r += kConsumerThreads) {
@@ -898,18 +902,19 @@ int decode_configure(DecodeParams &p, int num_sms, int max_smem) {
 
 int decode_launch(const DecodeParams &p, cudaStream_t stream) {
     const size_t smem = decode_smem_bytes(p);
-    // Raise the dynamic shared-memory limit once per device (the attribute is per context).
-    static int configured[64] = {0};
+    // Raise the dynamic shared-memory limit once per device (the attribute is per context);
+    // call_once keeps concurrent host threads from racing on it.
+    static std::once_flag once[64];
+    static cudaError_t set_rc[64];
     int dev = 0;
-    cudaGetDevice(&dev);
-    cudaError_t err = cudaSuccess;
-    if (dev < 0 || dev >= 64 || configured[dev] < (int)smem) {
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MMRS_ERR_LAUNCH;
+    std::call_once(once[dev], [dev] {
         int optin = 0;
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-        err = cudaFuncSetAttribute(moe_decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
-        if (err != cudaSuccess) return MMRS_ERR_LAUNCH;
-        if (dev >= 0 && dev < 64) configured[dev] = optin;
-    }
+        set_rc[dev] = cudaFuncSetAttribute(moe_decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+    });
+    if (set_rc[dev] != cudaSuccess) return MMRS_ERR_LAUNCH;
+    cudaError_t err = cudaSuccess;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.grid);
     cfg.blockDim = dim3(kThreads);

@@ -44,6 +44,9 @@ struct DecodeParams {
     uint8_t *xch;
     const uint8_t *xpeer[8];
     int world, rank, ep;
+    // operation token of the group (monotonic, the same on every rank, never 0): the exchange
+    // flags and double-buffered partial rows belong to the group, not to a layer's workspace
+    uint32_t token;
 };
 
 size_t decode_smem_bytes(const DecodeParams &p);

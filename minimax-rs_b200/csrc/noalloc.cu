@@ -17,7 +17,13 @@
 // on the GPU (different streams or host threads without ordering) race on the scratch.
 //
 // The first call on a device resolves the device address of the array (cudaGetSymbolAddress, with
-// that device current) and caches it; make that first call before any stream capture.
+// that device current) and caches it; make that first call before any stream capture.  The cached
+// address belongs to the device's current context: do not use these entry points across a
+// cudaDeviceReset (or any other teardown of the primary context) in the same process.
+//
+// A bounded device-side wait that expires leaves MMRS_ERR_TIMEOUT in the array's status word and
+// y unwritten; mmrs_moe_static_status() reads and clears that word (the next call clears it too,
+// so read it before the next call).
 #include <mutex>
 
 #include "common.cuh"
@@ -97,4 +103,22 @@ extern "C" int mmrs_moe_block_decode_static(const MmrsMoeWeights *w, const float
     // status word, barrier counter and epochs must start at zero (no allocation: a memset node)
     if (cudaMemsetAsync(base, 0, kControlBytes, (cudaStream_t)stream) != cudaSuccess) return MMRS_ERR_LAUNCH;
     return decode_launch(p, (cudaStream_t)stream);
+}
+
+extern "C" int mmrs_moe_static_status(mmrs_stream_t stream) {
+    void *base = nullptr;
+    int rc = scratch_address(&base);
+    if (rc != MMRS_OK) return rc;
+    cudaStream_t s = (cudaStream_t)stream;
+    uint32_t status = 0;
+    // the status word is the first field of the control block at the start of the array
+    if (cudaMemcpyFromSymbolAsync(&status, g_decode_scratch, sizeof(status), 0, cudaMemcpyDeviceToHost, s) !=
+        cudaSuccess)
+        return MMRS_ERR_LAUNCH;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return MMRS_ERR_LAUNCH;
+    if (status != 0) {
+        if (cudaMemsetAsync(base, 0, kControlBytes, s) != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess)
+            return MMRS_ERR_LAUNCH;
+    }
+    return (int)status;
 }

@@ -31,6 +31,8 @@
 #include <stddef.h>
 
 #include "../../include/minimax_sample.h"
+#include <mutex>
+
 #include "common.cuh"
 
 namespace mmrs {
@@ -802,15 +804,17 @@ __global__ void __launch_bounds__(kSpThreads, 1) sample_kernel(const SpParams p)
 
 int sp_launch(const SpParams &p, int grid, cudaStream_t stream) {
     const size_t smem = (size_t)8 * p.chunk + (size_t)8 * kSpBins;
-    static int configured[64] = {0};
+    // the dynamic shared-memory limit is raised once per device (the attribute is per context);
+    // call_once keeps concurrent host threads from racing on it
+    static std::once_flag once[64];
+    static cudaError_t set_rc[64];
     int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || configured[dev] < (int)smem) {
-        if (cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)((size_t)8 * kSpMaxSlice + (size_t)8 * kSpBins)) != cudaSuccess)
-            return MMRS_ERR_LAUNCH;
-        if (dev >= 0 && dev < 64) configured[dev] = (int)((size_t)8 * kSpMaxSlice + (size_t)8 * kSpBins);
-    }
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MMRS_ERR_LAUNCH;
+    std::call_once(once[dev], [dev] {
+        set_rc[dev] = cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)((size_t)8 * kSpMaxSlice + (size_t)8 * kSpBins));
+    });
+    if (set_rc[dev] != cudaSuccess) return MMRS_ERR_LAUNCH;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kSpThreads);
@@ -826,15 +830,16 @@ int sp_launch(const SpParams &p, int grid, cudaStream_t stream) {
 
 // One grid for every call on a device (the barrier's epoch words count on it): one CTA per SM.
 int sp_grid() {
-    static int grids[64] = {0};
+    static std::once_flag once[64];
+    static int grids[64];
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-    if (dev >= 0 && dev < 64 && grids[dev]) return grids[dev];
-    int sms = 0;
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) return 0;
-    const int g = sms < kMaxGridCtas ? sms : kMaxGridCtas;
-    if (dev >= 0 && dev < 64) grids[dev] = g;
-    return g;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    std::call_once(once[dev], [dev] {
+        int sms = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0)
+            grids[dev] = sms < kMaxGridCtas ? sms : kMaxGridCtas;
+    });
+    return grids[dev];
 }
 
 int sp_bind(SpParams &p, void *workspace, size_t workspace_bytes, int vocab, int *grid) {

@@ -147,7 +147,9 @@ class PeerGroup:
         if y is None:
             y = torch.empty_like(x)
         ws = layer.workspace(T)
-        tok = token if token is not None else (self.tokens.next() if T > 1 else 0)
+        # every call draws a group token, also for T == 1: the exchange flags and buffers belong
+        # to the group, and a layer-local counter would let one layer's wait pass on another's flag
+        tok = token if token is not None else self.tokens.next()
         rc = lib().mmrs_moe_block_forward_group(C.byref(layer.c), C.byref(self.c), x.data_ptr(), _ptr(residual),
                                                 y.data_ptr(), T, _ptr(topk_ids), _ptr(topk_w), ws.data_ptr(),
                                                 ws.numel(), tok, _stream(stream))

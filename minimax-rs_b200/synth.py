@@ -70,17 +70,20 @@ def normal_f32(n: int, seed: int, stream: int, scale: float = 1.0, bf16: bool = 
 
 
 def kquant(gguf_type: int, seed: int, stream: int, experts: int, rows: int, k: int,
-           row0: int = 0, nrows: int | None = None, kblk0: int = 0, nkblk: int | None = None) -> np.ndarray:
+           row0: int = 0, nrows: int | None = None, kblk0: int = 0, nkblk: int | None = None,
+           expert_ids=None) -> np.ndarray:
     """Window of a synthetic k-quant tensor [experts][rows][k/256] — mirrors mmrs_synth_kquant.
 
-    Returns uint8 of shape [experts, nrows, nkblk * block_bytes]."""
+    Returns uint8 of shape [experts, nrows, nkblk * block_bytes]; with `expert_ids`, only those
+    experts' windows, stacked in the given order (shape [len(expert_ids), nrows, ...])."""
     nblk = k // 256
     nrows = rows - row0 if nrows is None else nrows
     nkblk = nblk - kblk0 if nkblk is None else nkblk
     wpb = BLOCK_BYTES[gguf_type] // 8
     key = stream_key(seed, stream)
     key_d = stream_key(seed, stream + 0x10000)
-    e = np.arange(experts, dtype=np.int64)[:, None, None]
+    ids = np.arange(experts, dtype=np.int64) if expert_ids is None else np.asarray(expert_ids, dtype=np.int64)
+    e = ids[:, None, None]
     r = np.arange(nrows, dtype=np.int64)[None, :, None]
     b = np.arange(nkblk, dtype=np.int64)[None, None, :]
     gblk = (e * rows + row0 + r) * nblk + kblk0 + b  # [E, nrows, nkblk]
@@ -89,7 +92,7 @@ def kquant(gguf_type: int, seed: int, stream: int, experts: int, rows: int, k: i
     dm = (np.abs(normal(key_d, (2 * gblk + 1).astype(np.uint64))) * np.float32(0.01)).astype(np.float16)
     low = d.view(np.uint16).astype(np.uint64) | (dm.view(np.uint16).astype(np.uint64) << np.uint64(16))
     words[..., 0] = (words[..., 0] & np.uint64(0xFFFFFFFF00000000)) | low
-    return words.view(np.uint8).reshape(experts, nrows, nkblk * BLOCK_BYTES[gguf_type])
+    return words.view(np.uint8).reshape(len(ids), nrows, nkblk * BLOCK_BYTES[gguf_type])
 
 
 def q8_0_blocks(seed: int, stream: int, rows: int, k: int) -> np.ndarray:

@@ -101,6 +101,13 @@ int orc_num_threads(void) {
 #endif
 }
 
+/* Sets the OpenMP team size of the following calls (n <= 0: all hardware threads).  A launcher
+ * such as torchrun exports OMP_NUM_THREADS=1 to its workers; a timed CPU baseline sets the team
+ * size here instead of inheriting that. */
+void orc_set_threads(int n) {
+    omp_set_num_threads(n > 0 ? n : omp_get_num_procs());
+}
+
 /* ------------------------------------------------------------------------------------ */
 /* k-quant super-block unpacking                                                         */
 /* ------------------------------------------------------------------------------------ */

@@ -109,6 +109,7 @@ void orc_moe_block(const OrcMoeWeights *w, const float *x, const float *residual
 
 /* Number of OpenMP threads the oracle uses (for the CPU-baseline report). */
 int orc_num_threads(void);
+void orc_set_threads(int n);
 
 /* ---- decode attention (attn_oracle.c) ---- */
 uint16_t orc_double_to_half(double v);

@@ -64,6 +64,12 @@ def num_threads() -> int:
     return lib().orc_num_threads()
 
 
+def set_threads(n: int = 0) -> int:
+    """OpenMP team size of later calls (0: every hardware thread); returns the size now in force."""
+    lib().orc_set_threads(C.c_int(n))
+    return num_threads()
+
+
 def dequant(gguf_type: int, blocks: np.ndarray, fused: bool = True) -> np.ndarray:
     b = _c(blocks, np.uint8).reshape(-1)
     n = b.size // BLOCK_BYTES[gguf_type]

@@ -50,7 +50,47 @@ def test_token_counter_skips_zero(gm):
     t = gm.TokenCounter()
     assert [t.next() for _ in range(3)] == [1, 2, 3]
     t.value = 0xFFFFFFFF
-    assert t.next() == 1  # 0 is reserved (decode uses its own epoch)
+    assert t.next() == 1  # 0 is reserved (flags start at zero)
+
+
+def test_group_forward_draws_a_token_for_every_call(gm, monkeypatch):
+    """Single-token calls take the group's next token like multi-token calls: the exchange flags
+    and partial buffers are the group's, shared by every layer, so no two calls may share one."""
+    seen = []
+
+    class Lib:
+        def mmrs_moe_block_forward_group(self, w, g, x, res, y, T, ids, wts, ws, nbytes, token, stream):
+            seen.append((T, token))
+            return 0
+
+    class Layer:
+        c = None
+
+        def workspace(self, T):
+            return torch.zeros(16, dtype=torch.uint8)
+
+    class Stream:
+        cuda_stream = 0
+
+    monkeypatch.setattr(gm, "lib", lambda: Lib())
+    monkeypatch.setattr(gm.C, "byref", lambda o: o)
+    grp = gm.PeerGroup.__new__(gm.PeerGroup)
+    grp.tokens, grp.c = gm.TokenCounter(), None
+    layers = [Layer(), Layer(), Layer()]
+    for t in range(6):
+        T = 1 if t % 3 else 5
+        grp.forward(layers[t % 3], torch.zeros(T, 8), y=torch.zeros(T, 8), stream=Stream())
+    assert seen == [(5, 1), (1, 2), (1, 3), (5, 4), (1, 5), (1, 6)]
+
+
+def test_numpy_kquant_expert_subset_matches_full_tensor(pkg):
+    """The reference arm generates only the experts its tokens use; those windows must be the
+    same bytes as in the whole synthetic tensor."""
+    import importlib
+    synth = importlib.import_module("minimax_rs_b200.synth")
+    full = synth.kquant(Q5K, 7, 3, 6, 4, 512)
+    sub = synth.kquant(Q5K, 7, 3, 6, 4, 512, expert_ids=[4, 1])
+    assert np.array_equal(sub, full[[4, 1]])
 
 
 class _FakeLib:

@@ -60,7 +60,7 @@ def _run_group(pkg, groups, layers, x, residual, T):
             rs = None if residual is None else residual.to(dev)
             lay.workspace(T)
             torch.cuda.synchronize(dev)
-            y = g.forward(lay, xs, residual=rs, stream=s, token=1 if T > 1 else None)
+            y = g.forward(lay, xs, residual=rs, stream=s)
             ys.append(y)
             streams.append(s)
     for r, s in enumerate(streams):
@@ -114,6 +114,103 @@ def test_group_decode_repeated_tokens(pkg, synth, orc):
     for t in (0, T - 1):
         ry, _, _ = _oracle_block(orc, L, L["x"][t:t + 1].cpu().numpy(), None)
         assert np.linalg.norm(y0[t] - ry[0]) / np.linalg.norm(ry[0]) < 1e-4
+
+
+@needs2
+@pytest.mark.parametrize("ep", [False, True], ids=["tp2", "ep2"])
+def test_group_decode_layers_round_robin(pkg, synth, orc, ep):
+    """Three layers, each with its own workspace, share one group and take turns for twelve decode
+    tokens (as a model's layers do).  The exchange flags and partial buffers belong to the group,
+    so every call must wait for the peers' rows of *this* call: each step is checked against the
+    oracle and the ranks must agree bit for bit."""
+    import torch
+    gm = _group_mod(pkg)
+    E, H, I, NL, T = 16, 512, 512, 3, 12
+    Ls = [make_layer(pkg, synth, torch.device("cuda", 0), E, H, I, Q4K, Q5K, seed=3400 + l, layer=l, T=T)
+          for l in range(NL)]
+    groups = gm.PeerGroup.local([0, 1], ar_capacity=H, expert_parallel=ep)
+    layers = [_rank_layers(pkg, gm, L, 2, ep) for L in Ls]  # [layer][rank]
+    xs = [[L["x"].to(torch.device("cuda", r)) for r in range(2)] for L in Ls]
+    res = [[L["residual"].to(torch.device("cuda", r)) for r in range(2)] for L in Ls]
+    outs = []
+    for t in range(T):
+        l = t % NL
+        step = []
+        for r in range(2):
+            with torch.cuda.device(r):
+                layers[l][r].workspace(1)
+                step.append(groups[r].forward(layers[l][r], xs[l][r][t:t + 1], residual=res[l][r][t:t + 1]))
+        outs.append((l, t, step))
+    for r in range(2):
+        torch.cuda.synchronize(r)
+    for g in groups:
+        with torch.cuda.device(g._device):
+            assert g.status() == 0
+    for l in range(NL):
+        for r in range(2):
+            with torch.cuda.device(r):
+                assert layers[l][r].status() == 0
+    for l, t, (y0, y1) in outs:
+        a, b = y0.cpu().numpy(), y1.cpu().numpy()
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), (l, t)
+        L = Ls[l]
+        ry, _, _ = _oracle_block(orc, L, L["x"][t:t + 1].cpu().numpy(), L["residual"][t:t + 1].cpu().numpy())
+        rr = L["residual"][t:t + 1].cpu().numpy()
+        assert np.linalg.norm((a - rr) - (ry - rr)) / np.linalg.norm(ry - rr) < 1e-4, (l, t)
+
+
+def _owner_counts(ids, world):
+    return [sum(1 for e in ids if e % world == r) for r in range(world)]
+
+
+@pytest.mark.parametrize("world", [4, 8], ids=["ep4", "ep8"])
+def test_group_decode_full_size_ep(pkg, synth, orc, world):
+    """Expert parallel at full size (E = 256, H = 3072, I = 1536) on `world` GPUs, for tokens
+    chosen so that at least one rank owns none of the token's eight experts (that rank computes
+    nothing and only contributes zero rows to the exchange)."""
+    if _ngpu() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch
+    from moe_cases import oracle_decode
+    gm = _group_mod(pkg)
+    E, H, I = 256, 3072, 1536
+    T = 24
+    L = make_layer(pkg, synth, torch.device("cuda", 0), E, H, I, Q4K, Q5K, seed=3500 + world, T=T)
+    router, bias = L["router"].cpu().numpy(), L["bias"].cpu().numpy()
+    xh = L["x"].cpu().numpy()
+    picked = []
+    for t in range(T):
+        ids, _ = orc.route_topk(orc.router_logits(xh[t:t + 1], router), bias)
+        if min(_owner_counts(ids[0].tolist(), world)) == 0:
+            picked.append(t)
+    assert picked, "no token leaves a rank without experts"
+    picked = picked[:3]
+    groups = gm.PeerGroup.local(list(range(world)), ar_capacity=H, expert_parallel=True)
+    layers = _rank_layers(pkg, gm, L, world, True)
+    outs = []
+    for t in picked:
+        step = []
+        for r in range(world):
+            with torch.cuda.device(r):
+                layers[r].workspace(1)
+                x = L["x"][t:t + 1].to(f"cuda:{r}")
+                rr = L["residual"][t:t + 1].to(f"cuda:{r}")
+                step.append(groups[r].forward(layers[r], x, residual=rr))
+        outs.append((t, step))
+    for r in range(world):
+        torch.cuda.synchronize(r)
+    for g in groups:
+        with torch.cuda.device(g._device):
+            assert g.status() == 0
+    for t, ys in outs:
+        got = [y.cpu().numpy() for y in ys]
+        for r in range(1, world):
+            assert np.array_equal(got[0].view(np.uint32), got[r].view(np.uint32)), (t, r)
+        ry, _, _, _ = oracle_decode(orc, pkg, L, xh[t], L["residual"][t].cpu().numpy())
+        rr = L["residual"][t].cpu().numpy()
+        assert np.linalg.norm((got[0][0] - rr) - (ry - rr)) / np.linalg.norm(ry - rr) < 1e-4, t
+    for g in groups:
+        g.close()
 
 
 @needs2

@@ -35,7 +35,8 @@ def test_static_scratch_entry_matches_workspace_entry(pkg, synth, dev):
         rc = pkg.lib().mmrs_moe_block_decode_static(C.byref(layer.c), x.data_ptr(), res.data_ptr(), y.data_ptr(),
                                                      ids.data_ptr(), w.data_ptr(), stream)
         assert rc == pkg.MMRS_OK
-        torch.cuda.synchronize()
+        # the static call's own status word (in the library's fixed array), read before the next call
+        assert pkg.lib().mmrs_moe_static_status(stream) == pkg.MMRS_OK
         assert layer.status() == 0
         assert torch.equal(ids, ids_ref)
         np.testing.assert_allclose(w.cpu().numpy(), w_ref.cpu().numpy(), rtol=1e-6)
