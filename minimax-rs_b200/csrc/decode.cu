@@ -5,24 +5,27 @@
 //   -> quantize_q8_1 -> moe_gate_up_decode_kernel -> quantize_silu_mul_q8_1
 //   -> moe_down_decode_kernel (moe_gguf.cu:200-343, 426-567) -> + residual (model.rs:218)
 //
-// One CTA per SM: 12 consumer warps (three groups of 4) + 1 producer warp.
+// One CTA per SM: 12 consumer warps + 1 producer warp.
 //   P0  router GEMV in the canonical order (8 K-slices; the CTA's two experts x 8 slices are 16
-//       (expert, slice) pairs, pair w + 12 r to consumer warp w: 32 lane partials, butterfly,
-//       fixed slice tree); every CTA quantises x to Q8_1 in shared memory.  Grid barrier #1.
-//   P1  every CTA selects the top-8 with warp-shuffle argmax rounds on 64-bit keys
-//       (score desc, expert id asc — the stable descending order) and renormalises the weights
-//       with the reference's fixed tree.
-//   P2  gate/up: each CTA owns a contiguous range of (slot, row) pairs, streamed in units of up
-//       to 8 rows x {gate, up} into a ring of shared-memory stages by 1-D bulk TMA copies
-//       (cp.async.bulk + mbarrier complete_tx).  Consumer groups take alternate units; in a group
-//       a half-warp computes one gate row, the other half the matching up row, and
-//       act = up * silu(gate) stays in shared memory.  Q8_1 blocks of act inside the CTA's range
-//       are quantised locally; a block shared with a neighbour CTA goes through global scratch
-//       and is quantised by whichever CTA completes it.
-//   P3  grid barrier #2, one bulk copy of the quantised activation per CTA; down: each CTA owns a
-//       contiguous range of output rows, units of rows x 8 routed experts (the producer streams
-//       them during P2 already); the 8 expert values of a row are summed with the reference's
-//       tree ((v0+v4)+(v2+v6))+((v1+v5)+(v3+v7)) and the residual is added.
+//       (expert, slice) pairs over the 13 warps: 32 lane partials, butterfly, fixed slice tree).
+//       The router rows are requested before anything else.  Grid barrier #1: one
+//       fire-and-forget arrival per CTA.
+//   P1  the producer warp waits for barrier #1, selects the top-8 (one warp: 8 keys a lane,
+//       rounds of redux max / min on order-preserving keys) and builds the copy table with its
+//       32 lanes; meanwhile the consumer warps quantise x to Q8_1 and prefetch the residual.
+//   P2  gate/up: the CTA owns a contiguous range of (slot, row) pairs; copy units of up to four
+//       warp shares of rows of the gate or the up matrix (one bulk copy each) stream through a
+//       ring of shared-memory stages.  Consumer warps claim sub-units (one warp's rows) in unit
+//       order from a CTA counter, so a free warp always takes the oldest unclaimed rows; the last
+//       finisher of a unit frees its stage.  The producer issues every unit as soon as its stage
+//       is free, so the down units (this CTA's output rows of one expert: one contiguous copy
+//       each) land in the ring while gate/up is still being computed.
+//   P3  act = up * silu(gate) of the CTA's range goes to global memory as f32; grid barrier #2;
+//       every CTA reads the whole act vector back (one 16-byte load per lane and 128 values, all
+//       of a warp's loads in flight together) and quantises it to Q8_1 itself
+//       (quantize_silu_mul_q8_1 arithmetic, no cross-CTA hand-off); then the down sub-units,
+//       weighted by the route weight, the reference's fixed 8-way tree
+//       ((v0+v4)+(v2+v6))+((v1+v5)+(v3+v7)) per output row, + residual.
 // Lane work unit ("task"): one 64-weight sub-block pair (super-block sb, pair j) of a row: 32 B of
 // quants, dp4a against the Q8_1 activation, MMVQ combine of vec_dot_q4_K_q8_1 / _q5_K_
 // (gguf.cuh:727-750, 783-813): dall * sum d8*(dot*sc) - dmin * sum d8*sum(q8)*m.
@@ -36,18 +39,22 @@
 
 namespace mmrs {
 
-constexpr int kGroupWarps = 4;
-// 3 groups of 4 consumer warps + the producer = 13 warps (at most 4 on a scheduler): 128 registers
-// a thread; 4 groups (17 warps, 5 on one scheduler) capped the kernel at 96 with spills.
-constexpr int kGroups = 3;
-constexpr int kRowsPerLane = 2;   // rows a lane group computes per unit (same activation registers)
-constexpr int kMaxUnits = 96;
-constexpr int kConsumerWarps = kGroupWarps * kGroups;
+constexpr int kConsumerWarps = 12;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kRouterRounds = (16 + kConsumerWarps - 1) / kConsumerWarps;  // 2 experts x 8 K-slices per CTA
-constexpr int kThreads = kConsumerThreads + 32;
+constexpr int kWarps = kConsumerWarps + 1;  // + producer
+constexpr int kThreads = kWarps * 32;
+constexpr int kProducerWarp = kConsumerWarps;
+constexpr int kRowsPerLane = 2;  // rows a lane group computes per sub-unit (same activation registers)
+constexpr int kSubsPerGuUnit = 4;
+constexpr int kMaxUnits = 80;
+constexpr int kMaxSubs = 256;
 constexpr int kTopK = 8;
 constexpr int kTPL = 3;  // tasks (64-weight sub-block pairs) per lane
+constexpr int kRouterRounds = (16 + kWarps - 1) / kWarps;
+// named barriers: consumers, table ready (all threads), router partials (all threads)
+constexpr int kBarConsumers = 1, kBarTable = 3, kBarRouter = 4;
+// control words in shared memory
+enum { kCtlUnits, kCtlGuUnits, kCtlSubGu, kCtlSubs, kCtlNext, kCtlPositions, kCtlOk, kCtlFail, kCtlWords };
 
 // Q8_1 activation in shared memory: q int8 [K] and, per 64-element pair (task), the float4
 // {d8 lo block, d8 hi block, d8*sum(q) lo, d8*sum(q) hi}.
@@ -163,8 +170,8 @@ __device__ __forceinline__ float row_dot(const uint8_t *row, int lig, int L, int
 }
 
 // 128 consecutive values, lane l holding values 4l..4l+3 (Q8_1 blocks of 32 over 8 lanes):
-// d = amax/127, q = roundf(v/d) (quantize_q8_1, gguf.cuh:1234-1261).  Writes q, and per block the
-// fp16-rounded scale d and the sum of quants S.
+// d = amax/127, q = roundf(v/d) (quantize_q8_1, gguf.cuh:1234-1261, and quantize_silu_mul_q8_1,
+// moe_gguf.cu:255-284).  Writes q, and per block the fp16-rounded scale d and the sum of quants S.
 __device__ __forceinline__ void quant128(float4 v, int8_t *q, float *d, int *S, int lane) {
     float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
@@ -195,59 +202,67 @@ __device__ __forceinline__ void build_task_scales(float4 *ts, const float *d, co
     }
 }
 
-// Consumer wait for unit k in stage st: first the stage's ticket (the producer has issued unit k
-// there), then the phase of the full barrier.  Bounded by the deadline.
+// Bounded wait until unit k has landed in stage st: first the stage's ticket (the producer has
+// issued unit k there; a warp may claim unit k before unit k - stages has been issued), then the
+// phase of the stage's full barrier.
 __device__ __forceinline__ bool wait_unit(uint64_t *full, const int *ticket, int k, int st, int stages,
                                           uint64_t deadline) {
     uint32_t spins = 0;
     while (*reinterpret_cast<const volatile int *>(&ticket[st]) != k) {
-        __nanosleep(64);
+        __nanosleep(32);
         if ((++spins & 255u) == 0 && globaltimer_ns() > deadline) return false;
     }
-    // sleeping wait: a group waiting for its data leaves the issue slots to the groups computing
     return mbar_wait_sleep(&full[st], (uint32_t)(k / stages) & 1u, deadline);
 }
 
-// Unit enumeration shared by producer and consumers (identical sequences).
-struct GuUnit {
-    int slot, row0, n;
-};
-__device__ __forceinline__ GuUnit gu_unit_at(int p, int pend, int I, int U) {
-    GuUnit u;
-    u.slot = p / I;
-    u.row0 = p - u.slot * I;
-    const int a = pend - p, b = I - u.row0;
-    u.n = min(U, min(a, b));
-    return u;
+// arrive.expect_tx whose arrival state is not returned (the issuing thread does not wait for it)
+__device__ __forceinline__ void mbar_arrive_expect_tx_sink(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
+// Shared-memory add with acquire-release semantics at CTA scope (returns the old value): the
+// warps that finished a copy unit before release their reads of its stage to the last finisher.
+__device__ __forceinline__ int atom_add_acq_rel_cta(int *p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(smem_u32(p)), "r"(v) : "memory");
+    return old;
+}
+
+// Order-preserving selection key of sigmoid(l) + bias (-0 ranks as +0).
+__device__ __forceinline__ uint32_t sel_key(float sg, float b) {
+    float sv = sg + b;
+    if (sv == 0.0f) sv = 0.0f;
+    const uint32_t u = __float_as_uint(sv);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Copy unit: .x kind (0 gate, 1 up, 2 down), .y slot position, .z first row, .w rows.
+// Sub-unit: .x unit, .y first row within the unit | rows << 16.
 struct DecodeSmem {
     uint8_t *stages;
-    uint64_t *full, *empty, *abar;
+    uint64_t *full, *empty;
     int8_t *xq;                // [H]
     float *xd;                 // [H/32]
     int *xS;                   // [H/32]
     float4 *xts;               // [H/64]
-    int8_t *aq_s;              // [8][I]
+    int8_t *aq_s;              // [8][I] (positions)
     float *ad_s;               // [8][I/32]
     int *aS_s;                 // [8][I/32]
     float4 *ats;               // [8][I/64]
-    float *part;               // router slice sums [2][8] in P0, selection scores [E] in P1
-    float *sig;                // [E]
-    int *ids;                  // [8]
-    int *vslot;                // [8] slots in gate/up position order (valid first under EP)
-    int *vpos;                 // [8] position block of each slot in act / aq
+    float *part;               // router slice sums [2][8]
+    int *ids;                  // [8] expert of each slot (-1: none, or another rank's)
+    int *vslot;                // [8] slot of each position (the computed slots in order)
     float *w;                  // [8]
-    float *dn_acc;             // [res_slots][8]
-    float *act_s;              // [act_slots]
-    float *gval, *uval;        // [act_slots] gate / up row values of this CTA's range
-    int4 *units;               // [kMaxUnits] (kind, slot, first row, rows)
-    int *unit_off;             // [kMaxUnits] offset of the first row in the CTA's range
-    int *ticket;               // [stages] index of the unit last issued into each stage
-    int *n_gu;
+    float *dn_acc;             // [res_slots][8] weighted expert rows of this CTA's output range
+    float *gval, *uval;        // [act_slots] gate / up row values of this CTA's (position, row) range
     float *res_s;              // [res_slots]
-    uint32_t *base;
-    int *flag;
+    int4 *units;               // [kMaxUnits]
+    int *unit_off;             // [kMaxUnits] first row of a gate/up unit in the CTA's range
+    int *unit_nsub;            // [kMaxUnits] sub-units of the unit
+    int2 *subs;                // [kMaxSubs]
+    int *ticket;               // [stages] unit last issued into each stage
+    int *done;                 // [stages] sub-units of the stage's unit finished
+    int *ctl;                  // [kCtlWords]
 };
 
 __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __grid_constant__ DecodeParams p) {
@@ -257,6 +272,32 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     const int H = p.H, I = p.I, E = p.E;
     const uint64_t t_start = globaltimer_ns();
     const uint64_t deadline = t_start + p.timeout_ns;
+    const int dn_r0 = (int)((int64_t)cta * H / G), dn_r1 = (int)((int64_t)(cta + 1) * H / G);
+    const int nres = dn_r1 - dn_r0;
+
+    // ---- P0 loads first: the CTA's router rows and the matching x slices ---------------------
+    const int slice = H / 8, groups = slice / 4;
+    float4 xx[kRouterRounds][4], wv[kRouterRounds][4];
+#pragma unroll
+    for (int r = 0; r < kRouterRounds; ++r) {
+        const int pi = warp + kWarps * r, sl = pi & 7, le = pi >> 3;
+        const int e = cta + G * le;
+        if (pi < 16 && p.internal_routing && e < E) {
+            const float4 *xs = reinterpret_cast<const float4 *>(p.x + sl * slice);
+            const float4 *wr = reinterpret_cast<const float4 *>(p.router + (size_t)e * H + sl * slice);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int g = lane + 32 * i;
+                if (g < groups) {
+                    wv[r][i] = __ldg(wr + g);
+                    xx[r][i] = __ldg(xs + g);
+                }
+            }
+        }
+    }
+    // this CTA's launch count (2 per completed launch: the grid barriers' targets)
+    uint32_t epoch = 0;
+    if (lane == 0 && (warp == 0 || warp == kProducerWarp)) epoch = __ldcg(&p.ctl->epoch[cta]);
     if (tid == 0 && p.trace) p.trace[cta * 16 + 0] = t_start;
 
     DecodeSmem s;
@@ -270,7 +311,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         s.stages = take((size_t)p.stages * p.stage_bytes);
         s.full = reinterpret_cast<uint64_t *>(take(sizeof(uint64_t) * p.stages));
         s.empty = reinterpret_cast<uint64_t *>(take(sizeof(uint64_t) * p.stages));
-        s.abar = reinterpret_cast<uint64_t *>(take(sizeof(uint64_t)));
         s.xq = reinterpret_cast<int8_t *>(take(H));
         s.xd = reinterpret_cast<float *>(take(sizeof(float) * (H / 32)));
         s.xS = reinterpret_cast<int *>(take(sizeof(int) * (H / 32)));
@@ -279,23 +319,21 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         s.ad_s = reinterpret_cast<float *>(take(sizeof(float) * kTopK * (I / 32)));
         s.aS_s = reinterpret_cast<int *>(take(sizeof(int) * kTopK * (I / 32)));
         s.ats = reinterpret_cast<float4 *>(take(sizeof(float4) * kTopK * (I / 64)));
-        s.part = reinterpret_cast<float *>(take(sizeof(float) * (E > 16 ? E : 16)));
-        s.sig = reinterpret_cast<float *>(take(sizeof(float) * E));
+        s.part = reinterpret_cast<float *>(take(sizeof(float) * 16));
         s.ids = reinterpret_cast<int *>(take(sizeof(int) * kTopK));
         s.vslot = reinterpret_cast<int *>(take(sizeof(int) * kTopK));
-        s.vpos = reinterpret_cast<int *>(take(sizeof(int) * kTopK));
         s.w = reinterpret_cast<float *>(take(sizeof(float) * kTopK));
         s.dn_acc = reinterpret_cast<float *>(take(sizeof(float) * p.res_slots * kTopK));
-        s.act_s = reinterpret_cast<float *>(take(sizeof(float) * p.act_slots));
         s.gval = reinterpret_cast<float *>(take(sizeof(float) * p.act_slots));
         s.uval = reinterpret_cast<float *>(take(sizeof(float) * p.act_slots));
+        s.res_s = reinterpret_cast<float *>(take(sizeof(float) * p.res_slots));
         s.units = reinterpret_cast<int4 *>(take(sizeof(int4) * kMaxUnits));
         s.unit_off = reinterpret_cast<int *>(take(sizeof(int) * kMaxUnits));
+        s.unit_nsub = reinterpret_cast<int *>(take(sizeof(int) * kMaxUnits));
+        s.subs = reinterpret_cast<int2 *>(take(sizeof(int2) * kMaxSubs));
         s.ticket = reinterpret_cast<int *>(take(sizeof(int) * p.stages));
-        s.n_gu = reinterpret_cast<int *>(take(16));
-        s.res_s = reinterpret_cast<float *>(take(sizeof(float) * p.res_slots));
-        s.base = reinterpret_cast<uint32_t *>(take(16));
-        s.flag = reinterpret_cast<int *>(take(16));
+        s.done = reinterpret_cast<int *>(take(sizeof(int) * p.stages));
+        s.ctl = reinterpret_cast<int *>(take(sizeof(int) * kCtlWords));
         // the carve-up must fit the dynamic allocation computed by decode_smem_bytes()
         uint32_t dyn = 0;
         asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
@@ -307,301 +345,253 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     if (tid == 0) {
         for (int i = 0; i < p.stages; ++i) {
             mbar_init(&s.full[i], 1);
-            mbar_init(&s.empty[i], kGroupWarps);
+            mbar_init(&s.empty[i], 1);
             s.ticket[i] = -1;
+            s.done[i] = 0;
         }
-        mbar_init(s.abar, 1);
         fence_mbar_init();
-        s.flag[0] = 1;
-        s.flag[1] = 0;
+        for (int i = 0; i < kCtlWords; ++i) s.ctl[i] = 0;
     }
-    __syncthreads();
 
-    const int dn_r0 = (int)((int64_t)cta * H / G), dn_r1 = (int)((int64_t)(cta + 1) * H / G);
+    // ---- P0: router slices -------------------------------------------------------------------
+#pragma unroll
+    for (int r = 0; r < kRouterRounds; ++r) {
+        const int pi = warp + kWarps * r, sl = pi & 7, le = pi >> 3;
+        if (!(pi < 16 && p.internal_routing && cta + G * le < E)) continue;
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int g = lane + 32 * i;
+            if (g < groups) {
+                acc = fmaf(wv[r][i].x, xx[r][i].x, acc);
+                acc = fmaf(wv[r][i].y, xx[r][i].y, acc);
+                acc = fmaf(wv[r][i].z, xx[r][i].z, acc);
+                acc = fmaf(wv[r][i].w, xx[r][i].w, acc);
+            }
+        }
+        acc = warp_sum_butterfly(acc);
+        if (lane == 0) s.part[le * 8 + sl] = acc;
+    }
+    named_sync(kBarRouter, kThreads);
+    if (p.internal_routing && tid < 2) {
+        const int ee = cta + G * tid;
+        if (ee < E) {
+            const float *q = s.part + tid * 8;
+            p.logits[ee] = ((q[0] + q[1]) + (q[2] + q[3])) + ((q[4] + q[5]) + (q[6] + q[7]));
+        }
+    }
+    named_sync(kBarRouter, kThreads);  // both logits written before the release below
+    if (tid == 0) {
+        if (p.trace) p.trace[cta * 16 + 1] = globaltimer_ns();
+        // grid barrier #1 arrival (fire and forget); the producer warp waits for the count
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&p.ctl->count) : "memory");
+    }
+
     const size_t gu_row_bytes = kq_row_bytes(p.gu_type, H);
     const size_t dn_row_bytes = kq_row_bytes(p.dn_type, I);
     const size_t gu_expert_bytes = gu_row_bytes * I;
     const size_t dn_expert_bytes = dn_row_bytes * H;
+    const int Lg = p.gu_lanes, Ld = p.dn_lanes;
+    const int gu_sub = p.gu_sub_rows, dn_sub = p.dn_sub_rows, U_gu = p.gu_unit_rows;
 
-    // ---- P0: router slices, Q8_1 of x, residual prefetch (all loads issued before use) ----
-    if (warp < kConsumerWarps) {
-        const int nxc = H / 128;  // chunks of 128 values
-        float4 xv[2];
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int c = warp + kConsumerWarps * i;
-            if (c < nxc) xv[i] = __ldg(reinterpret_cast<const float4 *>(p.x) + c * 32 + lane);
+    if (warp == kProducerWarp) {
+        // ================================ producer warp ===================================
+        bool ok = true;
+        if (lane == 0) {
+            const uint32_t target = (uint32_t)G * (epoch + 1u);
+            uint32_t spins = 0;
+            while ((int)(ld_acquire_gpu(&p.ctl->count) - target) < 0) {
+                __nanosleep(16);
+                if ((++spins & 255u) == 0 && globaltimer_ns() > deadline) {
+                    atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
+                    ok = false;
+                    break;
+                }
+            }
+            if (p.trace) p.trace[cta * 16 + 2] = globaltimer_ns();
         }
-        float rv = 0.f;
-        const int rrow = dn_r0 + tid;
-        if (p.residual && rrow < dn_r1) rv = __ldg(p.residual + rrow);
-        // router pairs (expert le of this CTA's two, K-slice sl): pair pi = warp + kConsumerWarps * r
-        const int slice = H / 8, groups = slice / 4;
-        float4 xx[kRouterRounds][4], wv[kRouterRounds][4];
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        // ---- routing: lane l holds experts l + 32 i ------------------------------------------
+        int slot_id = -1;  // lane k < 8: expert of slot k
+        float slot_w = 0.f;
+        if (p.internal_routing) {
+            if (ok) {
+                uint32_t key[8];
+                float sg[8];
 #pragma unroll
-        for (int r = 0; r < kRouterRounds; ++r) {
-            const int pi = warp + kConsumerWarps * r, sl = pi & 7, le = pi >> 3;
-            const int e = cta + G * le;
-            if (pi < 16 && p.internal_routing && e < E) {
-                const float4 *xs = reinterpret_cast<const float4 *>(p.x + sl * slice);
-                const float4 *wr = reinterpret_cast<const float4 *>(p.router + (size_t)e * H + sl * slice);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int g = lane + 32 * i;
-                    if (g < groups) {
-                        xx[r][i] = __ldg(xs + g);
-                        wv[r][i] = __ldg(wr + g);
+                for (int i = 0; i < 8; ++i) {
+                    const int e = lane + 32 * i;
+                    key[i] = 0u;  // experts >= E are never selected (E >= 8 real keys are > 0)
+                    sg[i] = 0.f;
+                    if (e < E) {
+                        const float l = __ldcg(p.logits + e);
+                        sg[i] = __fdiv_rn(1.0f, 1.0f + expf(-l));
+                        key[i] = sel_key(sg[i], __ldg(p.bias + e));
                     }
                 }
-            }
-        }
-        // Per-block arrival counters are zeroed here: nothing increments them before barrier #1.
-        for (int b = cta * kConsumerThreads + tid; b < kTopK * (I / 32); b += G * kConsumerThreads)
-            p.blk_count[b] = 0u;
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int c = warp + kConsumerWarps * i;
-            if (c < nxc) quant128(xv[i], s.xq + c * 128, s.xd + c * 4, s.xS + c * 4, lane);
-        }
-        if (p.residual && rrow < dn_r1) s.res_s[tid] = rv;
-#pragma unroll
-        for (int r = 0; r < kRouterRounds; ++r) {
-            const int pi = warp + kConsumerWarps * r, sl = pi & 7, le = pi >> 3;
-            if (!(pi < 16 && p.internal_routing && cta + G * le < E)) continue;
-            float acc = 0.f;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int g = lane + 32 * i;
-                if (g < groups) {
-                    acc = fmaf(wv[r][i].x, xx[r][i].x, acc);
-                    acc = fmaf(wv[r][i].y, xx[r][i].y, acc);
-                    acc = fmaf(wv[r][i].z, xx[r][i].z, acc);
-                    acc = fmaf(wv[r][i].w, xx[r][i].w, acc);
-                }
-            }
-            acc = warp_sum_butterfly(acc);
-            if (lane == 0) s.part[le * 8 + sl] = acc;
-        }
-        if (tid == 0) s.base[0] = __ldcg(&p.ctl->epoch[cta]);
-        named_sync(1, kConsumerThreads);
-        build_task_scales(s.xts, s.xd, s.xS, H / 64, tid, kConsumerThreads);
-        if (p.internal_routing && tid < 2) {
-            const int ee = cta + G * tid;
-            if (ee < E) {
-                const float *q = s.part + tid * 8;
-                p.logits[ee] = ((q[0] + q[1]) + (q[2] + q[3])) + ((q[4] + q[5]) + (q[6] + q[7]));
-            }
-        }
-    }
-    if (tid == 0 && p.trace) p.trace[cta * 16 + 1] = globaltimer_ns();
-
-    // ---- P1: routing ----------------------------------------------------------------------
-    __syncthreads();
-    const uint32_t epoch = s.base[0];
-    bool ok = grid_sync(p.ctl, (uint32_t)G * (epoch + 1u), deadline, s.flag, 2, kThreads);
-    if (tid == 0 && p.trace) p.trace[cta * 16 + 2] = globaltimer_ns();
-    if (p.internal_routing) {
-        if (ok) {
-            // Selection score sigmoid(l) + bias as an order-preserving 32-bit key (-0 as +0); the
-            // stable descending order is "larger key first, lower expert id on equal keys".
-            // Warp w holds experts [32 w, 32 w + 32) and extracts its top 8 by rounds of redux max
-            // (key) and redux min (id among the lanes holding that key); warp 0 merges the
-            // candidates the same way.  Candidates (key, id) reuse the score array.
-            const int nw = (E + 31) / 32;
-            uint32_t *cand = reinterpret_cast<uint32_t *>(s.part);  // [2][8 nw] <= max(E, 16) words
-            if (warp < nw) {
-                const int e = tid;
-                uint32_t key = 0u;  // experts >= E: never selected (E >= 8 real keys are > 0)
-                if (e < E) {
-                    const float l = __ldcg(p.logits + e);
-                    const float sg = __fdiv_rn(1.0f, 1.0f + expf(-l));
-                    s.sig[e] = sg;
-                    float sv = sg + p.bias[e];
-                    if (sv == 0.0f) sv = 0.0f;
-                    const uint32_t u = __float_as_uint(sv);
-                    key = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-                }
-                bool taken = false;
+                // stable descending order of the score: larger key first, lower expert id on ties
+                uint32_t taken = 0u;
+                float my_sig = 0.f;
 #pragma unroll
                 for (int k = 0; k < kTopK; ++k) {
-                    const uint32_t mk = __reduce_max_sync(0xffffffffu, taken ? 0u : key);
-                    const uint32_t me =
-                        __reduce_min_sync(0xffffffffu, (!taken && key == mk) ? (uint32_t)e : 0xffffffffu);
-                    taken |= (uint32_t)e == me;
-                    if (lane == 0) {
-                        cand[warp * kTopK + k] = mk;
-                        cand[8 * nw + warp * kTopK + k] = me;
+                    uint32_t bk = 0u;
+                    int bi = 0;
+                    float bs = 0.f;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        if (!(taken & (1u << i)) && key[i] > bk) {
+                            bk = key[i];
+                            bi = i;
+                            bs = sg[i];
+                        }
+                    const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
+                    const uint32_t mine = (uint32_t)(lane + 32 * bi);
+                    const uint32_t me = __reduce_min_sync(0xffffffffu, bk == mk ? mine : 0xffffffffu);
+                    if (mine == me) taken |= 1u << bi;
+                    const float sme = __shfl_sync(0xffffffffu, bs, (int)(me & 31u));
+                    if (lane == k) {
+                        slot_id = (int)me;
+                        my_sig = sme;
                     }
                 }
-            }
-            __syncthreads();
-            if (warp == 0) {
-                const int nc = 8 * nw;
-                const uint32_t ka = lane < nc ? cand[lane] : 0u, ia = lane < nc ? cand[nc + lane] : 0xffffffffu;
-                const uint32_t kb = lane + 32 < nc ? cand[lane + 32] : 0u;
-                const uint32_t ib = lane + 32 < nc ? cand[nc + lane + 32] : 0xffffffffu;
-                bool ta = false, tb = false;
-                int myid = 0;
-#pragma unroll
-                for (int k = 0; k < kTopK; ++k) {
-                    const uint32_t mk = __reduce_max_sync(0xffffffffu, max(ta ? 0u : ka, tb ? 0u : kb));
-                    const uint32_t ca = (!ta && ka == mk) ? ia : 0xffffffffu;
-                    const uint32_t cb = (!tb && kb == mk) ? ib : 0xffffffffu;
-                    const uint32_t me = __reduce_min_sync(0xffffffffu, min(ca, cb));
-                    if (ca == me) ta = true;
-                    else if (cb == me) tb = true;
-                    if (lane == k) myid = (int)me;
-                }
-                // weights: sig / ((v0+v4)+(v2+v6))+((v1+v5)+(v3+v7)) on every lane, lane k keeps w_k
-                const float vk = lane < kTopK ? s.sig[myid] : 0.0f;
+                // weights: sig / ((v0+v4)+(v2+v6))+((v1+v5)+(v3+v7)), lane k keeps w_k
                 float v[kTopK];
 #pragma unroll
-                for (int k = 0; k < kTopK; ++k) v[k] = __shfl_sync(0xffffffffu, vk, k);
+                for (int k = 0; k < kTopK; ++k) v[k] = __shfl_sync(0xffffffffu, my_sig, k);
                 const float denom = ((v[0] + v[4]) + (v[2] + v[6])) + ((v[1] + v[5]) + (v[3] + v[7]));
                 if (lane < kTopK) {
-                    const float wk = __fdiv_rn(vk, denom);
-                    s.ids[lane] = myid;
-                    s.w[lane] = wk;
+                    slot_w = __fdiv_rn(my_sig, denom);
                     if (cta == 0) {
-                        if (p.topk_ids_out) p.topk_ids_out[lane] = (uint32_t)myid;
-                        if (p.topk_w_out) p.topk_w_out[lane] = wk;
+                        if (p.topk_ids_out) p.topk_ids_out[lane] = (uint32_t)slot_id;
+                        if (p.topk_w_out) p.topk_w_out[lane] = slot_w;
                     }
                 }
             }
-        }
-    } else {
-        if (tid < kTopK) {
-            s.ids[tid] = -1;
-            s.w[tid] = 0.f;
-        }
-        __syncthreads();
-        if (tid < kTopK) {
-            // (route, expert) pairs in expert order; routes outside [0, 8) and invalid experts
-            // contribute nothing, as in moe_down_decode_kernel (moe_gguf.cu:311)
-            const int slot = p.ext_route[tid];
-            const int e = p.ext_expert[tid];
-            if (slot >= 0 && slot < kTopK) {
-                s.ids[slot] = (e >= 0 && e < E) ? e : -1;
-                s.w[slot] = p.ext_w[slot];
+        } else {
+            // caller-supplied (route, expert) pairs in expert order, weights by route; routes
+            // outside [0, 8) and invalid experts contribute nothing (moe_gguf.cu:311)
+            if (lane < kTopK) {
+                s.ids[lane] = -1;
+                s.w[lane] = 0.f;
             }
-        }
-    }
-    // Gate/up position space: the (slot, row) pairs of the computed experts, partitioned evenly
-    // over the CTAs.  Single GPU and TP: all 8 slots in order.  Expert parallel: experts owned by
-    // other ranks contribute nothing here and their slots are left out, so this rank's CTAs share
-    // only its own experts' rows.  Warp 0 (whose lanes 0..7 wrote ids in both routing paths).
-    const bool compact = p.world > 1 && p.ep;
-    if (warp == 0) {
-        __syncwarp();
-        int id = lane < kTopK ? s.ids[lane] : -1;
-        if (compact && id >= 0 && id % p.world != p.rank) id = -1;
-        const bool keep = lane < kTopK && (!compact || id >= 0);
-        const uint32_t kept = __ballot_sync(0xffffffffu, keep);
-        const int nv = __popc(kept);
-        if (lane < kTopK) {
-            const uint32_t below = (1u << lane) - 1u;
-            const int pos = keep ? __popc(kept & below) : nv + __popc(~kept & 0xFFu & below);
-            s.ids[lane] = id;
-            s.vslot[pos] = lane;
-            s.vpos[lane] = pos;
-        }
-        if (lane == 0) s.n_gu[2] = nv;
-    }
-    __syncthreads();
-    const int nvs = s.n_gu[2];
-    const int gu_p0 = (int)((int64_t)cta * nvs * I / G), gu_p1 = (int)((int64_t)(cta + 1) * nvs * I / G);
-    if (!ok) return;  // nothing issued yet
-    if (tid == 0 && p.trace) p.trace[cta * 16 + 3] = globaltimer_ns();
-
-    // Unit table.  Every unit is ONE contiguous bulk copy (few, large TMA operations keep the
-    // per-SM copy engine at HBM rate): a chunk of up to U_gu rows of the gate or of the up matrix
-    // of one routed expert (gate chunk, then the matching up chunk), then one down unit per routed
-    // expert covering this CTA's output rows (split every U_dn rows).  Unit k goes to ring stage
-    // k % stages and to consumer group k % kGroups.  Entry: (kind 0 gate / 1 up / 2 down, slot,
-    // first row, rows); for gate/up the offset of the first row in the CTA's (slot,row) range is
-    // row-offset field .w >> 8 ... stored separately in gu_off.
-    const int U_gu = p.gu_unit_rows, U_dn = p.dn_unit_rows;
-    if (warp == kConsumerWarps) {
-        // ---------------------------- producer --------------------------------------------
-        // Lane 0 builds the unit table and releases the consumers (named barrier 3) before it
-        // issues the first copy: an issue can block on the copy engine, the consumers must not.
-        int n = 0, k = 0;
-        bool live = true;
-        int n_gu = 0x7fffffff;  // no "first down unit" stamp while the table grows
-        auto unit_src = [&](int k, uint32_t &bytes) -> const uint8_t * {
-            const int4 u = s.units[k];
-            const int e = s.ids[u.y];
-            if (e < 0) return nullptr;
-            if (u.x < 2) {
-                bytes = (uint32_t)(gu_row_bytes * u.w);
-                return (u.x == 0 ? p.gate : p.up) + (size_t)e * gu_expert_bytes + (size_t)u.z * gu_row_bytes;
-            }
-            bytes = (uint32_t)(dn_row_bytes * u.w);
-            return p.down + (size_t)e * dn_expert_bytes + (size_t)u.z * dn_row_bytes;
-        };
-        // issue unit k into ring stage k % stages; false when the stage wait expired
-        auto issue = [&](int k) -> bool {
-            const int st = k % p.stages;
-            if (!mbar_wait_sleep(&s.empty[st], ((uint32_t)(k / p.stages) & 1u) ^ 1u, deadline)) {
-                atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
-                return false;
-            }
-            if (k == 0 && p.trace) p.trace[cta * 16 + 8] = globaltimer_ns();
-            if (k == n_gu && p.trace) p.trace[cta * 16 + 10] = globaltimer_ns();
-            // Publish which unit this stage now holds.  Consumer groups take interleaved units,
-            // so a group can reach unit k before unit k - stages (another group's) has landed;
-            // waiting for the ticket first keeps the parity wait from aliasing onto that phase.
-            *reinterpret_cast<volatile int *>(&s.ticket[st]) = k;
-            const int4 u = s.units[k];
-            uint8_t *dst = s.stages + (size_t)st * p.stage_bytes;
-            if (u.x == 2) {
-                // rows [u.z, u.z + u.w) of all routed experts, expert q at dst + q * U_dn rows
-                const uint32_t bytes = (uint32_t)(dn_row_bytes * u.w);
-                uint32_t tx = 0;
-                for (int q = 0; q < kTopK; ++q) tx += s.ids[q] >= 0 ? bytes : 0;
-                mbar_arrive_expect_tx(&s.full[st], tx);
-                for (int q = 0; q < kTopK; ++q) {
-                    const int e = s.ids[q];
-                    if (e < 0) continue;
-                    bulk_g2s(dst + (size_t)q * dn_row_bytes * U_dn,
-                             p.down + (size_t)e * dn_expert_bytes + (size_t)u.z * dn_row_bytes, bytes, &s.full[st]);
+            __syncwarp();
+            if (ok && lane < kTopK) {
+                const int route = p.ext_route[lane];
+                const int e = p.ext_expert[lane];
+                if (route >= 0 && route < kTopK) {
+                    s.ids[route] = (e >= 0 && e < E) ? e : -1;
+                    s.w[route] = p.ext_w[route];
                 }
-                return true;
             }
-            uint32_t bytes = 0;
-            const uint8_t *src = unit_src(k, bytes);
-            if (!src) {
-                mbar_arrive(&s.full[st]);
-                return true;
+            __syncwarp();
+            if (lane < kTopK) {
+                slot_id = s.ids[lane];
+                slot_w = s.w[lane];
             }
-            mbar_arrive_expect_tx(&s.full[st], bytes);
-            bulk_g2s(dst, src, bytes, &s.full[st]);
-            return true;
-        };
-        if (lane == 0) {
-            // the table (each entry is written before its unit is issued)
-            for (int q = gu_p0; q < gu_p1 && n + 2 <= kMaxUnits;) {
-                const GuUnit u = gu_unit_at(q, gu_p1, I, U_gu);
-                const int slot = s.vslot[u.slot];
-                s.units[n] = make_int4(0, slot, u.row0, u.n);
-                s.unit_off[n++] = q - gu_p0;
-                s.units[n] = make_int4(1, slot, u.row0, u.n);
-                s.unit_off[n++] = q - gu_p0;
-                q += u.n;
-            }
-            s.n_gu[0] = n;
-            for (int r = dn_r0; r < dn_r1 && n < kMaxUnits; r += U_dn) {
-                s.units[n] = make_int4(2, 0, r, min(U_dn, dn_r1 - r));
-                s.unit_off[n++] = r - dn_r0;
-            }
-            s.n_gu[1] = n;
+            __syncwarp();
         }
-        __threadfence_block();
-        __syncwarp();
-        named_arrive(3, kThreads);  // the table is complete
+        // ---- positions: the computed slots in order (expert parallel: this rank's only) ------
+        const bool compact = p.world > 1 && p.ep;
+        int id = (ok && lane < kTopK) ? slot_id : -1;
+        if (compact && id >= 0 && id % p.world != p.rank) id = -1;
+        const bool keep = lane < kTopK && id >= 0;
+        const uint32_t kept = __ballot_sync(0xffffffffu, keep);
+        const int nvs = __popc(kept);
+        if (lane < kTopK) {
+            s.ids[lane] = id;
+            s.w[lane] = slot_w;
+            if (keep) s.vslot[__popc(kept & ((1u << lane) - 1u))] = lane;
+        }
+        // ---- copy table: lane c computes gate/up chunk c of the CTA's (position, row) range --
+        const int gu_p0 = (int)((int64_t)cta * nvs * I / G), gu_p1 = (int)((int64_t)(cta + 1) * nvs * I / G);
+        int n_chunks = 0, c_left = lane, my_pos = -1, my_row0 = 0, my_n = 0, my_off = 0;
+        for (int pos = gu_p0 / I, q = gu_p0; q < gu_p1; ++pos) {
+            const int seg_end = min(gu_p1, (pos + 1) * I);
+            const int nc = (seg_end - q + U_gu - 1) / U_gu;
+            if (c_left >= 0 && c_left < nc) {
+                const int r = q + c_left * U_gu;
+                my_pos = pos;
+                my_row0 = r - pos * I;
+                my_n = min(U_gu, seg_end - r);
+                my_off = r - gu_p0;
+            }
+            c_left -= nc;
+            n_chunks += nc;
+            q = seg_end;
+        }
+        const int n_gu_units = 2 * n_chunks;
+        const int ns = my_pos >= 0 ? (my_n + gu_sub - 1) / gu_sub : 0;
+        int incl = ns;  // inclusive prefix of sub-units over chunks
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
+        }
+        const int base = 2 * (incl - ns);  // gate and up sub-units of the earlier chunks
+        const int n_sub_gu = 2 * __shfl_sync(0xffffffffu, incl, 31);
+        if (my_pos >= 0) {
+            for (int h = 0; h < 2; ++h) {
+                const int k = 2 * lane + h;
+                s.units[k] = make_int4(h, my_pos, my_row0, my_n);
+                s.unit_off[k] = my_off;
+                s.unit_nsub[k] = ns;
+                for (int j = 0; j < ns; ++j) {
+                    const int r0 = j * gu_sub;
+                    s.subs[base + h * ns + j] = make_int2(k, r0 | (min(gu_sub, my_n - r0) << 16));
+                }
+            }
+        }
+        // down units: one per position, all of this CTA's output rows
+        const int nsd = nres > 0 ? (nres + dn_sub - 1) / dn_sub : 0;
+        const int n_dn_units = nsd > 0 ? nvs : 0;
+        if (lane < n_dn_units) {
+            const int k = n_gu_units + lane;
+            s.units[k] = make_int4(2, lane, dn_r0, nres);
+            s.unit_off[k] = 0;
+            s.unit_nsub[k] = nsd;
+            for (int j = 0; j < nsd; ++j) {
+                const int r0 = j * dn_sub;
+                s.subs[n_sub_gu + lane * nsd + j] = make_int2(k, r0 | (min(dn_sub, nres - r0) << 16));
+            }
+        }
         if (lane == 0) {
-            n_gu = s.n_gu[0];
-            for (; live && k < n; ++k) live = issue(k);
+            s.ctl[kCtlUnits] = n_gu_units + n_dn_units;
+            s.ctl[kCtlGuUnits] = n_gu_units;
+            s.ctl[kCtlSubGu] = n_sub_gu;
+            s.ctl[kCtlSubs] = n_sub_gu + n_dn_units * nsd;
+            s.ctl[kCtlPositions] = nvs;
+            s.ctl[kCtlOk] = ok ? 1 : 0;
+            if (p.trace) p.trace[cta * 16 + 3] = globaltimer_ns();
+        }
+        __syncwarp();
+        named_arrive(kBarTable, kThreads);  // table complete: the consumers may claim
+        // ---- issue loop (lane 0) ----------------------------------------------------------------
+        if (lane == 0 && ok) {
+            const int n = n_gu_units + n_dn_units;
+            int k = 0;
+            for (; k < n; ++k) {
+                const int st = k % p.stages;
+                if (!mbar_wait_sleep(&s.empty[st], ((uint32_t)(k / p.stages) & 1u) ^ 1u, deadline)) {
+                    atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
+                    break;
+                }
+                *reinterpret_cast<volatile int *>(&s.ticket[st]) = k;
+                const int4 u = s.units[k];
+                const int e = s.ids[s.vslot[u.y]];
+                const uint8_t *src;
+                uint32_t bytes;
+                if (u.x == 2) {
+                    src = p.down + (size_t)e * dn_expert_bytes + (size_t)u.z * dn_row_bytes;
+                    bytes = (uint32_t)(dn_row_bytes * u.w);
+                } else {
+                    src = (u.x == 0 ? p.gate : p.up) + (size_t)e * gu_expert_bytes + (size_t)u.z * gu_row_bytes;
+                    bytes = (uint32_t)(gu_row_bytes * u.w);
+                }
+                if (k == 0 && p.trace) p.trace[cta * 16 + 8] = globaltimer_ns();
+                if (k == n_gu_units && p.trace) p.trace[cta * 16 + 10] = globaltimer_ns();
+                mbar_arrive_expect_tx_sink(&s.full[st], bytes);
+                bulk_g2s(s.stages + (size_t)st * p.stage_bytes, src, bytes, &s.full[st]);
+            }
             if (p.trace) p.trace[cta * 16 + 9] = globaltimer_ns();
             // Drain: no copy may still be landing in shared memory when the CTA retires.
             const int first = k > p.stages ? k - p.stages : 0;
@@ -610,235 +600,245 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         }
         return;
     }
-    named_sync(3, kThreads);
-    const int n_gu = s.n_gu[0];
-    const int n_units = s.n_gu[1];
 
-    // ------------------------------- consumers ----------------------------------------------
-    const int grp = warp / kGroupWarps, gw = warp % kGroupWarps;
-    bool aborted = false;
+    // ================================ consumer warps ======================================
+    // While the producer waits for barrier #1 and routes: Q8_1 of x, residual, zeroed sums.
     {
-        // P2: gate / up chunks.  A lane group of L lanes computes two rows of the chunk against the
-        // register-resident Q8_1 x (6 independent 64-weight task dots per lane).
-        const int L = p.gu_lanes;
-        const int lgi = gw * (32 / L) + lane / L, lig = lane % L;
-        const int rA = lgi * kRowsPerLane, rB = rA + 1;
+        const int nxc = H / 128;
+        for (int c = warp; c < nxc; c += kConsumerWarps) {
+            const float4 xv = __ldg(reinterpret_cast<const float4 *>(p.x) + c * 32 + lane);
+            quant128(xv, s.xq + c * 128, s.xd + c * 4, s.xS + c * 4, lane);
+        }
+        for (int r = tid; r < nres; r += kConsumerThreads) s.res_s[r] = p.residual ? __ldg(p.residual + dn_r0 + r) : 0.f;
+        for (int i = tid; i < nres * kTopK; i += kConsumerThreads) s.dn_acc[i] = 0.f;
+        named_sync(kBarConsumers, kConsumerThreads);
+        build_task_scales(s.xts, s.xd, s.xS, H / 64, tid, kConsumerThreads);
+    }
+    named_sync(kBarTable, kThreads);
+    const bool ok1 = s.ctl[kCtlOk] != 0;
+    const int n_sub_gu = s.ctl[kCtlSubGu], n_sub = s.ctl[kCtlSubs], nvs = s.ctl[kCtlPositions];
+    bool aborted = !ok1;
+    auto claim = [&]() -> int {
+        int v = 0;
+        if (lane == 0) v = atomicAdd(&s.ctl[kCtlNext], 1);
+        return __shfl_sync(0xffffffffu, v, 0);
+    };
+    // A warp that finished a sub-unit of unit k: the last finisher frees the unit's stage.
+    auto finish = [&](int k, int st) {
+        __syncwarp();
+        if (lane == 0) {
+            const int old = atom_add_acq_rel_cta(&s.done[st], 1);
+            if (old + 1 == s.unit_nsub[k]) {
+                s.done[st] = 0;
+                mbar_arrive(&s.empty[st]);
+            }
+        }
+    };
+
+    // ---- P2: gate / up sub-units ----------------------------------------------------------------
+    int g = claim();
+    {
         const int ntasks = (H / QK_K) * 4;
+        const int lgi = lane / Lg, lig = lane % Lg;
         TaskAct ta[kTPL];
-        load_task_acts(ActView{s.xq, s.xts}, lig, L, ntasks, ta);
-        for (int k = grp; k < n_gu; k += kGroups) {
+        load_task_acts(ActView{s.xq, s.xts}, lig, Lg, ntasks, ta);
+        while (g < n_sub_gu) {
+            const int2 su = s.subs[g];
+            const int k = su.x, ro = su.y & 0xffff, nr = su.y >> 16;
             const int4 u = s.units[k];
             const int st = k % p.stages;
             if (!aborted && !wait_unit(s.full, s.ticket, k, st, p.stages, deadline)) {
                 atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
                 aborted = true;
             }
+            const int rA = ro + lgi * kRowsPerLane, rB = rA + 1, rend = ro + nr;
             float vA = 0.f, vB = 0.f;
-            if (!aborted && s.ids[u.y] >= 0 && rA < u.w) {
+            if (!aborted && rA < rend) {
                 const uint8_t *base = s.stages + (size_t)st * p.stage_bytes;
                 const uint8_t *rowA = base + (size_t)rA * gu_row_bytes;
-                const uint8_t *rowB = base + (size_t)min(rB, u.w - 1) * gu_row_bytes;
+                const uint8_t *rowB = base + (size_t)min(rB, rend - 1) * gu_row_bytes;
                 if (p.gu_type == MMRS_Q5K) {
-                    vA = row_dot<MMRS_Q5K>(rowA, lig, L, ntasks, ta);
-                    vB = row_dot<MMRS_Q5K>(rowB, lig, L, ntasks, ta);
+                    vA = row_dot<MMRS_Q5K>(rowA, lig, Lg, ntasks, ta);
+                    vB = row_dot<MMRS_Q5K>(rowB, lig, Lg, ntasks, ta);
                 } else {
-                    vA = row_dot<MMRS_Q4K>(rowA, lig, L, ntasks, ta);
-                    vB = row_dot<MMRS_Q4K>(rowB, lig, L, ntasks, ta);
+                    vA = row_dot<MMRS_Q4K>(rowA, lig, Lg, ntasks, ta);
+                    vB = row_dot<MMRS_Q4K>(rowB, lig, Lg, ntasks, ta);
                 }
             }
 #pragma unroll
             for (int m = 16; m > 0; m >>= 1)
-                if (m < L) {
+                if (m < Lg) {
                     vA += __shfl_xor_sync(0xffffffffu, vA, m);
                     vB += __shfl_xor_sync(0xffffffffu, vB, m);
                 }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s.empty[st]);
             if (lig == 0) {
                 float *gv = (u.x == 0 ? s.gval : s.uval) + s.unit_off[k];
-                if (rA < u.w) gv[rA] = vA;
-                if (rB < u.w) gv[rB] = vB;
+                if (rA < rend) gv[rA] = vA;
+                if (rB < rend) gv[rB] = vB;
             }
-        }
-        named_sync(1, kConsumerThreads);
-        // act = up * silu(gate) (moe_gguf.cu:272-273) for the CTA's whole range
-        for (int i = tid; i < gu_p1 - gu_p0; i += kConsumerThreads) {
-            const float g = s.gval[i];
-            const int slot = s.vslot[(gu_p0 + i) / I];
-            s.act_s[i] = (!aborted && s.ids[slot] >= 0) ? s.uval[i] * __fdiv_rn(g, 1.0f + expf(-g)) : 0.f;
-        }
-        // Q8_1 of act (quantize_silu_mul_q8_1, moe_gguf.cu:255-284) per 32-row block.  Blocks inside
-        // this CTA's range are quantised from shared memory; a block shared with neighbour CTAs is
-        // published through global scratch and quantised by whichever CTA completes it (one
-        // acq_rel arrival per CTA and block).
-        named_sync(1, kConsumerThreads);
-        if (gu_p1 > gu_p0) {
-            const int b_first = gu_p0 >> 5, b_last = (gu_p1 - 1) >> 5;
-            for (int b = b_first + warp; b <= b_last; b += kConsumerWarps) {
-                const int r = b * 32 + lane;
-                const bool inside = r >= gu_p0 && r < gu_p1;
-                const int lo = max(b * 32, gu_p0), hi = min(b * 32 + 32, gu_p1);
-                bool mine = true;
-                if (hi - lo < 32) {
-                    if (inside) p.act[r] = s.act_s[r - gu_p0];
-                    __syncwarp();
-                    uint32_t old = 0;
-                    if (lane == 0)
-                        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
-                                     : "=r"(old)
-                                     : "l"(p.blk_count + b), "r"((uint32_t)(hi - lo))
-                                     : "memory");
-                    old = __shfl_sync(0xffffffffu, old, 0);
-                    mine = old + (uint32_t)(hi - lo) == 32u;
-                    __syncwarp();
-                }
-                if (mine && !aborted) {
-                    const float v32 = inside ? s.act_s[r - gu_p0] : __ldcg(p.act + r);
-                    const float amax = warp_max_butterfly(fabsf(v32));
-                    const float dd = __fdiv_rn(amax, 127.0f);
-                    const int q = amax == 0.f ? 0 : (int)roundf(__fdiv_rn(v32, dd));
-                    int sq = q;
-#pragma unroll
-                    for (int m = 16; m > 0; m >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, m);
-                    p.aq[r] = (int8_t)q;
-                    if (lane == 0) {
-                        p.ad[b] = __half2float(__float2half_rn(dd));
-                        p.aS[b] = sq;
-                    }
-                }
-            }
+            finish(k, st);
+            g = claim();
         }
     }
 
-    // P3: grid barrier, activation copy, down.
+    // ---- P3: act of the CTA's range to global memory, grid barrier #2 -------------------------
+    named_sync(kBarConsumers, kConsumerThreads);  // every gate/up sub-unit of this CTA is done
     if (tid == 0 && p.trace) p.trace[cta * 16 + 4] = globaltimer_ns();
-    const bool sync_ok = grid_sync(p.ctl, (uint32_t)G * (epoch + 2u), deadline, s.flag, 7, kConsumerThreads);
-    if (!sync_ok) aborted = true;
+    {
+        const int gu_p0 = (int)((int64_t)cta * nvs * I / G), gu_p1 = (int)((int64_t)(cta + 1) * nvs * I / G);
+        for (int i = tid; i < gu_p1 - gu_p0; i += kConsumerThreads) {
+            const float gv = s.gval[i];
+            // act = up * silu(gate) (moe_gguf.cu:272-273)
+            p.act[gu_p0 + i] = aborted ? 0.f : s.uval[i] * __fdiv_rn(gv, 1.0f + expf(-gv));
+        }
+    }
+    named_sync(kBarConsumers, kConsumerThreads);
     if (tid == 0) {
-        if (sync_ok) p.ctl->epoch[cta] = epoch + 2u;  // read again only by this CTA's next launch
+        bool ok2 = ok1;
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&p.ctl->count) : "memory");
+        const uint32_t target = (uint32_t)G * (epoch + 2u);
+        uint32_t spins = 0;
+        while (ok2 && (int)(ld_acquire_gpu(&p.ctl->count) - target) < 0) {
+            __nanosleep(16);
+            if ((++spins & 255u) == 0 && globaltimer_ns() > deadline) {
+                atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
+                ok2 = false;
+            }
+        }
+        s.ctl[kCtlFail] = ok2 ? 0 : 1;
+        if (ok2) p.ctl->epoch[cta] = epoch + 2u;  // read again only by this CTA's next launch
         if (p.trace) p.trace[cta * 16 + 5] = globaltimer_ns();
     }
+    named_sync(kBarConsumers, kConsumerThreads);
+    if (s.ctl[kCtlFail]) aborted = true;
+    // Every CTA quantises the whole act vector: 128 values per warp step (one float4 a lane),
+    // all of a warp's loads in flight before its first block is quantised.
     {
-        // One bulk copy of the quantised activation [8][I] (+ scales, sums) per CTA.  Issue and
-        // wait depend only on the CTA-uniform barrier result, so the copy has always landed
-        // before any consumer thread moves on.
-        const uint32_t qb = (uint32_t)(kTopK * I), sb = (uint32_t)(sizeof(float) * kTopK * (I / 32));
-        if (tid == 0 && sync_ok) {
-            asm volatile("fence.proxy.async;" ::: "memory");  // generic writes -> async-proxy reads
-            mbar_arrive_expect_tx(s.abar, qb + 2 * sb);
-            bulk_g2s(s.aq_s, p.aq, qb, s.abar);
-            bulk_g2s(s.ad_s, p.ad, sb, s.abar);
-            bulk_g2s(s.aS_s, p.aS, sb, s.abar);
+        const int nchunk = nvs * I / 128;
+        constexpr int kLd = 8;
+        for (int c0 = warp * kLd; c0 < nchunk; c0 += kConsumerWarps * kLd) {
+            float4 v[kLd];
+#pragma unroll
+            for (int j = 0; j < kLd; ++j)
+                v[j] = (c0 + j < nchunk && !aborted) ? __ldcg(reinterpret_cast<const float4 *>(p.act) + (c0 + j) * 32 + lane)
+                                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int j = 0; j < kLd; ++j) {
+                const int c = c0 + j;
+                if (c < nchunk) quant128(v[j], s.aq_s + c * 128, s.ad_s + c * 4, s.aS_s + c * 4, lane);
+            }
         }
-        if (sync_ok && !mbar_wait_bounded(s.abar, 0u, deadline + 1000000000ull)) {
-            atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
-            aborted = true;
-        }
-        build_task_scales(s.ats, s.ad_s, s.aS_s, kTopK * (I / 64), tid, kConsumerThreads);
-        named_sync(1, kConsumerThreads);
+        named_sync(kBarConsumers, kConsumerThreads);
+        build_task_scales(s.ats, s.ad_s, s.aS_s, nvs * (I / 64), tid, kConsumerThreads);
+        named_sync(kBarConsumers, kConsumerThreads);
         if (tid == 0 && p.trace) p.trace[cta * 16 + 6] = globaltimer_ns();
+    }
 
-        // Down units: U_dn rows x all 8 routed experts.  A lane group of L lanes computes one expert
-        // (slot) for two rows, with that slot's activation in registers.
-        const int L = p.dn_lanes;
-        const int q = gw * (32 / L) + lane / L, lig = lane % L;
-        const int slot = q % kTopK, rA = (q / kTopK) * kRowsPerLane, rB = rA + 1;
+    // ---- P3: down sub-units -------------------------------------------------------------------
+    {
         const int ntasks = (I / QK_K) * 4;
+        const int lgi = lane / Ld, lig = lane % Ld;
         TaskAct ta[kTPL];
-        const int vp = s.vpos[slot];  // position block of this slot's activation
-        load_task_acts(ActView{s.aq_s + (size_t)vp * I, s.ats + vp * (I / 64)}, lig, L, ntasks, ta);
-        const float wslot = s.w[slot];
-        const bool valid = s.ids[slot] >= 0;
-        const int j0 = ((grp - n_gu) % kGroups + kGroups) % kGroups;
-        for (int k = n_gu + j0; k < n_units; k += kGroups) {
+        int cur_vp = -1;
+        while (g < n_sub) {
+            const int2 su = s.subs[g];
+            const int k = su.x, ro = su.y & 0xffff, nr = su.y >> 16;
             const int4 u = s.units[k];
             const int st = k % p.stages;
+            const int vp = u.y, slot = s.vslot[vp];
+            if (vp != cur_vp) {
+                load_task_acts(ActView{s.aq_s + (size_t)vp * I, s.ats + vp * (I / 64)}, lig, Ld, ntasks, ta);
+                cur_vp = vp;
+            }
             if (!aborted && !wait_unit(s.full, s.ticket, k, st, p.stages, deadline)) {
                 atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
                 aborted = true;
             }
+            const int rA = ro + lgi * kRowsPerLane, rB = rA + 1, rend = ro + nr;
             float vA = 0.f, vB = 0.f;
-            if (valid && !aborted && rA < u.w) {
-                const uint8_t *base = s.stages + (size_t)st * p.stage_bytes + (size_t)slot * dn_row_bytes * U_dn;
+            if (!aborted && rA < rend) {
+                const uint8_t *base = s.stages + (size_t)st * p.stage_bytes;
                 const uint8_t *rowA = base + (size_t)rA * dn_row_bytes;
-                const uint8_t *rowB = base + (size_t)min(rB, u.w - 1) * dn_row_bytes;
+                const uint8_t *rowB = base + (size_t)min(rB, rend - 1) * dn_row_bytes;
                 if (p.dn_type == MMRS_Q5K) {
-                    vA = row_dot<MMRS_Q5K>(rowA, lig, L, ntasks, ta);
-                    vB = row_dot<MMRS_Q5K>(rowB, lig, L, ntasks, ta);
+                    vA = row_dot<MMRS_Q5K>(rowA, lig, Ld, ntasks, ta);
+                    vB = row_dot<MMRS_Q5K>(rowB, lig, Ld, ntasks, ta);
                 } else {
-                    vA = row_dot<MMRS_Q4K>(rowA, lig, L, ntasks, ta);
-                    vB = row_dot<MMRS_Q4K>(rowB, lig, L, ntasks, ta);
+                    vA = row_dot<MMRS_Q4K>(rowA, lig, Ld, ntasks, ta);
+                    vB = row_dot<MMRS_Q4K>(rowB, lig, Ld, ntasks, ta);
                 }
             }
 #pragma unroll
             for (int m = 16; m > 0; m >>= 1)
-                if (m < L) {
+                if (m < Ld) {
                     vA += __shfl_xor_sync(0xffffffffu, vA, m);
                     vB += __shfl_xor_sync(0xffffffffu, vB, m);
                 }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s.empty[st]);
             if (lig == 0) {
-                const int off = s.unit_off[k];
-                if (rA < u.w) s.dn_acc[(off + rA) * kTopK + slot] = valid ? vA * wslot : 0.f;
-                if (rB < u.w) s.dn_acc[(off + rB) * kTopK + slot] = valid ? vB * wslot : 0.f;
+                const float wslot = s.w[slot];
+                if (rA < rend) s.dn_acc[rA * kTopK + slot] = vA * wslot;
+                if (rB < rend) s.dn_acc[rB * kTopK + slot] = vB * wslot;
             }
+            finish(k, st);
+            g = claim();
         }
-        // y = fixed 8-way tree over the routed experts (moe_gguf.cu:328-342) + residual
-        named_sync(1, kConsumerThreads);
-        if (p.world <= 1) {
-            for (int r = tid; r < dn_r1 - dn_r0; r += kConsumerThreads) {
-                const float *q = s.dn_acc + r * kTopK;
-                float y = ((q[0] + q[4]) + (q[2] + q[6])) + ((q[1] + q[5]) + (q[3] + q[7]));
-                if (p.residual) y = y + s.res_s[r];
-                p.y[dn_r0 + r] = y;
-            }
-        } else {
-            // Fused exchange of the partial rows with the other ranks over NVLink: publish this
-            // CTA's rows in the exchange region (buffer token & 1), release a per-CTA flag, wait
-            // (bounded) for the same CTA's flag on every peer, then sum the ranks' rows in rank
-            // order (bit-identical on all ranks) and add the residual
-            // (TensorParallelRankGroup::all_reduce_sum_with_residual, tensor_parallel.rs:786-812).
-            // The token is the group's operation counter: every layer sharing the group draws a
-            // fresh one, so a flag raised for another layer's exchange never satisfies this wait.
-            const uint32_t token = p.token;
-            const size_t part_off = kXchDPart + sizeof(float) * (size_t)(token & 1u) * kXchMaxHidden;
-            float *mine = reinterpret_cast<float *>(p.xch + part_off);
-            for (int r = tid; r < dn_r1 - dn_r0; r += kConsumerThreads) {
-                const float *q = s.dn_acc + r * kTopK;
-                mine[dn_r0 + r] = ((q[0] + q[4]) + (q[2] + q[6])) + ((q[1] + q[5]) + (q[3] + q[7]));
-            }
-            named_sync(1, kConsumerThreads);
-            if (tid == 0) {
-                st_release_sys(reinterpret_cast<uint32_t *>(p.xch + kXchDFlags) + cta, token);
-                const uint64_t xdl = globaltimer_ns() + p.timeout_ns;
-                for (int rk = 0; rk < p.world; ++rk) {
-                    if (rk == p.rank) continue;
-                    if (!wait_flag_sys(reinterpret_cast<const uint32_t *>(p.xpeer[rk] + kXchDFlags) + cta, token, xdl)) {
-                        atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
-                        atomicExch(reinterpret_cast<uint32_t *>(p.xch + kXchStatus), (uint32_t)MMRS_ERR_TIMEOUT);
-                        s.flag[1] = 1;
-                        break;
-                    }
+    }
+
+    // ---- y = fixed 8-way tree over the routed experts (moe_gguf.cu:328-342) + residual ---------
+    named_sync(kBarConsumers, kConsumerThreads);
+    if (p.world <= 1) {
+        for (int r = tid; r < nres && !aborted; r += kConsumerThreads) {
+            const float *q = s.dn_acc + r * kTopK;
+            float y = ((q[0] + q[4]) + (q[2] + q[6])) + ((q[1] + q[5]) + (q[3] + q[7]));
+            if (p.residual) y = y + s.res_s[r];
+            p.y[dn_r0 + r] = y;
+        }
+    } else {
+        // Fused exchange of the partial rows with the other ranks over NVLink: publish this
+        // CTA's rows in the exchange region (buffer token & 1), release a per-CTA flag, wait
+        // (bounded) for the same CTA's flag on every peer, then sum the ranks' rows in rank
+        // order (bit-identical on all ranks) and add the residual
+        // (TensorParallelRankGroup::all_reduce_sum_with_residual, tensor_parallel.rs:786-812).
+        // The token is the group's operation counter: every layer sharing the group draws a
+        // fresh one, so a flag raised for another layer's exchange never satisfies this wait.
+        const uint32_t token = p.token;
+        const size_t part_off = kXchDPart + sizeof(float) * (size_t)(token & 1u) * kXchMaxHidden;
+        float *mine = reinterpret_cast<float *>(p.xch + part_off);
+        for (int r = tid; r < nres; r += kConsumerThreads) {
+            const float *q = s.dn_acc + r * kTopK;
+            mine[dn_r0 + r] = ((q[0] + q[4]) + (q[2] + q[6])) + ((q[1] + q[5]) + (q[3] + q[7]));
+        }
+        named_sync(kBarConsumers, kConsumerThreads);
+        if (tid == 0) {
+            s.ctl[kCtlFail] = 0;
+            st_release_sys(reinterpret_cast<uint32_t *>(p.xch + kXchDFlags) + cta, token);
+            const uint64_t xdl = globaltimer_ns() + p.timeout_ns;
+            for (int rk = 0; rk < p.world; ++rk) {
+                if (rk == p.rank) continue;
+                if (!wait_flag_sys(reinterpret_cast<const uint32_t *>(p.xpeer[rk] + kXchDFlags) + cta, token, xdl)) {
+                    atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
+                    atomicExch(reinterpret_cast<uint32_t *>(p.xch + kXchStatus), (uint32_t)MMRS_ERR_TIMEOUT);
+                    s.ctl[kCtlFail] = 1;
+                    break;
                 }
             }
-            named_sync(1, kConsumerThreads);
-            const bool xfail = *reinterpret_cast<volatile int *>(&s.flag[1]) != 0;
-            for (int r = tid; r < dn_r1 - dn_r0 && !xfail; r += kConsumerThreads) {
-                const int row = dn_r0 + r;
-                float v[kMaxRanks];
+        }
+        named_sync(kBarConsumers, kConsumerThreads);
+        const bool xfail = *reinterpret_cast<volatile int *>(&s.ctl[kCtlFail]) != 0;
+        for (int r = tid; r < nres && !xfail; r += kConsumerThreads) {
+            const int row = dn_r0 + r;
+            float v[kMaxRanks];
 #pragma unroll
-                for (int rk = 0; rk < kMaxRanks; ++rk)  // all loads in flight before the sum
-                    if (rk < p.world)
-                        v[rk] = rk == p.rank ? mine[row]
-                                             : ld_relaxed_sys_f32(reinterpret_cast<const float *>(p.xpeer[rk] + part_off) + row);
-                float y = v[0];
+            for (int rk = 0; rk < kMaxRanks; ++rk)  // all loads in flight before the sum
+                if (rk < p.world)
+                    v[rk] = rk == p.rank ? mine[row]
+                                         : ld_relaxed_sys_f32(reinterpret_cast<const float *>(p.xpeer[rk] + part_off) + row);
+            float y = v[0];
 #pragma unroll
-                for (int rk = 1; rk < kMaxRanks; ++rk)
-                    if (rk < p.world) y = y + v[rk];
-                if (p.residual) y = y + s.res_s[r];
-                p.y[row] = y;
-            }
+            for (int rk = 1; rk < kMaxRanks; ++rk)
+                if (rk < p.world) y = y + v[rk];
+            if (p.residual) y = y + s.res_s[r];
+            p.y[row] = y;
         }
     }
     if (tid == 0 && p.trace) p.trace[cta * 16 + 7] = globaltimer_ns();
@@ -849,12 +849,13 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
 // ------------------------------------------------------------------------------------------
 size_t decode_smem_bytes(const DecodeParams &p) {
     auto a16 = [](size_t v) { return (v + 15) / 16 * 16; };
-    size_t b = a16((size_t)p.stages * p.stage_bytes) + 2 * a16(sizeof(uint64_t) * p.stages) + a16(8);
+    size_t b = a16((size_t)p.stages * p.stage_bytes) + 2 * a16(sizeof(uint64_t) * p.stages);
     b += a16(p.H) + 2 * a16(4 * (p.H / 32)) + a16(16 * (p.H / 64));
     b += a16((size_t)kTopK * p.I) + 2 * a16(4 * kTopK * (p.I / 32)) + a16(16 * kTopK * (p.I / 64));
-    b += a16(4 * (p.E > 16 ? p.E : 16)) + a16(4 * p.E) + 4 * a16(4 * kTopK);  // part, sig, ids, vslot, vpos, w
-    b += a16(4 * p.res_slots * kTopK) + 3 * a16(4 * p.act_slots) + a16(4 * p.res_slots) + 32;
-    b += a16(16 * kMaxUnits) + a16(4 * kMaxUnits) + 16 + a16(4 * p.stages);
+    b += a16(4 * 16) + 3 * a16(4 * kTopK);  // part, ids, vslot, w
+    b += a16(4 * (size_t)p.res_slots * kTopK) + 2 * a16(4 * (size_t)p.act_slots) + a16(4 * (size_t)p.res_slots);
+    b += a16(16 * kMaxUnits) + 2 * a16(4 * kMaxUnits) + a16(8 * kMaxSubs);
+    b += 2 * a16(4 * (size_t)p.stages) + a16(4 * kCtlWords);
     return b;
 }
 
@@ -868,27 +869,31 @@ int decode_configure(DecodeParams &p, int num_sms, int max_smem) {
     if (p.H % QK_K || p.I % QK_K || p.E < kTopK || p.E > 256 || p.E % 4) return MMRS_ERR_UNSUPPORTED;
     if ((p.gu_type != MMRS_Q4K && p.gu_type != MMRS_Q5K) || (p.dn_type != MMRS_Q4K && p.dn_type != MMRS_Q5K))
         return MMRS_ERR_UNSUPPORTED;
-    if (p.H / 128 > 2 * kConsumerWarps || p.H / 8 / 4 > 128) return MMRS_ERR_UNSUPPORTED;  // H <= 4096
+    if (p.H / 8 / 4 > 128) return MMRS_ERR_UNSUPPORTED;  // router slice: at most 4 float4 a lane (H <= 4096)
     const int gu_tasks = (p.H / QK_K) * 4, dn_tasks = (p.I / QK_K) * 4;
     p.gu_lanes = pow2_at_least((gu_tasks + kTPL - 1) / kTPL);
     p.dn_lanes = pow2_at_least((dn_tasks + kTPL - 1) / kTPL);
-    if (p.gu_lanes > 16 || p.dn_lanes > 32) return MMRS_ERR_UNSUPPORTED;  // H <= 3072, I <= 6144
-    // units: kGroupWarps warps x (32/L) lane groups x kRowsPerLane rows
-    p.gu_unit_rows = kGroupWarps * (32 / p.gu_lanes) * kRowsPerLane;
-    p.dn_unit_rows = kGroupWarps * (32 / p.dn_lanes) * kRowsPerLane / kTopK;
-    if (p.dn_unit_rows < kRowsPerLane) return MMRS_ERR_UNSUPPORTED;
+    if (p.gu_lanes > 32 || p.dn_lanes > 32) return MMRS_ERR_UNSUPPORTED;  // H, I <= 6144
+    // one warp's share: (32 / L) lane groups x 2 rows; a gate/up copy unit is four shares
+    p.gu_sub_rows = (32 / p.gu_lanes) * kRowsPerLane;
+    p.dn_sub_rows = (32 / p.dn_lanes) * kRowsPerLane;
+    p.gu_unit_rows = kSubsPerGuUnit * p.gu_sub_rows;
     p.act_slots = (kTopK * p.I + num_sms - 1) / num_sms + 1;
     p.res_slots = (p.H + num_sms - 1) / num_sms + 1;
-    if (p.res_slots > kConsumerThreads || p.E > 2 * num_sms) return MMRS_ERR_UNSUPPORTED;
-    const int max_gu_units = 2 * ((p.act_slots + p.gu_unit_rows - 1) / p.gu_unit_rows + kTopK);
-    const int max_dn_units = (p.res_slots + p.dn_unit_rows - 1) / p.dn_unit_rows;
-    if (max_gu_units + max_dn_units > kMaxUnits) return MMRS_ERR_UNSUPPORTED;
+    if (p.E > 2 * num_sms || num_sms > kMaxGridCtas) return MMRS_ERR_UNSUPPORTED;
+    // table bounds: a CTA's gate/up chunks (one lane each; each slot boundary may add one), units
+    // and sub-units
+    const int max_chunks = (p.act_slots + p.gu_unit_rows - 1) / p.gu_unit_rows + kTopK;
+    const int max_dn_sub = (p.res_slots + p.dn_sub_rows - 1) / p.dn_sub_rows;
+    if (max_chunks > 32 || 2 * max_chunks + kTopK > kMaxUnits ||
+        2 * max_chunks * kSubsPerGuUnit + kTopK * max_dn_sub > kMaxSubs || p.res_slots > 0xffff)
+        return MMRS_ERR_UNSUPPORTED;
     const size_t gu_stage = kq_row_bytes(p.gu_type, p.H) * p.gu_unit_rows;
-    const size_t dn_stage = kq_row_bytes(p.dn_type, p.I) * p.dn_unit_rows * kTopK;
+    const size_t dn_stage = kq_row_bytes(p.dn_type, p.I) * (p.res_slots - 1);
     p.stage_bytes = (int)(((gu_stage > dn_stage ? gu_stage : dn_stage) + 127) / 128 * 128);
     p.stages = 0;
     DecodeParams q = p;
-    for (int st = 16; st >= 2; --st) {
+    for (int st = 16; st >= 3; --st) {
         q.stages = st;
         if (decode_smem_bytes(q) <= (size_t)max_smem) {
             p.stages = st;
@@ -914,7 +919,6 @@ int decode_launch(const DecodeParams &p, cudaStream_t stream) {
         set_rc[dev] = cudaFuncSetAttribute(moe_decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
     });
     if (set_rc[dev] != cudaSuccess) return MMRS_ERR_LAUNCH;
-    cudaError_t err = cudaSuccess;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.grid);
     cfg.blockDim = dim3(kThreads);
@@ -925,7 +929,7 @@ int decode_launch(const DecodeParams &p, cudaStream_t stream) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    err = cudaLaunchKernelEx(&cfg, moe_decode_fused_kernel, p);
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, moe_decode_fused_kernel, p);
     return err == cudaSuccess ? MMRS_OK : MMRS_ERR_LAUNCH;
 }
 

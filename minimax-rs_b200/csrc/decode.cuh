@@ -29,14 +29,15 @@ struct DecodeParams {
     int8_t *aq;           // [8][I] Q8_1 quants of act
     float *ad;            // [8][I/32] fp16-rounded Q8_1 scales
     int *aS;              // [8][I/32] sums of quants
-    uint32_t *blk_count;  // [8][I/32] rows written per Q8_1 block (zero between launches)
+    uint32_t *blk_count;  // [8][I/32] (unused by the current kernel; kept in the layout)
     GridFlags *ctl;
     uint64_t *trace;  // [grid][16] globaltimer stamps per phase, or null
     // shape
     int E, H, I;
     int gu_type, dn_type;
-    // launch configuration (decode_configure)
-    int gu_lanes, gu_unit_rows, dn_lanes, dn_unit_rows, stages, stage_bytes, grid;
+    // launch configuration (decode_configure): lanes per row, rows per sub-unit (one warp's
+    // share) and rows per copy unit (one ring stage) of the gate/up and down matrices
+    int gu_lanes, gu_sub_rows, gu_unit_rows, dn_lanes, dn_sub_rows, stages, stage_bytes, grid;
     int act_slots, res_slots;
     uint64_t timeout_ns;
     // multi-GPU group (world > 1): this rank's exchange region and every rank's as mapped here;

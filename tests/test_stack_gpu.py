@@ -1,0 +1,183 @@
+"""End-of-stack logits through the product entry points against the CPU oracle.
+
+A small decode stack (two layers of attn_norm -> attention half -> ffn_norm -> MoE block, each
+with its own weights and KV cache, then output_norm -> Q6_K LM head -> greedy token) runs three
+decode positions on the GPU through mmrs_rmsnorm_f32, mmrs_attn_decode_forward,
+mmrs_moe_block_forward and mmrs_lm_head_forward (Layer::forward + TensorParallelModel::logits:
+src/model.rs:213-218, 295-332, src/tensor_parallel_model.rs:871-880).
+
+Two oracle chains:
+* stage by stage, every oracle stage fed the GPU's input to that stage: each stage within its own
+  parity bound, and the logits within 2e-2 max-abs with the same greedy token;
+* independent, the oracle on its own outputs throughout: the same greedy token at every position
+  and logits within the reference's own layer-comparison style of bound (mean-abs 2e-2, max-abs
+  1e-1; tests/tp_layer.rs:59-66, 112-115).  Two implementations of quantised inference diverge
+  at isolated rounding near-ties (a Q8_1 quant whose x/d lands within an ulp of .5 after a 1-ulp
+  difference upstream, an f16 rounding of an attention output), and a residual stream carries
+  such a difference to the logits; the stage-by-stage chain shows every stage agreeing.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+LOGIT_MAX_ABS = 2e-2                        # stage by stage
+CHAIN_MEAN_ABS, CHAIN_MAX_ABS = 2e-2, 1e-1  # independent chain
+H, QH, KVH, HD, ROT, NPOS = 1024, 6, 1, 128, 64, 16
+E, I = 32, 512
+VOCAB = 1001
+NL, STEPS = 2, 3
+
+
+def _unpack_scales(s12):
+    """[n, 12] packed bytes -> 6-bit (scale, min) pairs of the 8 sub-blocks (get_scale_min_k4,
+    quantized.cu:926-933)."""
+    s = s12.astype(np.int32)
+    sc, m = np.empty((s.shape[0], 8), np.int32), np.empty((s.shape[0], 8), np.int32)
+    for j in range(4):
+        sc[:, j], m[:, j] = s[:, j] & 63, s[:, j + 4] & 63
+        sc[:, j + 4] = (s[:, j + 8] & 0xF) | ((s[:, j] >> 6) << 4)
+        m[:, j + 4] = (s[:, j + 8] >> 4) | ((s[:, j + 4] >> 6) << 4)
+    return sc, m
+
+
+def _pack_scales(sc, m):
+    out = np.zeros((sc.shape[0], 12), np.int32)
+    for j in range(4):
+        out[:, j] = (sc[:, j] & 63) | ((sc[:, j + 4] >> 4) << 6)
+        out[:, j + 4] = (m[:, j] & 63) | ((m[:, j + 4] >> 4) << 6)
+        out[:, j + 8] = (sc[:, j + 4] & 0xF) | ((m[:, j + 4] & 0xF) << 4)
+    return out.astype(np.uint8)
+
+
+def _centre(blocks, gguf_type, pkg):
+    """Zero-mean k-quant weights, as trained checkpoints have: every sub-block's min is set so that
+    d*sc*q - dmin*m is centred on the middle of the quant range (dmin = 8 d and m = sc*15/16 for
+    Q4_K; 16 d and sc*31/32 for Q5_K).  The generator's unsigned quants with independent mins are
+    biased; through a residual stream that bias grows layer by layer until the half-precision
+    Q8_1 scales overflow, in the reference's numerics as in these."""
+    bb = 176 if gguf_type == pkg.Q5K else 144
+    b = blocks.reshape(-1, bb).copy()
+    d = b[:, 0:2].copy().view(np.float16).astype(np.float32)[:, 0]
+    mult, frac = (16.0, 31.0 / 32.0) if gguf_type == pkg.Q5K else (8.0, 15.0 / 16.0)
+    b[:, 2:4] = (d * mult).astype(np.float16).reshape(-1, 1).view(np.uint8)
+    sc, _ = _unpack_scales(b[:, 4:16])
+    b[:, 4:16] = _pack_scales(sc, np.clip(np.rint(sc * frac), 0, 63).astype(np.int32))
+    return b.reshape(-1)
+
+
+def _norm_ref(x, w, eps=1e-6):
+    x64 = x.astype(np.float64)
+    return (x64 / np.sqrt(np.mean(x64 * x64) + eps) * w).astype(np.float32)
+
+
+def test_scale_packing_round_trips():
+    rng = np.random.default_rng(0)
+    s = rng.integers(0, 256, (1000, 12)).astype(np.uint8)
+    sc, m = _unpack_scales(s)
+    assert np.array_equal(_pack_scales(sc, m), s)
+
+
+@pytest.mark.gpu
+def test_stack_logits_match_oracle(pkg, synth, orc, dev):
+    import torch
+    T_ = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+    seed = 4242
+    qr, kr = QH * HD, KVH * HD
+    cos, sin = synth.rope_tables(NPOS, ROT)
+    layers = []
+    for l in range(NL):
+        b = 100 * l
+        w = dict(wq=synth.q8_0_blocks(seed, b + 1, qr, H), wk=synth.q8_0_blocks(seed, b + 2, kr, H),
+                 wv=synth.q8_0_blocks(seed, b + 3, kr, H), wo=synth.q8_0_blocks(seed, b + 4, H, qr),
+                 qn=(1.0 + synth.normal_f32(qr, seed, b + 5, 0.1)).astype(np.float32),
+                 kn=(1.0 + synth.normal_f32(kr, seed, b + 6, 0.1)).astype(np.float32),
+                 an=(1.0 + synth.normal_f32(H, seed, b + 7, 0.1)).astype(np.float32),
+                 # ffn_norm weights of 0.1: the MoE output is then of the residual stream's size
+                 fn=(0.1 * (1.0 + synth.normal_f32(H, seed, b + 8, 0.1))).astype(np.float32))
+        st = synth.layer_streams(l)
+        w["router"] = synth.normal_f32(E * H, seed, st["router"], 0.02).reshape(E, H)
+        w["bias"] = synth.normal_f32(E, seed, st["bias"], 0.01)
+        w["gate"] = _centre(synth.kquant(pkg.Q4K, seed, st["gate"], E, I, H), pkg.Q4K, pkg)
+        w["up"] = _centre(synth.kquant(pkg.Q4K, seed, st["up"], E, I, H), pkg.Q4K, pkg)
+        w["down"] = _centre(synth.kquant(pkg.Q5K, seed, st["down"], E, H, I), pkg.Q5K, pkg)
+        w["attn"] = pkg.AttnLayer(T_(w["wq"]), T_(w["wk"]), T_(w["wv"]), T_(w["wo"]), T_(w["qn"]), T_(w["kn"]),
+                                  T_(cos), T_(sin), H, query_heads=QH, kv_heads=KVH, rope_dim=ROT)
+        w["moe"] = pkg.MoeLayer(T_(w["router"]), T_(w["bias"]), T_(w["gate"]), T_(w["up"]), T_(w["down"]),
+                                pkg.Q4K, pkg.Q5K)
+        w["an_t"], w["fn_t"] = T_(w["an"]), T_(w["fn"])
+        w["kc"] = np.zeros((KVH, NPOS, HD), dtype=np.uint16)
+        w["vc"] = np.zeros_like(w["kc"])
+        layers.append(w)
+    wl = synth.q6k_blocks(seed, 900, VOCAB, H).reshape(-1, 210)
+    # block scales d x 0.1: logits of magnitude ~10-20, as a trained head gives (the bound is absolute)
+    wl[:, 208:210] = (wl[:, 208:210].copy().view(np.float16) * np.float16(0.1)).view(np.uint8)
+    wl = wl.reshape(VOCAB, -1)
+    onw = (1.0 + synth.normal_f32(H, seed, 901, 0.1)).astype(np.float32)
+    head = pkg.LmHead(T_(wl), T_(onw), VOCAB, H)
+
+    def oracle_attn(w, x, pos, residual):
+        proj = np.concatenate([orc.q8_0_matvec(w["wq"], qr, H, x), orc.q8_0_matvec(w["wk"], kr, H, x),
+                               orc.q8_0_matvec(w["wv"], kr, H, x)])
+        nrm = orc.qkv_rmsnorm_f16(proj, w["qn"], w["kn"], qr, kr, kr, 1e-6)
+        rt = orc.partial_rope_f16(nrm[:qr], nrm[qr:qr + kr], cos, sin, HD, ROT, pos)
+        w["kc"][:, pos] = rt[qr:].reshape(KVH, HD)
+        w["vc"][:, pos] = nrm[qr + kr:].reshape(KVH, HD)
+        att = orc.gqa_decode_f16(rt[:qr], w["kc"], w["vc"], pos + 1, QH, KVH, HD, NPOS * HD, 1.0 / np.sqrt(HD))
+        return (orc.q8_0_matvec(w["wo"], H, qr, att.view(np.float16).astype(np.float32)) + residual).astype(np.float32)
+
+    def rel(a, b):
+        a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+        return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+    worst_stage, worst_chain, top = 0.0, 0.0, 0.0
+    kc_ind = [(w["kc"].copy(), w["vc"].copy()) for w in layers]  # the independent chain's own caches
+    for pos in range(STEPS):
+        x0 = synth.normal_f32(H, seed, 1000 + pos, 1.0)  # the position's token embedding (synthetic)
+        # GPU chain; the oracle follows stage by stage on the GPU's inputs
+        h = T_(x0).clone()
+        for w in layers:
+            hn = h.cpu().numpy()
+            n1 = pkg.rmsnorm(h, w["an_t"])
+            h2 = w["attn"].forward(n1, pos, residual=h)
+            n2 = pkg.rmsnorm(h2, w["fn_t"])
+            h = w["moe"].forward(n2.view(1, H), residual=h2.view(1, H)).view(H)
+            torch.cuda.synchronize()
+            assert w["attn"].status() == 0 and w["moe"].status() == 0
+            n1n, h2n, n2n, hn_out = n1.cpu().numpy(), h2.cpu().numpy(), n2.cpu().numpy(), h.cpu().numpy()
+            assert rel(n1n, _norm_ref(hn, w["an"])) < 1e-5
+            assert rel(h2n - hn, oracle_attn(w, n1n, pos, hn) - hn) < 5e-3, pos  # decode attention bound
+            assert rel(n2n, _norm_ref(h2n, w["fn"])) < 1e-5
+            yr, _, _ = orc.moe_block(w["router"], w["bias"], w["gate"], w["up"], w["down"], pkg.Q4K, pkg.Q5K,
+                                     n2n.reshape(1, H), h2n.reshape(1, H))
+            assert rel(hn_out - h2n, yr.reshape(H) - h2n) < 1e-3, pos  # MoE block bound
+        logits, tok = head.forward(h)
+        torch.cuda.synchronize()
+        assert head.status() == 0
+        got = logits.cpu().numpy().astype(np.float64)
+        ref = orc.q6k_matvec(wl, VOCAB, H, _norm_ref(h.cpu().numpy(), onw))
+        err = float(np.max(np.abs(got - ref)))
+        worst_stage = max(worst_stage, err)
+        assert err <= LOGIT_MAX_ABS, (pos, err)
+        assert int(tok.item()) == orc.argmax_f32(ref), pos
+        # independent oracle chain on its own outputs and its own KV caches
+        saved = [(w["kc"], w["vc"]) for w in layers]
+        for w, (kc, vc) in zip(layers, kc_ind):
+            w["kc"], w["vc"] = kc, vc
+        hr = x0.copy()
+        for w in layers:
+            h2r = oracle_attn(w, _norm_ref(hr, w["an"]), pos, hr)
+            yr, _, _ = orc.moe_block(w["router"], w["bias"], w["gate"], w["up"], w["down"], pkg.Q4K, pkg.Q5K,
+                                     _norm_ref(h2r, w["fn"]).reshape(1, H), h2r.reshape(1, H))
+            hr = yr.reshape(H).astype(np.float32)
+        for w, (kc, vc) in zip(layers, saved):
+            w["kc"], w["vc"] = kc, vc
+        ref_ind = orc.q6k_matvec(wl, VOCAB, H, _norm_ref(hr, onw))
+        d = np.abs(got - ref_ind)
+        worst_chain = max(worst_chain, float(d.max()))
+        top = max(top, float(np.max(np.abs(ref_ind))))
+        assert float(d.mean()) <= CHAIN_MEAN_ABS and float(d.max()) <= CHAIN_MAX_ABS, \
+            (pos, float(d.mean()), float(d.max()))
+        assert int(tok.item()) == orc.argmax_f32(ref_ind), pos
+    print(f"end-of-stack logits (largest |logit| {top:.1f}): stage by stage max-abs {worst_stage:.2e}, "
+          f"independent chain max-abs {worst_chain:.2e} over {STEPS} positions")
