@@ -10,21 +10,21 @@
 //       (expert, slice) pairs over the 13 warps: 32 lane partials, butterfly, fixed slice tree).
 //       The router rows are requested before anything else.  Grid barrier #1: one
 //       fire-and-forget arrival per CTA.
-//   P1  the producer warp waits for barrier #1, selects the top-8 (one warp: 8 keys a lane,
-//       rounds of redux max / min on order-preserving keys) and builds the copy table with its
-//       32 lanes; meanwhile the consumer warps quantise x to Q8_1 and prefetch the residual.
-//   P2  gate/up: the CTA owns a contiguous range of (slot, row) pairs; copy units of up to four
+//   P1  the consumer warps quantise x to Q8_1 while the producer warp waits for barrier #1;
+//       eight warps then take 32 experts each (sigmoid, order-preserving selection key, rounds of
+//       redux max / min: that warp's top-8) and the producer warp merges the 64 candidates the same
+//       way, renormalises the weights and builds the copy table with its 32 lanes.
+//   P2  gate/up: the CTA owns a contiguous range of (slot, row) pairs; copy units of up to three
 //       warp shares of rows of the gate or the up matrix (one bulk copy each) stream through a
 //       ring of shared-memory stages.  Consumer warps claim sub-units (one warp's rows) in unit
 //       order from a CTA counter, so a free warp always takes the oldest unclaimed rows; the last
 //       finisher of a unit frees its stage.  The producer issues every unit as soon as its stage
 //       is free, so the down units (this CTA's output rows of one expert: one contiguous copy
 //       each) land in the ring while gate/up is still being computed.
-//   P3  act = up * silu(gate) of the CTA's range goes to global memory as f32; grid barrier #2;
-//       every CTA reads the whole act vector back (one 16-byte load per lane and 128 values, all
-//       of a warp's loads in flight together) and quantises it to Q8_1 itself
-//       (quantize_silu_mul_q8_1 arithmetic, no cross-CTA hand-off); then the down sub-units,
-//       weighted by the route weight, the reference's fixed 8-way tree
+//   P3  the CTA's gate/up range is a whole number of 32-row Q8_1 blocks, so it quantises
+//       act = up * silu(gate) of its own blocks (quantize_silu_mul_q8_1 arithmetic) and writes them
+//       out; grid barrier #2; one bulk copy brings the whole quantised vector into every CTA; then
+//       the down sub-units, weighted by the route weight, the reference's fixed 8-way tree
 //       ((v0+v4)+(v2+v6))+((v1+v5)+(v3+v7)) per output row, + residual.
 // Lane work unit ("task"): one 64-weight sub-block pair (super-block sb, pair j) of a row: 32 B of
 // quants, dp4a against the Q8_1 activation, MMVQ combine of vec_dot_q4_K_q8_1 / _q5_K_
@@ -45,14 +45,16 @@ constexpr int kWarps = kConsumerWarps + 1;  // + producer
 constexpr int kThreads = kWarps * 32;
 constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kRowsPerLane = 2;  // rows a lane group computes per sub-unit (same activation registers)
-constexpr int kSubsPerGuUnit = 4;
+constexpr int kSubsPerGuUnit = 3;  // gate/up copy unit = 3 warp shares: stages sized by the down units
 constexpr int kMaxUnits = 80;
 constexpr int kMaxSubs = 256;
 constexpr int kTopK = 8;
 constexpr int kTPL = 3;  // tasks (64-weight sub-block pairs) per lane
 constexpr int kRouterRounds = (16 + kWarps - 1) / kWarps;
-// named barriers: consumers, table ready (all threads), router partials (all threads)
-constexpr int kBarConsumers = 1, kBarTable = 3, kBarRouter = 4;
+// named barriers: consumers; table ready, router partials, barrier #1 passed (all threads);
+// routing candidates ready (the eight routing warps + the producer)
+constexpr int kBarConsumers = 1, kBarTable = 3, kBarRouter = 4, kBarRoute = 5, kBarCand = 6;
+constexpr int kRouteWarps = 8;  // one expert a lane: E <= 256
 // control words in shared memory
 enum { kCtlUnits, kCtlGuUnits, kCtlSubGu, kCtlSubs, kCtlNext, kCtlPositions, kCtlOk, kCtlFail, kCtlWords };
 
@@ -169,6 +171,16 @@ __device__ __forceinline__ float row_dot(const uint8_t *row, int lig, int L, int
     return v;
 }
 
+// Distance of |y| from the nearest half-integer.  roundf(v / d) with the IEEE quotient (roundf:
+// halves away from zero), |v| <= 127 d: the product v * (1/d) is within 1.5e-5 of the quotient
+// (two roundings, |v/d| <= 127), so unless it lies within 1e-4 of a half-integer both round to the
+// same integer; only then (or for a non-finite product, from a subnormal d) is the exact quotient
+// formed, in a warp-voted branch.
+__device__ __forceinline__ float half_gap(float y) {
+    const float a = fabsf(y);
+    return fabsf((a - floorf(a)) - 0.5f);
+}
+
 // 128 consecutive values, lane l holding values 4l..4l+3 (Q8_1 blocks of 32 over 8 lanes):
 // d = amax/127, q = roundf(v/d) (quantize_q8_1, gguf.cuh:1234-1261, and quantize_silu_mul_q8_1,
 // moe_gguf.cu:255-284).  Writes q, and per block the fp16-rounded scale d and the sum of quants S.
@@ -178,11 +190,26 @@ __device__ __forceinline__ void quant128(float4 v, int8_t *q, float *d, int *S, 
     for (int m = 4; m > 0; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
     const float dd = __fdiv_rn(amax, 127.0f);
     int q0 = 0, q1 = 0, q2 = 0, q3 = 0;
+    bool exact = false;
+    float y0 = 0.f, y1 = 0.f, y2 = 0.f, y3 = 0.f;
     if (amax != 0.f) {
-        q0 = (int)roundf(__fdiv_rn(v.x, dd));
-        q1 = (int)roundf(__fdiv_rn(v.y, dd));
-        q2 = (int)roundf(__fdiv_rn(v.z, dd));
-        q3 = (int)roundf(__fdiv_rn(v.w, dd));
+        const float inv = __frcp_rn(dd);
+        y0 = v.x * inv;
+        y1 = v.y * inv;
+        y2 = v.z * inv;
+        y3 = v.w * inv;
+        q0 = (int)roundf(y0);
+        q1 = (int)roundf(y1);
+        q2 = (int)roundf(y2);
+        q3 = (int)roundf(y3);
+        exact = !(half_gap(y0) > 1e-4f) || !(half_gap(y1) > 1e-4f) || !(half_gap(y2) > 1e-4f) ||
+                !(half_gap(y3) > 1e-4f);
+    }
+    if (__any_sync(0xffffffffu, exact) && exact) {
+        if (!(half_gap(y0) > 1e-4f)) q0 = (int)roundf(__fdiv_rn(v.x, dd));
+        if (!(half_gap(y1) > 1e-4f)) q1 = (int)roundf(__fdiv_rn(v.y, dd));
+        if (!(half_gap(y2) > 1e-4f)) q2 = (int)roundf(__fdiv_rn(v.z, dd));
+        if (!(half_gap(y3) > 1e-4f)) q3 = (int)roundf(__fdiv_rn(v.w, dd));
     }
     reinterpret_cast<int *>(q)[lane] = (q0 & 0xff) | ((q1 & 0xff) << 8) | ((q2 & 0xff) << 16) | ((q3 & 0xff) << 24);
     int s = q0 + q1 + q2 + q3;
@@ -192,6 +219,37 @@ __device__ __forceinline__ void quant128(float4 v, int8_t *q, float *d, int *S, 
         d[lane >> 3] = __half2float(__float2half_rn(dd));
         S[lane >> 3] = s;
     }
+}
+
+// One Q8_1 block of 32 values, lane l holding value l: the quant128 arithmetic (d = amax/127,
+// q = roundf(v/d), fp16-rounded d, sum of quants).
+__device__ __forceinline__ void quant32(float v, int8_t *q, float *d, int *S, int lane) {
+    const float amax = warp_max_butterfly(fabsf(v));
+    const float dd = __fdiv_rn(amax, 127.0f);
+    int qi = 0;
+    bool exact = false;
+    if (amax != 0.f) {
+        const float y = v * __frcp_rn(dd);
+        qi = (int)roundf(y);
+        exact = !(half_gap(y) > 1e-4f);
+    }
+    if (__any_sync(0xffffffffu, exact) && exact) qi = (int)roundf(__fdiv_rn(v, dd));
+    q[lane] = (int8_t)qi;
+    int sq = qi;
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, m);
+    if (lane == 0) {
+        *d = __half2float(__float2half_rn(dd));
+        *S = sq;
+    }
+}
+
+// The CTA's gate/up range of (position, row) pairs: whole Q8_1 blocks of 32 rows, so that every
+// block of act is quantised by the one CTA that computed it.
+__device__ __forceinline__ void gu_range(int cta, int G, int nvs, int I, int &p0, int &p1) {
+    const int nblk = nvs * I / 32;
+    p0 = 32 * (int)((int64_t)cta * nblk / G);
+    p1 = 32 * (int)((int64_t)(cta + 1) * nblk / G);
 }
 
 // Per-task scale records from per-block (d, S) arrays: nt tasks, 2 blocks each.
@@ -240,7 +298,8 @@ __device__ __forceinline__ uint32_t sel_key(float sg, float b) {
 // Sub-unit: .x unit, .y first row within the unit | rows << 16.
 struct DecodeSmem {
     uint8_t *stages;
-    uint64_t *full, *empty;
+    uint64_t *full;
+    uint64_t *abar;            // the quantised act copy after barrier #2
     int8_t *xq;                // [H]
     float *xd;                 // [H/32]
     int *xS;                   // [H/32]
@@ -250,6 +309,8 @@ struct DecodeSmem {
     int *aS_s;                 // [8][I/32]
     float4 *ats;               // [8][I/64]
     float *part;               // router slice sums [2][8]
+    float *sig;                // [E] sigmoid of the router logits
+    uint32_t *cand;            // [2][64] routing candidates: keys, then expert ids
     int *ids;                  // [8] expert of each slot (-1: none, or another rank's)
     int *vslot;                // [8] slot of each position (the computed slots in order)
     float *w;                  // [8]
@@ -259,12 +320,17 @@ struct DecodeSmem {
     int4 *units;               // [kMaxUnits]
     int *unit_off;             // [kMaxUnits] first row of a gate/up unit in the CTA's range
     int *unit_nsub;            // [kMaxUnits] sub-units of the unit
+    const uint8_t **usrc;      // [kMaxUnits] global source of the unit's copy
+    uint32_t *ubytes;          // [kMaxUnits] its size
     int2 *subs;                // [kMaxSubs]
     int *ticket;               // [stages] unit last issued into each stage
     int *done;                 // [stages] sub-units of the stage's unit finished
     int *ctl;                  // [kCtlWords]
 };
 
+// GU / DN: GGUF types of the gate/up and down matrices (one instantiation per pair keeps each
+// launched kernel's code to the dot products it runs).
+template <int GU, int DN>
 __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __grid_constant__ DecodeParams p) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -310,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         };
         s.stages = take((size_t)p.stages * p.stage_bytes);
         s.full = reinterpret_cast<uint64_t *>(take(sizeof(uint64_t) * p.stages));
-        s.empty = reinterpret_cast<uint64_t *>(take(sizeof(uint64_t) * p.stages));
+        s.abar = reinterpret_cast<uint64_t *>(take(sizeof(uint64_t)));
         s.xq = reinterpret_cast<int8_t *>(take(H));
         s.xd = reinterpret_cast<float *>(take(sizeof(float) * (H / 32)));
         s.xS = reinterpret_cast<int *>(take(sizeof(int) * (H / 32)));
@@ -320,6 +386,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         s.aS_s = reinterpret_cast<int *>(take(sizeof(int) * kTopK * (I / 32)));
         s.ats = reinterpret_cast<float4 *>(take(sizeof(float4) * kTopK * (I / 64)));
         s.part = reinterpret_cast<float *>(take(sizeof(float) * 16));
+        s.sig = reinterpret_cast<float *>(take(sizeof(float) * 256));
+        s.cand = reinterpret_cast<uint32_t *>(take(sizeof(uint32_t) * 128));
         s.ids = reinterpret_cast<int *>(take(sizeof(int) * kTopK));
         s.vslot = reinterpret_cast<int *>(take(sizeof(int) * kTopK));
         s.w = reinterpret_cast<float *>(take(sizeof(float) * kTopK));
@@ -330,6 +398,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         s.units = reinterpret_cast<int4 *>(take(sizeof(int4) * kMaxUnits));
         s.unit_off = reinterpret_cast<int *>(take(sizeof(int) * kMaxUnits));
         s.unit_nsub = reinterpret_cast<int *>(take(sizeof(int) * kMaxUnits));
+        s.usrc = reinterpret_cast<const uint8_t **>(take(sizeof(void *) * kMaxUnits));
+        s.ubytes = reinterpret_cast<uint32_t *>(take(sizeof(uint32_t) * kMaxUnits));
         s.subs = reinterpret_cast<int2 *>(take(sizeof(int2) * kMaxSubs));
         s.ticket = reinterpret_cast<int *>(take(sizeof(int) * p.stages));
         s.done = reinterpret_cast<int *>(take(sizeof(int) * p.stages));
@@ -345,10 +415,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     if (tid == 0) {
         for (int i = 0; i < p.stages; ++i) {
             mbar_init(&s.full[i], 1);
-            mbar_init(&s.empty[i], 1);
             s.ticket[i] = -1;
             s.done[i] = 0;
         }
+        mbar_init(s.abar, 1);
         fence_mbar_init();
         for (int i = 0; i < kCtlWords; ++i) s.ctl[i] = 0;
     }
@@ -394,6 +464,22 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     const int Lg = p.gu_lanes, Ld = p.dn_lanes;
     const int gu_sub = p.gu_sub_rows, dn_sub = p.dn_sub_rows, U_gu = p.gu_unit_rows;
 
+    // Issue copy unit k into ring stage k % stages (one thread).  The first `stages` units are
+    // issued by the producer warp once the table is built; every later unit by the warp that
+    // finishes the last sub-unit of unit k - stages, which frees that stage.
+    auto issue = [&](int k) {
+        const int st = k % p.stages;
+        *reinterpret_cast<volatile int *>(&s.ticket[st]) = k;
+        const uint32_t bytes = s.ubytes[k];
+        if (p.trace) {
+            if (k == 0) p.trace[cta * 16 + 8] = globaltimer_ns();
+            if (k == s.ctl[kCtlGuUnits]) p.trace[cta * 16 + 10] = globaltimer_ns();
+            if (k == s.ctl[kCtlUnits] - 1) p.trace[cta * 16 + 9] = globaltimer_ns();
+        }
+        mbar_arrive_expect_tx_sink(&s.full[st], bytes);
+        bulk_g2s(s.stages + (size_t)st * p.stage_bytes, s.usrc[k], bytes, &s.full[st]);
+    };
+
     if (warp == kProducerWarp) {
         // ================================ producer warp ===================================
         bool ok = true;
@@ -411,50 +497,33 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             if (p.trace) p.trace[cta * 16 + 2] = globaltimer_ns();
         }
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        // ---- routing: lane l holds experts l + 32 i ------------------------------------------
+        if (lane == 0) s.ctl[kCtlOk] = ok ? 1 : 0;
+        __syncwarp();
+        named_arrive(kBarRoute, kThreads);  // barrier #1 passed: the routing warps may read the logits
+        named_sync(kBarCand, 32 * (kRouteWarps + 1));
+        // ---- merge of the routing warps' candidates (8 per warp, each warp's in rank order) --------
         int slot_id = -1;  // lane k < 8: expert of slot k
         float slot_w = 0.f;
         if (p.internal_routing) {
             if (ok) {
-                uint32_t key[8];
-                float sg[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int e = lane + 32 * i;
-                    key[i] = 0u;  // experts >= E are never selected (E >= 8 real keys are > 0)
-                    sg[i] = 0.f;
-                    if (e < E) {
-                        const float l = __ldcg(p.logits + e);
-                        sg[i] = __fdiv_rn(1.0f, 1.0f + expf(-l));
-                        key[i] = sel_key(sg[i], __ldg(p.bias + e));
-                    }
-                }
-                // stable descending order of the score: larger key first, lower expert id on ties
-                uint32_t taken = 0u;
-                float my_sig = 0.f;
+                const int nc = 8 * ((E + 31) / 32);
+                const uint32_t ka = lane < nc ? s.cand[lane] : 0u, ia = lane < nc ? s.cand[64 + lane] : 0xffffffffu;
+                const uint32_t kb = lane + 32 < nc ? s.cand[lane + 32] : 0u;
+                const uint32_t ib = lane + 32 < nc ? s.cand[64 + lane + 32] : 0xffffffffu;
+                bool ta = false, tb = false;
 #pragma unroll
                 for (int k = 0; k < kTopK; ++k) {
-                    uint32_t bk = 0u;
-                    int bi = 0;
-                    float bs = 0.f;
-#pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        if (!(taken & (1u << i)) && key[i] > bk) {
-                            bk = key[i];
-                            bi = i;
-                            bs = sg[i];
-                        }
-                    const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
-                    const uint32_t mine = (uint32_t)(lane + 32 * bi);
-                    const uint32_t me = __reduce_min_sync(0xffffffffu, bk == mk ? mine : 0xffffffffu);
-                    if (mine == me) taken |= 1u << bi;
-                    const float sme = __shfl_sync(0xffffffffu, bs, (int)(me & 31u));
-                    if (lane == k) {
-                        slot_id = (int)me;
-                        my_sig = sme;
-                    }
+                    // larger key first, lower expert id among equal keys (the stable descending order)
+                    const uint32_t mk = __reduce_max_sync(0xffffffffu, max(ta ? 0u : ka, tb ? 0u : kb));
+                    const uint32_t ca = (!ta && ka == mk) ? ia : 0xffffffffu;
+                    const uint32_t cb = (!tb && kb == mk) ? ib : 0xffffffffu;
+                    const uint32_t me = __reduce_min_sync(0xffffffffu, min(ca, cb));
+                    if (ca == me) ta = true;
+                    else if (cb == me) tb = true;
+                    if (lane == k) slot_id = (int)me;
                 }
                 // weights: sig / ((v0+v4)+(v2+v6))+((v1+v5)+(v3+v7)), lane k keeps w_k
+                const float my_sig = lane < kTopK ? s.sig[slot_id] : 0.f;
                 float v[kTopK];
 #pragma unroll
                 for (int k = 0; k < kTopK; ++k) v[k] = __shfl_sync(0xffffffffu, my_sig, k);
@@ -502,8 +571,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             s.w[lane] = slot_w;
             if (keep) s.vslot[__popc(kept & ((1u << lane) - 1u))] = lane;
         }
+        __syncwarp();
         // ---- copy table: lane c computes gate/up chunk c of the CTA's (position, row) range --
-        const int gu_p0 = (int)((int64_t)cta * nvs * I / G), gu_p1 = (int)((int64_t)(cta + 1) * nvs * I / G);
+        int gu_p0, gu_p1;
+        gu_range(cta, G, nvs, I, gu_p0, gu_p1);
         int n_chunks = 0, c_left = lane, my_pos = -1, my_row0 = 0, my_n = 0, my_off = 0;
         for (int pos = gu_p0 / I, q = gu_p0; q < gu_p1; ++pos) {
             const int seg_end = min(gu_p1, (pos + 1) * I);
@@ -535,6 +606,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
                 s.units[k] = make_int4(h, my_pos, my_row0, my_n);
                 s.unit_off[k] = my_off;
                 s.unit_nsub[k] = ns;
+                const int e = s.ids[s.vslot[my_pos]];
+                s.usrc[k] = (h == 0 ? p.gate : p.up) + (size_t)e * gu_expert_bytes + (size_t)my_row0 * gu_row_bytes;
+                s.ubytes[k] = (uint32_t)(gu_row_bytes * my_n);
                 for (int j = 0; j < ns; ++j) {
                     const int r0 = j * gu_sub;
                     s.subs[base + h * ns + j] = make_int2(k, r0 | (min(gu_sub, my_n - r0) << 16));
@@ -549,6 +623,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             s.units[k] = make_int4(2, lane, dn_r0, nres);
             s.unit_off[k] = 0;
             s.unit_nsub[k] = nsd;
+            const int e = s.ids[s.vslot[lane]];
+            s.usrc[k] = p.down + (size_t)e * dn_expert_bytes + (size_t)dn_r0 * dn_row_bytes;
+            s.ubytes[k] = (uint32_t)(dn_row_bytes * nres);
             for (int j = 0; j < nsd; ++j) {
                 const int r0 = j * dn_sub;
                 s.subs[n_sub_gu + lane * nsd + j] = make_int2(k, r0 | (min(dn_sub, nres - r0) << 16));
@@ -565,38 +642,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         }
         __syncwarp();
         named_arrive(kBarTable, kThreads);  // table complete: the consumers may claim
-        // ---- issue loop (lane 0) ----------------------------------------------------------------
+        __syncwarp();
+        // ---- first ring fill (lane 0); later units are issued by the consumer warps -------------
         if (lane == 0 && ok) {
-            const int n = n_gu_units + n_dn_units;
-            int k = 0;
-            for (; k < n; ++k) {
-                const int st = k % p.stages;
-                if (!mbar_wait_sleep(&s.empty[st], ((uint32_t)(k / p.stages) & 1u) ^ 1u, deadline)) {
-                    atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
-                    break;
-                }
-                *reinterpret_cast<volatile int *>(&s.ticket[st]) = k;
-                const int4 u = s.units[k];
-                const int e = s.ids[s.vslot[u.y]];
-                const uint8_t *src;
-                uint32_t bytes;
-                if (u.x == 2) {
-                    src = p.down + (size_t)e * dn_expert_bytes + (size_t)u.z * dn_row_bytes;
-                    bytes = (uint32_t)(dn_row_bytes * u.w);
-                } else {
-                    src = (u.x == 0 ? p.gate : p.up) + (size_t)e * gu_expert_bytes + (size_t)u.z * gu_row_bytes;
-                    bytes = (uint32_t)(gu_row_bytes * u.w);
-                }
-                if (k == 0 && p.trace) p.trace[cta * 16 + 8] = globaltimer_ns();
-                if (k == n_gu_units && p.trace) p.trace[cta * 16 + 10] = globaltimer_ns();
-                mbar_arrive_expect_tx_sink(&s.full[st], bytes);
-                bulk_g2s(s.stages + (size_t)st * p.stage_bytes, src, bytes, &s.full[st]);
-            }
-            if (p.trace) p.trace[cta * 16 + 9] = globaltimer_ns();
-            // Drain: no copy may still be landing in shared memory when the CTA retires.
-            const int first = k > p.stages ? k - p.stages : 0;
-            for (int j = first; j < k; ++j)
-                mbar_wait_bounded(&s.full[j % p.stages], (uint32_t)(j / p.stages) & 1u, deadline + 1000000000ull);
+            const int n = min(n_gu_units + n_dn_units, p.stages);
+            for (int k = 0; k < n; ++k) issue(k);
         }
         return;
     }
@@ -614,23 +664,51 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         named_sync(kBarConsumers, kConsumerThreads);
         build_task_scales(s.xts, s.xd, s.xS, H / 64, tid, kConsumerThreads);
     }
+    named_sync(kBarRoute, kThreads);  // grid barrier #1 passed (the producer polled it)
+    if (warp < kRouteWarps) {
+        // sigmoid, selection score as an order-preserving key, and this warp's top-8 of its 32
+        // experts by rounds of redux max (key) and redux min (id among the lanes holding it)
+        const int e = 32 * warp + lane;
+        if (p.internal_routing && s.ctl[kCtlOk] && 32 * warp < E) {
+            uint32_t key = 0u;  // experts >= E are never selected (E >= 8 real keys are > 0)
+            if (e < E) {
+                const float sg = __fdiv_rn(1.0f, 1.0f + expf(-__ldcg(p.logits + e)));
+                s.sig[e] = sg;
+                key = sel_key(sg, __ldg(p.bias + e));
+            }
+            bool taken = false;
+#pragma unroll
+            for (int k = 0; k < kTopK; ++k) {
+                const uint32_t mk = __reduce_max_sync(0xffffffffu, taken ? 0u : key);
+                const uint32_t me = __reduce_min_sync(0xffffffffu, (!taken && key == mk) ? (uint32_t)e : 0xffffffffu);
+                taken |= (uint32_t)e == me;
+                if (lane == 0) {
+                    s.cand[8 * warp + k] = mk;
+                    s.cand[64 + 8 * warp + k] = me;
+                }
+            }
+        }
+        named_arrive(kBarCand, 32 * (kRouteWarps + 1));
+    }
     named_sync(kBarTable, kThreads);
     const bool ok1 = s.ctl[kCtlOk] != 0;
     const int n_sub_gu = s.ctl[kCtlSubGu], n_sub = s.ctl[kCtlSubs], nvs = s.ctl[kCtlPositions];
+    const int n_units = s.ctl[kCtlUnits];
     bool aborted = !ok1;
     auto claim = [&]() -> int {
         int v = 0;
         if (lane == 0) v = atomicAdd(&s.ctl[kCtlNext], 1);
         return __shfl_sync(0xffffffffu, v, 0);
     };
-    // A warp that finished a sub-unit of unit k: the last finisher frees the unit's stage.
+    // A warp that finished a sub-unit of unit k: the last finisher (its acquire covers the other
+    // warps' reads of the stage) issues unit k + stages into the freed stage.
     auto finish = [&](int k, int st) {
         __syncwarp();
         if (lane == 0) {
             const int old = atom_add_acq_rel_cta(&s.done[st], 1);
             if (old + 1 == s.unit_nsub[k]) {
                 s.done[st] = 0;
-                mbar_arrive(&s.empty[st]);
+                if (k + p.stages < n_units && !aborted) issue(k + p.stages);
             }
         }
     };
@@ -657,13 +735,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
                 const uint8_t *base = s.stages + (size_t)st * p.stage_bytes;
                 const uint8_t *rowA = base + (size_t)rA * gu_row_bytes;
                 const uint8_t *rowB = base + (size_t)min(rB, rend - 1) * gu_row_bytes;
-                if (p.gu_type == MMRS_Q5K) {
-                    vA = row_dot<MMRS_Q5K>(rowA, lig, Lg, ntasks, ta);
-                    vB = row_dot<MMRS_Q5K>(rowB, lig, Lg, ntasks, ta);
-                } else {
-                    vA = row_dot<MMRS_Q4K>(rowA, lig, Lg, ntasks, ta);
-                    vB = row_dot<MMRS_Q4K>(rowB, lig, Lg, ntasks, ta);
-                }
+                vA = row_dot<GU>(rowA, lig, Lg, ntasks, ta);
+                vB = row_dot<GU>(rowB, lig, Lg, ntasks, ta);
             }
 #pragma unroll
             for (int m = 16; m > 0; m >>= 1)
@@ -681,16 +754,21 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         }
     }
 
-    // ---- P3: act of the CTA's range to global memory, grid barrier #2 -------------------------
+    // ---- P3: Q8_1 of act for the CTA's blocks, grid barrier #2, copy of the whole vector ---------
     named_sync(kBarConsumers, kConsumerThreads);  // every gate/up sub-unit of this CTA is done
     if (tid == 0 && p.trace) p.trace[cta * 16 + 4] = globaltimer_ns();
     {
-        const int gu_p0 = (int)((int64_t)cta * nvs * I / G), gu_p1 = (int)((int64_t)(cta + 1) * nvs * I / G);
+        int gu_p0, gu_p1;
+        gu_range(cta, G, nvs, I, gu_p0, gu_p1);
         for (int i = tid; i < gu_p1 - gu_p0; i += kConsumerThreads) {
             const float gv = s.gval[i];
-            // act = up * silu(gate) (moe_gguf.cu:272-273)
-            p.act[gu_p0 + i] = aborted ? 0.f : s.uval[i] * __fdiv_rn(gv, 1.0f + expf(-gv));
+            // act = up * silu(gate) (moe_gguf.cu:272-273), in place of the gate values
+            s.gval[i] = s.uval[i] * __fdiv_rn(gv, 1.0f + expf(-gv));
         }
+        named_sync(kBarConsumers, kConsumerThreads);
+        // quantize_silu_mul_q8_1 (moe_gguf.cu:255-284): one warp per block of 32 rows
+        for (int b = gu_p0 / 32 + warp; b < gu_p1 / 32 && !aborted; b += kConsumerWarps)
+            quant32(s.gval[32 * b - gu_p0 + lane], p.aq + 32 * b, p.ad + b, p.aS + b, lane);
     }
     named_sync(kBarConsumers, kConsumerThreads);
     if (tid == 0) {
@@ -705,34 +783,31 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
                 ok2 = false;
             }
         }
-        s.ctl[kCtlFail] = ok2 ? 0 : 1;
         if (ok2) p.ctl->epoch[cta] = epoch + 2u;  // read again only by this CTA's next launch
         if (p.trace) p.trace[cta * 16 + 5] = globaltimer_ns();
+        // the whole quantised act [positions][I] (+ scales, sums) in one bulk copy per array; the
+        // other CTAs' generic writes are ordered before these async-proxy reads
+        bool copied = false;
+        if (ok2 && nvs > 0) {
+            const uint32_t qb = (uint32_t)(nvs * I), sb = (uint32_t)(sizeof(float) * nvs * (I / 32));
+            asm volatile("fence.proxy.async;" ::: "memory");
+            mbar_arrive_expect_tx(s.abar, qb + 2 * sb);
+            bulk_g2s(s.aq_s, p.aq, qb, s.abar);
+            bulk_g2s(s.ad_s, p.ad, sb, s.abar);
+            bulk_g2s(s.aS_s, p.aS, sb, s.abar);
+            copied = true;
+        }
+        if (copied && !mbar_wait_bounded(s.abar, 0u, deadline + 1000000000ull)) {
+            atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
+            ok2 = false;
+        }
+        s.ctl[kCtlFail] = ok2 ? 0 : 1;
     }
     named_sync(kBarConsumers, kConsumerThreads);
     if (s.ctl[kCtlFail]) aborted = true;
-    // Every CTA quantises the whole act vector: 128 values per warp step (one float4 a lane),
-    // all of a warp's loads in flight before its first block is quantised.
-    {
-        const int nchunk = nvs * I / 128;
-        constexpr int kLd = 8;
-        for (int c0 = warp * kLd; c0 < nchunk; c0 += kConsumerWarps * kLd) {
-            float4 v[kLd];
-#pragma unroll
-            for (int j = 0; j < kLd; ++j)
-                v[j] = (c0 + j < nchunk && !aborted) ? __ldcg(reinterpret_cast<const float4 *>(p.act) + (c0 + j) * 32 + lane)
-                                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int j = 0; j < kLd; ++j) {
-                const int c = c0 + j;
-                if (c < nchunk) quant128(v[j], s.aq_s + c * 128, s.ad_s + c * 4, s.aS_s + c * 4, lane);
-            }
-        }
-        named_sync(kBarConsumers, kConsumerThreads);
-        build_task_scales(s.ats, s.ad_s, s.aS_s, nvs * (I / 64), tid, kConsumerThreads);
-        named_sync(kBarConsumers, kConsumerThreads);
-        if (tid == 0 && p.trace) p.trace[cta * 16 + 6] = globaltimer_ns();
-    }
+    build_task_scales(s.ats, s.ad_s, s.aS_s, nvs * (I / 64), tid, kConsumerThreads);
+    named_sync(kBarConsumers, kConsumerThreads);
+    if (tid == 0 && p.trace) p.trace[cta * 16 + 6] = globaltimer_ns();
 
     // ---- P3: down sub-units -------------------------------------------------------------------
     {
@@ -760,13 +835,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
                 const uint8_t *base = s.stages + (size_t)st * p.stage_bytes;
                 const uint8_t *rowA = base + (size_t)rA * dn_row_bytes;
                 const uint8_t *rowB = base + (size_t)min(rB, rend - 1) * dn_row_bytes;
-                if (p.dn_type == MMRS_Q5K) {
-                    vA = row_dot<MMRS_Q5K>(rowA, lig, Ld, ntasks, ta);
-                    vB = row_dot<MMRS_Q5K>(rowB, lig, Ld, ntasks, ta);
-                } else {
-                    vA = row_dot<MMRS_Q4K>(rowA, lig, Ld, ntasks, ta);
-                    vB = row_dot<MMRS_Q4K>(rowB, lig, Ld, ntasks, ta);
-                }
+                vA = row_dot<DN>(rowA, lig, Ld, ntasks, ta);
+                vB = row_dot<DN>(rowB, lig, Ld, ntasks, ta);
             }
 #pragma unroll
             for (int m = 16; m > 0; m >>= 1)
@@ -841,6 +911,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             p.y[row] = y;
         }
     }
+    // No copy may still be landing in shared memory when the CTA retires (after an expired wait
+    // a unit may have been issued and never waited for).
+    if (tid == 0 && ok1) {
+        for (int st = 0; st < p.stages; ++st) {
+            const int k = *reinterpret_cast<volatile int *>(&s.ticket[st]);
+            if (k >= 0) mbar_wait_bounded(&s.full[st], (uint32_t)(k / p.stages) & 1u, deadline + 1000000000ull);
+        }
+    }
     if (tid == 0 && p.trace) p.trace[cta * 16 + 7] = globaltimer_ns();
 }
 
@@ -849,12 +927,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
 // ------------------------------------------------------------------------------------------
 size_t decode_smem_bytes(const DecodeParams &p) {
     auto a16 = [](size_t v) { return (v + 15) / 16 * 16; };
-    size_t b = a16((size_t)p.stages * p.stage_bytes) + 2 * a16(sizeof(uint64_t) * p.stages);
+    size_t b = a16((size_t)p.stages * p.stage_bytes) + a16(sizeof(uint64_t) * p.stages) + a16(sizeof(uint64_t));
     b += a16(p.H) + 2 * a16(4 * (p.H / 32)) + a16(16 * (p.H / 64));
     b += a16((size_t)kTopK * p.I) + 2 * a16(4 * kTopK * (p.I / 32)) + a16(16 * kTopK * (p.I / 64));
-    b += a16(4 * 16) + 3 * a16(4 * kTopK);  // part, ids, vslot, w
+    b += a16(4 * 16) + a16(4 * 256) + a16(4 * 128) + 3 * a16(4 * kTopK);  // part, sig, cand, ids, vslot, w
     b += a16(4 * (size_t)p.res_slots * kTopK) + 2 * a16(4 * (size_t)p.act_slots) + a16(4 * (size_t)p.res_slots);
-    b += a16(16 * kMaxUnits) + 2 * a16(4 * kMaxUnits) + a16(8 * kMaxSubs);
+    b += a16(16 * kMaxUnits) + 2 * a16(4 * kMaxUnits) + a16(8 * kMaxUnits) + a16(4 * kMaxUnits) + a16(8 * kMaxSubs);
     b += 2 * a16(4 * (size_t)p.stages) + a16(4 * kCtlWords);
     return b;
 }
@@ -874,11 +952,11 @@ int decode_configure(DecodeParams &p, int num_sms, int max_smem) {
     p.gu_lanes = pow2_at_least((gu_tasks + kTPL - 1) / kTPL);
     p.dn_lanes = pow2_at_least((dn_tasks + kTPL - 1) / kTPL);
     if (p.gu_lanes > 32 || p.dn_lanes > 32) return MMRS_ERR_UNSUPPORTED;  // H, I <= 6144
-    // one warp's share: (32 / L) lane groups x 2 rows; a gate/up copy unit is four shares
+    // one warp's share: (32 / L) lane groups x 2 rows; a gate/up copy unit is three shares
     p.gu_sub_rows = (32 / p.gu_lanes) * kRowsPerLane;
     p.dn_sub_rows = (32 / p.dn_lanes) * kRowsPerLane;
     p.gu_unit_rows = kSubsPerGuUnit * p.gu_sub_rows;
-    p.act_slots = (kTopK * p.I + num_sms - 1) / num_sms + 1;
+    p.act_slots = 32 * ((kTopK * p.I / 32 + num_sms - 1) / num_sms) + 1;  // whole Q8_1 blocks a CTA
     p.res_slots = (p.H + num_sms - 1) / num_sms + 1;
     if (p.E > 2 * num_sms || num_sms > kMaxGridCtas) return MMRS_ERR_UNSUPPORTED;
     // table bounds: a CTA's gate/up chunks (one lane each; each slot boundary may add one), units
@@ -905,10 +983,10 @@ int decode_configure(DecodeParams &p, int num_sms, int max_smem) {
     return MMRS_OK;
 }
 
-int decode_launch(const DecodeParams &p, cudaStream_t stream) {
-    const size_t smem = decode_smem_bytes(p);
-    // Raise the dynamic shared-memory limit once per device (the attribute is per context);
-    // call_once keeps concurrent host threads from racing on it.
+template <int GU, int DN>
+static int launch_typed(const DecodeParams &p, size_t smem, cudaStream_t stream) {
+    // Raise the dynamic shared-memory limit once per device and instantiation (the attribute is
+    // per context); call_once keeps concurrent host threads from racing on it.
     static std::once_flag once[64];
     static cudaError_t set_rc[64];
     int dev = 0;
@@ -916,7 +994,8 @@ int decode_launch(const DecodeParams &p, cudaStream_t stream) {
     std::call_once(once[dev], [dev] {
         int optin = 0;
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-        set_rc[dev] = cudaFuncSetAttribute(moe_decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+        set_rc[dev] =
+            cudaFuncSetAttribute(moe_decode_fused_kernel<GU, DN>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
     });
     if (set_rc[dev] != cudaSuccess) return MMRS_ERR_LAUNCH;
     cudaLaunchConfig_t cfg = {};
@@ -929,8 +1008,15 @@ int decode_launch(const DecodeParams &p, cudaStream_t stream) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t err = cudaLaunchKernelEx(&cfg, moe_decode_fused_kernel, p);
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, moe_decode_fused_kernel<GU, DN>, p);
     return err == cudaSuccess ? MMRS_OK : MMRS_ERR_LAUNCH;
+}
+
+int decode_launch(const DecodeParams &p, cudaStream_t stream) {
+    const size_t smem = decode_smem_bytes(p);
+    const bool g5 = p.gu_type == MMRS_Q5K, d5 = p.dn_type == MMRS_Q5K;
+    if (g5) return d5 ? launch_typed<MMRS_Q5K, MMRS_Q5K>(p, smem, stream) : launch_typed<MMRS_Q5K, MMRS_Q4K>(p, smem, stream);
+    return d5 ? launch_typed<MMRS_Q4K, MMRS_Q5K>(p, smem, stream) : launch_typed<MMRS_Q4K, MMRS_Q4K>(p, smem, stream);
 }
 
 }  // namespace mmrs
