@@ -93,22 +93,21 @@ __global__ void __launch_bounds__(256) decode_topk_kernel(const float *__restric
 }
 
 // ------------------------------------------------------------------------------------------
-// Workspace layout of the fused block: [GridBarrier 256 B][logits E f32][act 8*I f32]
+// Workspace layout of the fused block
 // ------------------------------------------------------------------------------------------
 constexpr int kTraceCtas = 256, kTraceSlots = 16;
 constexpr size_t kTraceOffset = kControlBytes;
+static_assert(sizeof(DecodeCtl) <= kControlBytes, "the decode control block lies in the zeroed control bytes");
 static size_t up256(size_t v) { return (v + 255) / 256 * 256; }
-// [control block: status + per-CTA barrier flags (zero before first use)] | trace |
-// per-block counters (zeroed by the kernel) | logits | act | aq | ad | aS
+// [control block (DecodeCtl, zero before first use)] | trace | act | aq | ad | aS
 WsLayout ws_layout(int E, int I, int max_tokens) {
+    (void)E;
     (void)max_tokens;
     WsLayout l;
     const size_t nblk = (size_t)8 * I / 32;
     l.ctl = 0;
     l.trace = kTraceOffset;
-    l.blk_count = l.trace + sizeof(uint64_t) * kTraceCtas * kTraceSlots;
-    l.logits = l.blk_count + up256(nblk * 4);
-    l.act = l.logits + up256((size_t)E * 4);
+    l.act = l.trace + sizeof(uint64_t) * kTraceCtas * kTraceSlots;
     l.aq = l.act + up256((size_t)8 * I * 4);
     l.ad = l.aq + up256((size_t)8 * I);
     l.aS = l.ad + up256(nblk * 4);
@@ -117,10 +116,8 @@ WsLayout ws_layout(int E, int I, int max_tokens) {
 }
 
 void ws_bind(DecodeParams &p, uint8_t *ws, const WsLayout &l) {
-    p.ctl = reinterpret_cast<GridFlags *>(ws + l.ctl);
-    p.blk_count = reinterpret_cast<uint32_t *>(ws + l.blk_count);
+    p.ctl = reinterpret_cast<DecodeCtl *>(ws + l.ctl);
     p.trace = reinterpret_cast<uint64_t *>(ws + l.trace);
-    p.logits = reinterpret_cast<float *>(ws + l.logits);
     p.act = reinterpret_cast<float *>(ws + l.act);
     p.aq = reinterpret_cast<int8_t *>(ws + l.aq);
     p.ad = reinterpret_cast<float *>(ws + l.ad);

@@ -14,21 +14,28 @@
 //       eight warps then take 32 experts each (sigmoid, order-preserving selection key, rounds of
 //       redux max / min: that warp's top-8) and the producer warp merges the 64 candidates the same
 //       way, renormalises the weights and builds the copy table with its 32 lanes.
-//   P2  gate/up: the CTA owns a contiguous range of (slot, row) pairs; copy units of up to three
-//       warp shares of rows of the gate or the up matrix (one bulk copy each) stream through a
-//       ring of shared-memory stages.  Consumer warps claim sub-units (one warp's rows) in unit
-//       order from a CTA counter, so a free warp always takes the oldest unclaimed rows; the last
-//       finisher of a unit frees its stage.  The producer issues every unit as soon as its stage
-//       is free, so the down units (this CTA's output rows of one expert: one contiguous copy
-//       each) land in the ring while gate/up is still being computed.
-//   P3  the CTA's gate/up range is a whole number of 32-row Q8_1 blocks, so it quantises
-//       act = up * silu(gate) of its own blocks (quantize_silu_mul_q8_1 arithmetic) and writes them
-//       out; grid barrier #2; one bulk copy brings the whole quantised vector into every CTA; then
-//       the down sub-units, weighted by the route weight, the reference's fixed 8-way tree
-//       ((v0+v4)+(v2+v6))+((v1+v5)+(v3+v7)) per output row, + residual.
-// Lane work unit ("task"): one 64-weight sub-block pair (super-block sb, pair j) of a row: 32 B of
-// quants, dp4a against the Q8_1 activation, MMVQ combine of vec_dot_q4_K_q8_1 / _q5_K_
-// (gguf.cuh:727-750, 783-813): dall * sum d8*(dot*sc) - dmin * sum d8*sum(q8)*m.
+//   P2  gate/up: the CTA owns a contiguous range of (slot, row) pairs; copy units of rows of the
+//       gate or the up matrix (one bulk copy each) stream through a ring of shared-memory stages.
+//       Consumer lane t keeps the activation of x super-block t % (H/256) in registers for the
+//       whole phase and computes that block of rows t / (H/256), + slots, ... in unit order; the
+//       per-block partial sums go to shared memory.  Per unit, warp-aggregated counters find the
+//       lane that completes it, which frees its stage and issues the unit `stages` later into it,
+//       so the down units (this CTA's output rows of one expert: one contiguous copy each) land
+//       in the ring while gate/up is still being computed.
+//   P3  the CTA's gate/up range is a whole number of 32-row Q8_1 blocks, so it sums the block
+//       partials, quantises act = up * silu(gate) of its own blocks (quantize_silu_mul_q8_1
+//       arithmetic) and writes them out; grid barrier #2; one bulk copy brings the whole quantised
+//       vector into every CTA; lane t takes one (position, super-block) pair of the down rows and
+//       rows t / pairs, + slots, ...; then per output row the block partials of each expert, weighted
+//       by the route weight, the reference's fixed 8-way tree ((v0+v4)+(v2+v6))+((v1+v5)+(v3+v7)),
+//       + residual.
+// Lane work unit: one 256-weight super-block of a row against the lane's register copy of the
+// matching activation block: per 64-weight sub-block pair, dp4a over 32 B of quants and the MMVQ
+// combine of vec_dot_q4_K_q8_1 / _q5_K_ (gguf.cuh:727-750, 783-813):
+// dall * sum d8*(dot*sc) - dmin * sum d8*sum(q8)*m.  Integer work is the bound (the integer pipes
+// issue at half the FP32 rate), so the pair index is a compile-time constant (fixed shifts and
+// scale selection), the block header and fifth bits are loaded once per block, and activations
+// are stored swizzled so that a quarter warp's block loads hit distinct banks.
 // Every wait is bounded by a globaltimer deadline; on expiry the kernel records MMRS_ERR_TIMEOUT in
 // the workspace status word, keeps every named barrier matched, drains its copies and returns.
 #include <mutex>
@@ -44,26 +51,22 @@ constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kWarps = kConsumerWarps + 1;  // + producer
 constexpr int kThreads = kWarps * 32;
 constexpr int kProducerWarp = kConsumerWarps;
-constexpr int kRowsPerLane = 2;  // rows a lane group computes per sub-unit (same activation registers)
-constexpr int kSubsPerGuUnit = 3;  // gate/up copy unit = 3 warp shares: stages sized by the down units
 constexpr int kMaxUnits = 80;
-constexpr int kMaxSubs = 256;
 constexpr int kTopK = 8;
-constexpr int kTPL = 3;  // tasks (64-weight sub-block pairs) per lane
 constexpr int kRouterRounds = (16 + kWarps - 1) / kWarps;
-// named barriers: consumers; table ready, router partials, barrier #1 passed (all threads);
-// routing candidates ready (the eight routing warps + the producer)
-constexpr int kBarConsumers = 1, kBarTable = 3, kBarRouter = 4, kBarRoute = 5, kBarCand = 6;
+// named barriers: consumers; table ready, router partials (all threads); routing candidates
+// ready (the eight routing warps + the producer)
+constexpr int kBarConsumers = 1, kBarTable = 3, kBarRouter = 4, kBarCand = 6;
 constexpr int kRouteWarps = 8;  // one expert a lane: E <= 256
 // control words in shared memory
-enum { kCtlUnits, kCtlGuUnits, kCtlSubGu, kCtlSubs, kCtlNext, kCtlPositions, kCtlOk, kCtlFail, kCtlWords };
+enum { kCtlUnits, kCtlGuUnits, kCtlGuRows, kCtlPositions, kCtlOk, kCtlFail, kCtlWords };
 
-// Q8_1 activation in shared memory: q int8 [K] and, per 64-element pair (task), the float4
-// {d8 lo block, d8 hi block, d8*sum(q) lo, d8*sum(q) hi}.
-struct ActView {
-    const int8_t *q;
-    const float4 *ts;
-};
+// Q8_1 activations in shared memory are stored swizzled: the 16-byte chunk k of a 256-value block B
+// (B counted from the start of the vector, over all positions) sits at chunk slot k ^ (B & 7), so
+// that the lanes of a quarter warp, each reading a whole block of a different B, hit distinct banks.
+__device__ __forceinline__ int act_swz(int o) {
+    return (o & ~0xff) | ((((o >> 4) & 15) ^ ((o >> 8) & 7)) << 4) | (o & 15);
+}
 
 // a: unsigned bytes, b: signed bytes.
 __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
@@ -85,89 +88,121 @@ __device__ __forceinline__ void scale_pair(const uint4 &hdr, int j, uint32_t &sc
     }
 }
 
-// Per-lane register copy of one task's activation: 64 int8 (lo block, hi block) and the scale
+// A lane's register copy of the activation of one 256-value block: 64 int8 x 4 as 64 ints (pair
+// j: ints 16j..16j+7 the low sub-block 2j, 16j+8..16j+15 the high one) and per pair the scale
 // record {d8 lo, d8 hi, d8*sum(q) lo, d8*sum(q) hi}.
-struct TaskAct {
-    int lo[8], hi[8];
-    float4 ts;
+struct BlockAct {
+    int q[64];
+    float4 ts[4];
 };
 
-__device__ __forceinline__ void load_task_acts(const ActView &a, int lig, int L, int ntasks, TaskAct (&ta)[kTPL]) {
+// q: the block's 256 quants in the swizzled layout (B: the block's index); ts: its 4 pair records
+__device__ __forceinline__ void load_block_act(const int8_t *q, int B, const float4 *ts, BlockAct &a) {
+    const int4 *src = reinterpret_cast<const int4 *>(q);
 #pragma unroll
-    for (int i = 0; i < kTPL; ++i) {
-        const int tau = lig + L * i;
-        if (tau < ntasks) {
-            const int4 *q = reinterpret_cast<const int4 *>(a.q + 64 * tau);
-            const int4 a0 = q[0], a1 = q[1], a2 = q[2], a3 = q[3];
-            ta[i].lo[0] = a0.x; ta[i].lo[1] = a0.y; ta[i].lo[2] = a0.z; ta[i].lo[3] = a0.w;
-            ta[i].lo[4] = a1.x; ta[i].lo[5] = a1.y; ta[i].lo[6] = a1.z; ta[i].lo[7] = a1.w;
-            ta[i].hi[0] = a2.x; ta[i].hi[1] = a2.y; ta[i].hi[2] = a2.z; ta[i].hi[3] = a2.w;
-            ta[i].hi[4] = a3.x; ta[i].hi[5] = a3.y; ta[i].hi[6] = a3.z; ta[i].hi[7] = a3.w;
-            ta[i].ts = a.ts[tau];
-        } else {
-#pragma unroll
-            for (int c = 0; c < 8; ++c) ta[i].lo[c] = ta[i].hi[c] = 0;
-            ta[i].ts = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+    for (int k = 0; k < 16; ++k) {
+        const int4 v = src[k ^ (B & 7)];
+        a.q[4 * k] = v.x;
+        a.q[4 * k + 1] = v.y;
+        a.q[4 * k + 2] = v.z;
+        a.q[4 * k + 3] = v.w;
     }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) a.ts[j] = ts[j];
 }
 
-template <int TYPE>
-__device__ __forceinline__ float task_dot(const uint8_t *row, int tau, const TaskAct &a) {
-    constexpr int BB = TYPE == MMRS_Q5K ? Q5K_BYTES : Q4K_BYTES;
-    const int sb = tau >> 2, j = tau & 3;
-    const uint8_t *blk = row + sb * BB;
-    const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
-    int d[4] = {0, 0, 0, 0};
+// One 64-weight sub-block pair J of a super-block against its activation: dp4a over the quants,
+// then the MMVQ combine of vec_dot_q4_K_q8_1 / _q5_K_ (gguf.cuh:727-750, 783-813):
+// dall * (d8lo*dlo*sc_lo + d8hi*dhi*sc_hi) - dmin * (d8lo*S_lo*m_lo + d8hi*S_hi*m_hi).
+// J is a compile-time constant, so every shift and scale selection is fixed.
+template <int TYPE, int J>
+__device__ __forceinline__ float pair_dot(const uint8_t *blk, const uint4 &hdr, const uint32_t (&h)[8], const int *a,
+                                          const float4 &ts) {
+    int d0 = 0, d1 = 0, d2 = 0, d3 = 0;
+    int b0 = 0, b1 = 0, b2 = 0, b3 = 0;
     if (TYPE == MMRS_Q5K) {
-        const uint4 q0 = *reinterpret_cast<const uint4 *>(blk + 48 + 32 * j);
-        const uint4 q1 = *reinterpret_cast<const uint4 *>(blk + 64 + 32 * j);
-        const uint4 h0 = *reinterpret_cast<const uint4 *>(blk + 16);
-        const uint4 h1 = *reinterpret_cast<const uint4 *>(blk + 32);
+        const uint4 q0 = *reinterpret_cast<const uint4 *>(blk + 48 + 32 * J);
+        const uint4 q1 = *reinterpret_cast<const uint4 *>(blk + 64 + 32 * J);
         const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-        const uint32_t h[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-        const int rl = (4 - 2 * j) & 31, rh = (3 - 2 * j) & 31;
+        // The fifth bits stay where they are: bit m = 2J (low sub-block) or 2J + 1 (high) of each qh
+        // byte, masked, gives 2^m * hb per byte, so dp4a against the activation yields
+        // 2^m * dot(hb, a), rescaled to 16 * dot(hb, a) once per pair (exact: every term carries
+        // 2^m).  Likewise the high nibbles are taken in place (16 * q).  Only masks and dp4a: no
+        // shifts, which issue at half rate on the same pipe as the masks.
+        constexpr uint32_t ML = 0x01010101u << (2 * J), MH = 0x01010101u << (2 * J + 1);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-            const uint32_t lo = (w[c] & 0x0F0F0F0Fu) | (__funnelshift_l(h[c], h[c], rl) & 0x10101010u);
-            const uint32_t hi = ((w[c] >> 4) & 0x0F0F0F0Fu) | (__funnelshift_l(h[c], h[c], rh) & 0x10101010u);
-            d[c & 1] = __dp4a((int)lo, a.lo[c], d[c & 1]);
-            d[2 + (c & 1)] = __dp4a((int)hi, a.hi[c], d[2 + (c & 1)]);
+            if (c & 1) {
+                d1 = dp4a_us(w[c] & 0x0F0F0F0Fu, a[c], d1);
+                d3 = dp4a_us(w[c] & 0xF0F0F0F0u, a[8 + c], d3);
+                b1 = dp4a_us(h[c] & ML, a[c], b1);
+                b3 = dp4a_us(h[c] & MH, a[8 + c], b3);
+            } else {
+                d0 = dp4a_us(w[c] & 0x0F0F0F0Fu, a[c], d0);
+                d2 = dp4a_us(w[c] & 0xF0F0F0F0u, a[8 + c], d2);
+                b0 = dp4a_us(h[c] & ML, a[c], b0);
+                b2 = dp4a_us(h[c] & MH, a[8 + c], b2);
+            }
         }
-        d[2] += d[3];
     } else {
-        const uint4 q0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * j);
-        const uint4 q1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * j);
+        const uint4 q0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * J);
+        const uint4 q1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * J);
         const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-            d[c & 1] = dp4a_us(w[c] & 0x0F0F0F0Fu, a.lo[c], d[c & 1]);
-            d[2 + (c & 1)] = dp4a_us(w[c] & 0xF0F0F0F0u, a.hi[c], d[2 + (c & 1)]);
+            if (c & 1) {
+                d1 = dp4a_us(w[c] & 0x0F0F0F0Fu, a[c], d1);
+                d3 = dp4a_us(w[c] & 0xF0F0F0F0u, a[8 + c], d3);
+            } else {
+                d0 = dp4a_us(w[c] & 0x0F0F0F0Fu, a[c], d0);
+                d2 = dp4a_us(w[c] & 0xF0F0F0F0u, a[8 + c], d2);
+            }
         }
-        d[2] = (d[2] + d[3]) >> 4;  // every high-nibble term carries a factor 16: exact
     }
-    const int dlo = d[0] + d[1], dhi = d[2];
+    // high nibbles were taken in place: every term carries 16 (exact shift)
+    int dlo = d0 + d1, dhi = (d2 + d3) >> 4;
+    if (TYPE == MMRS_Q5K) {
+        const int bl = b0 + b1, bh = b2 + b3;
+        dlo += J < 2 ? bl << (4 - 2 * J) : bl >> (2 * J - 4);
+        dhi += J < 2 ? bh << (3 - 2 * J) : bh >> (2 * J - 3);
+    }
     uint32_t scp, mp;
-    scale_pair(hdr, j, scp, mp);
-    // |d * sc| < 2^22 for Q4_K (32 * 15 * 127 * 63); Q5_K products reach 2^23 and use the plain conversion
-    const int plo = dlo * (int)(scp & 0xffu), phi = dhi * (int)(scp >> 8);
-    const float flo = TYPE == MMRS_Q5K ? (float)plo : int22_to_float(plo);
-    const float fhi = TYPE == MMRS_Q5K ? (float)phi : int22_to_float(phi);
-    const float sd = a.ts.x * flo + a.ts.y * fhi;
-    const float sm = a.ts.z * small_uint_to_float(mp & 0xffu) + a.ts.w * small_uint_to_float(mp >> 8);
+    scale_pair(hdr, J, scp, mp);
+    // exact products: |dlo|, |dhi| < 2^17 and the 6-bit scales keep them below 2^24
+    const float flo = int22_to_float(dlo) * small_uint_to_float(scp & 0xffu);
+    const float fhi = int22_to_float(dhi) * small_uint_to_float(scp >> 8);
+    const float sd = ts.x * flo + ts.y * fhi;
+    const float sm = ts.z * small_uint_to_float(mp & 0xffu) + ts.w * small_uint_to_float(mp >> 8);
     const float2 dm = __half22float2(*reinterpret_cast<const __half2 *>(&hdr.x));
     return dm.x * sd - dm.y * sm;
 }
 
-// Dot of one row (in shared memory) over the lane's tasks tau = lig + L*i.
+// Dot of one 256-weight super-block (in shared memory) with its activation: pairs 0..3 in order.
 template <int TYPE>
-__device__ __forceinline__ float row_dot(const uint8_t *row, int lig, int L, int ntasks, const TaskAct (&ta)[kTPL]) {
-    float v = 0.f;
+__device__ __forceinline__ float block_dot(const uint8_t *blk, const BlockAct &a) {
+    const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
+    uint32_t h[8];
+    if (TYPE == MMRS_Q5K) {
+        const uint4 h0 = *reinterpret_cast<const uint4 *>(blk + 16);
+        const uint4 h1 = *reinterpret_cast<const uint4 *>(blk + 32);
+        h[0] = h0.x; h[1] = h0.y; h[2] = h0.z; h[3] = h0.w;
+        h[4] = h1.x; h[5] = h1.y; h[6] = h1.z; h[7] = h1.w;
+    } else {
 #pragma unroll
-    for (int i = 0; i < kTPL; ++i) {
-        const int tau = lig + L * i;
-        if (tau < ntasks) v += task_dot<TYPE>(row, tau, ta[i]);
+        for (int c = 0; c < 8; ++c) h[c] = 0u;
     }
+    float v = pair_dot<TYPE, 0>(blk, hdr, h, a.q, a.ts[0]);
+    v += pair_dot<TYPE, 1>(blk, hdr, h, a.q + 16, a.ts[1]);
+    v += pair_dot<TYPE, 2>(blk, hdr, h, a.q + 32, a.ts[2]);
+    v += pair_dot<TYPE, 3>(blk, hdr, h, a.q + 48, a.ts[3]);
+    return v;
+}
+
+// Fixed-order sum of a row's per-block partials.
+__device__ __forceinline__ float sum_blocks(const float *p, int nb) {
+    float v = p[0];
+#pragma unroll 4
+    for (int b = 1; b < nb; ++b) v += p[b];
     return v;
 }
 
@@ -183,8 +218,9 @@ __device__ __forceinline__ float half_gap(float y) {
 
 // 128 consecutive values, lane l holding values 4l..4l+3 (Q8_1 blocks of 32 over 8 lanes):
 // d = amax/127, q = roundf(v/d) (quantize_q8_1, gguf.cuh:1234-1261, and quantize_silu_mul_q8_1,
-// moe_gguf.cu:255-284).  Writes q, and per block the fp16-rounded scale d and the sum of quants S.
-__device__ __forceinline__ void quant128(float4 v, int8_t *q, float *d, int *S, int lane) {
+// moe_gguf.cu:255-284).  Writes q (value o + i at byte act_swz(o + i) of qv), and per block the
+// fp16-rounded scale d and the sum of quants S.
+__device__ __forceinline__ void quant128(float4 v, int8_t *qv, int o, float *d, int *S, int lane) {
     float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
     for (int m = 4; m > 0; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
@@ -211,7 +247,8 @@ __device__ __forceinline__ void quant128(float4 v, int8_t *q, float *d, int *S, 
         if (!(half_gap(y2) > 1e-4f)) q2 = (int)roundf(__fdiv_rn(v.z, dd));
         if (!(half_gap(y3) > 1e-4f)) q3 = (int)roundf(__fdiv_rn(v.w, dd));
     }
-    reinterpret_cast<int *>(q)[lane] = (q0 & 0xff) | ((q1 & 0xff) << 8) | ((q2 & 0xff) << 16) | ((q3 & 0xff) << 24);
+    *reinterpret_cast<int *>(qv + act_swz(o + 4 * lane)) =
+        (q0 & 0xff) | ((q1 & 0xff) << 8) | ((q2 & 0xff) << 16) | ((q3 & 0xff) << 24);
     int s = q0 + q1 + q2 + q3;
 #pragma unroll
     for (int m = 4; m > 0; m >>= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
@@ -221,9 +258,9 @@ __device__ __forceinline__ void quant128(float4 v, int8_t *q, float *d, int *S, 
     }
 }
 
-// One Q8_1 block of 32 values, lane l holding value l: the quant128 arithmetic (d = amax/127,
-// q = roundf(v/d), fp16-rounded d, sum of quants).
-__device__ __forceinline__ void quant32(float v, int8_t *q, float *d, int *S, int lane) {
+// One Q8_1 block of 32 values, lane l holding value o + l: the quant128 arithmetic (d = amax/127,
+// q = roundf(v/d) at byte act_swz(o + l) of qv, fp16-rounded d, sum of quants).
+__device__ __forceinline__ void quant32(float v, int8_t *qv, int o, float *d, int *S, int lane) {
     const float amax = warp_max_butterfly(fabsf(v));
     const float dd = __fdiv_rn(amax, 127.0f);
     int qi = 0;
@@ -234,7 +271,7 @@ __device__ __forceinline__ void quant32(float v, int8_t *q, float *d, int *S, in
         exact = !(half_gap(y) > 1e-4f);
     }
     if (__any_sync(0xffffffffu, exact) && exact) qi = (int)roundf(__fdiv_rn(v, dd));
-    q[lane] = (int8_t)qi;
+    qv[act_swz(o + lane)] = (int8_t)qi;
     int sq = qi;
 #pragma unroll
     for (int m = 16; m > 0; m >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, m);
@@ -247,9 +284,9 @@ __device__ __forceinline__ void quant32(float v, int8_t *q, float *d, int *S, in
 // The CTA's gate/up range of (position, row) pairs: whole Q8_1 blocks of 32 rows, so that every
 // block of act is quantised by the one CTA that computed it.
 __device__ __forceinline__ void gu_range(int cta, int G, int nvs, int I, int &p0, int &p1) {
-    const int nblk = nvs * I / 32;
-    p0 = 32 * (int)((int64_t)cta * nblk / G);
-    p1 = 32 * (int)((int64_t)(cta + 1) * nblk / G);
+    const uint32_t nblk = (uint32_t)(nvs * I / 32);  // cta * nblk < 2^31: G <= 256, 8 I / 32 <= 1536
+    p0 = 32 * (int)((uint32_t)cta * nblk / (uint32_t)G);
+    p1 = 32 * (int)((uint32_t)(cta + 1) * nblk / (uint32_t)G);
 }
 
 // Per-task scale records from per-block (d, S) arrays: nt tasks, 2 blocks each.
@@ -261,7 +298,7 @@ __device__ __forceinline__ void build_task_scales(float4 *ts, const float *d, co
 }
 
 // Bounded wait until unit k has landed in stage st: first the stage's ticket (the producer has
-// issued unit k there; a warp may claim unit k before unit k - stages has been issued), then the
+// issued unit k there; a lane may reach unit k before unit k - stages has been freed), then the
 // phase of the stage's full barrier.
 __device__ __forceinline__ bool wait_unit(uint64_t *full, const int *ticket, int k, int st, int stages,
                                           uint64_t deadline) {
@@ -296,6 +333,12 @@ __device__ __forceinline__ uint32_t sel_key(float sg, float b) {
 
 // Copy unit: .x kind (0 gate, 1 up, 2 down), .y slot position, .z first row, .w rows.
 // Sub-unit: .x unit, .y first row within the unit | rows << 16.
+// Floats of the per-block partial buffer: the gate/up rows' and, after them, the down rows'.
+__host__ __device__ inline size_t decode_part_floats(const DecodeParams &p) {
+    const size_t gu = (size_t)2 * p.act_slots * (p.H / QK_K), dn = (size_t)kTopK * p.res_slots * (p.I / QK_K);
+    return gu > dn ? gu : dn;
+}
+
 struct DecodeSmem {
     uint8_t *stages;
     uint64_t *full;
@@ -313,18 +356,20 @@ struct DecodeSmem {
     uint32_t *cand;            // [2][64] routing candidates: keys, then expert ids
     int *ids;                  // [8] expert of each slot (-1: none, or another rank's)
     int *vslot;                // [8] slot of each position (the computed slots in order)
+    int *posof;                // [8] position of each slot (-1: not computed here)
     float *w;                  // [8]
     float *dn_acc;             // [res_slots][8] weighted expert rows of this CTA's output range
+    float *bpart;              // per-block partial sums: gate/up [2][act_slots][H/256], then
+                               // down [positions][res_slots][I/256]
     float *gval, *uval;        // [act_slots] gate / up row values of this CTA's (position, row) range
     float *res_s;              // [res_slots]
     int4 *units;               // [kMaxUnits]
     int *unit_off;             // [kMaxUnits] first row of a gate/up unit in the CTA's range
-    int *unit_nsub;            // [kMaxUnits] sub-units of the unit
     const uint8_t **usrc;      // [kMaxUnits] global source of the unit's copy
     uint32_t *ubytes;          // [kMaxUnits] its size
-    int2 *subs;                // [kMaxSubs]
+    int2 *rowmap;              // [2 act_slots] gate/up row g: {unit | row in unit << 16, partial row}
     int *ticket;               // [stages] unit last issued into each stage
-    int *done;                 // [stages] sub-units of the stage's unit finished
+    int *done;                 // [stages] super-blocks of the stage's unit finished
     int *ctl;                  // [kCtlWords]
 };
 
@@ -338,7 +383,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     const int H = p.H, I = p.I, E = p.E;
     const uint64_t t_start = globaltimer_ns();
     const uint64_t deadline = t_start + p.timeout_ns;
-    const int dn_r0 = (int)((int64_t)cta * H / G), dn_r1 = (int)((int64_t)(cta + 1) * H / G);
+    // the CTA's output rows (cta * H < 2^31: G <= 256, H <= 4096)
+    const int dn_r0 = (int)((uint32_t)(cta * H) / (uint32_t)G), dn_r1 = (int)((uint32_t)((cta + 1) * H) / (uint32_t)G);
     const int nres = dn_r1 - dn_r0;
 
     // ---- P0 loads first: the CTA's router rows and the matching x slices ---------------------
@@ -361,9 +407,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             }
         }
     }
-    // this CTA's launch count (2 per completed launch: the grid barriers' targets)
-    uint32_t epoch = 0;
-    if (lane == 0 && (warp == 0 || warp == kProducerWarp)) epoch = __ldcg(&p.ctl->epoch[cta]);
+    // this launch's tag: one more than this CTA's last (its own arrival word counts its launches)
+    const uint32_t tag = __ldcg(&p.ctl->arrive[cta]) + 1u;
     if (tid == 0 && p.trace) p.trace[cta * 16 + 0] = t_start;
 
     DecodeSmem s;
@@ -390,17 +435,18 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         s.cand = reinterpret_cast<uint32_t *>(take(sizeof(uint32_t) * 128));
         s.ids = reinterpret_cast<int *>(take(sizeof(int) * kTopK));
         s.vslot = reinterpret_cast<int *>(take(sizeof(int) * kTopK));
+        s.posof = reinterpret_cast<int *>(take(sizeof(int) * kTopK));
         s.w = reinterpret_cast<float *>(take(sizeof(float) * kTopK));
-        s.dn_acc = reinterpret_cast<float *>(take(sizeof(float) * p.res_slots * kTopK));
+        s.dn_acc = reinterpret_cast<float *>(take(sizeof(float) * kTopK * p.res_slots));
+        s.bpart = reinterpret_cast<float *>(take(sizeof(float) * decode_part_floats(p)));
         s.gval = reinterpret_cast<float *>(take(sizeof(float) * p.act_slots));
         s.uval = reinterpret_cast<float *>(take(sizeof(float) * p.act_slots));
         s.res_s = reinterpret_cast<float *>(take(sizeof(float) * p.res_slots));
         s.units = reinterpret_cast<int4 *>(take(sizeof(int4) * kMaxUnits));
         s.unit_off = reinterpret_cast<int *>(take(sizeof(int) * kMaxUnits));
-        s.unit_nsub = reinterpret_cast<int *>(take(sizeof(int) * kMaxUnits));
         s.usrc = reinterpret_cast<const uint8_t **>(take(sizeof(void *) * kMaxUnits));
         s.ubytes = reinterpret_cast<uint32_t *>(take(sizeof(uint32_t) * kMaxUnits));
-        s.subs = reinterpret_cast<int2 *>(take(sizeof(int2) * kMaxSubs));
+        s.rowmap = reinterpret_cast<int2 *>(take(sizeof(int2) * 2 * p.act_slots));
         s.ticket = reinterpret_cast<int *>(take(sizeof(int) * p.stages));
         s.done = reinterpret_cast<int *>(take(sizeof(int) * p.stages));
         s.ctl = reinterpret_cast<int *>(take(sizeof(int) * kCtlWords));
@@ -421,6 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         mbar_init(s.abar, 1);
         fence_mbar_init();
         for (int i = 0; i < kCtlWords; ++i) s.ctl[i] = 0;
+        s.ctl[kCtlOk] = 1;  // cleared by a routing lane whose logit wait expires
     }
 
     // ---- P0: router slices -------------------------------------------------------------------
@@ -447,26 +494,23 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         const int ee = cta + G * tid;
         if (ee < E) {
             const float *q = s.part + tid * 8;
-            p.logits[ee] = ((q[0] + q[1]) + (q[2] + q[3])) + ((q[4] + q[5]) + (q[6] + q[7]));
+            const float lg = ((q[0] + q[1]) + (q[2] + q[3])) + ((q[4] + q[5]) + (q[6] + q[7]));
+            // published with this launch's tag in the same 64-bit word: no separate grid barrier
+            st_relaxed_gpu_u64(&p.ctl->logit[ee], ((unsigned long long)tag << 32) | __float_as_uint(lg));
         }
     }
-    named_sync(kBarRouter, kThreads);  // both logits written before the release below
-    if (tid == 0) {
-        if (p.trace) p.trace[cta * 16 + 1] = globaltimer_ns();
-        // grid barrier #1 arrival (fire and forget); the producer warp waits for the count
-        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&p.ctl->count) : "memory");
-    }
+    if (tid == 0 && p.trace) p.trace[cta * 16 + 1] = globaltimer_ns();
 
     const size_t gu_row_bytes = kq_row_bytes(p.gu_type, H);
     const size_t dn_row_bytes = kq_row_bytes(p.dn_type, I);
     const size_t gu_expert_bytes = gu_row_bytes * I;
     const size_t dn_expert_bytes = dn_row_bytes * H;
-    const int Lg = p.gu_lanes, Ld = p.dn_lanes;
-    const int gu_sub = p.gu_sub_rows, dn_sub = p.dn_sub_rows, U_gu = p.gu_unit_rows;
+    const int U_gu = p.gu_unit_rows;
+    const int NBg = H / QK_K, NBd = I / QK_K;  // super-blocks of a gate/up row, of a down row
 
     // Issue copy unit k into ring stage k % stages (one thread).  The first `stages` units are
-    // issued by the producer warp once the table is built; every later unit by the warp that
-    // finishes the last sub-unit of unit k - stages, which frees that stage.
+    // issued by the producer warp once the table is built; every later unit by the consumer lane
+    // that completes the last super-block of unit k - stages, which frees that stage.
     auto issue = [&](int k) {
         const int st = k % p.stages;
         *reinterpret_cast<volatile int *>(&s.ticket[st]) = k;
@@ -482,25 +526,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
 
     if (warp == kProducerWarp) {
         // ================================ producer warp ===================================
-        bool ok = true;
-        if (lane == 0) {
-            const uint32_t target = (uint32_t)G * (epoch + 1u);
-            uint32_t spins = 0;
-            while ((int)(ld_acquire_gpu(&p.ctl->count) - target) < 0) {
-                __nanosleep(16);
-                if ((++spins & 255u) == 0 && globaltimer_ns() > deadline) {
-                    atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
-                    ok = false;
-                    break;
-                }
-            }
-            if (p.trace) p.trace[cta * 16 + 2] = globaltimer_ns();
-        }
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        if (lane == 0) s.ctl[kCtlOk] = ok ? 1 : 0;
-        __syncwarp();
-        named_arrive(kBarRoute, kThreads);  // barrier #1 passed: the routing warps may read the logits
+        // the routing warps wait for the logits; their candidates (and verdict) arrive here
         named_sync(kBarCand, 32 * (kRouteWarps + 1));
+        const bool ok = s.ctl[kCtlOk] != 0;
+        if (lane == 0 && p.trace) p.trace[cta * 16 + 2] = globaltimer_ns();
         // ---- merge of the routing warps' candidates (8 per warp, each warp's in rank order) --------
         int slot_id = -1;  // lane k < 8: expert of slot k
         float slot_w = 0.f;
@@ -569,6 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         if (lane < kTopK) {
             s.ids[lane] = id;
             s.w[lane] = slot_w;
+            s.posof[lane] = keep ? __popc(kept & ((1u << lane) - 1u)) : -1;
             if (keep) s.vslot[__popc(kept & ((1u << lane) - 1u))] = lane;
         }
         __syncwarp();
@@ -591,88 +621,81 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             q = seg_end;
         }
         const int n_gu_units = 2 * n_chunks;
-        const int ns = my_pos >= 0 ? (my_n + gu_sub - 1) / gu_sub : 0;
-        int incl = ns;  // inclusive prefix of sub-units over chunks
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int t = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += t;
-        }
-        const int base = 2 * (incl - ns);  // gate and up sub-units of the earlier chunks
-        const int n_sub_gu = 2 * __shfl_sync(0xffffffffu, incl, 31);
+        // gate/up rows in unit order: chunk c's gate rows (unit 2c), then its up rows (2c + 1);
+        // the row map gives each its unit, its row in the unit and its partial-sum row
+        // (gate rows first, then up rows, by the (position, row) offset in the CTA's range)
+        const int cnt = gu_p1 - gu_p0;
         if (my_pos >= 0) {
             for (int h = 0; h < 2; ++h) {
                 const int k = 2 * lane + h;
                 s.units[k] = make_int4(h, my_pos, my_row0, my_n);
                 s.unit_off[k] = my_off;
-                s.unit_nsub[k] = ns;
                 const int e = s.ids[s.vslot[my_pos]];
                 s.usrc[k] = (h == 0 ? p.gate : p.up) + (size_t)e * gu_expert_bytes + (size_t)my_row0 * gu_row_bytes;
                 s.ubytes[k] = (uint32_t)(gu_row_bytes * my_n);
-                for (int j = 0; j < ns; ++j) {
-                    const int r0 = j * gu_sub;
-                    s.subs[base + h * ns + j] = make_int2(k, r0 | (min(gu_sub, my_n - r0) << 16));
-                }
+                for (int r = 0; r < my_n; ++r)
+                    s.rowmap[2 * my_off + h * my_n + r] = make_int2(k | (r << 16), h * cnt + my_off + r);
             }
         }
         // down units: one per position, all of this CTA's output rows
-        const int nsd = nres > 0 ? (nres + dn_sub - 1) / dn_sub : 0;
-        const int n_dn_units = nsd > 0 ? nvs : 0;
+        const int n_dn_units = nres > 0 ? nvs : 0;
         if (lane < n_dn_units) {
             const int k = n_gu_units + lane;
             s.units[k] = make_int4(2, lane, dn_r0, nres);
             s.unit_off[k] = 0;
-            s.unit_nsub[k] = nsd;
             const int e = s.ids[s.vslot[lane]];
             s.usrc[k] = p.down + (size_t)e * dn_expert_bytes + (size_t)dn_r0 * dn_row_bytes;
             s.ubytes[k] = (uint32_t)(dn_row_bytes * nres);
-            for (int j = 0; j < nsd; ++j) {
-                const int r0 = j * dn_sub;
-                s.subs[n_sub_gu + lane * nsd + j] = make_int2(k, r0 | (min(dn_sub, nres - r0) << 16));
-            }
         }
         if (lane == 0) {
             s.ctl[kCtlUnits] = n_gu_units + n_dn_units;
             s.ctl[kCtlGuUnits] = n_gu_units;
-            s.ctl[kCtlSubGu] = n_sub_gu;
-            s.ctl[kCtlSubs] = n_sub_gu + n_dn_units * nsd;
+            s.ctl[kCtlGuRows] = 2 * cnt;
             s.ctl[kCtlPositions] = nvs;
             s.ctl[kCtlOk] = ok ? 1 : 0;
             if (p.trace) p.trace[cta * 16 + 3] = globaltimer_ns();
         }
         __syncwarp();
-        named_arrive(kBarTable, kThreads);  // table complete: the consumers may claim
+        named_arrive(kBarTable, kThreads);  // table complete: the consumers may start
         __syncwarp();
-        // ---- first ring fill (lane 0); later units are issued by the consumer warps -------------
-        if (lane == 0 && ok) {
-            const int n = min(n_gu_units + n_dn_units, p.stages);
-            for (int k = 0; k < n; ++k) issue(k);
-        }
+        // ---- first ring fill, one unit per lane; later units are issued by the consumer lanes -----
+        if (ok && lane < min(n_gu_units + n_dn_units, p.stages)) issue(lane);
         return;
     }
 
     // ================================ consumer warps ======================================
-    // While the producer waits for barrier #1 and routes: Q8_1 of x, residual, zeroed sums.
+    // While the producer waits for barrier #1 and routes: Q8_1 of x and the residual.
     {
         const int nxc = H / 128;
         for (int c = warp; c < nxc; c += kConsumerWarps) {
             const float4 xv = __ldg(reinterpret_cast<const float4 *>(p.x) + c * 32 + lane);
-            quant128(xv, s.xq + c * 128, s.xd + c * 4, s.xS + c * 4, lane);
+            quant128(xv, s.xq, c * 128, s.xd + c * 4, s.xS + c * 4, lane);
         }
         for (int r = tid; r < nres; r += kConsumerThreads) s.res_s[r] = p.residual ? __ldg(p.residual + dn_r0 + r) : 0.f;
-        for (int i = tid; i < nres * kTopK; i += kConsumerThreads) s.dn_acc[i] = 0.f;
         named_sync(kBarConsumers, kConsumerThreads);
         build_task_scales(s.xts, s.xd, s.xS, H / 64, tid, kConsumerThreads);
     }
-    named_sync(kBarRoute, kThreads);  // grid barrier #1 passed (the producer polled it)
+    named_sync(kBarConsumers, kConsumerThreads);  // x's Q8_1 and its records are complete
     if (warp < kRouteWarps) {
-        // sigmoid, selection score as an order-preserving key, and this warp's top-8 of its 32
-        // experts by rounds of redux max (key) and redux min (id among the lanes holding it)
+        // this launch's logit of expert e (bounded wait for its tag); sigmoid, selection score as
+        // an order-preserving key, and this warp's top-8 of its 32 experts by rounds of redux max
+        // (key) and redux min (id among the lanes holding it)
         const int e = 32 * warp + lane;
-        if (p.internal_routing && s.ctl[kCtlOk] && 32 * warp < E) {
+        if (p.internal_routing && 32 * warp < E) {
             uint32_t key = 0u;  // experts >= E are never selected (E >= 8 real keys are > 0)
             if (e < E) {
-                const float sg = __fdiv_rn(1.0f, 1.0f + expf(-__ldcg(p.logits + e)));
+                unsigned long long v = ld_relaxed_gpu_u64(&p.ctl->logit[e]);
+                uint32_t spins = 0;
+                while ((uint32_t)(v >> 32) != tag) {
+                    __nanosleep(32);
+                    if ((++spins & 63u) == 0 && globaltimer_ns() > deadline) {
+                        atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
+                        s.ctl[kCtlOk] = 0;
+                        break;
+                    }
+                    v = ld_relaxed_gpu_u64(&p.ctl->logit[e]);
+                }
+                const float sg = __fdiv_rn(1.0f, 1.0f + expf(-__uint_as_float((uint32_t)v)));
                 s.sig[e] = sg;
                 key = sel_key(sg, __ldg(p.bias + e));
             }
@@ -690,103 +713,122 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         }
         named_arrive(kBarCand, 32 * (kRouteWarps + 1));
     }
+    // Gate/up lanes: lane t holds the activation of x block t % NBg and computes that block of
+    // rows t / NBg, t / NBg + slots, ... of the CTA's gate/up rows (in unit order).
+    const int g_slots = kConsumerThreads / NBg;
+    const bool g_lane = tid < NBg * g_slots;
+    const int g_sb = tid % NBg, g_first = tid / NBg;
+    BlockAct act;
+    load_block_act(s.xq + QK_K * g_sb, g_sb, s.xts + 4 * g_sb, act);
     named_sync(kBarTable, kThreads);
     const bool ok1 = s.ctl[kCtlOk] != 0;
-    const int n_sub_gu = s.ctl[kCtlSubGu], n_sub = s.ctl[kCtlSubs], nvs = s.ctl[kCtlPositions];
-    const int n_units = s.ctl[kCtlUnits];
+    const int nvs = s.ctl[kCtlPositions], n_units = s.ctl[kCtlUnits], n_gu_units = s.ctl[kCtlGuUnits];
+    const int n_gu_rows = s.ctl[kCtlGuRows], cnt = n_gu_rows / 2;
     bool aborted = !ok1;
-    auto claim = [&]() -> int {
-        int v = 0;
-        if (lane == 0) v = atomicAdd(&s.ctl[kCtlNext], 1);
-        return __shfl_sync(0xffffffffu, v, 0);
-    };
-    // A warp that finished a sub-unit of unit k: the last finisher (its acquire covers the other
-    // warps' reads of the stage) issues unit k + stages into the freed stage.
-    auto finish = [&](int k, int st) {
-        __syncwarp();
-        if (lane == 0) {
-            const int old = atom_add_acq_rel_cta(&s.done[st], 1);
-            if (old + 1 == s.unit_nsub[k]) {
+    // Gate/up: the lanes of a warp finished one super-block each (valid) of units k: per unit, the
+    // lowest such lane adds the group's count to the stage's counter (its acquire-release covers
+    // the group's reads of the stage, ordered before it by the warp sync); the lane that completes
+    // the unit's rows x blocks frees the stage and issues unit k + stages into it.  The warp sync
+    // is safe only while one warp's rows of a round (at most 31 / NBg + 2 consecutive rows, in as
+    // many units) fit in the ring: a lane must never wait for a unit that its own warp keeps
+    // unfreed.  Otherwise (small H) every lane counts its own block.
+    const bool lane_counts = 31 / NBg + 2 > p.stages;
+    auto finish = [&](bool valid, int k, int st, int total) {
+        bool leader = valid;
+        int n = 1;
+        if (!lane_counts) {
+            __syncwarp();
+            const unsigned grp = __match_any_sync(0xffffffffu, valid ? k : -1);
+            leader = valid && lane == __ffs(grp) - 1;
+            n = __popc(grp);
+        }
+        if (leader) {
+            const int old = atom_add_acq_rel_cta(&s.done[st], n);
+            if (old + n == total) {
                 s.done[st] = 0;
                 if (k + p.stages < n_units && !aborted) issue(k + p.stages);
             }
         }
     };
-
-    // ---- P2: gate / up sub-units ----------------------------------------------------------------
-    int g = claim();
-    {
-        const int ntasks = (H / QK_K) * 4;
-        const int lgi = lane / Lg, lig = lane % Lg;
-        TaskAct ta[kTPL];
-        load_task_acts(ActView{s.xq, s.xts}, lig, Lg, ntasks, ta);
-        while (g < n_sub_gu) {
-            const int2 su = s.subs[g];
-            const int k = su.x, ro = su.y & 0xffff, nr = su.y >> 16;
-            const int4 u = s.units[k];
-            const int st = k % p.stages;
-            if (!aborted && !wait_unit(s.full, s.ticket, k, st, p.stages, deadline)) {
-                atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
-                aborted = true;
-            }
-            const int rA = ro + lgi * kRowsPerLane, rB = rA + 1, rend = ro + nr;
-            float vA = 0.f, vB = 0.f;
-            if (!aborted && rA < rend) {
-                const uint8_t *base = s.stages + (size_t)st * p.stage_bytes;
-                const uint8_t *rowA = base + (size_t)rA * gu_row_bytes;
-                const uint8_t *rowB = base + (size_t)min(rB, rend - 1) * gu_row_bytes;
-                vA = row_dot<GU>(rowA, lig, Lg, ntasks, ta);
-                vB = row_dot<GU>(rowB, lig, Lg, ntasks, ta);
-            }
-#pragma unroll
-            for (int m = 16; m > 0; m >>= 1)
-                if (m < Lg) {
-                    vA += __shfl_xor_sync(0xffffffffu, vA, m);
-                    vB += __shfl_xor_sync(0xffffffffu, vB, m);
-                }
-            if (lig == 0) {
-                float *gv = (u.x == 0 ? s.gval : s.uval) + s.unit_off[k];
-                if (rA < rend) gv[rA] = vA;
-                if (rB < rend) gv[rB] = vB;
-            }
-            finish(k, st);
-            g = claim();
+    auto wait_landed = [&](int k, int st) {
+        if (!aborted && !wait_unit(s.full, s.ticket, k, st, p.stages, deadline)) {
+            atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
+            aborted = true;
         }
+    };
+
+    // ---- P2: gate / up: one super-block per lane and round -----------------------------------
+    {
+        constexpr int BB = GU == MMRS_Q5K ? Q5K_BYTES : Q4K_BYTES;
+        const int rounds = (n_gu_rows + g_slots - 1) / g_slots;
+        for (int m = 0; m < rounds; ++m) {
+            const int g = g_first + m * g_slots;
+            const bool valid = g_lane && g < n_gu_rows;
+            int k = -1, st = 0, total = 0;
+            if (valid) {
+                const int2 rm = s.rowmap[g];
+                k = rm.x & 0xffff;
+                st = k % p.stages;
+                total = s.units[k].w * NBg;
+                wait_landed(k, st);
+                float v = 0.f;
+                if (!aborted)
+                    v = block_dot<GU>(s.stages + (size_t)st * p.stage_bytes + (size_t)(rm.x >> 16) * gu_row_bytes + BB * g_sb, act);
+                s.bpart[rm.y * NBg + g_sb] = v;
+            }
+            finish(valid, k, st, total);
+        }
+        __syncwarp();  // a leader lane may still be issuing: the warp meets the barrier converged
     }
 
     // ---- P3: Q8_1 of act for the CTA's blocks, grid barrier #2, copy of the whole vector ---------
-    named_sync(kBarConsumers, kConsumerThreads);  // every gate/up sub-unit of this CTA is done
+    named_sync(kBarConsumers, kConsumerThreads);  // every gate/up block of this CTA is done
     if (tid == 0 && p.trace) p.trace[cta * 16 + 4] = globaltimer_ns();
     {
         int gu_p0, gu_p1;
         gu_range(cta, G, nvs, I, gu_p0, gu_p1);
-        for (int i = tid; i < gu_p1 - gu_p0; i += kConsumerThreads) {
+        // row sums of the gate rows (partial rows 0..cnt-1) and the up rows (cnt..2 cnt-1)
+        for (int t = tid; t < 2 * cnt; t += kConsumerThreads) {
+            const float v = sum_blocks(s.bpart + t * NBg, NBg);
+            if (t < cnt) s.gval[t] = v;
+            else s.uval[t - cnt] = v;
+        }
+        named_sync(kBarConsumers, kConsumerThreads);
+        for (int i = tid; i < cnt; i += kConsumerThreads) {
             const float gv = s.gval[i];
-            // act = up * silu(gate) (moe_gguf.cu:272-273), in place of the gate values
+            // act = up * silu(gate) (moe_gguf.cu:272-273)
             s.gval[i] = s.uval[i] * __fdiv_rn(gv, 1.0f + expf(-gv));
         }
         named_sync(kBarConsumers, kConsumerThreads);
         // quantize_silu_mul_q8_1 (moe_gguf.cu:255-284): one warp per block of 32 rows
         for (int b = gu_p0 / 32 + warp; b < gu_p1 / 32 && !aborted; b += kConsumerWarps)
-            quant32(s.gval[32 * b - gu_p0 + lane], p.aq + 32 * b, p.ad + b, p.aS + b, lane);
+            quant32(s.gval[32 * b - gu_p0 + lane], p.aq, 32 * b, p.ad + b, p.aS + b, lane);
+    }
+    named_sync(kBarConsumers, kConsumerThreads);
+    // grid barrier #2: release this CTA's tag (its act blocks are written; the CTA barrier above
+    // orders every thread's writes before it), then consumer thread c < G acquires CTA c's tag.
+    // The tag is released even after a failed routing wait, so that no other CTA waits for it.
+    if (tid == 0) {
+        if (p.trace) p.trace[cta * 16 + 11] = globaltimer_ns();
+        st_release_gpu(&p.ctl->arrive[cta], tag);
+    }
+    if (tid < G && ok1) {
+        uint32_t spins = 0;
+        while ((int)(ld_acquire_gpu(&p.ctl->arrive[tid]) - tag) < 0) {
+            __nanosleep(32);
+            if ((++spins & 63u) == 0 && globaltimer_ns() > deadline) {
+                atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
+                s.ctl[kCtlFail] = 1;
+                break;
+            }
+        }
     }
     named_sync(kBarConsumers, kConsumerThreads);
     if (tid == 0) {
-        bool ok2 = ok1;
-        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&p.ctl->count) : "memory");
-        const uint32_t target = (uint32_t)G * (epoch + 2u);
-        uint32_t spins = 0;
-        while (ok2 && (int)(ld_acquire_gpu(&p.ctl->count) - target) < 0) {
-            __nanosleep(16);
-            if ((++spins & 255u) == 0 && globaltimer_ns() > deadline) {
-                atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
-                ok2 = false;
-            }
-        }
-        if (ok2) p.ctl->epoch[cta] = epoch + 2u;  // read again only by this CTA's next launch
+        bool ok2 = ok1 && s.ctl[kCtlFail] == 0;
         if (p.trace) p.trace[cta * 16 + 5] = globaltimer_ns();
         // the whole quantised act [positions][I] (+ scales, sums) in one bulk copy per array; the
-        // other CTAs' generic writes are ordered before these async-proxy reads
+        // other CTAs' generic writes (acquired above) are ordered before these async-proxy reads
         bool copied = false;
         if (ok2 && nvs > 0) {
             const uint32_t qb = (uint32_t)(nvs * I), sb = (uint32_t)(sizeof(float) * nvs * (I / 32));
@@ -809,56 +851,54 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     named_sync(kBarConsumers, kConsumerThreads);
     if (tid == 0 && p.trace) p.trace[cta * 16 + 6] = globaltimer_ns();
 
-    // ---- P3: down sub-units -------------------------------------------------------------------
+    // ---- P3: down: lane t takes (position, block) pair t % pairs and rows t / pairs, + slots, ...
     {
-        const int ntasks = (I / QK_K) * 4;
-        const int lgi = lane / Ld, lig = lane % Ld;
-        TaskAct ta[kTPL];
-        int cur_vp = -1;
-        while (g < n_sub) {
-            const int2 su = s.subs[g];
-            const int k = su.x, ro = su.y & 0xffff, nr = su.y >> 16;
-            const int4 u = s.units[k];
-            const int st = k % p.stages;
-            const int vp = u.y, slot = s.vslot[vp];
-            if (vp != cur_vp) {
-                load_task_acts(ActView{s.aq_s + (size_t)vp * I, s.ats + vp * (I / 64)}, lig, Ld, ntasks, ta);
-                cur_vp = vp;
-            }
-            if (!aborted && !wait_unit(s.full, s.ticket, k, st, p.stages, deadline)) {
-                atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
-                aborted = true;
-            }
-            const int rA = ro + lgi * kRowsPerLane, rB = rA + 1, rend = ro + nr;
-            float vA = 0.f, vB = 0.f;
-            if (!aborted && rA < rend) {
-                const uint8_t *base = s.stages + (size_t)st * p.stage_bytes;
-                const uint8_t *rowA = base + (size_t)rA * dn_row_bytes;
-                const uint8_t *rowB = base + (size_t)min(rB, rend - 1) * dn_row_bytes;
-                vA = row_dot<DN>(rowA, lig, Ld, ntasks, ta);
-                vB = row_dot<DN>(rowB, lig, Ld, ntasks, ta);
-            }
-#pragma unroll
-            for (int m = 16; m > 0; m >>= 1)
-                if (m < Ld) {
-                    vA += __shfl_xor_sync(0xffffffffu, vA, m);
-                    vB += __shfl_xor_sync(0xffffffffu, vB, m);
-                }
-            if (lig == 0) {
-                const float wslot = s.w[slot];
-                if (rA < rend) s.dn_acc[rA * kTopK + slot] = vA * wslot;
-                if (rB < rend) s.dn_acc[rB * kTopK + slot] = vB * wslot;
-            }
-            finish(k, st);
-            g = claim();
+        constexpr int BB = DN == MMRS_Q5K ? Q5K_BYTES : Q4K_BYTES;
+        const int pairs = nvs * NBd;
+        const int slots = pairs > 0 ? kConsumerThreads / pairs : 0;
+        const bool d_lane = tid < pairs * slots;
+        const int P = d_lane ? tid % pairs : 0, first = d_lane ? tid / pairs : 0;
+        const int vp = P / NBd, sb = P % NBd;
+        if (d_lane) load_block_act(s.aq_s + (size_t)vp * I + QK_K * sb, P, s.ats + vp * (I / 64) + 4 * sb, act);
+        const int k = n_gu_units + vp, st = k % p.stages;
+        // A warp's lanes may hold positions a ring apart (the pairs wrap within a warp), so the
+        // down lanes take no warp-collective step: each lane computes its rows, then adds its
+        // count to the unit's stage once; the lane that completes the unit issues unit k + stages.
+        int done_rows = 0;
+        for (int r = first; d_lane && r < nres; r += slots) {
+            if (done_rows == 0) wait_landed(k, st);
+            float v = 0.f;
+            if (!aborted) v = block_dot<DN>(s.stages + (size_t)st * p.stage_bytes + (size_t)r * dn_row_bytes + BB * sb, act);
+            s.bpart[(vp * nres + r) * NBd + sb] = v;
+            ++done_rows;
         }
+        if (done_rows > 0) {
+            const int old = atom_add_acq_rel_cta(&s.done[st], done_rows);
+            if (old + done_rows == nres * NBd) {
+                s.done[st] = 0;
+                if (k + p.stages < n_units && !aborted) issue(k + p.stages);
+            }
+        }
+        __syncwarp();
     }
 
     // ---- y = fixed 8-way tree over the routed experts (moe_gguf.cu:328-342) + residual ---------
     named_sync(kBarConsumers, kConsumerThreads);
+    // expert row of slot j for output row r, weighted by the route weight (0 for a slot not
+    // computed here), one (row, slot) per thread; then the 8-way tree per row
+    for (int t = tid; t < nres * kTopK; t += kConsumerThreads) {
+        const int r = t / kTopK, j = t % kTopK, vp = s.posof[j];
+        s.dn_acc[t] = vp >= 0 ? sum_blocks(s.bpart + (vp * nres + r) * NBd, NBd) * s.w[j] : 0.f;
+    }
+    named_sync(kBarConsumers, kConsumerThreads);
+    auto slot_rows = [&](int r, float (&q)[kTopK]) {
+#pragma unroll
+        for (int j = 0; j < kTopK; ++j) q[j] = s.dn_acc[r * kTopK + j];
+    };
     if (p.world <= 1) {
         for (int r = tid; r < nres && !aborted; r += kConsumerThreads) {
-            const float *q = s.dn_acc + r * kTopK;
+            float q[kTopK];
+            slot_rows(r, q);
             float y = ((q[0] + q[4]) + (q[2] + q[6])) + ((q[1] + q[5]) + (q[3] + q[7]));
             if (p.residual) y = y + s.res_s[r];
             p.y[dn_r0 + r] = y;
@@ -875,7 +915,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         const size_t part_off = kXchDPart + sizeof(float) * (size_t)(token & 1u) * kXchMaxHidden;
         float *mine = reinterpret_cast<float *>(p.xch + part_off);
         for (int r = tid; r < nres; r += kConsumerThreads) {
-            const float *q = s.dn_acc + r * kTopK;
+            float q[kTopK];
+            slot_rows(r, q);
             mine[dn_r0 + r] = ((q[0] + q[4]) + (q[2] + q[6])) + ((q[1] + q[5]) + (q[3] + q[7]));
         }
         named_sync(kBarConsumers, kConsumerThreads);
@@ -930,17 +971,12 @@ size_t decode_smem_bytes(const DecodeParams &p) {
     size_t b = a16((size_t)p.stages * p.stage_bytes) + a16(sizeof(uint64_t) * p.stages) + a16(sizeof(uint64_t));
     b += a16(p.H) + 2 * a16(4 * (p.H / 32)) + a16(16 * (p.H / 64));
     b += a16((size_t)kTopK * p.I) + 2 * a16(4 * kTopK * (p.I / 32)) + a16(16 * kTopK * (p.I / 64));
-    b += a16(4 * 16) + a16(4 * 256) + a16(4 * 128) + 3 * a16(4 * kTopK);  // part, sig, cand, ids, vslot, w
-    b += a16(4 * (size_t)p.res_slots * kTopK) + 2 * a16(4 * (size_t)p.act_slots) + a16(4 * (size_t)p.res_slots);
-    b += a16(16 * kMaxUnits) + 2 * a16(4 * kMaxUnits) + a16(8 * kMaxUnits) + a16(4 * kMaxUnits) + a16(8 * kMaxSubs);
+    b += a16(4 * 16) + a16(4 * 256) + a16(4 * 128) + 4 * a16(4 * kTopK);  // part, sig, cand, ids, vslot, posof, w
+    b += a16(4 * (size_t)kTopK * p.res_slots);                           // dn_acc
+    b += a16(4 * decode_part_floats(p)) + 2 * a16(4 * (size_t)p.act_slots) + a16(4 * (size_t)p.res_slots);
+    b += a16(16 * kMaxUnits) + a16(4 * kMaxUnits) + a16(8 * kMaxUnits) + a16(4 * kMaxUnits) + a16(16 * (size_t)p.act_slots);
     b += 2 * a16(4 * (size_t)p.stages) + a16(4 * kCtlWords);
     return b;
-}
-
-static int pow2_at_least(int v) {
-    int r = 1;
-    while (r < v) r <<= 1;
-    return r;
 }
 
 int decode_configure(DecodeParams &p, int num_sms, int max_smem) {
@@ -948,26 +984,20 @@ int decode_configure(DecodeParams &p, int num_sms, int max_smem) {
     if ((p.gu_type != MMRS_Q4K && p.gu_type != MMRS_Q5K) || (p.dn_type != MMRS_Q4K && p.dn_type != MMRS_Q5K))
         return MMRS_ERR_UNSUPPORTED;
     if (p.H / 8 / 4 > 128) return MMRS_ERR_UNSUPPORTED;  // router slice: at most 4 float4 a lane (H <= 4096)
-    const int gu_tasks = (p.H / QK_K) * 4, dn_tasks = (p.I / QK_K) * 4;
-    p.gu_lanes = pow2_at_least((gu_tasks + kTPL - 1) / kTPL);
-    p.dn_lanes = pow2_at_least((dn_tasks + kTPL - 1) / kTPL);
-    if (p.gu_lanes > 32 || p.dn_lanes > 32) return MMRS_ERR_UNSUPPORTED;  // H, I <= 6144
-    // one warp's share: (32 / L) lane groups x 2 rows; a gate/up copy unit is three shares
-    p.gu_sub_rows = (32 / p.gu_lanes) * kRowsPerLane;
-    p.dn_sub_rows = (32 / p.dn_lanes) * kRowsPerLane;
-    p.gu_unit_rows = kSubsPerGuUnit * p.gu_sub_rows;
+    // one consumer lane per super-block of a gate/up row, and per (position, block) of the down rows
+    if (p.H / QK_K > kConsumerThreads || kTopK * (p.I / QK_K) > kConsumerThreads) return MMRS_ERR_UNSUPPORTED;
     p.act_slots = 32 * ((kTopK * p.I / 32 + num_sms - 1) / num_sms) + 1;  // whole Q8_1 blocks a CTA
     p.res_slots = (p.H + num_sms - 1) / num_sms + 1;
-    if (p.E > 2 * num_sms || num_sms > kMaxGridCtas) return MMRS_ERR_UNSUPPORTED;
-    // table bounds: a CTA's gate/up chunks (one lane each; each slot boundary may add one), units
-    // and sub-units
-    const int max_chunks = (p.act_slots + p.gu_unit_rows - 1) / p.gu_unit_rows + kTopK;
-    const int max_dn_sub = (p.res_slots + p.dn_sub_rows - 1) / p.dn_sub_rows;
-    if (max_chunks > 32 || 2 * max_chunks + kTopK > kMaxUnits ||
-        2 * max_chunks * kSubsPerGuUnit + kTopK * max_dn_sub > kMaxSubs || p.res_slots > 0xffff)
-        return MMRS_ERR_UNSUPPORTED;
-    const size_t gu_stage = kq_row_bytes(p.gu_type, p.H) * p.gu_unit_rows;
+    if (p.E > 2 * num_sms || num_sms > kDecodeMaxCtas) return MMRS_ERR_UNSUPPORTED;
+    const size_t gu_row = kq_row_bytes(p.gu_type, p.H);
     const size_t dn_stage = kq_row_bytes(p.dn_type, p.I) * (p.res_slots - 1);
+    // a gate/up copy unit: as many whole rows as a down unit's stage holds (at least 4)
+    p.gu_unit_rows = (int)(dn_stage / gu_row) > 4 ? (int)(dn_stage / gu_row) : 4;
+    // table bounds: a CTA's gate/up chunks (one producer lane each; each slot boundary may add one)
+    const int max_chunks = (p.act_slots + p.gu_unit_rows - 1) / p.gu_unit_rows + kTopK;
+    if (max_chunks > 32 || 2 * max_chunks + kTopK > kMaxUnits || p.gu_unit_rows > 0xffff || p.res_slots > 0xffff)
+        return MMRS_ERR_UNSUPPORTED;
+    const size_t gu_stage = gu_row * p.gu_unit_rows;
     p.stage_bytes = (int)(((gu_stage > dn_stage ? gu_stage : dn_stage) + 127) / 128 * 128);
     p.stages = 0;
     DecodeParams q = p;

@@ -5,7 +5,20 @@
 
 namespace mmrs {
 
-struct GridFlags;
+// Control block of the single-token kernel at the start of its workspace (zero before first use;
+// it lies within the zeroed control bytes of the workspace contract).  Launch n (n = 1, 2, ...)
+// of a workspace carries the tag n:
+//   arrive[c]  the tag of CTA c's last launch, released at the second grid barrier once the
+//              CTA's activation blocks are written (so a CTA's own word is also its launch count);
+//   logit[e]   the router logit of expert e with the tag of the launch that wrote it in the upper
+//              32 bits: a reader that sees the current tag sees the current value (one 64-bit word).
+constexpr int kDecodeMaxCtas = 256;
+struct DecodeCtl {
+    uint32_t status;  // MMRS_OK, or MMRS_ERR_TIMEOUT once any wait expired
+    uint32_t pad0[31];
+    uint32_t arrive[kDecodeMaxCtas];
+    unsigned long long logit[256];
+};
 
 struct DecodeParams {
     const float *x;       // [H] f32
@@ -24,20 +37,18 @@ struct DecodeParams {
     const float *ext_w;
     int internal_routing;
     // workspace
-    float *logits;        // [E]
     float *act;           // [8][I] f32 up * silu(gate)
     int8_t *aq;           // [8][I] Q8_1 quants of act
     float *ad;            // [8][I/32] fp16-rounded Q8_1 scales
     int *aS;              // [8][I/32] sums of quants
-    uint32_t *blk_count;  // [8][I/32] (unused by the current kernel; kept in the layout)
-    GridFlags *ctl;
+    DecodeCtl *ctl;
     uint64_t *trace;  // [grid][16] globaltimer stamps per phase, or null
     // shape
     int E, H, I;
     int gu_type, dn_type;
-    // launch configuration (decode_configure): lanes per row, rows per sub-unit (one warp's
-    // share) and rows per copy unit (one ring stage) of the gate/up and down matrices
-    int gu_lanes, gu_sub_rows, gu_unit_rows, dn_lanes, dn_sub_rows, stages, stage_bytes, grid;
+    // launch configuration (decode_configure): rows per gate/up copy unit, ring stages and their
+    // size, grid (one CTA per SM)
+    int gu_unit_rows, stages, stage_bytes, grid;
     int act_slots, res_slots;
     uint64_t timeout_ns;
     // multi-GPU group (world > 1): this rank's exchange region and every rank's as mapped here;

@@ -12,8 +12,8 @@
 // MMRS_ERR_SCRATCH_LIMIT before anything is launched.
 //
 // The scratch is shared by every call on a device and keeps the last call's contents.  Each call
-// clears the part that must start at zero (status word, grid-barrier counter and epochs) with a
-// memset on the caller's stream; the kernel zeroes its own per-block counters.  Calls that overlap
+// clears the part that must start at zero (the control block: status word, per-CTA arrival tags
+// and tagged router logits) with a memset on the caller's stream.  Calls that overlap
 // on the GPU (different streams or host threads without ordering) race on the scratch.
 //
 // The first call on a device resolves the device address of the array (cudaGetSymbolAddress, with
@@ -99,8 +99,8 @@ extern "C" int mmrs_moe_block_decode_static(const MmrsMoeWeights *w, const float
     cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     rc = decode_configure(p, sms, smem);
     if (rc != MMRS_OK) return rc;
-    if ((size_t)p.grid > (size_t)kMaxGridCtas) return MMRS_ERR_UNSUPPORTED;
-    // status word, barrier counter and epochs must start at zero (no allocation: a memset node)
+    if ((size_t)p.grid > (size_t)kDecodeMaxCtas) return MMRS_ERR_UNSUPPORTED;
+    // the control block (status, arrival tags, tagged logits) must start at zero (no allocation: a memset node)
     if (cudaMemsetAsync(base, 0, kControlBytes, (cudaStream_t)stream) != cudaSuccess) return MMRS_ERR_LAUNCH;
     return decode_launch(p, (cudaStream_t)stream);
 }

@@ -9,11 +9,11 @@
 namespace mmrs {
 
 struct WsLayout {
-    size_t ctl, trace, blk_count, logits, act, aq, ad, aS, total;
+    size_t ctl, trace, act, aq, ad, aS, total;
 };
 
-// [control block: status + barrier counter + per-CTA epochs (zero before first use)] | trace |
-// per-block counters (zeroed by the kernel) | logits | act | aq | ad | aS
+// [control block (DecodeCtl: status, per-CTA arrival tags, tagged router logits; zero before
+// first use)] | trace | act | aq | ad | aS
 WsLayout ws_layout(int E, int I, int max_tokens);
 void ws_bind(DecodeParams &p, uint8_t *ws, const WsLayout &l);
 int validate_weights(const MmrsMoeWeights *w);
