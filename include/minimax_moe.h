@@ -125,11 +125,13 @@ typedef struct {
     int inter;           /* 1536, or 768 per rank at TP=2 (multiple of 256)               */
 } MmrsMoeWeights;
 
-/* Device workspace the block needs for up to max_tokens tokens.  Its first 4096 bytes (status
- * word, grid-barrier tags and tagged routing logits) must be zero before first use; mmrs_moe_workspace_status()
- * clears them again after a call that reported MMRS_ERR_TIMEOUT.  Launches that share a
- * workspace must be ordered on one stream. */
+/* Device workspace the block needs for up to max_tokens tokens.  Its first
+ * mmrs_moe_workspace_zero_bytes(w) bytes (status word, launch tags, tagged routing logits, phase
+ * trace and the tagged activation records the CTAs exchange) must be zero before first use;
+ * mmrs_moe_workspace_status() clears them again after a call that reported MMRS_ERR_TIMEOUT.
+ * Launches that share a workspace must be ordered on one stream. */
 MMRS_API size_t mmrs_moe_workspace_bytes(const MmrsMoeWeights *w, int max_tokens);
+MMRS_API size_t mmrs_moe_workspace_zero_bytes(const MmrsMoeWeights *w);
 
 /* y[T][hidden] = MoE(x[T][hidden]) (+ residual[T][hidden] when non-null), f32.
  * Replaces FusedMoeGGUF::forward (fused_moe.rs:251-334) + the residual add of
@@ -153,10 +155,10 @@ MMRS_API int mmrs_moe_block_forward_host(const MmrsMoeWeights *w, const float *x
                                          size_t workspace_bytes, mmrs_stream_t stream);
 
 /* Copies the per-CTA phase timestamps (globaltimer ns, 16 slots per CTA: 0 start, 1 router done,
- * 2 routing candidates ready, 3 copy table done, 4 gate/up done, 5 second barrier passed,
- * 6 activation copied in, 7 end, 8 first weight copy issued, 9 last copy issued, 10 first down
- * copy issued, 11 second barrier arrival) of the last single-token launch into host_out.
- * Returns the number of entries copied, or -status. */
+ * 2 routing candidates ready, 3 copy table done, 4 gate/up done, 5 activation records read,
+ * 6 activation scales built, 7 end, 8 first weight copy issued, 9 last copy issued, 10 first
+ * down copy issued, 11 own activation blocks published) of the last single-token launch into
+ * host_out.  Returns the number of entries copied, or -status. */
 MMRS_API int mmrs_moe_workspace_trace(const void *workspace, uint64_t *host_out, int max_entries,
                                       mmrs_stream_t stream);
 

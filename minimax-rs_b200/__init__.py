@@ -111,6 +111,7 @@ PROTOTYPES = {
     "mmrs_moe_block_forward_group": (_I, [C.POINTER(MmrsMoeWeights), C.POINTER(MmrsPeerGroup), _VP, _VP, _VP, _I,
                                           _VP, _VP, _VP, _SZ, _U32, _VP]),
     "mmrs_moe_workspace_bytes": (_SZ, [C.POINTER(MmrsMoeWeights), _I]),
+    "mmrs_moe_workspace_zero_bytes": (_SZ, [C.POINTER(MmrsMoeWeights)]),
     "mmrs_moe_block_forward": (_I, [C.POINTER(MmrsMoeWeights), _VP, _VP, _VP, _I, _VP, _VP, _VP, _SZ, _VP]),
     "mmrs_moe_block_forward_host": (_I, [C.POINTER(MmrsMoeWeights), _VP, _VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _SZ,
                                          _VP]),

@@ -1,4 +1,5 @@
 // C ABI entry points: host-side validation, workspace layout and dispatch.
+#include <cstddef>
 #include <cstdio>
 #include <cstring>
 
@@ -97,9 +98,10 @@ __global__ void __launch_bounds__(256) decode_topk_kernel(const float *__restric
 // ------------------------------------------------------------------------------------------
 constexpr int kTraceCtas = 256, kTraceSlots = 16;
 constexpr size_t kTraceOffset = kControlBytes;
-static_assert(sizeof(DecodeCtl) <= kControlBytes, "the decode control block lies in the zeroed control bytes");
+static_assert(sizeof(DecodeCtl) <= kControlBytes, "the decode control block lies in the control bytes");
 static size_t up256(size_t v) { return (v + 255) / 256 * 256; }
-// [control block (DecodeCtl, zero before first use)] | trace | act | aq | ad | aS
+// [control block (DecodeCtl)] | trace | tagged act records (9 words a Q8_1 block); all of it
+// zero before first use (the tags of a fresh or reset workspace start again at 1)
 WsLayout ws_layout(int E, int I, int max_tokens) {
     (void)E;
     (void)max_tokens;
@@ -107,21 +109,16 @@ WsLayout ws_layout(int E, int I, int max_tokens) {
     const size_t nblk = (size_t)8 * I / 32;
     l.ctl = 0;
     l.trace = kTraceOffset;
-    l.act = l.trace + sizeof(uint64_t) * kTraceCtas * kTraceSlots;
-    l.aq = l.act + up256((size_t)8 * I * 4);
-    l.ad = l.aq + up256((size_t)8 * I);
-    l.aS = l.ad + up256(nblk * 4);
-    l.total = l.aS + up256(nblk * 4);
+    l.arec = l.trace + sizeof(uint64_t) * kTraceCtas * kTraceSlots;
+    l.total = l.arec + up256(nblk * 9 * sizeof(unsigned long long));
     return l;
 }
 
 void ws_bind(DecodeParams &p, uint8_t *ws, const WsLayout &l) {
     p.ctl = reinterpret_cast<DecodeCtl *>(ws + l.ctl);
     p.trace = reinterpret_cast<uint64_t *>(ws + l.trace);
-    p.act = reinterpret_cast<float *>(ws + l.act);
-    p.aq = reinterpret_cast<int8_t *>(ws + l.aq);
-    p.ad = reinterpret_cast<float *>(ws + l.ad);
-    p.aS = reinterpret_cast<int *>(ws + l.aS);
+    p.arec = reinterpret_cast<unsigned long long *>(ws + l.arec);
+    p.zero_bytes = (uint32_t)l.total;
 }
 
 // ------------------------------------------------------------------------------------------
@@ -314,7 +311,7 @@ extern "C" void moe_gemm_gguf_decode_silu(const float *input, const void *gate_w
         set_err(MMRS_ERR_ALLOC);
         return;
     }
-    cudaMemsetAsync(ws, 0, kControlBytes, s);
+    cudaMemsetAsync(ws, 0, l.total, s);
     ws_bind(p, ws, l);
     p.trace = nullptr;
     rc = decode_launch(p, s);
@@ -347,6 +344,10 @@ extern "C" void moe_sort_routes(const uint32_t *expert_ids_unsorted, uint32_t *e
     }
     set_err(pf_sort_routes(expert_ids_unsorted, size, end_bit, expert_ids_sorted, route_ids_sorted,
                            (cudaStream_t)stream));
+}
+
+extern "C" size_t mmrs_moe_workspace_zero_bytes(const MmrsMoeWeights *w) {
+    return w ? ws_layout(w->num_experts, w->inter, 1).total : 0;
 }
 
 extern "C" size_t mmrs_moe_workspace_bytes(const MmrsMoeWeights *w, int max_tokens) {
@@ -510,8 +511,13 @@ extern "C" int mmrs_moe_workspace_status(void *workspace, mmrs_stream_t stream) 
         return MMRS_ERR_LAUNCH;
     if (cudaStreamSynchronize(s) != cudaSuccess) return MMRS_ERR_LAUNCH;
     if (status != 0) {
-        // reset status and barrier flags so the workspace is usable again
-        cudaMemsetAsync(workspace, 0, kControlBytes, s);
+        // reset the zeroed prefix (control block, trace, tagged records: its size is kept in the
+        // control block by the kernel) so the workspace is usable again
+        uint32_t zero = 0;
+        cudaMemcpyAsync(&zero, (const uint8_t *)workspace + offsetof(DecodeCtl, zero_bytes), sizeof(zero),
+                        cudaMemcpyDeviceToHost, s);
+        cudaStreamSynchronize(s);
+        cudaMemsetAsync(workspace, 0, zero > kControlBytes ? zero : kControlBytes, s);
         cudaStreamSynchronize(s);
     }
     return (int)status;

@@ -5,15 +5,17 @@
 //   -> quantize_q8_1 -> moe_gate_up_decode_kernel -> quantize_silu_mul_q8_1
 //   -> moe_down_decode_kernel (moe_gguf.cu:200-343, 426-567) -> + residual (model.rs:218)
 //
-// One CTA per SM: 12 consumer warps + 1 producer warp.
+// One CTA per SM: 12 consumer warps + 1 producer warp.  There is no grid barrier: what one CTA
+// hands to the others travels in 64-bit words {launch tag, payload} in the workspace, written
+// and read with relaxed accesses (a release fence costs ~0.6 us, more while copies stream), and
+// a reader waits (bounded) until the words it needs carry this launch's tag.
 //   P0  router GEMV in the canonical order (8 K-slices; the CTA's two experts x 8 slices are 16
 //       (expert, slice) pairs over the 13 warps: 32 lane partials, butterfly, fixed slice tree).
-//       The router rows are requested before anything else.  Grid barrier #1: one
-//       fire-and-forget arrival per CTA.
-//   P1  the consumer warps quantise x to Q8_1 while the producer warp waits for barrier #1;
-//       eight warps then take 32 experts each (sigmoid, order-preserving selection key, rounds of
-//       redux max / min: that warp's top-8) and the producer warp merges the 64 candidates the same
-//       way, renormalises the weights and builds the copy table with its 32 lanes.
+//       The router rows are requested before anything else; the two logits are published tagged.
+//   P1  the consumer warps quantise x to Q8_1; eight warps then take 32 experts each (wait for
+//       the tagged logit, sigmoid, order-preserving selection key, rounds of redux max / min:
+//       that warp's top-8) and the producer warp merges the 64 candidates the same way,
+//       renormalises the weights and builds the copy table with its 32 lanes.
 //   P2  gate/up: the CTA owns a contiguous range of (slot, row) pairs; copy units of rows of the
 //       gate or the up matrix (one bulk copy each) stream through a ring of shared-memory stages.
 //       Consumer lane t keeps the activation of x super-block t % (H/256) in registers for the
@@ -24,18 +26,18 @@
 //       in the ring while gate/up is still being computed.
 //   P3  the CTA's gate/up range is a whole number of 32-row Q8_1 blocks, so it sums the block
 //       partials, quantises act = up * silu(gate) of its own blocks (quantize_silu_mul_q8_1
-//       arithmetic) and writes them out; grid barrier #2; one bulk copy brings the whole quantised
-//       vector into every CTA; lane t takes one (position, super-block) pair of the down rows and
-//       rows t / pairs, + slots, ...; then per output row the block partials of each expert, weighted
-//       by the route weight, the reference's fixed 8-way tree ((v0+v4)+(v2+v6))+((v1+v5)+(v3+v7)),
-//       + residual.
+//       arithmetic) and publishes each as nine tagged words; every CTA then reads all blocks
+//       into shared memory (the act exchange); lane t takes one (position, super-block) pair of
+//       the down rows and rows t / pairs, + slots, ...; then per output row the block partials
+//       of each expert, weighted by the route weight, the reference's fixed 8-way tree
+//       ((v0+v4)+(v2+v6))+((v1+v5)+(v3+v7)), + residual.
 // Lane work unit: one 256-weight super-block of a row against the lane's register copy of the
 // matching activation block: per 64-weight sub-block pair, dp4a over 32 B of quants and the MMVQ
 // combine of vec_dot_q4_K_q8_1 / _q5_K_ (gguf.cuh:727-750, 783-813):
 // dall * sum d8*(dot*sc) - dmin * sum d8*sum(q8)*m.  Integer work is the bound (the integer pipes
-// issue at half the FP32 rate), so the pair index is a compile-time constant (fixed shifts and
-// scale selection), the block header and fifth bits are loaded once per block, and activations
-// are stored swizzled so that a quarter warp's block loads hit distinct banks.
+// issue at half the FP32 rate), so the pair index is a compile-time constant (fixed scale
+// selection), the block header and fifth bits are loaded once per block, and activations are
+// stored swizzled so that a quarter warp's block loads hit distinct banks.
 // Every wait is bounded by a globaltimer deadline; on expiry the kernel records MMRS_ERR_TIMEOUT in
 // the workspace status word, keeps every named barrier matched, drains its copies and returns.
 #include <mutex>
@@ -52,11 +54,12 @@ constexpr int kWarps = kConsumerWarps + 1;  // + producer
 constexpr int kThreads = kWarps * 32;
 constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kMaxUnits = 80;
+constexpr int kActWords = 9;  // act record words a consumer thread loads at once (384 blocks: one pass)
 constexpr int kTopK = 8;
 constexpr int kRouterRounds = (16 + kWarps - 1) / kWarps;
-// named barriers: consumers; table ready, router partials (all threads); routing candidates
-// ready (the eight routing warps + the producer)
-constexpr int kBarConsumers = 1, kBarTable = 3, kBarRouter = 4, kBarCand = 6;
+// named barriers: consumers; table ready, router partials (all threads); logits counted in (the
+// eight routing warps); routing candidates ready (the eight routing warps + the producer)
+constexpr int kBarConsumers = 1, kBarTable = 3, kBarRouter = 4, kBarLogits = 5, kBarCand = 6;
 constexpr int kRouteWarps = 8;  // one expert a lane: E <= 256
 // control words in shared memory
 enum { kCtlUnits, kCtlGuUnits, kCtlGuRows, kCtlPositions, kCtlOk, kCtlFail, kCtlWords };
@@ -258,9 +261,11 @@ __device__ __forceinline__ void quant128(float4 v, int8_t *qv, int o, float *d, 
     }
 }
 
-// One Q8_1 block of 32 values, lane l holding value o + l: the quant128 arithmetic (d = amax/127,
-// q = roundf(v/d) at byte act_swz(o + l) of qv, fp16-rounded d, sum of quants).
-__device__ __forceinline__ void quant32(float v, int8_t *qv, int o, float *d, int *S, int lane) {
+// One Q8_1 block of 32 values, lane l holding value l: the quant128 arithmetic (d = amax/127,
+// q = roundf(v/d), fp16-rounded d, sum of quants), published as the block's nine tagged words:
+// quants 4j..4j+3 (word j < 8) and {fp16 bits of d, int16 sum of quants} (word 8), each with the
+// launch tag in its upper half (relaxed 64-bit stores: no fence).
+__device__ __forceinline__ void publish_block(float v, unsigned long long *rec, uint32_t tag, int lane) {
     const float amax = warp_max_butterfly(fabsf(v));
     const float dd = __fdiv_rn(amax, 127.0f);
     int qi = 0;
@@ -271,13 +276,19 @@ __device__ __forceinline__ void quant32(float v, int8_t *qv, int o, float *d, in
         exact = !(half_gap(y) > 1e-4f);
     }
     if (__any_sync(0xffffffffu, exact) && exact) qi = (int)roundf(__fdiv_rn(v, dd));
-    qv[act_swz(o + lane)] = (int8_t)qi;
     int sq = qi;
 #pragma unroll
     for (int m = 16; m > 0; m >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, m);
+    const uint32_t qb = (uint32_t)qi & 0xffu;
+    uint32_t w = qb;
+    w |= __shfl_down_sync(0xffffffffu, qb, 1) << 8;
+    w |= __shfl_down_sync(0xffffffffu, qb, 2) << 16;
+    w |= __shfl_down_sync(0xffffffffu, qb, 3) << 24;
+    const unsigned long long hi = (unsigned long long)tag << 32;
+    if ((lane & 3) == 0) st_relaxed_gpu_u64(rec + (lane >> 2), hi | w);
     if (lane == 0) {
-        *d = __half2float(__float2half_rn(dd));
-        *S = sq;
+        const uint32_t dbits = __half_as_ushort(__float2half_rn(dd));  // |sum of quants| <= 32 * 127
+        st_relaxed_gpu_u64(rec + 8, hi | dbits | ((uint32_t)(sq & 0xffff) << 16));
     }
 }
 
@@ -308,6 +319,16 @@ __device__ __forceinline__ bool wait_unit(uint64_t *full, const int *ticket, int
         if ((++spins & 255u) == 0 && globaltimer_ns() > deadline) return false;
     }
     return mbar_wait_sleep(&full[st], (uint32_t)(k / stages) & 1u, deadline);
+}
+
+// One thread's bounded wait until an exchange counter reaches `target` (wrap-safe).
+__device__ __forceinline__ bool wait_count(const uint32_t *cnt, uint32_t target, uint64_t deadline) {
+    uint32_t spins = 0;
+    while ((int)(ld_relaxed_gpu(cnt) - target) < 0) {
+        __nanosleep(32);
+        if ((++spins & 255u) == 0 && globaltimer_ns() > deadline) return false;
+    }
+    return true;
 }
 
 // arrive.expect_tx whose arrival state is not returned (the issuing thread does not wait for it)
@@ -342,7 +363,6 @@ __host__ __device__ inline size_t decode_part_floats(const DecodeParams &p) {
 struct DecodeSmem {
     uint8_t *stages;
     uint64_t *full;
-    uint64_t *abar;            // the quantised act copy after barrier #2
     int8_t *xq;                // [H]
     float *xd;                 // [H/32]
     int *xS;                   // [H/32]
@@ -421,7 +441,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         };
         s.stages = take((size_t)p.stages * p.stage_bytes);
         s.full = reinterpret_cast<uint64_t *>(take(sizeof(uint64_t) * p.stages));
-        s.abar = reinterpret_cast<uint64_t *>(take(sizeof(uint64_t)));
         s.xq = reinterpret_cast<int8_t *>(take(H));
         s.xd = reinterpret_cast<float *>(take(sizeof(float) * (H / 32)));
         s.xS = reinterpret_cast<int *>(take(sizeof(int) * (H / 32)));
@@ -464,10 +483,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             s.ticket[i] = -1;
             s.done[i] = 0;
         }
-        mbar_init(s.abar, 1);
         fence_mbar_init();
         for (int i = 0; i < kCtlWords; ++i) s.ctl[i] = 0;
         s.ctl[kCtlOk] = 1;  // cleared by a routing lane whose logit wait expires
+        if (cta == 0) p.ctl->zero_bytes = p.zero_bytes;
     }
 
     // ---- P0: router slices -------------------------------------------------------------------
@@ -495,11 +514,17 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         if (ee < E) {
             const float *q = s.part + tid * 8;
             const float lg = ((q[0] + q[1]) + (q[2] + q[3])) + ((q[4] + q[5]) + (q[6] + q[7]));
-            // published with this launch's tag in the same 64-bit word: no separate grid barrier
+            // published with this launch's tag in the same 64-bit word
             st_relaxed_gpu_u64(&p.ctl->logit[ee], ((unsigned long long)tag << 32) | __float_as_uint(lg));
         }
     }
-    if (tid == 0 && p.trace) p.trace[cta * 16 + 1] = globaltimer_ns();
+    if (warp == 0) {
+        __syncwarp();
+        if (lane == 0) {
+            red_relaxed_gpu_add(&p.ctl->n_logit, 1u);  // every launch: the count stays G * tag
+            if (p.trace) p.trace[cta * 16 + 1] = globaltimer_ns();
+        }
+    }
 
     const size_t gu_row_bytes = kq_row_bytes(p.gu_type, H);
     const size_t dn_row_bytes = kq_row_bytes(p.dn_type, I);
@@ -681,12 +706,20 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         // an order-preserving key, and this warp's top-8 of its 32 experts by rounds of redux max
         // (key) and redux min (id among the lanes holding it)
         const int e = 32 * warp + lane;
+        if (p.internal_routing) {
+            // every CTA has counted its logits in: one thread waits, the routing warps follow
+            if (tid == 0 && !wait_count(&p.ctl->n_logit, (uint32_t)G * tag, deadline)) {
+                atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
+                s.ctl[kCtlOk] = 0;
+            }
+            named_sync(kBarLogits, 32 * kRouteWarps);
+        }
         if (p.internal_routing && 32 * warp < E) {
             uint32_t key = 0u;  // experts >= E are never selected (E >= 8 real keys are > 0)
             if (e < E) {
                 unsigned long long v = ld_relaxed_gpu_u64(&p.ctl->logit[e]);
                 uint32_t spins = 0;
-                while ((uint32_t)(v >> 32) != tag) {
+                while ((uint32_t)(v >> 32) != tag && s.ctl[kCtlOk]) {
                     __nanosleep(32);
                     if ((++spins & 63u) == 0 && globaltimer_ns() > deadline) {
                         atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
@@ -800,51 +833,60 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             s.gval[i] = s.uval[i] * __fdiv_rn(gv, 1.0f + expf(-gv));
         }
         named_sync(kBarConsumers, kConsumerThreads);
-        // quantize_silu_mul_q8_1 (moe_gguf.cu:255-284): one warp per block of 32 rows
+        // quantize_silu_mul_q8_1 (moe_gguf.cu:255-284): one warp per block of 32 rows, published
         for (int b = gu_p0 / 32 + warp; b < gu_p1 / 32 && !aborted; b += kConsumerWarps)
-            quant32(s.gval[32 * b - gu_p0 + lane], p.aq, 32 * b, p.ad + b, p.aS + b, lane);
+            publish_block(s.gval[32 * b - gu_p0 + lane], p.arec + (size_t)9 * b, tag, lane);
+    }
+    // ---- the act exchange (in place of a grid barrier): this CTA's records are written, so it
+    // counts itself in; one thread waits for every CTA's count, then the consumer threads read
+    // the record words coalesced (thread t: words t, t + 384, ...), re-reading any word whose tag
+    // is not yet current, and unpack them into the shared copy of act
+    named_sync(kBarConsumers, kConsumerThreads);
+    if (tid == 0) {
+        red_relaxed_gpu_add(&p.ctl->n_act, 1u);
+        if (p.trace) p.trace[cta * 16 + 11] = globaltimer_ns();
+        if (ok1 && !wait_count(&p.ctl->n_act, (uint32_t)G * tag, deadline)) {
+            atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
+            s.ctl[kCtlFail] = 1;
+        }
     }
     named_sync(kBarConsumers, kConsumerThreads);
-    // grid barrier #2: release this CTA's tag (its act blocks are written; the CTA barrier above
-    // orders every thread's writes before it), then consumer thread c < G acquires CTA c's tag.
-    // The tag is released even after a failed routing wait, so that no other CTA waits for it.
-    if (tid == 0) {
-        if (p.trace) p.trace[cta * 16 + 11] = globaltimer_ns();
-        st_release_gpu(&p.ctl->arrive[cta], tag);
-    }
-    if (tid < G && ok1) {
-        uint32_t spins = 0;
-        while ((int)(ld_acquire_gpu(&p.ctl->arrive[tid]) - tag) < 0) {
-            __nanosleep(32);
-            if ((++spins & 63u) == 0 && globaltimer_ns() > deadline) {
-                atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
-                s.ctl[kCtlFail] = 1;
-                break;
+    {
+        // all of a thread's loads in flight at once (kActWords per pass), then the tag checks
+        const int nwords = 9 * (nvs * I / 32);
+        for (int w0 = 0; w0 < nwords && ok1 && !s.ctl[kCtlFail]; w0 += kActWords * kConsumerThreads) {
+            unsigned long long v[kActWords];
+#pragma unroll
+            for (int i = 0; i < kActWords; ++i) {
+                const int wi = w0 + tid + i * kConsumerThreads;
+                v[i] = wi < nwords ? ld_relaxed_gpu_u64(p.arec + wi) : 0ull;
+            }
+#pragma unroll
+            for (int i = 0; i < kActWords; ++i) {
+                const int wi = w0 + tid + i * kConsumerThreads;
+                if (wi >= nwords) continue;
+                uint32_t spins = 0;
+                while ((uint32_t)(v[i] >> 32) != tag) {
+                    __nanosleep(64);
+                    if ((++spins & 63u) == 0 && globaltimer_ns() > deadline) {
+                        atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
+                        s.ctl[kCtlFail] = 1;
+                        break;
+                    }
+                    v[i] = ld_relaxed_gpu_u64(p.arec + wi);
+                }
+                const int b = wi / 9, j = wi - 9 * b;
+                if (j < 8) {
+                    *reinterpret_cast<uint32_t *>(s.aq_s + act_swz(32 * b + 4 * j)) = (uint32_t)v[i];
+                } else {
+                    s.ad_s[b] = __half2float(__ushort_as_half((unsigned short)(v[i] & 0xffffu)));
+                    s.aS_s[b] = (int)(short)((uint32_t)v[i] >> 16);
+                }
             }
         }
     }
-    named_sync(kBarConsumers, kConsumerThreads);
-    if (tid == 0) {
-        bool ok2 = ok1 && s.ctl[kCtlFail] == 0;
-        if (p.trace) p.trace[cta * 16 + 5] = globaltimer_ns();
-        // the whole quantised act [positions][I] (+ scales, sums) in one bulk copy per array; the
-        // other CTAs' generic writes (acquired above) are ordered before these async-proxy reads
-        bool copied = false;
-        if (ok2 && nvs > 0) {
-            const uint32_t qb = (uint32_t)(nvs * I), sb = (uint32_t)(sizeof(float) * nvs * (I / 32));
-            asm volatile("fence.proxy.async;" ::: "memory");
-            mbar_arrive_expect_tx(s.abar, qb + 2 * sb);
-            bulk_g2s(s.aq_s, p.aq, qb, s.abar);
-            bulk_g2s(s.ad_s, p.ad, sb, s.abar);
-            bulk_g2s(s.aS_s, p.aS, sb, s.abar);
-            copied = true;
-        }
-        if (copied && !mbar_wait_bounded(s.abar, 0u, deadline + 1000000000ull)) {
-            atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
-            ok2 = false;
-        }
-        s.ctl[kCtlFail] = ok2 ? 0 : 1;
-    }
+    if (!ok1 && tid == 0) s.ctl[kCtlFail] = 1;
+    if (tid == 0 && p.trace) p.trace[cta * 16 + 5] = globaltimer_ns();
     named_sync(kBarConsumers, kConsumerThreads);
     if (s.ctl[kCtlFail]) aborted = true;
     build_task_scales(s.ats, s.ad_s, s.aS_s, nvs * (I / 64), tid, kConsumerThreads);
@@ -960,7 +1002,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             if (k >= 0) mbar_wait_bounded(&s.full[st], (uint32_t)(k / p.stages) & 1u, deadline + 1000000000ull);
         }
     }
-    if (tid == 0 && p.trace) p.trace[cta * 16 + 7] = globaltimer_ns();
+    if (tid == 0) {
+        p.ctl->arrive[cta] = tag;  // this CTA's launch count (read only by this CTA's next launch)
+        if (p.trace) p.trace[cta * 16 + 7] = globaltimer_ns();
+    }
 }
 
 // ------------------------------------------------------------------------------------------
@@ -968,7 +1013,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
 // ------------------------------------------------------------------------------------------
 size_t decode_smem_bytes(const DecodeParams &p) {
     auto a16 = [](size_t v) { return (v + 15) / 16 * 16; };
-    size_t b = a16((size_t)p.stages * p.stage_bytes) + a16(sizeof(uint64_t) * p.stages) + a16(sizeof(uint64_t));
+    size_t b = a16((size_t)p.stages * p.stage_bytes) + a16(sizeof(uint64_t) * p.stages);
     b += a16(p.H) + 2 * a16(4 * (p.H / 32)) + a16(16 * (p.H / 64));
     b += a16((size_t)kTopK * p.I) + 2 * a16(4 * kTopK * (p.I / 32)) + a16(16 * kTopK * (p.I / 64));
     b += a16(4 * 16) + a16(4 * 256) + a16(4 * 128) + 4 * a16(4 * kTopK);  // part, sig, cand, ids, vslot, posof, w

@@ -5,17 +5,28 @@
 
 namespace mmrs {
 
-// Control block of the single-token kernel at the start of its workspace (zero before first use;
-// it lies within the zeroed control bytes of the workspace contract).  Launch n (n = 1, 2, ...)
-// of a workspace carries the tag n:
-//   arrive[c]  the tag of CTA c's last launch, released at the second grid barrier once the
-//              CTA's activation blocks are written (so a CTA's own word is also its launch count);
-//   logit[e]   the router logit of expert e with the tag of the launch that wrote it in the upper
-//              32 bits: a reader that sees the current tag sees the current value (one 64-bit word).
+// Control block of the single-token kernel at the start of its workspace.  Launch n (n = 1, 2,
+// ...) of a workspace carries the tag n, and everything one CTA hands to the others travels in
+// 64-bit words {tag, payload} written and read with relaxed stores and loads: a reader that sees
+// the current tag sees the current payload, with no fence.  After writing its words, each CTA
+// adds 1 (relaxed) to the exchange's counter, which reaches G * n in launch n: one thread per
+// CTA waits for that, then the CTA reads the words (coalesced), re-reading any whose tag is not
+// yet current.  (Polling the data words themselves from every CTA piles thousands of requests a
+// round onto a few L2 lines.)
+//   n_logit, n_act  the two exchange counters (each on its own 128-byte line);
+//   arrive[c]   the tag of CTA c's last launch (its launch count; read only by CTA c);
+//   logit[e]    the router logit of expert e (payload: the f32 bits);
+//   zero_bytes  the size of the workspace prefix that must be zero before first use (control
+//               block, trace and the tagged activation records), for the status reset.
 constexpr int kDecodeMaxCtas = 256;
 struct DecodeCtl {
     uint32_t status;  // MMRS_OK, or MMRS_ERR_TIMEOUT once any wait expired
-    uint32_t pad0[31];
+    uint32_t zero_bytes;
+    uint32_t pad0[30];
+    uint32_t n_logit;
+    uint32_t pad1[31];
+    uint32_t n_act;
+    uint32_t pad2[31];
     uint32_t arrive[kDecodeMaxCtas];
     unsigned long long logit[256];
 };
@@ -37,10 +48,9 @@ struct DecodeParams {
     const float *ext_w;
     int internal_routing;
     // workspace
-    float *act;           // [8][I] f32 up * silu(gate)
-    int8_t *aq;           // [8][I] Q8_1 quants of act
-    float *ad;            // [8][I/32] fp16-rounded Q8_1 scales
-    int *aS;              // [8][I/32] sums of quants
+    unsigned long long *arec;  // [8 I / 32][9] tagged Q8_1 records of act: quants 4j..4j+3 (word
+                               // j < 8), {fp16 scale, int16 sum of quants} (word 8)
+    uint32_t zero_bytes;       // workspace prefix that must start at zero
     DecodeCtl *ctl;
     uint64_t *trace;  // [grid][16] globaltimer stamps per phase, or null
     // shape

@@ -12,8 +12,9 @@
 // MMRS_ERR_SCRATCH_LIMIT before anything is launched.
 //
 // The scratch is shared by every call on a device and keeps the last call's contents.  Each call
-// clears the part that must start at zero (the control block: status word, per-CTA arrival tags
-// and tagged router logits) with a memset on the caller's stream.  Calls that overlap
+// starts at zero and is never cleared between calls: its launch tags keep counting, so the
+// tagged words a call hands between CTAs never match a stale word of an earlier call
+// (mmrs_moe_static_status clears it after a call that failed).  Calls that overlap
 // on the GPU (different streams or host threads without ordering) race on the scratch.
 //
 // The first call on a device resolves the device address of the array (cudaGetSymbolAddress, with
@@ -100,8 +101,8 @@ extern "C" int mmrs_moe_block_decode_static(const MmrsMoeWeights *w, const float
     rc = decode_configure(p, sms, smem);
     if (rc != MMRS_OK) return rc;
     if ((size_t)p.grid > (size_t)kDecodeMaxCtas) return MMRS_ERR_UNSUPPORTED;
-    // the control block (status, arrival tags, tagged logits) must start at zero (no allocation: a memset node)
-    if (cudaMemsetAsync(base, 0, kControlBytes, (cudaStream_t)stream) != cudaSuccess) return MMRS_ERR_LAUNCH;
+    // the scratch starts at zero (a device array) and its launch tags keep counting from call to
+    // call: nothing is cleared here (mmrs_moe_static_status clears it after a failed call)
     return decode_launch(p, (cudaStream_t)stream);
 }
 
@@ -117,7 +118,8 @@ extern "C" int mmrs_moe_static_status(mmrs_stream_t stream) {
         return MMRS_ERR_LAUNCH;
     if (cudaStreamSynchronize(s) != cudaSuccess) return MMRS_ERR_LAUNCH;
     if (status != 0) {
-        if (cudaMemsetAsync(base, 0, kControlBytes, s) != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess)
+        // the whole scratch: control block, trace and tagged records
+        if (cudaMemsetAsync(base, 0, kStaticScratchBytes, s) != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess)
             return MMRS_ERR_LAUNCH;
     }
     return (int)status;

@@ -9,11 +9,10 @@
 namespace mmrs {
 
 struct WsLayout {
-    size_t ctl, trace, act, aq, ad, aS, total;
+    size_t ctl, trace, arec, total;
 };
 
-// [control block (DecodeCtl: status, per-CTA arrival tags, tagged router logits; zero before
-// first use)] | trace | act | aq | ad | aS
+// [control block (DecodeCtl)] | trace | tagged act records; all of it zero before first use
 WsLayout ws_layout(int E, int I, int max_tokens);
 void ws_bind(DecodeParams &p, uint8_t *ws, const WsLayout &l);
 int validate_weights(const MmrsMoeWeights *w);
