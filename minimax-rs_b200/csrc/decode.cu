@@ -407,7 +407,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     const int dn_r0 = (int)((uint32_t)(cta * H) / (uint32_t)G), dn_r1 = (int)((uint32_t)((cta + 1) * H) / (uint32_t)G);
     const int nres = dn_r1 - dn_r0;
 
-    // ---- P0 loads first: the CTA's router rows and the matching x slices ---------------------
+    // ---- P0 loads first: the CTA's router rows (weights: they do not depend on the previous
+    // kernel in the stream, so they are requested before the programmatic-launch wait), then,
+    // after it, the matching x slices ---------------------------------------------------------
     const int slice = H / 8, groups = slice / 4;
     float4 xx[kRouterRounds][4], wv[kRouterRounds][4];
 #pragma unroll
@@ -415,13 +417,26 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         const int pi = warp + kWarps * r, sl = pi & 7, le = pi >> 3;
         const int e = cta + G * le;
         if (pi < 16 && p.internal_routing && e < E) {
-            const float4 *xs = reinterpret_cast<const float4 *>(p.x + sl * slice);
             const float4 *wr = reinterpret_cast<const float4 *>(p.router + (size_t)e * H + sl * slice);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const int g = lane + 32 * i;
+                if (g < groups) wv[r][i] = __ldg(wr + g);
+            }
+        }
+    }
+    // everything below reads the previous kernel's outputs (x, the workspace)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+#pragma unroll
+    for (int r = 0; r < kRouterRounds; ++r) {
+        const int pi = warp + kWarps * r, sl = pi & 7, le = pi >> 3;
+        const int e = cta + G * le;
+        if (pi < 16 && p.internal_routing && e < E) {
+            const float4 *xs = reinterpret_cast<const float4 *>(p.x + sl * slice);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int g = lane + 32 * i;
                 if (g < groups) {
-                    wv[r][i] = __ldg(wr + g);
                     xx[r][i] = __ldg(xs + g);
                 }
             }
@@ -893,6 +908,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     named_sync(kBarConsumers, kConsumerThreads);
     if (tid == 0 && p.trace) p.trace[cta * 16 + 6] = globaltimer_ns();
 
+    // the next kernel in the stream may start its CTAs as this kernel's CTAs retire
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // ---- P3: down: lane t takes (position, block) pair t % pairs and rows t / pairs, + slots, ...
     {
         constexpr int BB = DN == MMRS_Q5K ? Q5K_BYTES : Q4K_BYTES;
@@ -1078,9 +1095,13 @@ static int launch_typed(const DecodeParams &p, size_t smem, cudaStream_t stream)
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
+    // Programmatic dependent launch: the CTAs start (router weights in flight) while the previous
+    // kernel retires; griddepcontrol.wait in the kernel orders everything that reads its outputs.
+    // No cooperative launch: one CTA per SM always fits (grid = SM count, whole-SM shared memory)
+    // and every cross-CTA wait is bounded.
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     const cudaError_t err = cudaLaunchKernelEx(&cfg, moe_decode_fused_kernel<GU, DN>, p);
