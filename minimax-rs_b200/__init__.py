@@ -112,6 +112,7 @@ PROTOTYPES = {
                                           _VP, _VP, _VP, _SZ, _U32, _VP]),
     "mmrs_moe_workspace_bytes": (_SZ, [C.POINTER(MmrsMoeWeights), _I]),
     "mmrs_moe_workspace_zero_bytes": (_SZ, [C.POINTER(MmrsMoeWeights)]),
+    "mmrs_int8_tensor_peak": (_I, [_I, _I, C.POINTER(C.c_double), _VP]),
     "mmrs_moe_block_forward": (_I, [C.POINTER(MmrsMoeWeights), _VP, _VP, _VP, _I, _VP, _VP, _VP, _SZ, _VP]),
     "mmrs_moe_block_forward_host": (_I, [C.POINTER(MmrsMoeWeights), _VP, _VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _SZ,
                                          _VP]),
@@ -244,6 +245,13 @@ def sort_routes(expert_ids, end_bit: int, stream=None):
     lib().moe_sort_routes(expert_ids.data_ptr(), keys.data_ptr(), routes.data_ptr(), n, end_bit, _stream(stream))
     check(last_error(), "moe_sort_routes")
     return keys, routes
+
+
+def int8_tensor_peak(chunks: int = 4096, reps: int = 5, stream=None) -> float:
+    """Measured dense int8 tensor-core throughput of the current device, TOPS (mmrs_int8_tensor_peak)."""
+    out = C.c_double(0.0)
+    check(lib().mmrs_int8_tensor_peak(chunks, reps, C.byref(out), _stream(stream)), "mmrs_int8_tensor_peak")
+    return out.value
 
 
 def synth_normal(t, seed: int, stream_id: int, scale: float = 1.0, bf16: bool = False, stream=None):

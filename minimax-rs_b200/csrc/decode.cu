@@ -57,9 +57,9 @@ constexpr int kMaxUnits = 80;
 constexpr int kActWords = 9;  // act record words a consumer thread loads at once (384 blocks: one pass)
 constexpr int kTopK = 8;
 constexpr int kRouterRounds = (16 + kWarps - 1) / kWarps;
-// named barriers: consumers; table ready, router partials (all threads); logits counted in (the
-// eight routing warps); routing candidates ready (the eight routing warps + the producer)
-constexpr int kBarConsumers = 1, kBarTable = 3, kBarRouter = 4, kBarLogits = 5, kBarCand = 6;
+// named barriers: consumers; table ready, router partials (all threads); routing candidates
+// ready (the eight routing warps + the producer)
+constexpr int kBarConsumers = 1, kBarTable = 3, kBarRouter = 4, kBarCand = 6;
 constexpr int kRouteWarps = 8;  // one expert a lane: E <= 256
 // control words in shared memory
 enum { kCtlUnits, kCtlGuUnits, kCtlGuRows, kCtlPositions, kCtlOk, kCtlFail, kCtlWords };
@@ -533,13 +533,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             st_relaxed_gpu_u64(&p.ctl->logit[ee], ((unsigned long long)tag << 32) | __float_as_uint(lg));
         }
     }
-    if (warp == 0) {
-        __syncwarp();
-        if (lane == 0) {
-            red_relaxed_gpu_add(&p.ctl->n_logit, 1u);  // every launch: the count stays G * tag
-            if (p.trace) p.trace[cta * 16 + 1] = globaltimer_ns();
-        }
-    }
+    if (tid == 0 && p.trace) p.trace[cta * 16 + 1] = globaltimer_ns();
 
     const size_t gu_row_bytes = kq_row_bytes(p.gu_type, H);
     const size_t dn_row_bytes = kq_row_bytes(p.dn_type, I);
@@ -575,22 +569,29 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         float slot_w = 0.f;
         if (p.internal_routing) {
             if (ok) {
+                // rank of candidates lane and lane + 32 among all nc (larger key first, lower expert
+                // id among equal keys: the stable descending order); the 8 best are the slots.
+                // Every real expert's key is > 0, and the per-warp lists hold the global top-8.
                 const int nc = 8 * ((E + 31) / 32);
                 const uint32_t ka = lane < nc ? s.cand[lane] : 0u, ia = lane < nc ? s.cand[64 + lane] : 0xffffffffu;
                 const uint32_t kb = lane + 32 < nc ? s.cand[lane + 32] : 0u;
                 const uint32_t ib = lane + 32 < nc ? s.cand[64 + lane + 32] : 0xffffffffu;
-                bool ta = false, tb = false;
+                int ra = 0, rb = 0;
+                for (int j = 0; j < nc; j += 4) {  // nc is a multiple of 8
+                    const uint4 kj = *reinterpret_cast<const uint4 *>(s.cand + j);
+                    const uint4 ij = *reinterpret_cast<const uint4 *>(s.cand + 64 + j);
+                    const uint32_t kk[4] = {kj.x, kj.y, kj.z, kj.w}, ii[4] = {ij.x, ij.y, ij.z, ij.w};
 #pragma unroll
-                for (int k = 0; k < kTopK; ++k) {
-                    // larger key first, lower expert id among equal keys (the stable descending order)
-                    const uint32_t mk = __reduce_max_sync(0xffffffffu, max(ta ? 0u : ka, tb ? 0u : kb));
-                    const uint32_t ca = (!ta && ka == mk) ? ia : 0xffffffffu;
-                    const uint32_t cb = (!tb && kb == mk) ? ib : 0xffffffffu;
-                    const uint32_t me = __reduce_min_sync(0xffffffffu, min(ca, cb));
-                    if (ca == me) ta = true;
-                    else if (cb == me) tb = true;
-                    if (lane == k) slot_id = (int)me;
+                    for (int q = 0; q < 4; ++q) {  // branch-free: (key greater) | (key equal & id lower)
+                        ra += (int)(kk[q] > ka) | ((int)(kk[q] == ka) & (int)(ii[q] < ia));
+                        rb += (int)(kk[q] > kb) | ((int)(kk[q] == kb) & (int)(ii[q] < ib));
+                    }
                 }
+                __syncwarp();
+                if (lane < nc && ra < kTopK) s.ids[ra] = (int)ia;
+                if (lane + 32 < nc && rb < kTopK) s.ids[rb] = (int)ib;
+                __syncwarp();
+                if (lane < kTopK) slot_id = s.ids[lane];
                 // weights: sig / ((v0+v4)+(v2+v6))+((v1+v5)+(v3+v7)), lane k keeps w_k
                 const float my_sig = lane < kTopK ? s.sig[slot_id] : 0.f;
                 float v[kTopK];
@@ -661,9 +662,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             q = seg_end;
         }
         const int n_gu_units = 2 * n_chunks;
-        // gate/up rows in unit order: chunk c's gate rows (unit 2c), then its up rows (2c + 1);
-        // the row map gives each its unit, its row in the unit and its partial-sum row
-        // (gate rows first, then up rows, by the (position, row) offset in the CTA's range)
         const int cnt = gu_p1 - gu_p0;
         if (my_pos >= 0) {
             for (int h = 0; h < 2; ++h) {
@@ -673,8 +671,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
                 const int e = s.ids[s.vslot[my_pos]];
                 s.usrc[k] = (h == 0 ? p.gate : p.up) + (size_t)e * gu_expert_bytes + (size_t)my_row0 * gu_row_bytes;
                 s.ubytes[k] = (uint32_t)(gu_row_bytes * my_n);
-                for (int r = 0; r < my_n; ++r)
-                    s.rowmap[2 * my_off + h * my_n + r] = make_int2(k | (r << 16), h * cnt + my_off + r);
             }
         }
         // down units: one per position, all of this CTA's output rows
@@ -693,13 +689,23 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             s.ctl[kCtlGuRows] = 2 * cnt;
             s.ctl[kCtlPositions] = nvs;
             s.ctl[kCtlOk] = ok ? 1 : 0;
-            if (p.trace) p.trace[cta * 16 + 3] = globaltimer_ns();
         }
+        __syncwarp();
+        // ---- first ring fill, one unit per lane, before the row map: later units are issued by
+        // the consumer lanes -------------------------------------------------------------------
+        if (ok && lane < min(n_gu_units + n_dn_units, p.stages)) issue(lane);
+        // gate/up rows in unit order: chunk c's gate rows (unit 2c), then its up rows (2c + 1);
+        // the row map gives each its unit, its row in the unit and its partial-sum row
+        // (gate rows first, then up rows, by the (position, row) offset in the CTA's range)
+        if (my_pos >= 0) {
+            for (int h = 0; h < 2; ++h)
+                for (int r = 0; r < my_n; ++r)
+                    s.rowmap[2 * my_off + h * my_n + r] = make_int2((2 * lane + h) | (r << 16), h * cnt + my_off + r);
+        }
+        if (lane == 0 && p.trace) p.trace[cta * 16 + 3] = globaltimer_ns();
         __syncwarp();
         named_arrive(kBarTable, kThreads);  // table complete: the consumers may start
         __syncwarp();
-        // ---- first ring fill, one unit per lane; later units are issued by the consumer lanes -----
-        if (ok && lane < min(n_gu_units + n_dn_units, p.stages)) issue(lane);
         return;
     }
 
@@ -718,24 +724,17 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     named_sync(kBarConsumers, kConsumerThreads);  // x's Q8_1 and its records are complete
     if (warp < kRouteWarps) {
         // this launch's logit of expert e (bounded wait for its tag); sigmoid, selection score as
-        // an order-preserving key, and this warp's top-8 of its 32 experts by rounds of redux max
-        // (key) and redux min (id among the lanes holding it)
+        // an order-preserving key, and this warp's top-8 of its 32 experts by rank
         const int e = 32 * warp + lane;
-        if (p.internal_routing) {
-            // every CTA has counted its logits in: one thread waits, the routing warps follow
-            if (tid == 0 && !wait_count(&p.ctl->n_logit, (uint32_t)G * tag, deadline)) {
-                atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
-                s.ctl[kCtlOk] = 0;
-            }
-            named_sync(kBarLogits, 32 * kRouteWarps);
-        }
+        // each routing lane polls its expert's tagged logit directly (one coalesced 256-byte
+        // request per warp and round: ~150 requests per L2 line and round over the grid)
         if (p.internal_routing && 32 * warp < E) {
             uint32_t key = 0u;  // experts >= E are never selected (E >= 8 real keys are > 0)
             if (e < E) {
                 unsigned long long v = ld_relaxed_gpu_u64(&p.ctl->logit[e]);
                 uint32_t spins = 0;
-                while ((uint32_t)(v >> 32) != tag && s.ctl[kCtlOk]) {
-                    __nanosleep(32);
+                while ((uint32_t)(v >> 32) != tag) {
+                    __nanosleep(64);
                     if ((++spins & 63u) == 0 && globaltimer_ns() > deadline) {
                         atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
                         s.ctl[kCtlOk] = 0;
@@ -747,16 +746,18 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
                 s.sig[e] = sg;
                 key = sel_key(sg, __ldg(p.bias + e));
             }
-            bool taken = false;
-#pragma unroll
-            for (int k = 0; k < kTopK; ++k) {
-                const uint32_t mk = __reduce_max_sync(0xffffffffu, taken ? 0u : key);
-                const uint32_t me = __reduce_min_sync(0xffffffffu, (!taken && key == mk) ? (uint32_t)e : 0xffffffffu);
-                taken |= (uint32_t)e == me;
-                if (lane == 0) {
-                    s.cand[8 * warp + k] = mk;
-                    s.cand[64 + 8 * warp + k] = me;
-                }
+            // rank of this lane's expert among the warp's 32: lanes with a larger key, or an equal
+            // key and a lower expert id (the stable descending order); the warp's best 8 go to
+            // shared memory in rank order
+            int rank = 0;
+#pragma unroll 8
+            for (int j = 0; j < 32; ++j) {
+                const uint32_t kj = __shfl_sync(0xffffffffu, key, j);
+                rank += (int)(kj > key) | ((int)(kj == key) & (int)(j < lane));
+            }
+            if (rank < kTopK) {
+                s.cand[8 * warp + rank] = key;
+                s.cand[64 + 8 * warp + rank] = (uint32_t)e;
             }
         }
         named_arrive(kBarCand, 32 * (kRouteWarps + 1));
@@ -853,9 +854,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             publish_block(s.gval[32 * b - gu_p0 + lane], p.arec + (size_t)9 * b, tag, lane);
     }
     // ---- the act exchange (in place of a grid barrier): this CTA's records are written, so it
-    // counts itself in; one thread waits for every CTA's count, then the consumer threads read
-    // the record words coalesced (thread t: words t, t + 384, ...), re-reading any word whose tag
-    // is not yet current, and unpack them into the shared copy of act
+    // counts itself in; one thread waits until every CTA has, then the consumer threads read the
+    // record words coalesced (thread t: words t, t + 384, ...), re-reading any word whose tag is
+    // not yet current (the count is relaxed), and unpack them into the shared act.  (Starting
+    // the reads before the last CTAs count in and re-polling their words cost ~0.9 us.)
     named_sync(kBarConsumers, kConsumerThreads);
     if (tid == 0) {
         red_relaxed_gpu_add(&p.ctl->n_act, 1u);
@@ -882,7 +884,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
                 if (wi >= nwords) continue;
                 uint32_t spins = 0;
                 while ((uint32_t)(v[i] >> 32) != tag) {
-                    __nanosleep(64);
+                    __nanosleep(128);
                     if ((++spins & 63u) == 0 && globaltimer_ns() > deadline) {
                         atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
                         s.ctl[kCtlFail] = 1;

@@ -8,12 +8,11 @@ namespace mmrs {
 // Control block of the single-token kernel at the start of its workspace.  Launch n (n = 1, 2,
 // ...) of a workspace carries the tag n, and everything one CTA hands to the others travels in
 // 64-bit words {tag, payload} written and read with relaxed stores and loads: a reader that sees
-// the current tag sees the current payload, with no fence.  After writing its words, each CTA
-// adds 1 (relaxed) to the exchange's counter, which reaches G * n in launch n: one thread per
-// CTA waits for that, then the CTA reads the words (coalesced), re-reading any whose tag is not
-// yet current.  (Polling the data words themselves from every CTA piles thousands of requests a
-// round onto a few L2 lines.)
-//   n_logit, n_act  the two exchange counters (each on its own 128-byte line);
+// the current tag sees the current payload, with no fence.  The routing lanes poll the logit
+// words directly.  For the activation records, each CTA adds 1 (relaxed) to a counter after
+// writing its words, which reaches G * n in launch n: one thread per CTA waits for that, then the
+// CTA reads the words (coalesced), re-reading any whose tag is not yet current.
+//   n_act       the activation exchange counter (on its own 128-byte line);
 //   arrive[c]   the tag of CTA c's last launch (its launch count; read only by CTA c);
 //   logit[e]    the router logit of expert e (payload: the f32 bits);
 //   zero_bytes  the size of the workspace prefix that must be zero before first use (control
@@ -23,8 +22,6 @@ struct DecodeCtl {
     uint32_t status;  // MMRS_OK, or MMRS_ERR_TIMEOUT once any wait expired
     uint32_t zero_bytes;
     uint32_t pad0[30];
-    uint32_t n_logit;
-    uint32_t pad1[31];
     uint32_t n_act;
     uint32_t pad2[31];
     uint32_t arrive[kDecodeMaxCtas];

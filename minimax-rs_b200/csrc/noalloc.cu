@@ -43,11 +43,22 @@ static __device__ __align__(256) uint8_t g_decode_scratch[kStaticScratchBytes];
 static std::mutex g_scratch_mu;
 static void *g_scratch_addr[64];
 
-// Device address of g_decode_scratch on the current device (resolved once per device).
+// Device address of g_decode_scratch on the current device, cached per device and checked on
+// every call: after a device reset the context (and the array's address) is new, so a cached
+// address that no longer resolves to device memory of this context is looked up again (the array
+// itself is zero again then, as its launch tags require).
 static int scratch_address(void **out) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MMRS_ERR_LAUNCH;
     std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (g_scratch_addr[dev]) {
+        cudaPointerAttributes a = {};
+        if (cudaPointerGetAttributes(&a, g_scratch_addr[dev]) != cudaSuccess || a.type != cudaMemoryTypeDevice ||
+            a.device != dev) {
+            cudaGetLastError();  // clear the lookup's error state
+            g_scratch_addr[dev] = nullptr;
+        }
+    }
     if (!g_scratch_addr[dev]) {
         void *ptr = nullptr;
         if (cudaGetSymbolAddress(&ptr, g_decode_scratch) != cudaSuccess || !ptr) return MMRS_ERR_LAUNCH;
