@@ -211,7 +211,8 @@ MMRS_API void launch_tp2_peer_broadcast_f32(const void *source, void *output, vo
  * a group of `world` GPUs.  `mine` is this rank's exchange region (mmrs_peer_alloc of
  * mmrs_xch_bytes(ar_capacity) bytes, zeroed); peers[r] is rank r's region as mapped in this
  * process (CUDA IPC between processes, or plain device pointers with peer access inside one
- * process); peers[rank] == mine.  expert_parallel = 0: tensor parallel, every rank holds
+ * process), read-write: the single-token exchange stores this rank's rows into every peer's
+ * region; peers[rank] == mine.  expert_parallel = 0: tensor parallel, every rank holds
  * gate/up rows [rank * inter, (rank + 1) * inter) and the matching down K range of every expert
  * (MmrsMoeWeights.inter is the per-rank inter); 1: expert parallel, rank r holds the full
  * experts e with e % world == r (MmrsMoeWeights still points at [num_experts] tensors; the
@@ -220,7 +221,7 @@ typedef struct {
     int world;
     int rank;
     void *mine;
-    const void *peers[8];
+    void *peers[8];
     size_t ar_capacity; /* floats per all-reduce buffer: >= T * hidden of the largest T > 1 call */
     int expert_parallel;
 } MmrsPeerGroup;

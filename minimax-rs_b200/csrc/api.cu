@@ -4,6 +4,7 @@
 #include <cstring>
 
 #include <algorithm>
+#include <mutex>
 #include "common.cuh"
 #include "decode.cuh"
 #include "peer.cuh"
@@ -19,18 +20,25 @@ static int set_err(int e) {
 }
 void record_error(int status) { g_last_error = status; }
 
-static int device_sms() {
-    int dev = 0, sms = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    return sms;
+// SM count and opt-in shared memory of the current device, queried once per device (they are on
+// every call's path; the queries cost more than the rest of the host work of a decode call).
+struct DeviceLimits {
+    int sms = 0, max_smem = 0;
+};
+static const DeviceLimits &device_limits() {
+    static std::once_flag once[64];
+    static DeviceLimits lim[64];
+    static DeviceLimits none;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return none;
+    std::call_once(once[dev], [dev] {
+        cudaDeviceGetAttribute(&lim[dev].sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaDeviceGetAttribute(&lim[dev].max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    });
+    return lim[dev];
 }
-static int device_max_smem() {
-    int dev = 0, v = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    return v;
-}
+static int device_sms() { return device_limits().sms; }
+static int device_max_smem() { return device_limits().max_smem; }
 
 static bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
@@ -589,7 +597,7 @@ extern "C" int mmrs_moe_block_forward_group(const MmrsMoeWeights *w, const MmrsP
     p.dn_type = w->down_type;
     p.timeout_ns = kTimeoutNs;
     p.xch = static_cast<uint8_t *>(g->mine);
-    for (int r = 0; r < g->world; ++r) p.xpeer[r] = static_cast<const uint8_t *>(g->peers[r]);
+    for (int r = 0; r < g->world; ++r) p.xpeer[r] = static_cast<uint8_t *>(g->peers[r]);
     p.world = g->world;
     p.rank = g->rank;
     p.ep = ep;

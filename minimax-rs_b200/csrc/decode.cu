@@ -965,50 +965,56 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             p.y[dn_r0 + r] = y;
         }
     } else {
-        // Fused exchange of the partial rows with the other ranks over NVLink: publish this
-        // CTA's rows in the exchange region (buffer token & 1), release a per-CTA flag, wait
-        // (bounded) for the same CTA's flag on every peer, then sum the ranks' rows in rank
-        // order (bit-identical on all ranks) and add the residual
+        // Fused exchange of the partial rows with the other ranks over NVLink, pushed: this
+        // CTA's rows go to every rank's receive buffer (slot [token & 1][this rank]) as 64-bit
+        // words {token, f32 bits}; then each thread waits (bounded) until its rows from every
+        // rank carry the token in this rank's own memory, sums them in rank order (bit-identical
+        // on all ranks) and adds the residual
         // (TensorParallelRankGroup::all_reduce_sum_with_residual, tensor_parallel.rs:786-812).
-        // The token is the group's operation counter: every layer sharing the group draws a
-        // fresh one, so a flag raised for another layer's exchange never satisfies this wait.
+        // The token is the group's operation counter: every layer sharing the group draws a fresh
+        // one, so a word written for another layer's exchange never satisfies this wait.  The
+        // rows are pushed even after a failed wait, so that no peer waits for them in vain.
         const uint32_t token = p.token;
-        const size_t part_off = kXchDPart + sizeof(float) * (size_t)(token & 1u) * kXchMaxHidden;
-        float *mine = reinterpret_cast<float *>(p.xch + part_off);
+        const unsigned long long hi = (unsigned long long)token << 32;
+        const size_t slot = (size_t)(token & 1u) * kMaxRanks;
         for (int r = tid; r < nres; r += kConsumerThreads) {
             float q[kTopK];
             slot_rows(r, q);
-            mine[dn_r0 + r] = ((q[0] + q[4]) + (q[2] + q[6])) + ((q[1] + q[5]) + (q[3] + q[7]));
-        }
-        named_sync(kBarConsumers, kConsumerThreads);
-        if (tid == 0) {
-            s.ctl[kCtlFail] = 0;
-            st_release_sys(reinterpret_cast<uint32_t *>(p.xch + kXchDFlags) + cta, token);
-            const uint64_t xdl = globaltimer_ns() + p.timeout_ns;
+            const float v = ((q[0] + q[4]) + (q[2] + q[6])) + ((q[1] + q[5]) + (q[3] + q[7]));
+            const unsigned long long w = hi | __float_as_uint(v);
             for (int rk = 0; rk < p.world; ++rk) {
-                if (rk == p.rank) continue;
-                if (!wait_flag_sys(reinterpret_cast<const uint32_t *>(p.xpeer[rk] + kXchDFlags) + cta, token, xdl)) {
-                    atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
-                    atomicExch(reinterpret_cast<uint32_t *>(p.xch + kXchStatus), (uint32_t)MMRS_ERR_TIMEOUT);
-                    s.ctl[kCtlFail] = 1;
-                    break;
-                }
+                uint8_t *base = rk == p.rank ? p.xch : p.xpeer[rk];
+                st_relaxed_sys_u64(reinterpret_cast<unsigned long long *>(base + kXchDRecv) +
+                                       (slot + p.rank) * kXchMaxHidden + dn_r0 + r, w);
             }
         }
-        named_sync(kBarConsumers, kConsumerThreads);
-        const bool xfail = *reinterpret_cast<volatile int *>(&s.ctl[kCtlFail]) != 0;
-        for (int r = tid; r < nres && !xfail; r += kConsumerThreads) {
+        const unsigned long long *recv = reinterpret_cast<const unsigned long long *>(p.xch + kXchDRecv) + slot * kXchMaxHidden;
+        const uint64_t xdl = globaltimer_ns() + p.timeout_ns;
+        for (int r = tid; r < nres; r += kConsumerThreads) {
             const int row = dn_r0 + r;
-            float v[kMaxRanks];
+            unsigned long long w[kMaxRanks];
 #pragma unroll
-            for (int rk = 0; rk < kMaxRanks; ++rk)  // all loads in flight before the sum
-                if (rk < p.world)
-                    v[rk] = rk == p.rank ? mine[row]
-                                         : ld_relaxed_sys_f32(reinterpret_cast<const float *>(p.xpeer[rk] + part_off) + row);
-            float y = v[0];
+            for (int rk = 0; rk < kMaxRanks; ++rk)  // all loads in flight before the checks
+                w[rk] = rk < p.world ? ld_relaxed_sys_u64(recv + (size_t)rk * kXchMaxHidden + row) : hi;
+            bool xok = true;
+#pragma unroll
+            for (int rk = 0; rk < kMaxRanks; ++rk) {
+                uint32_t spins = 0;
+                while (xok && (uint32_t)(w[rk] >> 32) != token) {
+                    __nanosleep(32);
+                    if ((++spins & 63u) == 0 && globaltimer_ns() > xdl) {
+                        atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
+                        atomicExch(reinterpret_cast<uint32_t *>(p.xch + kXchStatus), (uint32_t)MMRS_ERR_TIMEOUT);
+                        xok = false;
+                    }
+                    if (xok) w[rk] = ld_relaxed_sys_u64(recv + (size_t)rk * kXchMaxHidden + row);
+                }
+            }
+            if (!xok) continue;
+            float y = __uint_as_float((uint32_t)w[0]);
 #pragma unroll
             for (int rk = 1; rk < kMaxRanks; ++rk)
-                if (rk < p.world) y = y + v[rk];
+                if (rk < p.world) y = y + __uint_as_float((uint32_t)w[rk]);
             if (p.residual) y = y + s.res_s[r];
             p.y[row] = y;
         }

@@ -61,7 +61,7 @@ struct DecodeParams {
     // multi-GPU group (world > 1): this rank's exchange region and every rank's as mapped here;
     // ep = 1: only experts e with e % world == rank are computed on this rank
     uint8_t *xch;
-    const uint8_t *xpeer[8];
+    uint8_t *xpeer[8];  // peer-mapped regions (the decode kernel stores its rows into them)
     int world, rank, ep;
     // operation token of the group (monotonic, the same on every rank, never 0): the exchange
     // flags and double-buffered partial rows belong to the group, not to a layer's workspace

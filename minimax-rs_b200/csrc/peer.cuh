@@ -13,15 +13,20 @@ constexpr int kXchMaxHidden = 8192;   // decode partial rows per buffer
 constexpr int kXchMaxCtas = 1024;
 
 // Layout of one rank's exchange region (bytes).  Flags hold the token of the last operation that
-// published data (monotonic; readers wait until flag >= token).  Partials are double buffered by
+// published data (monotonic; readers wait until flag >= token).  Buffers are double buffered by
 // token parity: a rank writes buffer (token & 1) only after every peer has published a later
 // token than the last reader of that buffer.
+//
+// The fused decode kernel pushes instead of pulling: each rank stores its partial rows into every
+// rank's receive buffer, slot [token & 1][source rank], as 64-bit words {token, f32 bits} (relaxed
+// system-scope stores over NVLink), and each rank polls only its own memory until every word it
+// needs carries the operation's token.  One NVLink write and no fence: a system-scope release
+// costs microseconds, and every poll of a peer's flag is an NVLink round trip.
 constexpr size_t kXchStatus = 0;       // u32: MMRS_ERR_TIMEOUT after an expired wait
-constexpr size_t kXchDFlags = 4096;    // u32[kXchMaxCtas]: fused decode kernel, one per CTA
 constexpr size_t kXchAFlags = 8192;    // u32[kXchMaxCtas]: all-reduce kernel, one per CTA
 constexpr size_t kXchA2Flags = 12288;  // u32[kXchMaxCtas]: two-shot all-reduce, reduced chunk ready
-constexpr size_t kXchDPart = 16384;    // f32[2][kXchMaxHidden]: decode partial y
-constexpr size_t kXchAPart = kXchDPart + 2 * sizeof(float) * kXchMaxHidden;  // f32[2][cap]
+constexpr size_t kXchDRecv = 16384;    // u64[2][kMaxRanks][kXchMaxHidden]: decode rows received
+constexpr size_t kXchAPart = kXchDRecv + 2 * sizeof(unsigned long long) * kMaxRanks * kXchMaxHidden;  // f32[2][cap]
 
 __host__ __device__ inline size_t xch_bytes(size_t ar_capacity) {
     return kXchAPart + 2 * sizeof(float) * ar_capacity;
@@ -58,6 +63,17 @@ __device__ __forceinline__ float ld_relaxed_sys_f32(const float *p) {
 __device__ __forceinline__ float4 ld_relaxed_sys_f4(const float4 *p) {
     float4 v;
     asm volatile("ld.relaxed.sys.global.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
+
+// 64-bit relaxed accesses at system scope (the peers' GPUs): a tagged word is written and read
+// whole, so a reader that sees the token sees the payload stored with it.
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 
