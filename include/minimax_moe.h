@@ -154,11 +154,15 @@ MMRS_API int mmrs_moe_block_forward_host(const MmrsMoeWeights *w, const float *x
                                          uint32_t *topk_ids, float *topk_weights, void *workspace,
                                          size_t workspace_bytes, mmrs_stream_t stream);
 
-/* Copies the per-CTA phase timestamps (globaltimer ns, 16 slots per CTA: 0 start, 1 router done,
+/* Copies the per-CTA phase timestamps (globaltimer ns, 32 slots per CTA: 0 start, 1 router done,
  * 2 routing candidates ready, 3 copy table done, 4 gate/up done, 5 activation records read,
  * 6 activation scales built, 7 end, 8 first weight copy issued, 9 last copy issued, 10 first
- * down copy issued, 11 own activation blocks published) of the last single-token launch into
- * host_out.  Returns the number of entries copied, or -status. */
+ * down copy issued, 11 own activation blocks published, 12 x quantised, 13 routing warp 0's
+ * candidates written, 14 slots and weights merged, 15 copy table computed, 16 weighted expert
+ * rows summed, 17 thread 0's down dots done, 18 multi-GPU rows pushed, 19 routing lane 0's
+ * score seen, 20 slots merged, 22 own activation blocks published (thread 0), 24 + w routing
+ * warp w's candidates written; 21 and 23 unused) of the
+ * last single-token launch into host_out.  Returns the number of entries copied, or -status. */
 MMRS_API int mmrs_moe_workspace_trace(const void *workspace, uint64_t *host_out, int max_entries,
                                       mmrs_stream_t stream);
 

@@ -214,13 +214,13 @@ class MoeLayer:
         return y_host
 
     def trace(self, stream=None):
-        """Per-CTA phase timestamps (ns) of the last single-token launch: array [256, 16]."""
+        """Per-CTA phase timestamps (ns) of the last single-token launch: array [256, 32]."""
         import numpy as np
-        out = np.zeros(256 * 16, dtype=np.uint64)
+        out = np.zeros(256 * 32, dtype=np.uint64)
         n = lib().mmrs_moe_workspace_trace(self._ws.data_ptr(), out.ctypes.data, out.size, _stream(stream))
         if n < 0:
             raise MoeError(-n, "mmrs_moe_workspace_trace")
-        return out.reshape(256, 16)
+        return out.reshape(256, 32)
 
     def status(self, stream=None) -> int:
         return lib().mmrs_moe_workspace_status(self._ws.data_ptr(), _stream(stream)) if self._ws is not None else 0

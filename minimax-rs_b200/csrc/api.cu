@@ -104,12 +104,12 @@ __global__ void __launch_bounds__(256) decode_topk_kernel(const float *__restric
 // ------------------------------------------------------------------------------------------
 // Workspace layout of the fused block
 // ------------------------------------------------------------------------------------------
-constexpr int kTraceCtas = 256, kTraceSlots = 16;
+constexpr int kTraceCtas = 256;
 constexpr size_t kTraceOffset = kControlBytes;
 static_assert(sizeof(DecodeCtl) <= kControlBytes, "the decode control block lies in the control bytes");
 static size_t up256(size_t v) { return (v + 255) / 256 * 256; }
-// [control block (DecodeCtl)] | trace | tagged act records (9 words a Q8_1 block); all of it
-// zero before first use (the tags of a fresh or reset workspace start again at 1)
+// [control block (DecodeCtl)] | trace | tagged score copies | tagged act records (9 words a Q8_1
+// block); all of it zero before first use (the tags of a fresh or reset workspace start again at 1)
 WsLayout ws_layout(int E, int I, int max_tokens) {
     (void)E;
     (void)max_tokens;
@@ -117,7 +117,8 @@ WsLayout ws_layout(int E, int I, int max_tokens) {
     const size_t nblk = (size_t)8 * I / 32;
     l.ctl = 0;
     l.trace = kTraceOffset;
-    l.arec = l.trace + sizeof(uint64_t) * kTraceCtas * kTraceSlots;
+    l.score = l.trace + sizeof(uint64_t) * kTraceCtas * kTraceSlots;
+    l.arec = l.score + sizeof(unsigned long long) * kScoreReplicas * 256;
     l.total = l.arec + up256(nblk * 9 * sizeof(unsigned long long));
     return l;
 }
@@ -125,6 +126,7 @@ WsLayout ws_layout(int E, int I, int max_tokens) {
 void ws_bind(DecodeParams &p, uint8_t *ws, const WsLayout &l) {
     p.ctl = reinterpret_cast<DecodeCtl *>(ws + l.ctl);
     p.trace = reinterpret_cast<uint64_t *>(ws + l.trace);
+    p.score = reinterpret_cast<unsigned long long *>(ws + l.score);
     p.arec = reinterpret_cast<unsigned long long *>(ws + l.arec);
     p.zero_bytes = (uint32_t)l.total;
 }

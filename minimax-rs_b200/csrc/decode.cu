@@ -11,11 +11,13 @@
 // a reader waits (bounded) until the words it needs carry this launch's tag.
 //   P0  router GEMV in the canonical order (8 K-slices; the CTA's two experts x 8 slices are 16
 //       (expert, slice) pairs over the 13 warps: 32 lane partials, butterfly, fixed slice tree).
-//       The router rows are requested before anything else; the two logits are published tagged.
-//   P1  the consumer warps quantise x to Q8_1; eight warps then take 32 experts each (wait for
-//       the tagged logit, sigmoid, order-preserving selection key, rounds of redux max / min:
-//       that warp's top-8) and the producer warp merges the 64 candidates the same way,
-//       renormalises the weights and builds the copy table with its 32 lanes.
+//       The router rows are requested before anything else; the sigmoids of the two logits are
+//       published tagged.
+//   P1  eight consumer warps take 32 experts each (wait for the tagged sigmoid, order-preserving
+//       selection key with the bias loaded at kernel start, rank among the warp's 32: that
+//       warp's top-8), then rank their 8 candidates among all 64 (the global top-8) and quantise
+//       their slice of x to Q8_1; the producer warp, which built the copy-table structure while
+//       they waited, renormalises the weights and fills in the copy sources with its 32 lanes.
 //   P2  gate/up: the CTA owns a contiguous range of (slot, row) pairs; copy units of rows of the
 //       gate or the up matrix (one bulk copy each) stream through a ring of shared-memory stages.
 //       Consumer lane t keeps the activation of x super-block t % (H/256) in registers for the
@@ -57,9 +59,9 @@ constexpr int kMaxUnits = 80;
 constexpr int kActWords = 9;  // act record words a consumer thread loads at once (384 blocks: one pass)
 constexpr int kTopK = 8;
 constexpr int kRouterRounds = (16 + kWarps - 1) / kWarps;
-// named barriers: consumers; table ready, router partials (all threads); routing candidates
-// ready (the eight routing warps + the producer)
-constexpr int kBarConsumers = 1, kBarTable = 3, kBarRouter = 4, kBarCand = 6;
+// named barriers: consumers; table ready, router partials (all threads); the eight routing
+// warps' candidates written (routing warps); the slots ready (the routing warps + the producer)
+constexpr int kBarConsumers = 1, kBarTable = 3, kBarRouter = 4, kBarRoute = 5, kBarCand = 6;
 constexpr int kRouteWarps = 8;  // one expert a lane: E <= 256
 // control words in shared memory
 enum { kCtlUnits, kCtlGuUnits, kCtlGuRows, kCtlPositions, kCtlOk, kCtlFail, kCtlWords };
@@ -222,8 +224,9 @@ __device__ __forceinline__ float half_gap(float y) {
 // 128 consecutive values, lane l holding values 4l..4l+3 (Q8_1 blocks of 32 over 8 lanes):
 // d = amax/127, q = roundf(v/d) (quantize_q8_1, gguf.cuh:1234-1261, and quantize_silu_mul_q8_1,
 // moe_gguf.cu:255-284).  Writes q (value o + i at byte act_swz(o + i) of qv), and per block the
-// fp16-rounded scale d and the sum of quants S.
-__device__ __forceinline__ void quant128(float4 v, int8_t *qv, int o, float *d, int *S, int lane) {
+// fp16-rounded scale d and the sum of quants S.  Out of line: it runs once per launch, and one
+// copy of its code keeps the kernel's instruction footprint down.
+__device__ __noinline__ void quant128(float4 v, int8_t *qv, int o, float *d, int *S, int lane) {
     float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
     for (int m = 4; m > 0; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
@@ -315,8 +318,7 @@ __device__ __forceinline__ bool wait_unit(uint64_t *full, const int *ticket, int
                                           uint64_t deadline) {
     uint32_t spins = 0;
     while (*reinterpret_cast<const volatile int *>(&ticket[st]) != k) {
-        __nanosleep(32);
-        if ((++spins & 255u) == 0 && globaltimer_ns() > deadline) return false;
+        if ((++spins & 1023u) == 0 && globaltimer_ns() > deadline) return false;
     }
     return mbar_wait_sleep(&full[st], (uint32_t)(k / stages) & 1u, deadline);
 }
@@ -324,9 +326,8 @@ __device__ __forceinline__ bool wait_unit(uint64_t *full, const int *ticket, int
 // One thread's bounded wait until an exchange counter reaches `target` (wrap-safe).
 __device__ __forceinline__ bool wait_count(const uint32_t *cnt, uint32_t target, uint64_t deadline) {
     uint32_t spins = 0;
-    while ((int)(ld_relaxed_gpu(cnt) - target) < 0) {
-        __nanosleep(32);
-        if ((++spins & 255u) == 0 && globaltimer_ns() > deadline) return false;
+    while ((int)(ld_relaxed_gpu(cnt) - target) < 0) {  // one L2 round trip a poll
+        if ((++spins & 63u) == 0 && globaltimer_ns() > deadline) return false;
     }
     return true;
 }
@@ -356,7 +357,7 @@ __device__ __forceinline__ uint32_t sel_key(float sg, float b) {
 // Sub-unit: .x unit, .y first row within the unit | rows << 16.
 // Floats of the per-block partial buffer: the gate/up rows' and, after them, the down rows'.
 __host__ __device__ inline size_t decode_part_floats(const DecodeParams &p) {
-    const size_t gu = (size_t)2 * p.act_slots * (p.H / QK_K), dn = (size_t)kTopK * p.res_slots * (p.I / QK_K);
+    const size_t gu = (size_t)2 * p.act_slots * ((p.H / QK_K) | 1), dn = (size_t)kTopK * p.res_slots * (p.I / QK_K);
     return gu > dn ? gu : dn;
 }
 
@@ -372,16 +373,16 @@ struct DecodeSmem {
     int *aS_s;                 // [8][I/32]
     float4 *ats;               // [8][I/64]
     float *part;               // router slice sums [2][8]
-    float *sig;                // [E] sigmoid of the router logits
-    uint32_t *cand;            // [2][64] routing candidates: keys, then expert ids
+    uint2 *cand;               // [64] routing candidates {key, expert id}, warp w's at 8 w + rank
+    float *csig;               // [64] their sigmoids
+    float *slotsig;            // [8] sigmoid of the expert of each slot
     int *ids;                  // [8] expert of each slot (-1: none, or another rank's)
     int *vslot;                // [8] slot of each position (the computed slots in order)
     int *posof;                // [8] position of each slot (-1: not computed here)
     float *w;                  // [8]
     float *dn_acc;             // [res_slots][8] weighted expert rows of this CTA's output range
-    float *bpart;              // per-block partial sums: gate/up [2][act_slots][H/256], then
+    float *bpart;              // per-block partial sums: gate/up [2][act_slots][H/256 | 1], then
                                // down [positions][res_slots][I/256]
-    float *gval, *uval;        // [act_slots] gate / up row values of this CTA's (position, row) range
     float *res_s;              // [res_slots]
     int4 *units;               // [kMaxUnits]
     int *unit_off;             // [kMaxUnits] first row of a gate/up unit in the CTA's range
@@ -392,6 +393,57 @@ struct DecodeSmem {
     int *done;                 // [stages] super-blocks of the stage's unit finished
     int *ctl;                  // [kCtlWords]
 };
+
+// Copy-table structure of a CTA for nv computed positions (one producer lane each): lane c
+// describes gate/up chunk c of the CTA's (position, row) range (its position, first row, rows,
+// offset in the range); units 2c / 2c + 1 are the chunk's gate / up rows, then one down unit per
+// position (all of the CTA's output rows); the row map gives each gate/up row its unit, its row
+// in the unit and its partial-sum row (gate rows first, then up rows).  It depends on the number
+// of positions only, not on the experts (the source addresses are filled in once the routing is
+// known).  Out of line: one copy of its code for both call sites.
+struct TableLane {
+    int pos, row0, n, off, n_chunks, cnt;
+};
+__device__ __noinline__ TableLane table_structure(int cta, int G, int nv, int I, int U_gu, int lane, uint32_t gu_row_bytes,
+                                                  uint32_t dn_row_bytes, int nres, int dn_r0, int4 *units, int *unit_off,
+                                                  uint32_t *ubytes, int2 *rowmap) {
+    TableLane t = {-1, 0, 0, 0, 0, 0};
+    int gu_p0, gu_p1;
+    gu_range(cta, G, nv, I, gu_p0, gu_p1);
+    int c_left = lane;
+    for (int pos = gu_p0 / I, q = gu_p0; q < gu_p1; ++pos) {
+        const int seg_end = min(gu_p1, (pos + 1) * I);
+        const int nc = (seg_end - q + U_gu - 1) / U_gu;
+        if (c_left >= 0 && c_left < nc) {
+            const int r = q + c_left * U_gu;
+            t.pos = pos;
+            t.row0 = r - pos * I;
+            t.n = min(U_gu, seg_end - r);
+            t.off = r - gu_p0;
+        }
+        c_left -= nc;
+        t.n_chunks += nc;
+        q = seg_end;
+    }
+    t.cnt = gu_p1 - gu_p0;
+    if (t.pos >= 0) {
+        for (int h = 0; h < 2; ++h) {
+            const int k = 2 * lane + h;
+            units[k] = make_int4(h, t.pos, t.row0, t.n);
+            unit_off[k] = t.off;
+            ubytes[k] = gu_row_bytes * (uint32_t)t.n;
+#pragma unroll 1
+            for (int r = 0; r < t.n; ++r) rowmap[2 * t.off + h * t.n + r] = make_int2(k | (r << 16), h * t.cnt + t.off + r);
+        }
+    }
+    if (nres > 0 && lane < nv) {
+        const int k = 2 * t.n_chunks + lane;
+        units[k] = make_int4(2, lane, dn_r0, nres);
+        unit_off[k] = 0;
+        ubytes[k] = dn_row_bytes * (uint32_t)nres;
+    }
+    return t;
+}
 
 // GU / DN: GGUF types of the gate/up and down matrices (one instantiation per pair keeps each
 // launched kernel's code to the dot products it runs).
@@ -425,6 +477,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             }
         }
     }
+    // the routing lane's selection bias (a weight as well)
+    const int route_e = 32 * warp + lane;
+    const float route_bias = (p.internal_routing && warp < kRouteWarps && route_e < E) ? __ldg(p.bias + route_e) : 0.f;
     // everything below reads the previous kernel's outputs (x, the workspace)
     asm volatile("griddepcontrol.wait;" ::: "memory");
 #pragma unroll
@@ -444,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     }
     // this launch's tag: one more than this CTA's last (its own arrival word counts its launches)
     const uint32_t tag = __ldcg(&p.ctl->arrive[cta]) + 1u;
-    if (tid == 0 && p.trace) p.trace[cta * 16 + 0] = t_start;
+    if (tid == 0 && p.trace) p.trace[cta * kTraceSlots + 0] = t_start;
 
     DecodeSmem s;
     {
@@ -465,16 +520,15 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         s.aS_s = reinterpret_cast<int *>(take(sizeof(int) * kTopK * (I / 32)));
         s.ats = reinterpret_cast<float4 *>(take(sizeof(float4) * kTopK * (I / 64)));
         s.part = reinterpret_cast<float *>(take(sizeof(float) * 16));
-        s.sig = reinterpret_cast<float *>(take(sizeof(float) * 256));
-        s.cand = reinterpret_cast<uint32_t *>(take(sizeof(uint32_t) * 128));
+        s.cand = reinterpret_cast<uint2 *>(take(sizeof(uint2) * 64));
+        s.csig = reinterpret_cast<float *>(take(sizeof(float) * 64));
+        s.slotsig = reinterpret_cast<float *>(take(sizeof(float) * kTopK));
         s.ids = reinterpret_cast<int *>(take(sizeof(int) * kTopK));
         s.vslot = reinterpret_cast<int *>(take(sizeof(int) * kTopK));
         s.posof = reinterpret_cast<int *>(take(sizeof(int) * kTopK));
         s.w = reinterpret_cast<float *>(take(sizeof(float) * kTopK));
         s.dn_acc = reinterpret_cast<float *>(take(sizeof(float) * kTopK * p.res_slots));
         s.bpart = reinterpret_cast<float *>(take(sizeof(float) * decode_part_floats(p)));
-        s.gval = reinterpret_cast<float *>(take(sizeof(float) * p.act_slots));
-        s.uval = reinterpret_cast<float *>(take(sizeof(float) * p.act_slots));
         s.res_s = reinterpret_cast<float *>(take(sizeof(float) * p.res_slots));
         s.units = reinterpret_cast<int4 *>(take(sizeof(int4) * kMaxUnits));
         s.unit_off = reinterpret_cast<int *>(take(sizeof(int) * kMaxUnits));
@@ -500,7 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         }
         fence_mbar_init();
         for (int i = 0; i < kCtlWords; ++i) s.ctl[i] = 0;
-        s.ctl[kCtlOk] = 1;  // cleared by a routing lane whose logit wait expires
+        s.ctl[kCtlOk] = 1;  // cleared by a routing lane whose score wait expires
         if (cta == 0) p.ctl->zero_bytes = p.zero_bytes;
     }
 
@@ -524,16 +578,21 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         if (lane == 0) s.part[le * 8 + sl] = acc;
     }
     named_sync(kBarRouter, kThreads);
-    if (p.internal_routing && tid < 2) {
-        const int ee = cta + G * tid;
+    if (p.internal_routing && tid < 2 * kScoreReplicas) {
+        // thread t publishes the score of the CTA's expert t / kScoreReplicas into copy
+        // t % kScoreReplicas (the 16 threads of an expert form the same value)
+        const int le = tid / kScoreReplicas, ee = cta + G * le;
         if (ee < E) {
-            const float *q = s.part + tid * 8;
+            const float *q = s.part + le * 8;
             const float lg = ((q[0] + q[1]) + (q[2] + q[3])) + ((q[4] + q[5]) + (q[6] + q[7]));
-            // published with this launch's tag in the same 64-bit word
-            st_relaxed_gpu_u64(&p.ctl->logit[ee], ((unsigned long long)tag << 32) | __float_as_uint(lg));
+            // the sigmoid (minimax_moe_decode_topk's arithmetic), published with this launch's tag
+            // in the same 64-bit word
+            const float sg = __fdiv_rn(1.0f, 1.0f + expf(-lg));
+            publish_gpu_u64(p.score + (size_t)(tid % kScoreReplicas) * 256 + ee,
+                            ((unsigned long long)tag << 32) | __float_as_uint(sg));
         }
     }
-    if (tid == 0 && p.trace) p.trace[cta * 16 + 1] = globaltimer_ns();
+    if (tid == 0 && p.trace) p.trace[cta * kTraceSlots + 1] = globaltimer_ns();
 
     const size_t gu_row_bytes = kq_row_bytes(p.gu_type, H);
     const size_t dn_row_bytes = kq_row_bytes(p.dn_type, I);
@@ -541,6 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     const size_t dn_expert_bytes = dn_row_bytes * H;
     const int U_gu = p.gu_unit_rows;
     const int NBg = H / QK_K, NBd = I / QK_K;  // super-blocks of a gate/up row, of a down row
+    const int NBgs = NBg | 1;  // row stride of the gate/up block partials (odd: conflict-free row sums)
 
     // Issue copy unit k into ring stage k % stages (one thread).  The first `stages` units are
     // issued by the producer warp once the table is built; every later unit by the consumer lane
@@ -550,9 +610,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         *reinterpret_cast<volatile int *>(&s.ticket[st]) = k;
         const uint32_t bytes = s.ubytes[k];
         if (p.trace) {
-            if (k == 0) p.trace[cta * 16 + 8] = globaltimer_ns();
-            if (k == s.ctl[kCtlGuUnits]) p.trace[cta * 16 + 10] = globaltimer_ns();
-            if (k == s.ctl[kCtlUnits] - 1) p.trace[cta * 16 + 9] = globaltimer_ns();
+            if (k == 0) p.trace[cta * kTraceSlots + 8] = globaltimer_ns();
+            if (k == s.ctl[kCtlGuUnits]) p.trace[cta * kTraceSlots + 10] = globaltimer_ns();
+            if (k == s.ctl[kCtlUnits] - 1) p.trace[cta * kTraceSlots + 9] = globaltimer_ns();
         }
         mbar_arrive_expect_tx_sink(&s.full[st], bytes);
         bulk_g2s(s.stages + (size_t)st * p.stage_bytes, s.usrc[k], bytes, &s.full[st]);
@@ -560,40 +620,30 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
 
     if (warp == kProducerWarp) {
         // ================================ producer warp ===================================
-        // the routing warps wait for the logits; their candidates (and verdict) arrive here
+        // The copy-table structure (table_structure) is built while the routing warps wait for
+        // the scores when the number of computed positions is known in advance.
+        TableLane tl;
+        auto structure = [&](int nv) {
+            tl = table_structure(cta, G, nv, I, U_gu, lane, (uint32_t)gu_row_bytes, (uint32_t)dn_row_bytes, nres, dn_r0,
+                                 s.units, s.unit_off, s.ubytes, s.rowmap);
+        };
+        // every slot is computed here unless experts are split over ranks
+        const bool compact = p.world > 1 && p.ep;
+        const int nv_guess = compact ? -1 : kTopK;
+        if (nv_guess > 0) structure(nv_guess);
+        // the routing warps wait for the scores; their candidates (and verdict) arrive here
         named_sync(kBarCand, 32 * (kRouteWarps + 1));
         const bool ok = s.ctl[kCtlOk] != 0;
-        if (lane == 0 && p.trace) p.trace[cta * 16 + 2] = globaltimer_ns();
-        // ---- merge of the routing warps' candidates (8 per warp, each warp's in rank order) --------
+        if (lane == 0 && p.trace) p.trace[cta * kTraceSlots + 2] = globaltimer_ns();
+        // ---- slots (merged by the routing warps) and their weights ---------------------------------
         int slot_id = -1;  // lane k < 8: expert of slot k
         float slot_w = 0.f;
         if (p.internal_routing) {
             if (ok) {
-                // rank of candidates lane and lane + 32 among all nc (larger key first, lower expert
-                // id among equal keys: the stable descending order); the 8 best are the slots.
-                // Every real expert's key is > 0, and the per-warp lists hold the global top-8.
-                const int nc = 8 * ((E + 31) / 32);
-                const uint32_t ka = lane < nc ? s.cand[lane] : 0u, ia = lane < nc ? s.cand[64 + lane] : 0xffffffffu;
-                const uint32_t kb = lane + 32 < nc ? s.cand[lane + 32] : 0u;
-                const uint32_t ib = lane + 32 < nc ? s.cand[64 + lane + 32] : 0xffffffffu;
-                int ra = 0, rb = 0;
-                for (int j = 0; j < nc; j += 4) {  // nc is a multiple of 8
-                    const uint4 kj = *reinterpret_cast<const uint4 *>(s.cand + j);
-                    const uint4 ij = *reinterpret_cast<const uint4 *>(s.cand + 64 + j);
-                    const uint32_t kk[4] = {kj.x, kj.y, kj.z, kj.w}, ii[4] = {ij.x, ij.y, ij.z, ij.w};
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {  // branch-free: (key greater) | (key equal & id lower)
-                        ra += (int)(kk[q] > ka) | ((int)(kk[q] == ka) & (int)(ii[q] < ia));
-                        rb += (int)(kk[q] > kb) | ((int)(kk[q] == kb) & (int)(ii[q] < ib));
-                    }
-                }
-                __syncwarp();
-                if (lane < nc && ra < kTopK) s.ids[ra] = (int)ia;
-                if (lane + 32 < nc && rb < kTopK) s.ids[rb] = (int)ib;
-                __syncwarp();
+                // the routing warps wrote the expert and sigmoid of each slot
                 if (lane < kTopK) slot_id = s.ids[lane];
                 // weights: sig / ((v0+v4)+(v2+v6))+((v1+v5)+(v3+v7)), lane k keeps w_k
-                const float my_sig = lane < kTopK ? s.sig[slot_id] : 0.f;
+                const float my_sig = lane < kTopK ? s.slotsig[lane] : 0.f;
                 float v[kTopK];
 #pragma unroll
                 for (int k = 0; k < kTopK; ++k) v[k] = __shfl_sync(0xffffffffu, my_sig, k);
@@ -629,8 +679,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             }
             __syncwarp();
         }
+        if (lane == 0 && p.trace) p.trace[cta * kTraceSlots + 14] = globaltimer_ns();
         // ---- positions: the computed slots in order (expert parallel: this rank's only) ------
-        const bool compact = p.world > 1 && p.ep;
         int id = (ok && lane < kTopK) ? slot_id : -1;
         if (compact && id >= 0 && id % p.world != p.rank) id = -1;
         const bool keep = lane < kTopK && id >= 0;
@@ -642,67 +692,32 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             s.posof[lane] = keep ? __popc(kept & ((1u << lane) - 1u)) : -1;
             if (keep) s.vslot[__popc(kept & ((1u << lane) - 1u))] = lane;
         }
+        if (nvs != nv_guess) structure(nvs);
         __syncwarp();
-        // ---- copy table: lane c computes gate/up chunk c of the CTA's (position, row) range --
-        int gu_p0, gu_p1;
-        gu_range(cta, G, nvs, I, gu_p0, gu_p1);
-        int n_chunks = 0, c_left = lane, my_pos = -1, my_row0 = 0, my_n = 0, my_off = 0;
-        for (int pos = gu_p0 / I, q = gu_p0; q < gu_p1; ++pos) {
-            const int seg_end = min(gu_p1, (pos + 1) * I);
-            const int nc = (seg_end - q + U_gu - 1) / U_gu;
-            if (c_left >= 0 && c_left < nc) {
-                const int r = q + c_left * U_gu;
-                my_pos = pos;
-                my_row0 = r - pos * I;
-                my_n = min(U_gu, seg_end - r);
-                my_off = r - gu_p0;
-            }
-            c_left -= nc;
-            n_chunks += nc;
-            q = seg_end;
-        }
-        const int n_gu_units = 2 * n_chunks;
-        const int cnt = gu_p1 - gu_p0;
-        if (my_pos >= 0) {
-            for (int h = 0; h < 2; ++h) {
-                const int k = 2 * lane + h;
-                s.units[k] = make_int4(h, my_pos, my_row0, my_n);
-                s.unit_off[k] = my_off;
-                const int e = s.ids[s.vslot[my_pos]];
-                s.usrc[k] = (h == 0 ? p.gate : p.up) + (size_t)e * gu_expert_bytes + (size_t)my_row0 * gu_row_bytes;
-                s.ubytes[k] = (uint32_t)(gu_row_bytes * my_n);
-            }
-        }
-        // down units: one per position, all of this CTA's output rows
+        // ---- source addresses of the units, then the first ring fill (one unit per lane);
+        // later units are issued by the consumer lanes ------------------------------------------
+        const int n_gu_units = 2 * tl.n_chunks;
         const int n_dn_units = nres > 0 ? nvs : 0;
+        if (tl.pos >= 0) {
+            const size_t e = (size_t)s.ids[s.vslot[tl.pos]];
+            s.usrc[2 * lane] = p.gate + e * gu_expert_bytes + (size_t)tl.row0 * gu_row_bytes;
+            s.usrc[2 * lane + 1] = p.up + e * gu_expert_bytes + (size_t)tl.row0 * gu_row_bytes;
+        }
         if (lane < n_dn_units) {
-            const int k = n_gu_units + lane;
-            s.units[k] = make_int4(2, lane, dn_r0, nres);
-            s.unit_off[k] = 0;
-            const int e = s.ids[s.vslot[lane]];
-            s.usrc[k] = p.down + (size_t)e * dn_expert_bytes + (size_t)dn_r0 * dn_row_bytes;
-            s.ubytes[k] = (uint32_t)(dn_row_bytes * nres);
+            const size_t e = (size_t)s.ids[s.vslot[lane]];
+            s.usrc[n_gu_units + lane] = p.down + e * dn_expert_bytes + (size_t)dn_r0 * dn_row_bytes;
         }
         if (lane == 0) {
             s.ctl[kCtlUnits] = n_gu_units + n_dn_units;
             s.ctl[kCtlGuUnits] = n_gu_units;
-            s.ctl[kCtlGuRows] = 2 * cnt;
+            s.ctl[kCtlGuRows] = 2 * tl.cnt;
             s.ctl[kCtlPositions] = nvs;
             s.ctl[kCtlOk] = ok ? 1 : 0;
         }
         __syncwarp();
-        // ---- first ring fill, one unit per lane, before the row map: later units are issued by
-        // the consumer lanes -------------------------------------------------------------------
+        if (lane == 0 && p.trace) p.trace[cta * kTraceSlots + 15] = globaltimer_ns();
         if (ok && lane < min(n_gu_units + n_dn_units, p.stages)) issue(lane);
-        // gate/up rows in unit order: chunk c's gate rows (unit 2c), then its up rows (2c + 1);
-        // the row map gives each its unit, its row in the unit and its partial-sum row
-        // (gate rows first, then up rows, by the (position, row) offset in the CTA's range)
-        if (my_pos >= 0) {
-            for (int h = 0; h < 2; ++h)
-                for (int r = 0; r < my_n; ++r)
-                    s.rowmap[2 * my_off + h * my_n + r] = make_int2((2 * lane + h) | (r << 16), h * cnt + my_off + r);
-        }
-        if (lane == 0 && p.trace) p.trace[cta * 16 + 3] = globaltimer_ns();
+        if (lane == 0 && p.trace) p.trace[cta * kTraceSlots + 3] = globaltimer_ns();
         __syncwarp();
         named_arrive(kBarTable, kThreads);  // table complete: the consumers may start
         __syncwarp();
@@ -710,41 +725,38 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     }
 
     // ================================ consumer warps ======================================
-    // While the producer waits for barrier #1 and routes: Q8_1 of x and the residual.
-    {
-        const int nxc = H / 128;
-        for (int c = warp; c < nxc; c += kConsumerWarps) {
-            const float4 xv = __ldg(reinterpret_cast<const float4 *>(p.x) + c * 32 + lane);
-            quant128(xv, s.xq, c * 128, s.xd + c * 4, s.xS + c * 4, lane);
-        }
-        for (int r = tid; r < nres; r += kConsumerThreads) s.res_s[r] = p.residual ? __ldg(p.residual + dn_r0 + r) : 0.f;
-        named_sync(kBarConsumers, kConsumerThreads);
-        build_task_scales(s.xts, s.xd, s.xS, H / 64, tid, kConsumerThreads);
-    }
-    named_sync(kBarConsumers, kConsumerThreads);  // x's Q8_1 and its records are complete
+    // Routing warps first: the copy table waits for their candidates.  Routing warp w computed
+    // the router slice w of the CTA's first expert, so it holds x's slice w in registers (lane l:
+    // values 4l..4l+3 of each 128-value chunk), which it quantises (Q8_1) once its candidates
+    // are out, while the producer merges them.  Without that slice (external
+    // routing, a CTA without a first expert, H not a multiple of 1024) the other consumer warps
+    // load and quantise x.  They load the residual.
+    const bool xq_router = p.internal_routing && H % 1024 == 0 && cta < E;
     if (warp < kRouteWarps) {
-        // this launch's logit of expert e (bounded wait for its tag); sigmoid, selection score as
-        // an order-preserving key, and this warp's top-8 of its 32 experts by rank
-        const int e = 32 * warp + lane;
-        // each routing lane polls its expert's tagged logit directly (one coalesced 256-byte
-        // request per warp and round: ~150 requests per L2 line and round over the grid)
-        if (p.internal_routing && 32 * warp < E) {
+        // this launch's score of expert e (bounded wait for its tag), the selection key, this
+        // warp's top-8 of its 32 experts by rank, then the global top-8 of the 64 candidates
+        const int e = route_e;
+        // each routing lane polls its expert's tagged score in the CTA's copy directly (one
+        // coalesced 256-byte request per warp and round: ~10 requests per L2 line and round over
+        // the grid)
+        if (p.internal_routing) {
             uint32_t key = 0u;  // experts >= E are never selected (E >= 8 real keys are > 0)
+            float sg = 0.f;
             if (e < E) {
-                unsigned long long v = ld_relaxed_gpu_u64(&p.ctl->logit[e]);
+                const unsigned long long *word = p.score + (size_t)(cta % kScoreReplicas) * 256 + e;
+                unsigned long long v = ld_relaxed_gpu_u64(word);
                 uint32_t spins = 0;
-                while ((uint32_t)(v >> 32) != tag) {
-                    __nanosleep(64);
+                while ((uint32_t)(v >> 32) != tag) {  // one L2 round trip a poll
                     if ((++spins & 63u) == 0 && globaltimer_ns() > deadline) {
                         atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
                         s.ctl[kCtlOk] = 0;
                         break;
                     }
-                    v = ld_relaxed_gpu_u64(&p.ctl->logit[e]);
+                    v = ld_relaxed_gpu_u64(word);
                 }
-                const float sg = __fdiv_rn(1.0f, 1.0f + expf(-__uint_as_float((uint32_t)v)));
-                s.sig[e] = sg;
-                key = sel_key(sg, __ldg(p.bias + e));
+                if (tid == 0 && p.trace) p.trace[cta * kTraceSlots + 19] = globaltimer_ns();
+                sg = __uint_as_float((uint32_t)v);
+                key = sel_key(sg, route_bias);
             }
             // rank of this lane's expert among the warp's 32: lanes with a larger key, or an equal
             // key and a lower expert id (the stable descending order); the warp's best 8 go to
@@ -756,12 +768,55 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
                 rank += (int)(kj > key) | ((int)(kj == key) & (int)(j < lane));
             }
             if (rank < kTopK) {
-                s.cand[8 * warp + rank] = key;
-                s.cand[64 + 8 * warp + rank] = (uint32_t)e;
+                s.cand[8 * warp + rank] = make_uint2(key, (uint32_t)e);
+                s.csig[8 * warp + rank] = sg;
             }
+            if (tid == 0 && p.trace) p.trace[cta * kTraceSlots + 13] = globaltimer_ns();
+            if (lane == 0 && p.trace) p.trace[cta * kTraceSlots + 24 + warp] = globaltimer_ns();
+            named_sync(kBarRoute, 32 * kRouteWarps);
+            // The global top-8 from the 64 candidates (every warp's list holds its share of it):
+            // candidate 8 w + (lane & 7)'s rank among all 64 in the same order, lanes l, l ^ 8,
+            // l ^ 16, l ^ 24 counting over 16 candidates each; ranks below 8 are the slots.
+            const int ci = 8 * warp + (lane & 7);
+            const uint2 me = s.cand[ci];
+            const uint4 *grp = reinterpret_cast<const uint4 *>(s.cand + 16 * (lane >> 3));
+            int gr = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {  // branch-free: (key greater) | (key equal & id lower)
+                const uint4 q = grp[j];
+                gr += (int)(q.x > me.x) | ((int)(q.x == me.x) & (int)(q.y < me.y));
+                gr += (int)(q.z > me.x) | ((int)(q.z == me.x) & (int)(q.w < me.y));
+            }
+            gr += __shfl_xor_sync(0xffffffffu, gr, 8);
+            gr += __shfl_xor_sync(0xffffffffu, gr, 16);
+            if (lane < 8 && gr < kTopK) {
+                s.ids[gr] = (int)me.y;
+                s.slotsig[gr] = s.csig[ci];
+            }
+            if (tid == 0 && p.trace) p.trace[cta * kTraceSlots + 20] = globaltimer_ns();
         }
         named_arrive(kBarCand, 32 * (kRouteWarps + 1));
+        if (xq_router) {
+            const int cps = slice / 128;  // chunks per router slice
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int c = warp * cps + i;
+                if (i < cps) quant128(xx[0][i], s.xq, c * 128, s.xd + c * 4, s.xS + c * 4, lane);
+            }
+        }
+    } else {
+        const int nxc = H / 128, xw = warp - kRouteWarps, xt = tid - 32 * kRouteWarps;
+        constexpr int kXWarps = kConsumerWarps - kRouteWarps;
+        for (int c = xw; c < nxc && !xq_router; c += kXWarps) {
+            const float4 xv = __ldg(reinterpret_cast<const float4 *>(p.x) + c * 32 + lane);
+            quant128(xv, s.xq, c * 128, s.xd + c * 4, s.xS + c * 4, lane);
+        }
+        for (int r = xt; r < nres; r += 32 * kXWarps) s.res_s[r] = p.residual ? __ldg(p.residual + dn_r0 + r) : 0.f;
     }
+    named_sync(kBarConsumers, kConsumerThreads);  // x's Q8_1 blocks are complete
+    build_task_scales(s.xts, s.xd, s.xS, H / 64, tid, kConsumerThreads);
+    named_sync(kBarConsumers, kConsumerThreads);  // and their scale records
+    if (tid == 0 && p.trace) p.trace[cta * kTraceSlots + 12] = globaltimer_ns();
     // Gate/up lanes: lane t holds the activation of x block t % NBg and computes that block of
     // rows t / NBg, t / NBg + slots, ... of the CTA's gate/up rows (in unit order).
     const int g_slots = kConsumerThreads / NBg;
@@ -802,6 +857,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     auto wait_landed = [&](int k, int st) {
         if (!aborted && !wait_unit(s.full, s.ticket, k, st, p.stages, deadline)) {
             atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
+            s.ctl[kCtlFail] = 1;  // the CTA drains its ring before it retires
             aborted = true;
         }
     };
@@ -823,7 +879,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
                 float v = 0.f;
                 if (!aborted)
                     v = block_dot<GU>(s.stages + (size_t)st * p.stage_bytes + (size_t)(rm.x >> 16) * gu_row_bytes + BB * g_sb, act);
-                s.bpart[rm.y * NBg + g_sb] = v;
+                s.bpart[rm.y * NBgs + g_sb] = v;
             }
             finish(valid, k, st, total);
         }
@@ -832,26 +888,24 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
 
     // ---- P3: Q8_1 of act for the CTA's blocks, grid barrier #2, copy of the whole vector ---------
     named_sync(kBarConsumers, kConsumerThreads);  // every gate/up block of this CTA is done
-    if (tid == 0 && p.trace) p.trace[cta * 16 + 4] = globaltimer_ns();
+    if (tid == 0 && p.trace) p.trace[cta * kTraceSlots + 4] = globaltimer_ns();
     {
         int gu_p0, gu_p1;
         gu_range(cta, G, nvs, I, gu_p0, gu_p1);
-        // row sums of the gate rows (partial rows 0..cnt-1) and the up rows (cnt..2 cnt-1)
-        for (int t = tid; t < 2 * cnt; t += kConsumerThreads) {
-            const float v = sum_blocks(s.bpart + t * NBg, NBg);
-            if (t < cnt) s.gval[t] = v;
-            else s.uval[t - cnt] = v;
+        // one warp per block of 32 rows: lane l sums the block partials of gate row 32 b + l
+        // (partial row i) and of its up row (partial row cnt + i), forms act = up * silu(gate)
+        // (moe_gguf.cu:272-273), and the warp quantises the block (quantize_silu_mul_q8_1,
+        // moe_gguf.cu:255-284) and publishes it
+        for (int b = gu_p0 / 32 + warp; b < gu_p1 / 32 && !aborted; b += kConsumerWarps) {
+            const int i = 32 * b - gu_p0 + lane;
+            if (tid == 0 && p.trace) p.trace[cta * kTraceSlots + 21] = globaltimer_ns();
+            const float gv = sum_blocks(s.bpart + i * NBgs, NBg);
+            const float uv = sum_blocks(s.bpart + (cnt + i) * NBgs, NBg);
+            const float av = uv * __fdiv_rn(gv, 1.0f + expf(-gv));
+            if (tid == 0 && p.trace) p.trace[cta * kTraceSlots + 23] = globaltimer_ns();
+            publish_block(av, p.arec + (size_t)9 * b, tag, lane);
         }
-        named_sync(kBarConsumers, kConsumerThreads);
-        for (int i = tid; i < cnt; i += kConsumerThreads) {
-            const float gv = s.gval[i];
-            // act = up * silu(gate) (moe_gguf.cu:272-273)
-            s.gval[i] = s.uval[i] * __fdiv_rn(gv, 1.0f + expf(-gv));
-        }
-        named_sync(kBarConsumers, kConsumerThreads);
-        // quantize_silu_mul_q8_1 (moe_gguf.cu:255-284): one warp per block of 32 rows, published
-        for (int b = gu_p0 / 32 + warp; b < gu_p1 / 32 && !aborted; b += kConsumerWarps)
-            publish_block(s.gval[32 * b - gu_p0 + lane], p.arec + (size_t)9 * b, tag, lane);
+        if (tid == 0 && p.trace) p.trace[cta * kTraceSlots + 22] = globaltimer_ns();
     }
     // ---- the act exchange (in place of a grid barrier): this CTA's records are written, so it
     // counts itself in; one thread waits until every CTA has, then the consumer threads read the
@@ -861,7 +915,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     named_sync(kBarConsumers, kConsumerThreads);
     if (tid == 0) {
         red_relaxed_gpu_add(&p.ctl->n_act, 1u);
-        if (p.trace) p.trace[cta * 16 + 11] = globaltimer_ns();
+        if (p.trace) p.trace[cta * kTraceSlots + 11] = globaltimer_ns();
         if (ok1 && !wait_count(&p.ctl->n_act, (uint32_t)G * tag, deadline)) {
             atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
             s.ctl[kCtlFail] = 1;
@@ -869,8 +923,19 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     }
     named_sync(kBarConsumers, kConsumerThreads);
     {
-        // all of a thread's loads in flight at once (kActWords per pass), then the tag checks
+        // all of a thread's loads in flight at once (kActWords per pass), then one check of their
+        // tags; a word from before this launch (the count is relaxed) sends the thread through
+        // the compact path that re-polls each word
         const int nwords = 9 * (nvs * I / 32);
+        auto unpack = [&](unsigned long long v, int wi) {
+            const int b = wi / 9, j = wi - 9 * b;
+            if (j < 8) {
+                *reinterpret_cast<uint32_t *>(s.aq_s + act_swz(32 * b + 4 * j)) = (uint32_t)v;
+            } else {
+                s.ad_s[b] = __half2float(__ushort_as_half((unsigned short)(v & 0xffffu)));
+                s.aS_s[b] = (int)(short)((uint32_t)v >> 16);
+            }
+        };
         for (int w0 = 0; w0 < nwords && ok1 && !s.ctl[kCtlFail]; w0 += kActWords * kConsumerThreads) {
             unsigned long long v[kActWords];
 #pragma unroll
@@ -878,37 +943,43 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
                 const int wi = w0 + tid + i * kConsumerThreads;
                 v[i] = wi < nwords ? ld_relaxed_gpu_u64(p.arec + wi) : 0ull;
             }
+            bool stale = false;
 #pragma unroll
+            for (int i = 0; i < kActWords; ++i)
+                stale |= w0 + tid + i * kConsumerThreads < nwords && (uint32_t)(v[i] >> 32) != tag;
+            if (!stale) {
+#pragma unroll
+                for (int i = 0; i < kActWords; ++i) {
+                    const int wi = w0 + tid + i * kConsumerThreads;
+                    if (wi < nwords) unpack(v[i], wi);
+                }
+                continue;
+            }
+#pragma unroll 1
             for (int i = 0; i < kActWords; ++i) {
                 const int wi = w0 + tid + i * kConsumerThreads;
-                if (wi >= nwords) continue;
+                if (wi >= nwords) break;
+                unsigned long long x = ld_relaxed_gpu_u64(p.arec + wi);
                 uint32_t spins = 0;
-                while ((uint32_t)(v[i] >> 32) != tag) {
-                    __nanosleep(128);
+                while ((uint32_t)(x >> 32) != tag) {
                     if ((++spins & 63u) == 0 && globaltimer_ns() > deadline) {
                         atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
                         s.ctl[kCtlFail] = 1;
                         break;
                     }
-                    v[i] = ld_relaxed_gpu_u64(p.arec + wi);
+                    x = ld_relaxed_gpu_u64(p.arec + wi);
                 }
-                const int b = wi / 9, j = wi - 9 * b;
-                if (j < 8) {
-                    *reinterpret_cast<uint32_t *>(s.aq_s + act_swz(32 * b + 4 * j)) = (uint32_t)v[i];
-                } else {
-                    s.ad_s[b] = __half2float(__ushort_as_half((unsigned short)(v[i] & 0xffffu)));
-                    s.aS_s[b] = (int)(short)((uint32_t)v[i] >> 16);
-                }
+                unpack(x, wi);
             }
         }
     }
     if (!ok1 && tid == 0) s.ctl[kCtlFail] = 1;
-    if (tid == 0 && p.trace) p.trace[cta * 16 + 5] = globaltimer_ns();
+    if (tid == 0 && p.trace) p.trace[cta * kTraceSlots + 5] = globaltimer_ns();
     named_sync(kBarConsumers, kConsumerThreads);
     if (s.ctl[kCtlFail]) aborted = true;
     build_task_scales(s.ats, s.ad_s, s.aS_s, nvs * (I / 64), tid, kConsumerThreads);
     named_sync(kBarConsumers, kConsumerThreads);
-    if (tid == 0 && p.trace) p.trace[cta * 16 + 6] = globaltimer_ns();
+    if (tid == 0 && p.trace) p.trace[cta * kTraceSlots + 6] = globaltimer_ns();
 
     // the next kernel in the stream may start its CTAs as this kernel's CTAs retire
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -933,6 +1004,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             s.bpart[(vp * nres + r) * NBd + sb] = v;
             ++done_rows;
         }
+        if (tid == 0 && p.trace) p.trace[cta * kTraceSlots + 17] = globaltimer_ns();
         if (done_rows > 0) {
             const int old = atom_add_acq_rel_cta(&s.done[st], done_rows);
             if (old + done_rows == nres * NBd) {
@@ -952,6 +1024,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
         s.dn_acc[t] = vp >= 0 ? sum_blocks(s.bpart + (vp * nres + r) * NBd, NBd) * s.w[j] : 0.f;
     }
     named_sync(kBarConsumers, kConsumerThreads);
+    if (tid == 0 && p.trace) p.trace[cta * kTraceSlots + 16] = globaltimer_ns();
     auto slot_rows = [&](int r, float (&q)[kTopK]) {
 #pragma unroll
         for (int j = 0; j < kTopK; ++j) q[j] = s.dn_acc[r * kTopK + j];
@@ -985,9 +1058,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             for (int rk = 0; rk < p.world; ++rk) {
                 uint8_t *base = rk == p.rank ? p.xch : p.xpeer[rk];
                 st_relaxed_sys_u64(reinterpret_cast<unsigned long long *>(base + kXchDRecv) +
-                                       (slot + p.rank) * kXchMaxHidden + dn_r0 + r, w);
+                                   (slot + p.rank) * kXchMaxHidden + dn_r0 + r, w);
             }
         }
+        if (tid == 0 && p.trace) p.trace[cta * kTraceSlots + 18] = globaltimer_ns();
         const unsigned long long *recv = reinterpret_cast<const unsigned long long *>(p.xch + kXchDRecv) + slot * kXchMaxHidden;
         const uint64_t xdl = globaltimer_ns() + p.timeout_ns;
         for (int r = tid; r < nres; r += kConsumerThreads) {
@@ -996,32 +1070,43 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
 #pragma unroll
             for (int rk = 0; rk < kMaxRanks; ++rk)  // all loads in flight before the checks
                 w[rk] = rk < p.world ? ld_relaxed_sys_u64(recv + (size_t)rk * kXchMaxHidden + row) : hi;
-            bool xok = true;
+            bool stale = false;
 #pragma unroll
-            for (int rk = 0; rk < kMaxRanks; ++rk) {
-                uint32_t spins = 0;
-                while (xok && (uint32_t)(w[rk] >> 32) != token) {
-                    __nanosleep(32);
-                    if ((++spins & 63u) == 0 && globaltimer_ns() > xdl) {
-                        atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
-                        atomicExch(reinterpret_cast<uint32_t *>(p.xch + kXchStatus), (uint32_t)MMRS_ERR_TIMEOUT);
-                        xok = false;
+            for (int rk = 0; rk < kMaxRanks; ++rk) stale |= (uint32_t)(w[rk] >> 32) != token;
+            float y = 0.f;
+            if (!stale) {
+                y = __uint_as_float((uint32_t)w[0]);
+#pragma unroll
+                for (int rk = 1; rk < kMaxRanks; ++rk)
+                    if (rk < p.world) y = y + __uint_as_float((uint32_t)w[rk]);
+            } else {
+                // a rank's row has not arrived yet: poll each rank's word in turn (rank order)
+                bool xok = true;
+#pragma unroll 1
+                for (int rk = 0; rk < p.world && xok; ++rk) {
+                    unsigned long long x = ld_relaxed_sys_u64(recv + (size_t)rk * kXchMaxHidden + row);
+                    uint32_t spins = 0;
+                    while ((uint32_t)(x >> 32) != token) {
+                        if ((++spins & 63u) == 0 && globaltimer_ns() > xdl) {
+                            atomicExch(&p.ctl->status, (uint32_t)MMRS_ERR_TIMEOUT);
+                            atomicExch(reinterpret_cast<uint32_t *>(p.xch + kXchStatus), (uint32_t)MMRS_ERR_TIMEOUT);
+                            xok = false;
+                            break;
+                        }
+                        x = ld_relaxed_sys_u64(recv + (size_t)rk * kXchMaxHidden + row);
                     }
-                    if (xok) w[rk] = ld_relaxed_sys_u64(recv + (size_t)rk * kXchMaxHidden + row);
+                    y = rk == 0 ? __uint_as_float((uint32_t)x) : y + __uint_as_float((uint32_t)x);
                 }
+                if (!xok) continue;
             }
-            if (!xok) continue;
-            float y = __uint_as_float((uint32_t)w[0]);
-#pragma unroll
-            for (int rk = 1; rk < kMaxRanks; ++rk)
-                if (rk < p.world) y = y + __uint_as_float((uint32_t)w[rk]);
             if (p.residual) y = y + s.res_s[r];
             p.y[row] = y;
         }
     }
-    // No copy may still be landing in shared memory when the CTA retires (after an expired wait
-    // a unit may have been issued and never waited for).
-    if (tid == 0 && ok1) {
+    // No copy may still be landing in shared memory when the CTA retires.  Without a failed wait
+    // every issued unit has been waited for by the lanes that computed it; after an expired wait
+    // a unit may have been issued and never waited for, so the CTA waits for each stage's last.
+    if (tid == 0 && ok1 && s.ctl[kCtlFail]) {
         for (int st = 0; st < p.stages; ++st) {
             const int k = *reinterpret_cast<volatile int *>(&s.ticket[st]);
             if (k >= 0) mbar_wait_bounded(&s.full[st], (uint32_t)(k / p.stages) & 1u, deadline + 1000000000ull);
@@ -1029,7 +1114,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
     }
     if (tid == 0) {
         p.ctl->arrive[cta] = tag;  // this CTA's launch count (read only by this CTA's next launch)
-        if (p.trace) p.trace[cta * 16 + 7] = globaltimer_ns();
+        if (p.trace) p.trace[cta * kTraceSlots + 7] = globaltimer_ns();
     }
 }
 
@@ -1041,9 +1126,9 @@ size_t decode_smem_bytes(const DecodeParams &p) {
     size_t b = a16((size_t)p.stages * p.stage_bytes) + a16(sizeof(uint64_t) * p.stages);
     b += a16(p.H) + 2 * a16(4 * (p.H / 32)) + a16(16 * (p.H / 64));
     b += a16((size_t)kTopK * p.I) + 2 * a16(4 * kTopK * (p.I / 32)) + a16(16 * kTopK * (p.I / 64));
-    b += a16(4 * 16) + a16(4 * 256) + a16(4 * 128) + 4 * a16(4 * kTopK);  // part, sig, cand, ids, vslot, posof, w
+    b += a16(4 * 16) + a16(8 * 64) + a16(4 * 64) + 5 * a16(4 * kTopK);  // part, cand, csig, slotsig, ids, vslot, posof, w
     b += a16(4 * (size_t)kTopK * p.res_slots);                           // dn_acc
-    b += a16(4 * decode_part_floats(p)) + 2 * a16(4 * (size_t)p.act_slots) + a16(4 * (size_t)p.res_slots);
+    b += a16(4 * decode_part_floats(p)) + a16(4 * (size_t)p.res_slots);
     b += a16(16 * kMaxUnits) + a16(4 * kMaxUnits) + a16(8 * kMaxUnits) + a16(4 * kMaxUnits) + a16(16 * (size_t)p.act_slots);
     b += 2 * a16(4 * (size_t)p.stages) + a16(4 * kCtlWords);
     return b;

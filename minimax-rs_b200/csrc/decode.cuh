@@ -8,16 +8,22 @@ namespace mmrs {
 // Control block of the single-token kernel at the start of its workspace.  Launch n (n = 1, 2,
 // ...) of a workspace carries the tag n, and everything one CTA hands to the others travels in
 // 64-bit words {tag, payload} written and read with relaxed stores and loads: a reader that sees
-// the current tag sees the current payload, with no fence.  The routing lanes poll the logit
+// the current tag sees the current payload, with no fence.  The routing lanes poll the score
 // words directly.  For the activation records, each CTA adds 1 (relaxed) to a counter after
 // writing its words, which reaches G * n in launch n: one thread per CTA waits for that, then the
 // CTA reads the words (coalesced), re-reading any whose tag is not yet current.
 //   n_act       the activation exchange counter (on its own 128-byte line);
 //   arrive[c]   the tag of CTA c's last launch (its launch count; read only by CTA c);
-//   logit[e]    the router logit of expert e (payload: the f32 bits);
+// The sigmoid of the router logit of expert e (payload: the f32 bits) is published by the CTA
+// that computed the logit into every one of kScoreReplicas copies of the score array (workspace,
+// after the trace); CTA c polls copy c % kScoreReplicas, so each line is polled by a few CTAs
+// instead of all of them.
 //   zero_bytes  the size of the workspace prefix that must be zero before first use (control
 //               block, trace and the tagged activation records), for the status reset.
 constexpr int kDecodeMaxCtas = 256;
+// globaltimer stamps a CTA records per launch (trace slots, see the phase list in decode.cu)
+constexpr int kTraceSlots = 32;
+constexpr int kScoreReplicas = 16;
 struct DecodeCtl {
     uint32_t status;  // MMRS_OK, or MMRS_ERR_TIMEOUT once any wait expired
     uint32_t zero_bytes;
@@ -25,7 +31,6 @@ struct DecodeCtl {
     uint32_t n_act;
     uint32_t pad2[31];
     uint32_t arrive[kDecodeMaxCtas];
-    unsigned long long logit[256];
 };
 
 struct DecodeParams {
@@ -49,7 +54,8 @@ struct DecodeParams {
                                // j < 8), {fp16 scale, int16 sum of quants} (word 8)
     uint32_t zero_bytes;       // workspace prefix that must start at zero
     DecodeCtl *ctl;
-    uint64_t *trace;  // [grid][16] globaltimer stamps per phase, or null
+    uint64_t *trace;  // [grid][kTraceSlots] globaltimer stamps per phase, or null
+    unsigned long long *score;  // [kScoreReplicas][256] tagged sigmoids of the router logits
     // shape
     int E, H, I;
     int gu_type, dn_type;

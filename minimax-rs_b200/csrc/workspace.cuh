@@ -9,10 +9,11 @@
 namespace mmrs {
 
 struct WsLayout {
-    size_t ctl, trace, arec, total;
+    size_t ctl, trace, score, arec, total;
 };
 
-// [control block (DecodeCtl)] | trace | tagged act records; all of it zero before first use
+// [control block (DecodeCtl)] | trace | tagged score copies | tagged act records; all of it zero
+// before first use
 WsLayout ws_layout(int E, int I, int max_tokens);
 void ws_bind(DecodeParams &p, uint8_t *ws, const WsLayout &l);
 int validate_weights(const MmrsMoeWeights *w);

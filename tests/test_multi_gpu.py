@@ -187,15 +187,21 @@ def test_group_decode_full_size_ep(pkg, synth, orc, world):
     picked = picked[:3]
     groups = gm.PeerGroup.local(list(range(world)), ar_capacity=H, expert_parallel=True)
     layers = _rank_layers(pkg, gm, L, world, True)
+    # Inputs and workspaces go to every device before the first group launch: a copy from cuda:0
+    # issued after rank 0's kernel would wait behind it on cuda:0's stream, while that kernel
+    # waits for the rows of the ranks whose launches the copy holds up.
+    xs = [L["x"].to(f"cuda:{r}") for r in range(world)]
+    rs = [L["residual"].to(f"cuda:{r}") for r in range(world)]
+    for r in range(world):
+        with torch.cuda.device(r):
+            layers[r].workspace(1)
+        torch.cuda.synchronize(r)
     outs = []
     for t in picked:
         step = []
         for r in range(world):
             with torch.cuda.device(r):
-                layers[r].workspace(1)
-                x = L["x"][t:t + 1].to(f"cuda:{r}")
-                rr = L["residual"][t:t + 1].to(f"cuda:{r}")
-                step.append(groups[r].forward(layers[r], x, residual=rr))
+                step.append(groups[r].forward(layers[r], xs[r][t:t + 1], residual=rs[r][t:t + 1]))
         outs.append((t, step))
     for r in range(world):
         torch.cuda.synchronize(r)
