@@ -143,9 +143,8 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, 
 __device__ __forceinline__ bool ring_wait(uint64_t *full, const int *ticket, int slot, int fill, int slots,
                                           uint64_t deadline) {
     uint32_t spins = 0;
-    while (*reinterpret_cast<const volatile int *>(&ticket[slot]) != fill) {
-        __nanosleep(32);
-        if ((++spins & 255u) == 0 && globaltimer_ns() > deadline) return false;
+    while (*reinterpret_cast<const volatile int *>(&ticket[slot]) != fill) {  // no __nanosleep: see grid_sync
+        if ((++spins & 1023u) == 0 && globaltimer_ns() > deadline) return false;
     }
     return mbar_wait_sleep(&full[slot], (uint32_t)(fill / slots) & 1u, deadline);
 }
@@ -250,9 +249,10 @@ __device__ inline bool grid_sync(GridFlags *gf, uint32_t target, uint64_t deadli
     if (threadIdx.x == 0 && *s_ok) {
         asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&gf->count) : "memory");
         uint32_t spins = 0;
+        // one L2 round trip a poll; no __nanosleep between polls (a warp woken from it was
+        // measured to resume microseconds after the requested time)
         while ((int)(ld_acquire_gpu(&gf->count) - target) < 0) {
-            __nanosleep(16);
-            if ((++spins & 255u) == 0 && globaltimer_ns() > deadline) {
+            if ((++spins & 63u) == 0 && globaltimer_ns() > deadline) {
                 atomicExch(&gf->status, (uint32_t)MMRS_ERR_TIMEOUT);
                 *s_ok = 0;
                 break;

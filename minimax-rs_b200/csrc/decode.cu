@@ -323,7 +323,10 @@ __device__ __forceinline__ bool wait_unit(uint64_t *full, const int *ticket, int
     return mbar_wait_sleep(&full[st], (uint32_t)(k / stages) & 1u, deadline);
 }
 
-// One thread's bounded wait until an exchange counter reaches `target` (wrap-safe).
+// One thread's bounded wait until an exchange counter reaches `target` (wrap-safe).  None of the
+// decode kernel's polls sleep between reads (__nanosleep): on B200 a warp woken from a 32-128 ns
+// sleep was measured to resume microseconds later, which put whole microseconds on the routing
+// and exchange paths; a spin issues one load per memory round trip.
 __device__ __forceinline__ bool wait_count(const uint32_t *cnt, uint32_t target, uint64_t deadline) {
     uint32_t spins = 0;
     while ((int)(ld_relaxed_gpu(cnt) - target) < 0) {  // one L2 round trip a poll
