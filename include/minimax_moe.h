@@ -160,8 +160,9 @@ MMRS_API int mmrs_moe_block_forward_host(const MmrsMoeWeights *w, const float *x
  * down copy issued, 11 own activation blocks published, 12 x quantised, 13 routing warp 0's
  * candidates written, 14 slots and weights merged, 15 copy table computed, 16 weighted expert
  * rows summed, 17 thread 0's down dots done, 18 multi-GPU rows pushed, 19 routing lane 0's
- * score seen, 20 slots merged, 22 own activation blocks published (thread 0), 24 + w routing
- * warp w's candidates written; 21 and 23 unused) of the
+ * score seen, 20 slots merged, 21 thread 0's first activation block begun, 22 own activation
+ * blocks published (thread 0), 23 its act values formed, 24 + w routing warp w's candidates
+ * written) of the
  * last single-token launch into host_out.  Returns the number of entries copied, or -status. */
 MMRS_API int mmrs_moe_workspace_trace(const void *workspace, uint64_t *host_out, int max_entries,
                                       mmrs_stream_t stream);

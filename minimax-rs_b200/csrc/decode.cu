@@ -618,7 +618,15 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const __g
             if (k == s.ctl[kCtlUnits] - 1) p.trace[cta * kTraceSlots + 9] = globaltimer_ns();
         }
         mbar_arrive_expect_tx_sink(&s.full[st], bytes);
-        bulk_g2s(s.stages + (size_t)st * p.stage_bytes, s.usrc[k], bytes, &s.full[st]);
+        // the expert weights are read once per token: first out of L2, so the stream does not
+        // push the lines the CTAs exchange out of it (measured ~1 % faster)
+        uint64_t pol;
+        asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+        asm volatile(
+            "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+                smem_u32(s.stages + (size_t)st * p.stage_bytes)),
+            "l"(s.usrc[k]), "r"(bytes), "r"(smem_u32(&s.full[st])), "l"(pol)
+            : "memory");
     };
 
     if (warp == kProducerWarp) {
