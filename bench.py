@@ -1017,9 +1017,13 @@ def main():
         else:
             group.forward(L, xs[t:t + 1], residual=res[t:t + 1], y=ys[t:t + 1], stream=s)
 
-    # CUDA graph of G consecutive steps (G multiple of the layer count)
-    G = max(len(layers), 64 // len(layers) * len(layers))
-    graphs = []
+    # Exactly K = args.steps timed steps, replayed from CUDA graphs: full graphs of G consecutive
+    # steps (G = min(K, 64)) and one graph of the remaining K % G steps; every graph is replayed
+    # once untimed first (the first replay of a graph also uploads it).
+    G = min(args.steps, 64)
+    n_full, rem = divmod(args.steps, G)
+    n_tok_graphs = max(1, min(n_full, n_tok // G))  # distinct token ranges of the full graphs
+    graphs, tail = [], None
     if world > 1:
         dist.barrier()
     with torch.cuda.stream(stream):
@@ -1027,20 +1031,29 @@ def main():
             step(i, stream)
         stream.synchronize()
         try:
-            for gi in range(n_tok // G if n_tok % G == 0 else 1):
+            if world > 1 and G < 3:  # a group graph of 1-2 steps would meet its own exchange words
+                raise RuntimeError("fewer than 3 steps per graph")
+            for gi in range(n_tok_graphs):
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=stream):
                     for j in range(G):
                         step(gi * G + j, stream)
                 graphs.append(g)
+            if rem:
+                tail = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(tail, stream=stream):
+                    for j in range(rem):
+                        step(n_tok_graphs * G + j, stream)
+            for g in graphs + ([tail] if tail is not None else []):
+                g.replay()
+            stream.synchronize()
         except Exception as e:  # capture unsupported: fall back to direct launches
             print(f"[bench] graph capture failed ({e}); timing direct launches", file=sys.stderr)
-            graphs = []
+            graphs, tail = [], None
     torch.cuda.synchronize()
     check_status(layers, "decode warm-up")
 
-    n_graph_reps = (args.steps + G - 1) // G if graphs else 0
-    steps = n_graph_reps * G if graphs else args.steps
+    steps = args.steps
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
@@ -1049,8 +1062,10 @@ def main():
         with torch.cuda.stream(stream):
             start.record(stream)
             if graphs:
-                for r in range(n_graph_reps):
+                for r in range(n_full):
                     graphs[r % len(graphs)].replay()
+                if tail is not None:
+                    tail.replay()
             else:
                 for i in range(steps):
                     step(i, stream)
@@ -1157,6 +1172,7 @@ def main():
 
     n_layers = len(layers)
     graph_steps = G if graphs else 0
+    tail = None
     layer_bytes = layers[0].gate.numel() * 2 + layers[0].down.numel() + E * H * 4
     del layers, graphs
     torch.cuda.empty_cache()
