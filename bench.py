@@ -240,7 +240,12 @@ def run_prefill(pkg, synth, dev, args, rank: int, world: int, group=None):
     import torch
     import torch.distributed as dist
     tp = group is not None and not group.expert_parallel
-    layers = build_prefill_layers(pkg, synth, dev, 2, tp_world=world if tp else 1, tp_rank=rank if tp else 0)
+    # two layer slots in turn; with --prefill-layers 1 both slots hold the same weights (a smaller
+    # device footprint for profiling; one layer's 2.19 GB of experts is still far larger than L2)
+    layers = build_prefill_layers(pkg, synth, dev, max(1, min(2, args.prefill_layers)), tp_world=world if tp else 1,
+                                  tp_rank=rank if tp else 0)
+    if len(layers) == 1:
+        layers = layers * 2
 
     def fwd(L, x, **kw):
         return L.forward(x, **kw) if group is None else group.forward(L, x, **kw)
@@ -378,7 +383,8 @@ def run_prefill(pkg, synth, dev, args, rank: int, world: int, group=None):
     out = {"metric": "moe_block_prefill_tokens_per_s", "value": PF_T * steps / (ms / 1e3),
            "unit": "tokens/s", "steps": steps, "ms_per_step": ms / steps,
            "config": {"workload": "prefill T=512 MoE block (BASELINE configs[2]), Zipf(1.1) expert popularity",
-                      "tokens_per_step": PF_T, "layers_rotated": 2, "distinct_experts": distinct,
+                      "tokens_per_step": PF_T, "layers_rotated": len({id(L) for L in layers}),
+                      "distinct_experts": distinct,
                       "max_routes_per_expert": int(counts.max()), "mode": "MMQ numerics (T >= 32)",
                       "x": "N(0,1) f32 (MMQ half block sums of the down input overflow with these synthetic "
                            "weights, as in the reference's numerics; finite_inputs times the same routing with "
@@ -508,7 +514,7 @@ def run_config3(pkg, synth, dev, args) -> dict:
     (configs[1] weights) + residual.  Four layers rotate (4 x ~152 MB per step, larger than L2);
     steps are replayed from CUDA graphs.  The attention half is also timed alone."""
     import torch
-    NL, qr, kr = 4, 48 * 128, 8 * 128
+    NL, qr, kr = max(1, args.c3_layers), 48 * 128, 8 * 128
     gen = torch.Generator(device=dev)
     gen.manual_seed(C3_SEED)
 
@@ -942,6 +948,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill-steps", type=int, default=40)
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--prefill-layers", type=int, default=2, help="prefill layers in turn (1 or 2)")
+    ap.add_argument("--only-prefill", action="store_true",
+                    help="run only the configs[2] prefill measurement on one GPU and print its object (profiling)")
+    ap.add_argument("--c3-layers", type=int, default=4, help="configs[3] decoder layers in turn")
     ap.add_argument("--no-ar-sweep", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -972,6 +982,10 @@ def main():
         return
     if args.only_config4:
         print(json.dumps(run_config4(pkg, synth, dev, args)))
+        return
+    if args.only_prefill and world == 1:
+        args.no_cpu_baseline = True
+        print(json.dumps(run_prefill(pkg, synth, dev, args, 0, 1)))
         return
     group = None
     if world > 1:
