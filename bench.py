@@ -149,6 +149,17 @@ def check_status(objs, where: str):
         raise RuntimeError(f"rank {os.environ.get('RANK', '0')}: device status in {where}: {bad}")
 
 
+def align_ranks(world: int, dev):
+    """Lines the ranks' streams up on the device right before a timed region: a one-element
+    all-reduce on the current stream completes on every rank at about the same time, so the host
+    launch skew between the rank processes stays out of the timed region (the first exchange of a
+    step would otherwise wait for the rank that started later)."""
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        dist.all_reduce(torch.zeros(1, device=dev))
+
+
 def rel_l2(got, ref, base) -> float:
     """||got - ref|| / ||ref - base|| in float64 (base: the residual the block adds)."""
     import numpy as np
@@ -293,6 +304,7 @@ def run_prefill(pkg, synth, dev, args, rank: int, world: int, group=None):
     torch.cuda.synchronize()
     with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
         with torch.cuda.stream(stream):
+            align_ranks(world, dev)
             e0.record(stream)
             for i in range(steps):
                 L = i % 2
@@ -324,6 +336,7 @@ def run_prefill(pkg, synth, dev, args, rank: int, world: int, group=None):
     with torch.cuda.stream(stream):
         for i in range(2):
             fwd(layers_f[i], xs_f[i], y=ys, topk_ids=ids_f[i], topk_w=wts[i], stream=stream)
+        align_ranks(world, dev)
         e0.record(stream)
         for i in range(steps):
             L = i % 2
@@ -360,6 +373,7 @@ def run_prefill(pkg, synth, dev, args, rank: int, world: int, group=None):
         if world > 1:
             dist.barrier()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        align_ranks(world, dev)
         f0.record(stream)
         for i in range(e2e_steps):
             step_e2e(i)
@@ -1045,8 +1059,8 @@ def main():
             step(i, stream)
         stream.synchronize()
         try:
-            if world > 1 and G < 3:  # a group graph of 1-2 steps would meet its own exchange words
-                raise RuntimeError("fewer than 3 steps per graph")
+            if world > 1 and G < 4:  # see the e2e graph below: a group graph needs 4+ steps
+                raise RuntimeError("fewer than 4 steps per graph")
             for gi in range(n_tok_graphs):
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=stream):
@@ -1074,6 +1088,7 @@ def main():
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         with torch.cuda.stream(stream):
+            align_ranks(world, dev)
             start.record(stream)
             if graphs:
                 for r in range(n_full):
@@ -1101,10 +1116,8 @@ def main():
     def fwd(L, t, xd, rd, yd):
         if group is None:  # one library call: copy in, block, copy out
             L.forward_host(x_host[t:t + 1], y_host[t:t + 1], xd, yd, residual=rd, stream=stream)
-        else:
-            xd.copy_(x_host[t:t + 1], non_blocking=True)
-            group.forward(L, xd, residual=rd, y=yd, stream=stream)
-            y_host[t:t + 1].copy_(yd, non_blocking=True)
+        else:  # the group's form of the same call
+            group.forward_host(L, x_host[t:t + 1], y_host[t:t + 1], xd, yd, residual=rd, stream=stream)
 
     x_host = torch.empty(n_tok, H, dtype=torch.float32, pin_memory=True)
     x_host.copy_(xs.cpu())
@@ -1120,6 +1133,7 @@ def main():
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        align_ranks(world, dev)
         e0.record(stream)
         for i in range(e2e_steps):
             t = i % n_tok
@@ -1133,32 +1147,43 @@ def main():
     e2e_per_call = e2e_steps / (e2e_ms / 1e3)
     e2e_method = "one public-API call per step from Python"
     e2e_graph = None
-    if group is None:
-        # The same public-API calls captured once in a CUDA graph of 64 steps and replayed, as a
-        # decode engine issues them: every step still reads its x from pinned host memory and
-        # stores its y to pinned host memory; only the per-call host launch cost is gone.  (The
-        # group path draws a fresh exchange token per call, which a graph would freeze.)
+    # The same public-API calls captured once in a CUDA graph of G2 = min(64, steps) steps and
+    # replayed, as a decode engine issues them: every step still reads its x from pinned host memory
+    # and stores its y to pinned host memory; only the per-call host launch cost is gone.  With a
+    # group the graph freezes the exchange tokens it drew at capture: each replay reuses them, which
+    # is safe from 4 steps a graph on (the receive slots are double-buffered by token parity; with
+    # at least two tokens of each parity in the graph, a slot holds another token of its parity
+    # when a step starts waiting on it, never the same token from the previous replay).
+    G2 = min(64, e2e_steps)
+    if G2 >= (4 if group is not None else 1):
         with torch.cuda.stream(stream):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
-                for i in range(64):
+                for i in range(G2):
                     t = i % n_tok
                     fwd(layers[i % len(layers)], t, x_dev, res[t:t + 1], y_dev)
             for _ in range(3):
                 g.replay()
             stream.synchronize()
-            reps = max(1, e2e_steps // 64)
+            if world > 1:
+                dist.barrier()
+            reps = max(1, e2e_steps // G2)
+            align_ranks(world, dev)
             e0.record(stream)
             for _ in range(reps):
                 g.replay()
             e1.record(stream)
             e1.synchronize()
-        e2e_graph = 64 * reps / (e0.elapsed_time(e1) / 1e3)
+        gms = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        if world > 1:
+            dist.all_reduce(gms, op=dist.ReduceOp.MAX)
+        e2e_graph = G2 * reps / (float(gms.item()) / 1e3)
         del g
         check_status(layers, "decode e2e (graph)")
     e2e_value = e2e_graph if e2e_graph is not None else e2e_per_call
     if e2e_graph is not None:
-        e2e_method = "public-API calls (mmrs_moe_block_forward_host) captured in a CUDA graph of 64 steps"
+        e2e_method = (f"public-API calls ({'mmrs_moe_block_forward_host' if group is None else 'mmrs_moe_block_forward_group_host'}) "
+                      f"captured in a CUDA graph of {G2} steps")
 
     # one token per step for the whole group (TP / EP split each token over the GPUs)
     value = steps / (ms_max / 1e3)

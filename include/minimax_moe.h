@@ -263,6 +263,17 @@ MMRS_API int mmrs_moe_block_forward_group(const MmrsMoeWeights *w, const MmrsPee
                                           void *workspace, size_t workspace_bytes, uint32_t token,
                                           mmrs_stream_t stream);
 
+/* No counterpart in the reference.  mmrs_moe_block_forward_group for a rank holding x and y in
+ * host memory, num_tokens * hidden floats each way, enqueued on `stream` in one call, as
+ * mmrs_moe_block_forward_host does on one GPU: pinned (mapped) host buffers are read by a small
+ * kernel into x_dev and written by the group's final stores directly; other host buffers go
+ * through copy-engine transfers via x_dev / y_dev.  Same token rules as the device form. */
+MMRS_API int mmrs_moe_block_forward_group_host(const MmrsMoeWeights *w, const MmrsPeerGroup *g,
+                                               const float *x_host, const float *residual, float *y_host,
+                                               int num_tokens, float *x_dev, float *y_dev, uint32_t *topk_ids,
+                                               float *topk_weights, void *workspace, size_t workspace_bytes,
+                                               uint32_t token, mmrs_stream_t stream);
+
 /* ===================================================================================== */
 /* 3. Seeded synthetic data (bench / test inputs; same generator as the numpy mirror)     */
 /* ===================================================================================== */

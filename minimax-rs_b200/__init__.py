@@ -110,6 +110,8 @@ PROTOTYPES = {
     "mmrs_peer_status": (_I, [C.POINTER(MmrsPeerGroup), _VP]),
     "mmrs_moe_block_forward_group": (_I, [C.POINTER(MmrsMoeWeights), C.POINTER(MmrsPeerGroup), _VP, _VP, _VP, _I,
                                           _VP, _VP, _VP, _SZ, _U32, _VP]),
+    "mmrs_moe_block_forward_group_host": (_I, [C.POINTER(MmrsMoeWeights), C.POINTER(MmrsPeerGroup), _VP, _VP, _VP,
+                                               _I, _VP, _VP, _VP, _VP, _VP, _SZ, _U32, _VP]),
     "mmrs_moe_workspace_bytes": (_SZ, [C.POINTER(MmrsMoeWeights), _I]),
     "mmrs_moe_workspace_zero_bytes": (_SZ, [C.POINTER(MmrsMoeWeights)]),
     "mmrs_int8_tensor_peak": (_I, [_I, _I, C.POINTER(C.c_double), _VP]),

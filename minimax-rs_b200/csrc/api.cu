@@ -485,6 +485,21 @@ __global__ void __launch_bounds__(256) host_in_kernel(const float4 *__restrict__
         dst[i] = src[i];
 }
 
+// n floats of x from host memory into x_dev on `s`: loads from the mapped pinned buffer by a small
+// kernel (the next launch then follows it on the device at once), else a copy-engine transfer.
+static int host_input(const float *x_host, float *x_dev, size_t n, cudaStream_t s) {
+    const void *xm = aligned16(x_host) ? mapped_host(x_host) : nullptr;
+    if (xm) {
+        const size_t n4 = n / 4;  // hidden is a multiple of 256
+        const unsigned blocks = (unsigned)std::min<size_t>((n4 + 255) / 256, 1184);
+        host_in_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const float4 *>(xm), reinterpret_cast<float4 *>(x_dev), n4);
+        return cudaGetLastError() == cudaSuccess ? MMRS_OK : MMRS_ERR_LAUNCH;
+    }
+    return cudaMemcpyAsync(x_dev, x_host, n * sizeof(float), cudaMemcpyHostToDevice, s) == cudaSuccess
+               ? MMRS_OK
+               : MMRS_ERR_LAUNCH;
+}
+
 extern "C" int mmrs_moe_block_forward_host(const MmrsMoeWeights *w, const float *x_host, const float *residual,
                                            float *y_host, int num_tokens, float *x_dev, float *y_dev,
                                            uint32_t *topk_ids, float *topk_weights, void *workspace,
@@ -493,24 +508,17 @@ extern "C" int mmrs_moe_block_forward_host(const MmrsMoeWeights *w, const float 
     if (rc != MMRS_OK) return rc;
     if (!x_host || !y_host || !x_dev || !y_dev || num_tokens < 0) return MMRS_ERR_ARG;
     if (num_tokens == 0) return MMRS_OK;
-    const size_t n = (size_t)num_tokens * w->hidden, bytes = n * sizeof(float);
+    const size_t n = (size_t)num_tokens * w->hidden;
     cudaStream_t s = (cudaStream_t)stream;
-    // input: loads from the mapped pinned buffer, else a copy-engine transfer
-    const void *xm = aligned16(x_host) ? mapped_host(x_host) : nullptr;
-    if (xm) {
-        const size_t n4 = n / 4;  // hidden is a multiple of 256
-        const unsigned blocks = (unsigned)std::min<size_t>((n4 + 255) / 256, 1184);
-        host_in_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const float4 *>(xm), reinterpret_cast<float4 *>(x_dev), n4);
-        if (cudaGetLastError() != cudaSuccess) return MMRS_ERR_LAUNCH;
-    } else if (cudaMemcpyAsync(x_dev, x_host, bytes, cudaMemcpyHostToDevice, s) != cudaSuccess) {
-        return MMRS_ERR_LAUNCH;
-    }
+    rc = host_input(x_host, x_dev, n, s);
+    if (rc != MMRS_OK) return rc;
     // output: the block's final stores go straight to the mapped pinned buffer, else via y_dev
     void *ym = aligned16(y_host) ? mapped_host(y_host) : nullptr;
     rc = mmrs_moe_block_forward(w, x_dev, residual, ym ? static_cast<float *>(ym) : y_dev, num_tokens, topk_ids,
                                 topk_weights, workspace, workspace_bytes, stream);
     if (rc != MMRS_OK || ym) return rc;
-    return cudaMemcpyAsync(y_host, y_dev, bytes, cudaMemcpyDeviceToHost, s) == cudaSuccess ? MMRS_OK : MMRS_ERR_LAUNCH;
+    return cudaMemcpyAsync(y_host, y_dev, n * sizeof(float), cudaMemcpyDeviceToHost, s) == cudaSuccess ? MMRS_OK
+                                                                                                      : MMRS_ERR_LAUNCH;
 }
 
 extern "C" int mmrs_moe_workspace_status(void *workspace, mmrs_stream_t stream) {
@@ -607,4 +615,27 @@ extern "C" int mmrs_moe_block_forward_group(const MmrsMoeWeights *w, const MmrsP
     rc = decode_configure(p, device_sms(), device_max_smem());
     if (rc != MMRS_OK) return rc;
     return decode_launch(p, s);
+}
+
+extern "C" int mmrs_moe_block_forward_group_host(const MmrsMoeWeights *w, const MmrsPeerGroup *g, const float *x_host,
+                                                 const float *residual, float *y_host, int num_tokens, float *x_dev,
+                                                 float *y_dev, uint32_t *topk_ids, float *topk_weights,
+                                                 void *workspace, size_t workspace_bytes, uint32_t token,
+                                                 mmrs_stream_t stream) {
+    int rc = validate_weights(w);
+    if (rc != MMRS_OK) return rc;
+    if (!g || !x_host || !y_host || !x_dev || !y_dev || num_tokens < 0) return MMRS_ERR_ARG;
+    if (num_tokens == 0) return MMRS_OK;
+    const size_t n = (size_t)num_tokens * w->hidden;
+    cudaStream_t s = (cudaStream_t)stream;
+    rc = host_input(x_host, x_dev, n, s);
+    if (rc != MMRS_OK) return rc;
+    // output: the group's final stores (the decode kernel's rank-ordered sums, or the peer
+    // all-reduce) go straight to the mapped pinned buffer, else via y_dev
+    void *ym = aligned16(y_host) ? mapped_host(y_host) : nullptr;
+    rc = mmrs_moe_block_forward_group(w, g, x_dev, residual, ym ? static_cast<float *>(ym) : y_dev, num_tokens, topk_ids,
+                                      topk_weights, workspace, workspace_bytes, token, stream);
+    if (rc != MMRS_OK || ym) return rc;
+    return cudaMemcpyAsync(y_host, y_dev, n * sizeof(float), cudaMemcpyDeviceToHost, s) == cudaSuccess ? MMRS_OK
+                                                                                                      : MMRS_ERR_LAUNCH;
 }

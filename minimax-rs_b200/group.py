@@ -157,6 +157,23 @@ class PeerGroup:
             raise MoeError(rc, "mmrs_moe_block_forward_group")
         return y
 
+    def forward_host(self, layer, x_host, y_host, x_dev, y_dev, residual=None, topk_ids=None, topk_w=None,
+                     token: int | None = None, stream=None):
+        """y_host = MoE(x_host) (+ residual) of the whole group in one library call
+        (mmrs_moe_block_forward_group_host): x_host / y_host in pinned host memory, x_dev / y_dev
+        device staging buffers of the same shape; residual / topk_* as in forward()."""
+        from . import _ptr, _stream
+        T = x_host.shape[0]
+        ws = layer.workspace(T)
+        tok = token if token is not None else self.tokens.next()
+        rc = lib().mmrs_moe_block_forward_group_host(C.byref(layer.c), C.byref(self.c), x_host.data_ptr(),
+                                                     _ptr(residual), y_host.data_ptr(), T, x_dev.data_ptr(),
+                                                     y_dev.data_ptr(), _ptr(topk_ids), _ptr(topk_w), ws.data_ptr(),
+                                                     ws.numel(), tok, _stream(stream))
+        if rc:
+            raise MoeError(rc, "mmrs_moe_block_forward_group_host")
+        return y_host
+
     def all_reduce(self, partial_writer, count: int, residual=None, y=None, stream=None):
         """Writes this rank's partial through partial_writer(ptr) then reduces over the group."""
         import torch

@@ -159,6 +159,47 @@ def test_group_decode_layers_round_robin(pkg, synth, orc, ep):
         assert np.linalg.norm((a - rr) - (ry - rr)) / np.linalg.norm(ry - rr) < 1e-4, (l, t)
 
 
+@needs2
+@pytest.mark.parametrize("ep", [False, True], ids=["tp2", "ep2"])
+@pytest.mark.parametrize("T", [1, 5])
+def test_group_forward_host_matches_device_form(pkg, synth, ep, T):
+    """mmrs_moe_block_forward_group_host (x and y in pinned host memory, one call) gives the device
+    form's output bit for bit, on two calls in a row."""
+    import torch
+    gm = _group_mod(pkg)
+    E, H, I = 16, 512, 512
+    L = make_layer(pkg, synth, torch.device("cuda", 0), E, H, I, Q4K, Q5K, seed=3600 + T, T=T, x_scale=0.05)
+    groups = gm.PeerGroup.local([0, 1], ar_capacity=T * H, expert_parallel=ep)
+    layers = _rank_layers(pkg, gm, L, 2, ep)
+    xs = [L["x"].to(f"cuda:{r}") for r in range(2)]
+    rs = [L["residual"].to(f"cuda:{r}") for r in range(2)]
+    x_host = [L["x"].cpu().pin_memory() for _ in range(2)]
+    y_host = [torch.empty(T, H, dtype=torch.float32).pin_memory() for _ in range(2)]
+    x_dev = [torch.empty(T, H, dtype=torch.float32, device=f"cuda:{r}") for r in range(2)]
+    y_dev = [torch.empty(T, H, dtype=torch.float32, device=f"cuda:{r}") for r in range(2)]
+    for r in range(2):
+        with torch.cuda.device(r):
+            layers[r].workspace(T)
+        torch.cuda.synchronize(r)
+    for call in range(2):
+        ref = []
+        for r in range(2):
+            with torch.cuda.device(r):
+                ref.append(groups[r].forward(layers[r], xs[r], residual=rs[r]))
+        for r in range(2):
+            with torch.cuda.device(r):
+                groups[r].forward_host(layers[r], x_host[r], y_host[r], x_dev[r], y_dev[r], residual=rs[r])
+        for r in range(2):
+            torch.cuda.synchronize(r)
+        for g in groups:
+            with torch.cuda.device(g._device):
+                assert g.status() == 0
+        for r in range(2):
+            assert torch.equal(y_host[r].view(torch.int32), ref[r].cpu().view(torch.int32)), (call, r)
+    for g in groups:
+        g.close()
+
+
 def _owner_counts(ids, world):
     return [sum(1 for e in ids if e % world == r) for r in range(world)]
 
