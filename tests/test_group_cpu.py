@@ -176,3 +176,40 @@ def test_peer_group_handshake_gloo():
         assert opened == [r for r in range(world) if r != rank]
         assert toks == [1, 2, 3]
         assert freed == [0x100000 * (rank + 1)]
+
+
+def test_group_forward_host_shares_the_token_sequence(gm, monkeypatch):
+    """The host-buffer form of the group block draws from the same monotonic token counter as the
+    device form, so the two may be mixed on one group without two calls sharing a token."""
+    seen = []
+
+    class Lib:
+        def mmrs_moe_block_forward_group(self, w, g, x, res, y, T, ids, wts, ws, nbytes, token, stream):
+            seen.append(("dev", T, token))
+            return 0
+
+        def mmrs_moe_block_forward_group_host(self, w, g, xh, res, yh, T, xd, yd, ids, wts, ws, nbytes, token,
+                                              stream):
+            seen.append(("host", T, token))
+            return 0
+
+    class Layer:
+        c = None
+
+        def workspace(self, T):
+            return torch.zeros(16, dtype=torch.uint8)
+
+    class Stream:
+        cuda_stream = 0
+
+    monkeypatch.setattr(gm, "lib", lambda: Lib())
+    monkeypatch.setattr(gm.C, "byref", lambda o: o)
+    grp = gm.PeerGroup.__new__(gm.PeerGroup)
+    grp.tokens, grp.c = gm.TokenCounter(), None
+    L = Layer()
+    x, y = torch.zeros(1, 8), torch.zeros(1, 8)
+    grp.forward(L, x, y=y, stream=Stream())
+    grp.forward_host(L, x, y, x, y, stream=Stream())
+    grp.forward_host(L, torch.zeros(3, 8), torch.zeros(3, 8), x, y, stream=Stream())
+    grp.forward(L, x, y=y, stream=Stream())
+    assert seen == [("dev", 1, 1), ("host", 1, 2), ("host", 3, 3), ("dev", 1, 4)]
